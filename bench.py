@@ -1,0 +1,453 @@
+"""Benchmark of the B200 EXL3 backend (driver contract: one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload W]
+
+Workloads (synthetic, seeded):
+* ``linears`` (default): the EXL3 linear layers of one decode step of the
+  Llama-70B-shaped model (config 4: 80 layers, hidden 8192, 64/8 heads x 128,
+  SwiGLU 28672, all linears 4 bpw 3INST) at batch 1: q/k/v/o/gate/up/down = 560
+  matmuls over 34.23 GB of trellis codes per step.  Inputs exceed L2, so no flush
+  is needed.  Under torchrun the step is tensor-parallel over N GPUs:
+  q/k/v/gate/up column-sharded, o/down row-sharded with an NCCL all-reduce.
+* ``gemv-c1``: config 1, one 4096x4096 4-bpw 3INST linear at M=1, rotating 40
+  weight copies (> 2x L2) between calls.
+
+``--impl reference`` times the reference's own CPU path for the same workload on
+the host cores: its compiled ``dequant_trellis`` + ``at::mm``
+(``csrc/bindings.cpp:15-147``, built into ``oracle/_ref`` by
+``oracle/build_ref.py``) on a bounded sample (one 4096x4096 linear per step),
+scaled to the workload's unit.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "sglang-exl3_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "decode tok/s (70B-shape 4bpw); EXL3 GEMV HBM GB/s vs roofline"
+
+# Llama-70B shape (config 4)
+L70 = dict(layers=80, hidden=8192, heads=64, kv_heads=8, head_dim=128, inter=28672, vocab=128256, K=4, cb=0)
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), float(d.get("bf16_tflops", 1590.0)), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.path or not os.path.exists(self.path):
+            return None
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = sorted(r[0] for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[2]) if v.lower().startswith("active")})
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": rows[0][1], "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+
+def dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(world, v: float) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+
+def make_linear(gen, k_in, n_out, K, device):
+    tr = torch.randint(-32768, 32768, (k_in // 16, n_out // 16, 16 * K), dtype=torch.int16, device=device,
+                       generator=gen)
+    su = ((torch.randint(0, 2, (k_in,), device=device, generator=gen) * 2 - 1).half()
+          * (torch.rand(k_in, device=device, generator=gen) + 0.5).half())
+    sv = ((torch.randint(0, 2, (n_out,), device=device, generator=gen) * 2 - 1).half()
+          * (torch.rand(n_out, device=device, generator=gen) + 0.5).half())
+    return tr, su, sv
+
+
+def linear_bytes(k_in, n_out, K, m):
+    return k_in * n_out * K // 8 + 2 * (m * k_in + m * n_out) + 2 * (k_in + n_out)
+
+
+def build_linear_stack(world, rank, device, batch):
+    """Per-rank shards of the 80-layer EXL3 linear stack (TP = world)."""
+    from exl3_b200 import ops  # noqa: F401
+
+    c = L70
+    H, I, K = c["hidden"], c["inter"], c["K"]
+    q_out = c["heads"] * c["head_dim"] // world
+    kv_out = c["kv_heads"] * c["head_dim"] // world
+    i_loc = I // world
+    h_in_loc = H // world  # row-parallel o input
+    gen = torch.Generator(device=device)
+    gen.manual_seed(3 + 1000 * rank)
+    layers = []
+    for _ in range(c["layers"]):
+        layers.append({
+            "q": make_linear(gen, H, q_out, K, device),
+            "k": make_linear(gen, H, kv_out, K, device),
+            "v": make_linear(gen, H, kv_out, K, device),
+            "o": make_linear(gen, h_in_loc, H, K, device),
+            "gate": make_linear(gen, H, i_loc, K, device),
+            "up": make_linear(gen, H, i_loc, K, device),
+            "down": make_linear(gen, i_loc, H, K, device),
+        })
+    shapes = [(H, q_out), (H, kv_out), (H, kv_out), (h_in_loc, H), (H, i_loc), (H, i_loc), (i_loc, H)]
+    step_bytes = c["layers"] * sum(linear_bytes(a, b, K, batch) for a, b in shapes)
+    bufs = {
+        "x": torch.randn(batch, H, dtype=torch.float16, device=device),
+        "qkv": torch.empty(batch, q_out + 2 * kv_out, dtype=torch.float16, device=device),
+        "attn": torch.randn(batch, h_in_loc, dtype=torch.float16, device=device),
+        "o": torch.empty(batch, H, dtype=torch.float16, device=device),
+        "gu": torch.empty(batch, 2 * i_loc, dtype=torch.float16, device=device),
+        "act": torch.empty(batch, i_loc, dtype=torch.float16, device=device),
+        "down": torch.empty(batch, H, dtype=torch.float16, device=device),
+    }
+    return layers, bufs, step_bytes, (q_out, kv_out, i_loc)
+
+
+def linear_stack_step(layers, bufs, dims, world, K, cb, group=None):
+    """One decode step's EXL3 matmuls (+ the TP all-reduces)."""
+    from exl3_b200 import ops
+
+    q_out, kv_out, i_loc = dims
+    x = bufs["x"]
+    for L in layers:
+        ops.matmul(x, *L["q"], K, cb, out=bufs["qkv"][:, :q_out])
+        ops.matmul(x, *L["k"], K, cb, out=bufs["qkv"][:, q_out:q_out + kv_out])
+        ops.matmul(x, *L["v"], K, cb, out=bufs["qkv"][:, q_out + kv_out:])
+        ops.matmul(bufs["attn"], *L["o"], K, cb, out=bufs["o"])
+        if world > 1:
+            torch.distributed.all_reduce(bufs["o"], group=group)
+        ops.matmul(x, *L["gate"], K, cb, out=bufs["gu"][:, :i_loc])
+        ops.matmul(x, *L["up"], K, cb, out=bufs["gu"][:, i_loc:])
+        g, u = bufs["gu"][:, :i_loc], bufs["gu"][:, i_loc:]
+        torch.mul(torch.nn.functional.silu(g), u, out=bufs["act"])
+        ops.matmul(bufs["act"], *L["down"], K, cb, out=bufs["down"])
+        if world > 1:
+            torch.distributed.all_reduce(bufs["down"], group=group)
+
+
+def time_graph(graph, steps, stream):
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(steps):
+        graph.replay()
+    end.record(stream)
+    end.synchronize()
+    return start.elapsed_time(end) / steps
+
+
+def isolated_kernel_time(tr_list, su_list, sv_list, K, cb, m, reps, device):
+    """Average device time of one small-M matmul launch pair (input + gemv) over
+    rotating weights, captured in a graph; returns ms per call."""
+    from exl3_b200 import ops
+
+    k_in = tr_list[0].size(0) * 16
+    n_out = tr_list[0].size(1) * 16
+    x = torch.randn(m, k_in, dtype=torch.float16, device=device)
+    out = torch.empty(m, n_out, dtype=torch.float16, device=device)
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        for i in range(3):
+            ops.matmul(x, tr_list[i % len(tr_list)], su_list[i % len(su_list)], sv_list[i % len(sv_list)], K, cb, out=out)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for i in range(len(tr_list)):
+                ops.matmul(x, tr_list[i], su_list[i], sv_list[i], K, cb, out=out)
+        g.replay()
+        t = time_graph(g, reps, s)
+    torch.cuda.current_stream(device).wait_stream(s)
+    return t / len(tr_list)
+
+
+def cpu_baseline_sample(steps_hint: int = 1):
+    """The reference's CPU path (compiled dequant_trellis + at::mm) on one config-1
+    linear (4096 x 4096, 4 bpw; the binding reaches only MCG/mul1, so MCG) - the
+    bounded sample.  Returns (seconds per linear, weights per linear, threads)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from build_ref import load_ref_module
+
+    ref = load_ref_module()
+    if ref is None:
+        return None
+    rng = np.random.default_rng(0)
+    tr = torch.from_numpy(rng.integers(-32768, 32768, size=(256, 256, 64)).astype(np.int16))
+    su = torch.from_numpy((np.where(rng.integers(0, 2, 4096) == 0, -1.0, 1.0) * rng.uniform(0.5, 1.5, 4096)).astype(np.float16))
+    sv = torch.from_numpy((np.where(rng.integers(0, 2, 4096) == 0, -1.0, 1.0) * rng.uniform(0.5, 1.5, 4096)).astype(np.float16))
+    x = torch.from_numpy(rng.standard_normal((1, 4096)).astype(np.float16))
+    ts = []
+    for _ in range(max(1, steps_hint)):
+        t0 = time.perf_counter()
+        ref.exl3_gemv(x, tr, su, sv, 4, True, 1)
+        ts.append(time.perf_counter() - t0)
+    return float(np.median(ts)), 4096 * 4096, torch.get_num_threads()
+
+
+# ---------------------------------------------------------------------------
+# arms
+# ---------------------------------------------------------------------------
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 3))
+    sample = cpu_baseline_sample(steps)
+    if sample is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (python oracle/build_ref.py)"}))
+        return
+    sec, weights, threads = sample
+    c = L70
+    if args.workload == "gemv-c1":
+        value, unit = (4096 * 4096 * 0.5) / sec / 1e9, "GB/s"
+        ms = sec * 1e3
+    else:
+        model_weights = c["layers"] * (2 * c["hidden"] ** 2 + 2 * c["hidden"] * c["kv_heads"] * c["head_dim"]
+                                       + 3 * c["hidden"] * c["inter"])
+        step_s = sec * model_weights / weights
+        value, unit = 1.0 / step_s, "tok/s"
+        ms = step_s * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp32 (reference CPU dequant + at::mm)", "data": "synthetic (seeded)",
+        "config": {"workload": args.workload, "sample": "one 4096x4096 4-bpw MCG linear per step, scaled by weight count"},
+        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "reference",
+                         "sample": "reference dequant_trellis + at::mm on one 4096x4096 linear (MCG: the binding cannot select 3INST)"},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+
+
+def run_ours(args, world, rank, local):
+    device = torch.device("cuda", local)
+    from exl3_b200 import ops
+
+    hbm_peak, tc_peak, peak_kind = peaks()
+    c = L70
+    K, cb = c["K"], c["cb"]
+    batch = args.batch
+    group = None
+    if args.workload == "gemv-c1":
+        if world > 1:
+            raise SystemExit("gemv-c1 is a single-GPU workload (replicas only)")
+        gen = torch.Generator(device=device)
+        gen.manual_seed(0)
+        copies = [make_linear(gen, 4096, 4096, 4, device) for _ in range(40)]
+        trs, sus, svs = zip(*copies)
+        for _ in range(args.warmup):
+            isolated_kernel_time(trs, sus, svs, 4, 0, batch, 2, device)
+        with ClockSampler(local) as clk:
+            ms = isolated_kernel_time(trs, sus, svs, 4, 0, batch, args.steps, device)
+        byts = linear_bytes(4096, 4096, 4, batch)
+        gbs = byts / (ms * 1e-3) / 1e9
+        line = {"metric": METRIC, "value": gbs, "unit": "GB/s", "ms_per_step": ms,
+                "config": {"workload": "gemv-c1", "m": batch, "l2": "40 rotating weight copies (336 MB > 2x L2)"},
+                "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                             "frac": gbs / hbm_peak, "traffic": None, "peak_kind": peak_kind},
+                "clocks": clk.summary()}
+        return finish(line, args, world)
+
+    layers, bufs, step_bytes, dims = build_linear_stack(world, rank, device, batch)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        linear_stack_step(layers, bufs, dims, world, K, cb, group)  # warm workspaces
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            linear_stack_step(layers, bufs, dims, world, K, cb, group)
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        with ClockSampler(local) as clk:
+            ms = time_graph(g, args.steps, s)
+        ms = max_over_ranks(world, ms)
+    torch.cuda.current_stream(device).wait_stream(s)
+    tok_s = batch / (ms * 1e-3)
+
+    # dominant kernel in isolation: the gate/up shape over the 80 layers' distinct copies
+    q_out, kv_out, i_loc = dims
+    trs = [L["gate"][0] for L in layers]
+    sus = [L["gate"][1] for L in layers]
+    svs = [L["gate"][2] for L in layers]
+    ms_k = isolated_kernel_time(trs, sus, svs, K, cb, batch, 5, device)
+    kb = linear_bytes(c["hidden"], i_loc, K, batch)
+    k_gbs = kb / (ms_k * 1e-3) / 1e9
+
+    # end to end through the public API: host x -> device, the 560 op calls, result -> host
+    pinned_x = torch.randn(batch, c["hidden"], dtype=torch.float16).pin_memory()
+    pinned_y = torch.empty(batch, c["hidden"], dtype=torch.float16).pin_memory()
+    e2e_steps = max(1, min(args.steps, 3))
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        bufs["x"].copy_(pinned_x, non_blocking=True)
+        linear_stack_step(layers, bufs, dims, world, K, cb, group)
+        pinned_y.copy_(bufs["down"], non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(world, (time.perf_counter() - t0) / e2e_steps * 1e3)
+
+    line = {
+        "metric": METRIC, "value": tok_s, "unit": "tok/s", "ms_per_step": ms,
+        "config": {"workload": "llama70b-shape decode step, EXL3 linears only (attention, norms, lm_head not included)",
+                   "model": "llama-70b-shape", "layers": c["layers"], "global_batch": batch, "seq_len": 1,
+                   "parallelism": f"tp{world}", "bpw": K, "codebook": "3INST",
+                   "l2": "no flush needed: 34.2 GB of codes per step >> 126 MB L2",
+                   "step_weight_bytes_per_rank": step_bytes},
+        "step_gbs_per_rank": step_bytes / (ms * 1e-3) / 1e9,
+        "roofline": {"bound": "hbm", "achieved": k_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": k_gbs / hbm_peak,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "kernel": f"exl3_gemv_kernel 8192x{i_loc} 4bpw M={batch} (input stage included)"},
+        "e2e": {"value": batch / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": pinned_x.numel() * 2, "d2h_bytes_per_step": pinned_y.numel() * 2,
+                "path": "exl3_b200.ops.matmul eager calls (no graph), host pinned x in, y out"},
+        "gpu_launches": 2 * 7 * c["layers"] * ((batch + 15) // 16),
+        "clocks": clk.summary(),
+    }
+    del g
+    return finish(line, args, world)
+
+
+def finish(line, args, world):
+    base = {"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp16 x 4-bit trellis -> fp32 acc",
+            "data": "synthetic (seeded random trellis codes, random-init)"}
+    base.update(line)
+    if int(os.environ.get("RANK", "0")) == 0:
+        if args.cpu_baseline:
+            sample = cpu_baseline_sample(1)
+            if sample is not None:
+                sec, weights, threads = sample
+                if base.get("unit") == "GB/s":
+                    v, u = weights * 0.5 / sec / 1e9, "GB/s"
+                else:
+                    c = L70
+                    model_weights = c["layers"] * (2 * c["hidden"] ** 2 + 2 * c["hidden"] * c["kv_heads"] * c["head_dim"]
+                                                   + 3 * c["hidden"] * c["inter"])
+                    v, u = 1.0 / (sec * model_weights / weights), "tok/s"
+                base["cpu_baseline"] = {"value": v, "unit": u, "cores": threads, "kind": "reference",
+                                        "sample": "reference dequant_trellis + at::mm, one 4096x4096 4-bpw MCG linear"}
+        print(json.dumps(base))
+    return base
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="linears", choices=["linears", "gemv-c1"])
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = ap.parse_args()
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,112 @@
+/*
+ * exl3_b200.h - C ABI of the B200-native EXL3 trellis-decode matmul library
+ * (libexl3b200.so).
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer, every
+ * stream argument a cudaStream_t passed as void*.  Functions return 0 on success
+ * or one of the EXL3B200_E* codes below; they never exit the process and never
+ * allocate device memory: outputs and workspaces are the caller's.  All work is
+ * enqueued on the given stream; nothing synchronises the host.
+ *
+ * Data formats are the reference's (vcruz305/sglang-exl3):
+ *   trellis  int16 [k/16, n/16, 16*K]   16x16 tiles of K-bit trellis codes
+ *            (src/sglang_exl3/dense.py:140-150, exl3.py:1987-2071)
+ *   suh      fp16 [k]   input sign/scale,  svh fp16 [n]  output sign/scale
+ *   K        bits per weight; cb codebook: 0 = 3INST, 1 = MCG, 2 = mul1
+ *            (the reference's bool mcg maps to cb 1 / cb 2, dense.py:151-157)
+ * The weight the codes stand for is W = diag(suh) H W_raw H diag(svh) / 128 with H
+ * the 128-point Walsh-Hadamard matrix, and the matmul ops compute y = x @ W.
+ */
+#ifndef EXL3_B200_H
+#define EXL3_B200_H
+
+#include <stddef.h>
+
+#if defined(__GNUC__)
+#define EXL3B200_API __attribute__((visibility("default")))
+#else
+#define EXL3B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define EXL3B200_OK 0
+#define EXL3B200_EBADSHAPE 1
+#define EXL3B200_EBADBITS 2
+#define EXL3B200_EBADCODEBOOK 3
+#define EXL3B200_EUNALIGNED 4
+#define EXL3B200_ELAUNCH 5
+#define EXL3B200_EWORKSPACE 6
+#define EXL3B200_ENULL 7
+#define EXL3B200_EBADARG 8
+#define EXL3B200_ETIMEOUT 9
+
+/* output dtypes */
+#define EXL3B200_DTYPE_F16 0
+#define EXL3B200_DTYPE_BF16 1
+#define EXL3B200_DTYPE_F32 2
+
+/* flags of the matmul entry points */
+#define EXL3B200_FLAG_INPUT_ROTATED 1 /* x is already H128(x*suh)/sqrt(128) in fp16; suh unused */
+#define EXL3B200_FLAG_NO_FOLD 2       /* decode the fp16 codebook add in ALU instead of the MMA */
+
+/* largest row count of the small-M matmul */
+#define EXL3B200_GEMV_MAX_M 16
+
+/* ABI version of this header (the reference exposes P2B_MOE_ABI_VERSION = 2,
+ * csrc/bindings.cpp:170; this library's ABI is versioned separately) */
+#define EXL3B200_ABI_VERSION 1
+
+EXL3B200_API int exl3b200_abi_version(void);
+EXL3B200_API const char* exl3b200_status_string(int status);
+
+/*
+ * Reconstruct the fp16 weight W [k, n] (row-major) from its trellis.
+ * Replaces sglang_exl3_c.dequant_trellis (reference csrc/bindings.cpp:117-132,
+ * op signature src/sglang_exl3/ops.py:38-54).  k and n must be multiples of 128,
+ * K in 1..8.  rounding 0: codebook rounded to nearest, as the reference's device
+ * decode (csrc/quant/codebook.cuh); rounding 1: truncated, bit-identical to the
+ * reference's CPU dequant_trellis output (csrc/exl3_dequant.cuh:41-93).
+ */
+EXL3B200_API int exl3b200_dequant(const void* trellis, int k_tiles, int n_tiles, int K, int cb,
+                     const void* suh, const void* svh, void* out, int rounding, void* stream);
+
+/*
+ * Small-M matmul: out[m, n] = x[m, k] @ W for 1 <= m <= 16.
+ * Replaces sglang_exl3_c.exl3_gemv (reference csrc/bindings.cpp:134-147,
+ * csrc/exl3_gemv.cu:26-63; op src/sglang_exl3/ops.py:57-74) and the row chunks of
+ * exl3_gemm (csrc/exl3_gemm.cu:9-31).  x fp16 with row stride x_stride elements;
+ * out in out_dtype with row stride out_stride elements (so outputs can be written
+ * into a slice of a wider buffer).  K in 2..4, k and n multiples of 128.
+ *
+ * state:   exl3b200_gemv_state_size(n) bytes, 256-byte aligned, ZEROED once when
+ *          allocated; every call leaves it zeroed again.  Calls that may run
+ *          concurrently (different streams) need distinct state buffers.
+ * scratch: exl3b200_gemv_scratch_size(m, k) bytes, 256-byte aligned, no
+ *          initialisation; also per concurrent stream.
+ */
+EXL3B200_API size_t exl3b200_gemv_state_size(int n);
+EXL3B200_API size_t exl3b200_gemv_scratch_size(int m, int k);
+EXL3B200_API int exl3b200_gemv(const void* x, long long x_stride, int m, int k, const void* trellis, int n, int K,
+                  int cb, const void* suh, const void* svh, void* out, long long out_stride,
+                  int out_dtype, int flags, void* state, size_t state_bytes, void* scratch,
+                  size_t scratch_bytes, void* stream);
+
+/*
+ * out[m, k] = H128(x * suh) / sqrt(128) in fp16 over 128-element blocks of each row,
+ * with the reference's roundings (fp16 product, float transform, one fp16
+ * rounding: had_hf_r_128_inner<true,false>, csrc/quant/hadamard_inner.cuh:93-147).
+ * suh may be NULL (no pre-scale).  Replaces the upstream exllamav3 had_r_128 that
+ * the reference's fat-GEMM path calls (src/sglang_exl3/exl3.py:1184-1193).
+ */
+EXL3B200_API int exl3b200_hadamard_in(const void* x, long long x_stride, int m, int k, const void* suh,
+                                      void* out, long long out_stride, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXL3_B200_H */

@@ -1,0 +1,10 @@
+// Internal include for the C-ABI translation units: the public header plus the
+// standard headers the host-side launch code needs.
+#pragma once
+
+#include <algorithm>
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "exl3_b200.h"

@@ -1,0 +1,84 @@
+"""ctypes binding of ``libexl3b200.so`` (declared in ``include/exl3_b200.h``).
+
+The library is the only compute path: if it is missing or fails to load, every
+op raises; there is no CPU or eager-torch fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libexl3b200.so")
+
+OK = 0
+STATUS_NAMES = {
+    0: "EXL3B200_OK",
+    1: "EXL3B200_EBADSHAPE",
+    2: "EXL3B200_EBADBITS",
+    3: "EXL3B200_EBADCODEBOOK",
+    4: "EXL3B200_EUNALIGNED",
+    5: "EXL3B200_ELAUNCH",
+    6: "EXL3B200_EWORKSPACE",
+    7: "EXL3B200_ENULL",
+    8: "EXL3B200_EBADARG",
+    9: "EXL3B200_ETIMEOUT",
+}
+
+DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
+FLAG_INPUT_ROTATED = 1
+FLAG_NO_FOLD = 2
+GEMV_MAX_M = 16
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_ll = ctypes.c_longlong
+_sz = ctypes.c_size_t
+
+# name -> (restype, argtypes); one entry per declaration in include/exl3_b200.h
+SIGNATURES = {
+    "exl3b200_abi_version": (_i, []),
+    "exl3b200_status_string": (ctypes.c_char_p, [_i]),
+    "exl3b200_dequant": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp]),
+    "exl3b200_gemv_state_size": (_sz, [_i]),
+    "exl3b200_gemv_scratch_size": (_sz, [_i, _i]),
+    "exl3b200_gemv": (_i, [_vp, _ll, _i, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _ll, _i, _i, _vp, _sz, _vp, _sz, _vp]),
+    "exl3b200_hadamard_in": (_i, [_vp, _ll, _i, _i, _vp, _vp, _ll, _vp]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+class Exl3LibraryError(RuntimeError):
+    pass
+
+
+def lib() -> ctypes.CDLL:
+    """Load (once) and return the CUDA library; raise if it is not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise Exl3LibraryError(
+                    f"{LIB_PATH} is not built; run `python sglang-exl3_b200/build.py`. "
+                    "The EXL3 B200 ops have no CPU fallback.")
+            L = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().exl3b200_status_string(int(status)).decode()
+
+
+def check(status: int, what: str) -> None:
+    if status != OK:
+        raise RuntimeError(f"{what} failed: {status_string(status)} ({STATUS_NAMES.get(status, status)})")

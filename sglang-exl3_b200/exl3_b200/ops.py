@@ -1,0 +1,236 @@
+"""Tensor-level EXL3 ops over the C ABI, with the reference's op surface.
+
+Functions here take torch tensors, validate them with the reference's error
+messages (``TORCH_CHECK`` -> ``RuntimeError``), fetch persistent workspaces and
+call ``libexl3b200.so`` on the current CUDA stream.  ``register_custom_ops``
+registers them as ``torch.ops.sglang_exl3.*`` with the schemas and fake kernels
+of the reference (``src/sglang_exl3/ops.py:29-230``), so callers written for the
+reference run unchanged.
+
+Codebook selection: the reference ops take ``mcg: bool`` and reach only MCG
+(cb 1) or mul1 (cb 2) (``csrc/bindings.cpp:48``, ``csrc/exl3_gemv.cu:32``).  Every
+op here also accepts ``cb`` (0 = 3INST, 1 = MCG, 2 = mul1); ``cb=None`` keeps
+the legacy mapping.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import _lib
+from . import workspace
+
+_OUT_DTYPES = {torch.float16: _lib.DTYPE_F16, torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
+
+
+def codebook_id(mcg: bool = False, mul1: bool = False, cb: Optional[int] = None) -> int:
+    """Codebook id from the reference's flags (``dense.py:151-157``): explicit cb wins."""
+    if cb is not None and int(cb) >= 0:
+        if int(cb) not in (0, 1, 2):
+            raise RuntimeError(f"unsupported EXL3 codebook {cb}")
+        return int(cb)
+    if mcg and mul1:
+        raise ValueError("EXL3 linear has both mcg and mul1 markers set")
+    return 1 if mcg else (2 if mul1 else 0)
+
+
+def legacy_codebook(mcg: bool, cb: Optional[int] = None) -> int:
+    """The ``sglang_exl3_c`` binding's mapping: mcg -> 1, else mul1 (2)."""
+    if cb is not None and int(cb) >= 0:
+        return codebook_id(cb=cb)
+    return 1 if mcg else 2
+
+
+def bits_of(trellis: torch.Tensor) -> int:
+    """K from the trellis' last dimension (16*K int16 per tile, ``dense.py:149-150``)."""
+    k = trellis.shape[-1] // 16
+    if trellis.shape[-1] != 16 * k:
+        raise RuntimeError("trellis last dimension must be 16*K")
+    return int(k)
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    dev = tensors[0].device
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError("EXL3 B200 ops require CUDA tensors (there is no CPU path)")
+        if t.device != dev:
+            raise RuntimeError("EXL3 tensors must share a CUDA device")
+    return dev
+
+
+# ---------------------------------------------------------------------------
+# dequant
+# ---------------------------------------------------------------------------
+
+def dequant(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: Optional[int] = None,
+            cb: int = 0, rounding: str = "rn", out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp16 weight ``W [k, n]`` with ``y = x @ W``.  ``rounding="rn"``: codebook
+    rounded to nearest (reference device decode); ``"trunc"``: bit-identical to
+    the reference's CPU ``dequant_trellis`` (``csrc/bindings.cpp:15-132``)."""
+    if K is None:
+        K = bits_of(trellis)
+    if K not in range(1, 9):
+        raise RuntimeError("K must be one of 1..8")
+    if trellis.dim() != 3 or trellis.dtype != torch.int16:
+        raise RuntimeError("trellis must be int16 [rows/16, cols/16, 16*K]")
+    if trellis.size(2) != 16 * K:
+        raise RuntimeError("trellis last dimension must be 16*K")
+    if trellis.size(0) <= 0 or trellis.size(1) <= 0:
+        raise RuntimeError("trellis dimensions must be positive")
+    if suh.dtype != torch.float16 or svh.dtype != torch.float16:
+        raise RuntimeError("suh and svh must be float16")
+    rows, cols = trellis.size(0) * 16, trellis.size(1) * 16
+    if suh.numel() < rows or svh.numel() < cols:
+        raise RuntimeError("suh/svh are too short")
+    if rows % 128 or cols % 128:
+        raise RuntimeError("trellis dimensions must reconstruct whole 128-element Hadamard blocks")
+    dev = _require_cuda(trellis, suh, svh)
+    trellis, suh, svh = trellis.contiguous(), suh.contiguous(), svh.contiguous()
+    if out is None:
+        out = torch.empty((rows, cols), dtype=torch.float16, device=dev)
+    mode = {"rn": 0, "trunc": 1}[rounding]
+    with torch.cuda.device(dev):
+        st = _lib.lib().exl3b200_dequant(trellis.data_ptr(), trellis.size(0), trellis.size(1), K, cb,
+                                         suh.data_ptr(), svh.data_ptr(), out.data_ptr(), mode, _stream_ptr(dev))
+    _lib.check(st, "exl3b200_dequant")
+    return out
+
+
+# ---------------------------------------------------------------------------
+# input transform
+# ---------------------------------------------------------------------------
+
+def hadamard_in(x: torch.Tensor, suh: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """fp16 ``H128(x * suh) / sqrt(128)`` over 128-blocks of the last dimension."""
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.dtype != torch.float16:
+        raise RuntimeError("hadamard_in requires fp16 input")
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    m, k = x2.shape
+    dev = _require_cuda(x2) if suh is None else _require_cuda(x2, suh)
+    if out is None:
+        out = torch.empty((m, k), dtype=torch.float16, device=dev)
+    with torch.cuda.device(dev):
+        st = _lib.lib().exl3b200_hadamard_in(x2.data_ptr(), x2.stride(0), m, k,
+                                             suh.contiguous().data_ptr() if suh is not None else None,
+                                             out.data_ptr(), out.stride(0), _stream_ptr(dev))
+    _lib.check(st, "exl3b200_hadamard_in")
+    return out.view(*x.shape[:-1], k)
+
+
+# ---------------------------------------------------------------------------
+# matmul
+# ---------------------------------------------------------------------------
+
+def _gemv_into(x2: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], svh: torch.Tensor,
+               K: int, cb: int, out: torch.Tensor, flags: int) -> None:
+    m, k = x2.shape
+    n = trellis.size(1) * 16
+    dev = x2.device
+    L = _lib.lib()
+    state_n = L.exl3b200_gemv_state_size(n)
+    scratch_n = L.exl3b200_gemv_scratch_size(m, k)
+    with torch.cuda.device(dev):
+        state = workspace.state_buffer(dev, state_n)
+        scratch = workspace.scratch_buffer(dev, scratch_n)
+        st = L.exl3b200_gemv(x2.data_ptr(), x2.stride(0), m, k, trellis.data_ptr(), n, K, cb,
+                             suh.data_ptr() if suh is not None else None, svh.data_ptr(),
+                             out.data_ptr(), out.stride(0), _OUT_DTYPES[out.dtype], flags,
+                             state.data_ptr(), state.numel(), scratch.data_ptr(), scratch.numel(),
+                             _stream_ptr(dev))
+    _lib.check(st, "exl3b200_gemv")
+
+
+def _check_linear(x2: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int):
+    if x2.dtype != torch.float16:
+        raise RuntimeError("CUDA GEMV requires fp16 input")
+    if trellis.dim() != 3 or trellis.dtype != torch.int16:
+        raise RuntimeError("trellis must be int16 [rows/16, cols/16, 16*K]")
+    if trellis.size(2) != 16 * K:
+        raise RuntimeError("trellis last dimension must be 16*K")
+    if x2.size(-1) != trellis.size(0) * 16:
+        raise RuntimeError("x feature dimension does not match trellis")
+    if svh.numel() != trellis.size(1) * 16:
+        raise RuntimeError("svh N dimension does not match trellis")
+    if suh is not None and suh.numel() != trellis.size(0) * 16:
+        raise RuntimeError("suh K dimension does not match trellis")
+
+
+def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], svh: torch.Tensor,
+           K: Optional[int] = None, cb: int = 0, out_dtype: torch.dtype = torch.float16,
+           out: Optional[torch.Tensor] = None, input_rotated: bool = False, fold: bool = True) -> torch.Tensor:
+    """``y = x @ W`` for any number of rows: ``x [..., k]`` fp16 -> ``[..., n]``.
+
+    Rows go to the small-M kernel in chunks of at most 16 (replaces
+    ``exl3_gemm_cuda``'s chunks of 8, ``csrc/exl3_gemm.cu:20-29``).  ``out`` may be a
+    row-strided 2D view (e.g. a column slice of a fused qkv output)."""
+    if K is None:
+        K = bits_of(trellis)
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1 or (x2.stride(0) % 2):
+        x2 = x2.contiguous()
+    _check_linear(x2, trellis, suh, svh, K)
+    dev = _require_cuda(x2, trellis, svh)
+    m = x2.size(0)
+    n = trellis.size(1) * 16
+    if out is None:
+        out2 = torch.empty((m, n), dtype=out_dtype, device=dev)
+    else:
+        out2 = out.reshape(m, n) if out.dim() != 2 else out
+        if out2.stride(-1) != 1:
+            raise RuntimeError("out must have unit stride in its last dimension")
+        if out2.dtype not in _OUT_DTYPES:
+            raise RuntimeError("out must be fp16, bf16 or fp32")
+    flags = (_lib.FLAG_INPUT_ROTATED if input_rotated else 0) | (0 if fold else _lib.FLAG_NO_FOLD)
+    for r0 in range(0, m, _lib.GEMV_MAX_M):
+        r1 = min(m, r0 + _lib.GEMV_MAX_M)
+        _gemv_into(x2[r0:r1], trellis, suh, svh, K, cb, out2[r0:r1], flags)
+    if out is not None:
+        return out
+    return out2.view(*lead, n)
+
+
+# ---------------------------------------------------------------------------
+# reference-named entry points (semantics of sglang_exl3_c, csrc/bindings.cpp)
+# ---------------------------------------------------------------------------
+
+def dequant_trellis(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, bits: int, mcg: bool,
+                    cb: Optional[int] = None, rounding: str = "trunc") -> torch.Tensor:
+    """``sglang_exl3_c.dequant_trellis`` (``csrc/bindings.cpp:117-132``).  The
+    reference op's output is the truncating CPU decode; ``rounding="trunc"`` (the
+    default here) reproduces it bit for bit, ``"rn"`` gives the device decode."""
+    if bits not in (2, 3, 4, 8) and cb is None:
+        raise RuntimeError("K must be one of 2, 3, 4, or 8")
+    return dequant(trellis, suh, svh, int(bits), legacy_codebook(mcg, cb), rounding)
+
+
+def exl3_gemv(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
+              mcg: bool, mmode: int = 1, cb: Optional[int] = None) -> torch.Tensor:
+    """``sglang_exl3_c.exl3_gemv`` (``csrc/bindings.cpp:134-147``): fp16 ``[m, n]``,
+    1 <= m <= 16 (the reference allows 8)."""
+    if x.dim() < 2:
+        raise RuntimeError("x must have shape [..., in_features]")
+    m = x.numel() // x.size(-1)
+    if not (1 <= m <= _lib.GEMV_MAX_M):
+        raise RuntimeError(f"native GEMV supports 1 <= m <= {_lib.GEMV_MAX_M}")
+    if x.size(-1) != trellis.size(0) * 16:
+        raise RuntimeError("x feature dimension does not match trellis")
+    if mmode not in (0, 1):
+        raise RuntimeError("mmode must be 0 or 1")
+    return matmul(x.reshape(m, x.size(-1)), trellis, suh, svh, int(K), legacy_codebook(mcg, cb))
+
+
+def exl3_gemm(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
+              mcg: bool, cb: Optional[int] = None) -> torch.Tensor:
+    """``sglang_exl3_c.exl3_gemm`` (``csrc/exl3_gemm.cu:9-31``): fp16 ``[m, n]``."""
+    x2 = x.contiguous().view(x.numel() // x.size(-1), x.size(-1))
+    return matmul(x2, trellis, suh, svh, int(K), legacy_codebook(mcg, cb))
