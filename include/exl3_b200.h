@@ -51,7 +51,6 @@ extern "C" {
 
 /* flags of the matmul entry points */
 #define EXL3B200_FLAG_INPUT_ROTATED 1 /* x is already H128(x*suh)/sqrt(128) in fp16; suh unused */
-#define EXL3B200_FLAG_NO_FOLD 2       /* decode the fp16 codebook add in ALU instead of the MMA */
 
 /* largest row count of the small-M matmul */
 #define EXL3B200_GEMV_MAX_M 16

@@ -172,21 +172,66 @@ __device__ __forceinline__ LaneWords lane_words(int lane)
     return lw;
 }
 
-// The 8 windows of a lane (j = 0..7) from its two words.
+// Clean 16-bit window at bit offset off (0..16) of v: shift it to the top, then
+// take the top half with one byte permute.  The left shift can issue on the FMA
+// pipe (IMAD.SHL), which keeps the integer-logic pipe (half rate on sm_100) free.
+template <int OFF>
+__device__ __forceinline__ uint32_t win_at(uint32_t v)
+{
+    static_assert(OFF >= 0 && OFF <= 16, "window offset");
+    if constexpr (OFF == 0) return v & 0xffffu;
+    else if constexpr (OFF == 8) return prmt(v, 0u, 0x4421);
+    else if constexpr (OFF == 16) return prmt(v, 0u, 0x4432);
+    else return prmt(v << (16 - OFF), 0u, 0x4432);
+}
+
+__device__ __forceinline__ uint32_t win_at_rt(uint32_t v, uint32_t mul)
+{
+    // mul = 2^(16 - off), a per-lane constant
+    return prmt(v * mul, 0u, 0x4432);
+}
+
+// The 8 windows of a lane (j = 0..7) from its two words a (earlier in the
+// stream) and b.  Window j sits at offset shift7 + (7-j)*K of the 64-bit (a:b).
 template <int K>
 __device__ __forceinline__ void lane_windows(uint32_t a, uint32_t b, int shift7, uint32_t (&w)[8])
 {
     if constexpr (K == 4) {
-        // shift7 is 0 for every lane: windows at nibble offsets of (a:b)
-        w[7] = b & 0xffffu;
-        w[6] = (b >> 4) & 0xffffu;
-        w[5] = prmt(b, 0u, 0x4421);            // bytes 1,2 of b
-        w[4] = (b >> 12) & 0xffffu;
-        w[3] = b >> 16;
-        const uint32_t s = __funnelshift_r(b, a, 20);
-        w[2] = s & 0xffffu;
-        w[1] = prmt(b, a, 0x4443) & 0xffffu;    // byte 3 of b, byte 0 of a
-        w[0] = (s >> 8) & 0xffffu;
+        // shift7 is 0 for every lane; offsets 0,4,...,28
+        const uint32_t c = __funnelshift_r(b, a, 16);  // bits 16..47 of (a:b)
+        w[7] = win_at<0>(b);
+        w[6] = win_at<4>(b);
+        w[5] = win_at<8>(b);
+        w[4] = win_at<12>(b);
+        w[3] = win_at<16>(b);
+        w[2] = win_at<4>(c);
+        w[1] = win_at<8>(c);
+        w[0] = win_at<12>(c);
+    } else if constexpr (K == 2) {
+        // shift7 in {0, 16}; offsets shift7 + 0,2,...,14
+        const uint32_t v = __funnelshift_r(b, a, shift7);
+        w[7] = win_at<0>(v);
+        w[6] = win_at<2>(v);
+        w[5] = win_at<4>(v);
+        w[4] = win_at<6>(v);
+        w[3] = win_at<8>(v);
+        w[2] = win_at<10>(v);
+        w[1] = win_at<12>(v);
+        w[0] = win_at<14>(v);
+    } else if constexpr (K == 3) {
+        // shift7 in 0..31 per lane; offsets shift7 + 0,3,...,21 (<= 52)
+        const uint64_t pr = ((uint64_t) a << 32) | (uint64_t) b;
+        const uint64_t t = pr >> shift7;
+        const uint32_t v0 = (uint32_t) t;
+        const uint32_t v1 = __funnelshift_r(v0, (uint32_t) (t >> 32), 16);  // offsets 16..47
+        w[7] = win_at<0>(v0);
+        w[6] = win_at<3>(v0);
+        w[5] = win_at<6>(v0);
+        w[4] = win_at<9>(v0);
+        w[3] = win_at<12>(v0);
+        w[2] = win_at<15>(v0);
+        w[1] = win_at<2>(v1);
+        w[0] = win_at<5>(v1);
     } else {
         const uint64_t v = ((uint64_t) a << 32) | (uint64_t) b;
 #pragma unroll

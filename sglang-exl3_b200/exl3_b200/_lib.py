@@ -28,7 +28,6 @@ STATUS_NAMES = {
 
 DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 FLAG_INPUT_ROTATED = 1
-FLAG_NO_FOLD = 2
 GEMV_MAX_M = 16
 
 _vp = ctypes.c_void_p

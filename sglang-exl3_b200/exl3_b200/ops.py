@@ -166,7 +166,8 @@ def _check_linear(x2: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, sv
 
 def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], svh: torch.Tensor,
            K: Optional[int] = None, cb: int = 0, out_dtype: torch.dtype = torch.float16,
-           out: Optional[torch.Tensor] = None, input_rotated: bool = False, fold: bool = True) -> torch.Tensor:
+           out: Optional[torch.Tensor] = None, input_rotated: bool = False,
+           variant: Optional[int] = None) -> torch.Tensor:
     """``y = x @ W`` for any number of rows: ``x [..., k]`` fp16 -> ``[..., n]``.
 
     Rows go to the small-M kernel in chunks of at most 16 (replaces
@@ -190,7 +191,9 @@ def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], 
             raise RuntimeError("out must have unit stride in its last dimension")
         if out2.dtype not in _OUT_DTYPES:
             raise RuntimeError("out must be fp16, bf16 or fp32")
-    flags = (_lib.FLAG_INPUT_ROTATED if input_rotated else 0) | (0 if fold else _lib.FLAG_NO_FOLD)
+    flags = _lib.FLAG_INPUT_ROTATED if input_rotated else 0
+    if variant is not None:
+        flags |= (int(variant) & 3) << 8
     for r0 in range(0, m, _lib.GEMV_MAX_M):
         r1 = min(m, r0 + _lib.GEMV_MAX_M)
         _gemv_into(x2[r0:r1], trellis, suh, svh, K, cb, out2[r0:r1], flags)

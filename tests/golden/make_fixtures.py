@@ -18,8 +18,8 @@ Fixtures (inputs are seeded; outputs come from the reference's own code):
   ``csrc/bindings.cpp:134-147``) on a seeded small case.
 * ``ref_device_decode.npz`` - the reference's device decode functions
   (``decode_3inst<cb>``, ``dq_dispatch<K, cb>``) run on a B200 by
-  ``oracle/_ref/ref_codebook_dump``: the three codebook tables and 64 tiles per K
-  in 1..8, converted from the raw dump.
+  ``oracle/_ref/ref_codebook_dump``: the three codebook tables and the first 16 of the
+  dump's 64 tiles per K in 1..8.
 """
 
 from __future__ import annotations
@@ -104,6 +104,10 @@ def convert_device_dump(path: str) -> None:
             off += ntiles * 256 * 2
     if off != len(raw):
         raise SystemExit(f"{path}: {len(raw) - off} trailing bytes")
+    # keep the full tables and the first 16 tiles per K (the dump holds 64)
+    for key in list(arrays):
+        if key.startswith(("tiles_", "decoded_")):
+            arrays[key] = arrays[key][:16]
     np.savez_compressed(os.path.join(HERE, "ref_device_decode.npz"), **arrays)
 
 

@@ -51,15 +51,6 @@ def test_gemv_parity(cuda_device, K, cb, m):
     assert O.normwise_rel_err(y.float().cpu().numpy(), ref) < TOL_F32_ACC
 
 
-@pytest.mark.parametrize("K", [2, 3, 4])
-@pytest.mark.parametrize("cb", [0, 1])
-def test_gemv_no_fold_parity(cuda_device, K, cb):
-    x, tr, su, sv = _case(7 + K + cb, 5, 256, 256, K)
-    y = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), K, cb,
-                   fold=False)
-    assert O.normwise_rel_err(y.float().cpu().numpy(), O.gemv_ref(x, tr, su, sv, K, cb)) < TOL_F32_ACC
-
-
 def test_gemv_c1_shape(cuda_device):
     """Config 1: K = N = 4096, 4 bpw, 3INST, seed 0, x ~ N(0, 1) [1, 4096]."""
     x, tr, su, sv = _case(0, 1, 4096, 4096, 4)
