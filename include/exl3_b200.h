@@ -54,6 +54,8 @@ extern "C" {
 
 /* largest row count of the small-M matmul */
 #define EXL3B200_GEMV_MAX_M 16
+/* most linears in one exl3b200_gemv_multi call */
+#define EXL3B200_MULTI_MAX 8
 
 /* ABI version of this header (the reference exposes P2B_MOE_ABI_VERSION = 2,
  * csrc/bindings.cpp:170; this library's ABI is versioned separately) */
@@ -93,6 +95,77 @@ EXL3B200_API int exl3b200_gemv(const void* x, long long x_stride, int m, int k, 
                   int cb, const void* suh, const void* svh, void* out, long long out_stride,
                   int out_dtype, int flags, void* state, size_t state_bytes, void* scratch,
                   size_t scratch_bytes, void* stream);
+
+/*
+ * Small-M matmul with a routed, weighted fp32 accumulation instead of a store:
+ * out[out_rows[r], :] += (out_scale ? out_scale[r] : 1) * (x[r] @ W) for r < m.
+ * out_rows (int32) and out_scale (fp32) are DEVICE arrays of m entries; rows of
+ * one call must be distinct.  Replaces sglang_exl3_c.exl3_fat_gemm_scatter's
+ * accumulation (reference csrc/exl3_fat_gemm.cu:177-190) for small row counts.
+ * Workspaces as for exl3b200_gemv.
+ */
+EXL3B200_API int exl3b200_gemv_combine(const void* x, long long x_stride, int m, int k, const void* trellis, int n,
+                                       int K, int cb, const void* suh, const void* svh, float* out,
+                                       long long out_stride, const int* out_rows, const float* out_scale,
+                                       int flags, void* state, size_t state_bytes, void* scratch,
+                                       size_t scratch_bytes, void* stream);
+
+/*
+ * Several linears over one input in a single launch sequence: out_i = x @ W_i for
+ * i < count (count <= EXL3B200_MULTI_MAX), all with the same K, codebook and k.
+ * Replaces the upstream exllamav3 exl3_mgemm pair GEMM the reference calls for
+ * merged gate_up / k,v projections (src/sglang_exl3/dense.py:91-119,345-357) and
+ * serves fused q/k/v.  Arrays are host arrays of device pointers.  state:
+ * sum over i of exl3b200_gemv_state_size(n[i]) bytes, zeroed once; scratch:
+ * count * exl3b200_gemv_scratch_size(m, k) bytes.
+ */
+EXL3B200_API int exl3b200_gemv_multi(int count, const void* x, long long x_stride, int m, int k, int K, int cb,
+                                     const void* const* trellis, const int* n, const void* const* suh,
+                                     const void* const* svh, void* const* out, const long long* out_stride,
+                                     int out_dtype, int flags, void* state, size_t state_bytes, void* scratch,
+                                     size_t scratch_bytes, void* stream);
+
+/*
+ * Batched experts: out[e] = x_e @ W_{expert_ids[e]} for e < count, out laid out
+ * [count][m][n] in out_dtype; x_e = x (x_per_expert 0) or x + e*m*x_stride.
+ * trellis/suh/svh_ptrs are DEVICE int64 tables of device pointers indexed by
+ * expert id (table_size entries); expert_ids is a DEVICE int32 list read on the
+ * device (ids are clamped to the table).  Replaces sglang_exl3_c.p2b_gemv_batched
+ * (reference csrc/p2b_batched.cu:13-101, op src/sglang_exl3/ops.py:96-118) for
+ * any codebook.  state: exl3b200_batched_state_size bytes, zeroed once.
+ */
+EXL3B200_API size_t exl3b200_batched_state_size(int count, int m, int n);
+EXL3B200_API size_t exl3b200_batched_scratch_size(int count, int m, int k);
+EXL3B200_API int exl3b200_batched_gemv(const void* x, int x_per_expert, long long x_stride, int m, int k, int n,
+                                       int K, int cb, const long long* trellis_ptrs, const long long* suh_ptrs,
+                                       const long long* svh_ptrs, int table_size, const int* expert_ids, int count,
+                                       void* out, int out_dtype, void* state, size_t state_bytes, void* scratch,
+                                       size_t scratch_bytes, void* stream);
+
+/*
+ * Routed SwiGLU MoE for tokens <= max_tokens rows of x [tokens, hidden] (fp16):
+ *   out[t] (+)= sum_j w[t,j] * down_e(silu(min(gate_e x_t, L)) * clamp(up_e x_t, -L, L)),
+ *   e = topk_ids[t, j], w = topk_weights[t, j]; ids outside [0, num_experts) are
+ *   skipped.  L = swiglu_limit (0 or infinite: no clip).  out is fp32 [tokens,
+ *   out_stride]; it is zeroed first unless accumulate != 0 (use accumulate to add a
+ *   shared expert with a second call).  All tables are DEVICE int64 arrays of
+ *   device pointers [num_experts]; topk_ids (int32) and topk_weights (fp32) are
+ *   DEVICE [tokens, topk].  No host synchronisation.  Replaces
+ *   sglang_exl3_c.p2b_fused_moe (reference csrc/p2b_moe.cu:418-468, op
+ *   src/sglang_exl3/ops.py:121-184; fixed there to one row, hidden 4096) and the
+ *   per-token batched GEMV path (src/sglang_exl3/exl3.py:960-1110).
+ *   max_tokens * topk <= 2048, num_experts <= 2048.
+ */
+EXL3B200_API size_t exl3b200_moe_state_size(int max_tokens, int topk, int hidden, int inter);
+EXL3B200_API size_t exl3b200_moe_scratch_size(int max_tokens, int topk, int hidden, int inter);
+EXL3B200_API int exl3b200_moe(const void* x, long long x_stride, int tokens, int hidden, int inter,
+                              const int* topk_ids, const float* topk_weights, int topk, int num_experts,
+                              const long long* gate_trellis, const long long* gate_suh, const long long* gate_svh,
+                              const long long* up_trellis, const long long* up_suh, const long long* up_svh,
+                              const long long* down_trellis, const long long* down_suh, const long long* down_svh,
+                              int K_gate, int K_up, int K_down, int cb, float swiglu_limit, float* out,
+                              long long out_stride, int accumulate, int max_tokens, void* state, size_t state_bytes,
+                              void* scratch, size_t scratch_bytes, void* stream);
 
 /*
  * out[m, k] = H128(x * suh) / sqrt(128) in fp16 over 128-element blocks of each row,

@@ -255,38 +255,37 @@ def swiglu(gate: np.ndarray, up: np.ndarray, limit: float = 0.0) -> np.ndarray:
     return silu(g) * u
 
 
+def linear_device_ref(x: np.ndarray, trellis: np.ndarray, suh: np.ndarray, svh: np.ndarray, K: int,
+                      cb: int) -> np.ndarray:
+    """``x @ W`` with the device pipeline's roundings: fp16 rotated input
+    (``input_transform``), float64 product with the raw decoded tile matrix, then the
+    output transform.  Differs from ``gemv_ref`` only in where fp16 roundings sit."""
+    xh = input_transform(x, suh).astype(np.float64)
+    raw = decode_raw(trellis, K, cb, "rn").astype(np.float64)
+    return output_transform(xh @ raw, svh)
+
+
 def moe_ref(x: np.ndarray, experts: list, ids: np.ndarray, weights: np.ndarray,
-            limit: float = 0.0, act_fp16: bool = True) -> np.ndarray:
+            limit: float = 0.0) -> np.ndarray:
     """Routed SwiGLU MoE for rows of ``x``: ``sum_j w[t,j] * down_e(swiglu(gate_e x, up_e x))``
     (``p2b_moe.cu:202-379``, ``exl3.py:960-1110``).  ``experts[e]`` is a dict with
     ``gate``/``up``/``down`` each ``(trellis, suh, svh, K, cb)``.  Ids outside
-    ``[0, len(experts))`` contribute nothing (``exl3.py:494-509``).  The
-    activation is rounded to fp16 before the down projection, as the reference
-    feeds an fp16 tensor to the down GEMV."""
+    ``[0, len(experts))`` contribute nothing (``exl3.py:494-509``).  The fp16
+    intermediates sit where the reference keeps them: rotated inputs, the SwiGLU
+    activation, and the rotated down-projection input."""
     x = np.asarray(x, dtype=np.float16)
     T = x.shape[0]
     out = np.zeros((T, x.shape[1]), dtype=np.float64)
-    cache = {}
-
-    def wmat(e, which):
-        key = (e, which)
-        if key not in cache:
-            tr, su, sv, K, cb = experts[e][which]
-            cache[key] = dequant(tr, su, sv, K, cb, "rn").astype(np.float64)
-        return cache[key]
-
     for t in range(T):
         for j in range(ids.shape[1]):
             e = int(ids[t, j])
             if e < 0 or e >= len(experts):
                 continue
-            xf = x[t].astype(np.float64)
-            g = xf @ wmat(e, "gate")
-            u = xf @ wmat(e, "up")
-            a = swiglu(g, u, limit)
-            if act_fp16:
-                a = a.astype(np.float16).astype(np.float64)
-            out[t] += float(weights[t, j]) * (a @ wmat(e, "down"))
+            xt = x[t:t + 1]
+            g = linear_device_ref(xt, *experts[e]["gate"])
+            u = linear_device_ref(xt, *experts[e]["up"])
+            a = swiglu(g, u, limit).astype(np.float16)
+            out[t] += float(weights[t, j]) * linear_device_ref(a, *experts[e]["down"])[0]
     return out.astype(np.float32)
 
 

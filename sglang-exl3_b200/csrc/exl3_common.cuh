@@ -276,6 +276,29 @@ __device__ __forceinline__ void warp_fwht128(float (&v)[4], int lane)
     }
 }
 
+// fp16 H128(x * suh) / sqrt(128) of one 128-block over a warp, with the
+// reference's roundings (had_hf_r_128_inner<true,false>,
+// csrc/quant/hadamard_inner.cuh:93-147): fp16 product, float transform and scale,
+// one fp16 rounding.  suh null: plain copy of an already rotated input.
+__device__ __forceinline__ void rotate_block(const __half* __restrict__ src, const __half* __restrict__ suh, int lane,
+                                             __half (&h)[4])
+{
+    float v[4];
+    if (suh) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float xv = __half2float(src[lane + 32 * i]);
+            v[i] = __half2float(__float2half_rn(__fmul_rn(xv, __half2float(suh[lane + 32 * i]))));
+        }
+        warp_fwht128(v, lane);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __float2half_rn(__fmul_rn(v[i], kHadScale));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = src[lane + 32 * i];
+    }
+}
+
 // ---------------------------------------------------------------------------
 // tensor-core MMA (m16n8k16, fp16 inputs, fp32 accumulate)
 // ---------------------------------------------------------------------------

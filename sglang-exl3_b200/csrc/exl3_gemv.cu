@@ -1,43 +1,47 @@
-// Small-M EXL3 matmul (M <= 16 rows): y = H128(H128(x * suh) @ W_raw) * svh / 128.
+// Small-M EXL3 matmul (m <= 16 rows per problem), grouped over a table of
+// problems: y = H128(H128(x * suh) @ W_raw) * svh / 128 for every problem.
 //
 // Replaces the reference's cooperative QTIP-style GEMV
-// (csrc/quant/exl3_gemv_kernel.cuh:138-402, host csrc/exl3_gemv.cu:26-63) with a
-// design for B200:
+// (csrc/quant/exl3_gemv_kernel.cuh:138-402, host csrc/exl3_gemv.cu:26-63), its
+// per-expert batched form (csrc/p2b_batched.cu:13-101) and the row chunks of
+// exl3_gemm (csrc/exl3_gemm.cu:9-31) with three kernels chained by programmatic
+// dependent launch (PDL), none of which waits on another CTA:
 //
-// * input stage (exl3_input_kernel): one warp per (row, 128-block) computes the
-//   fp16 x_had = H128(x * suh) / sqrt(128) with the reference's roundings
-//   (had_hf_r_128_inner<true,false>, csrc/quant/hadamard_inner.cuh:93-147) into
-//   the caller's workspace.  The matmul kernel is launched as its programmatic
-//   dependent (PDL), so its trellis loads start while the input stage runs and
-//   only the x_had reads wait (griddepcontrol.wait).  No grid-wide barrier.
-// * matmul (exl3_gemv_kernel): the iteration space is the list of units
-//   (128-column block nb, 16-row k-slice kr), nb-major; the grid (2 CTAs per
-//   SM) splits it evenly ("stream-K"), so any shape load-balances over 148 SMs.
-//   Each warp of a CTA takes k-slices of the current block and, per slice,
-//   streams the block's 8 tiles with coalesced 32-bit loads (one 128-byte
-//   transaction per tile at 4 bpw) through a register ring a few slices deep,
-//   resolves each lane's two stream words with one or two shuffles, extracts the
-//   8 windows and runs the codebook in registers.  The decoded 16x16 tile is
-//   used transposed as the A operand of mma.m16n8k16 (rows = output columns,
-//   cols = k) and x_had as B (k x 8 tokens), fp32 accumulate, so at M <= 8 no
-//   tensor work is spent on padding rows.  The codebook's final fp16 add
+// * input stage (exl3_gv_input_kernel): one warp per (problem, row, 128-block)
+//   computes the fp16 x_had = H128(x * suh) / sqrt(128) with the reference's
+//   roundings (had_hf_r_128_inner<true,false>, csrc/quant/hadamard_inner.cuh:93-147)
+//   and stores it as duplicated pairs {h, h}: the B fragments of the folded MMA.
+// * matmul (exl3_gv_matmul_kernel): the iteration space is every problem's list
+//   of units (128-column block nb, 16-row k-slice kr); the grid (2 CTAs per SM)
+//   splits the concatenated list evenly ("stream-K"), so any mix of shapes
+//   load-balances over the 148 SMs.  Each warp of a CTA takes k-slices of the
+//   current block and, per slice, streams the block's tiles with coalesced 32-bit
+//   loads (one 128-byte transaction per tile at 4 bpw) through a register ring
+//   three slices deep, resolves each lane's two stream words with shuffles,
+//   extracts the 8 windows and runs the codebook in registers.  The decoded 16x16
+//   tile is used transposed as the A operand of mma.m16n8k16 (rows = output
+//   columns, cols = k) and x_had as B (k x 8 rows), fp32 accumulate, so at m <= 8
+//   no tensor work is spent on padding rows.  The codebook's final fp16 add
 //   (cb 0/1) is folded into the MMA: the LOP3 word {lo, hi} goes in as a k pair
-//   against a duplicated activation {h, h} (written so by the input stage),
-//   which saves the PRMT/HADD2 of every weight pair for one extra MMA per tile;
-//   the integer-logic pipe (half rate on sm_100) is what bounds this kernel, so
-//   window extraction uses byte permutes and FMA-pipe shifts where it can.
-//   mul1 (cb 2) feeds the exact
-//   integer-valued fp16 h = 1024 + bytesum and applies
-//   y = k_inv * sum(x h) + k_bias * sum(x) in float in the epilogue.
-// * reduction: warps add their fragments into a shared [rows][128] block; a CTA
-//   that covered all k-slices of the block runs the epilogue itself, otherwise it
-//   adds the block into an fp32 workspace slice and the last of the block's
-//   contributors (an atomic arrival counter, no waiting) runs the epilogue and
-//   re-zeroes the slice and counter for the next call.
-// * epilogue: one warp per row: H128 over the 128 columns, * 1/sqrt(128) * svh,
-//   one rounding to the output dtype (fp16 / bf16 / fp32), strided store.
+//   against the duplicated activation.  mul1 (cb 2) feeds the exact
+//   integer-valued fp16 h = 1024 + bytesum; the epilogue applies
+//   y = k_inv * sum(x h) + k_bias * sum(x).  The integer-logic and IMAD pipes
+//   (both half rate on sm_100) bound the decode, so window extraction uses byte
+//   permutes and shifts the compiler can place on either pipe.  Warps reduce
+//   their fragments in shared memory and the CTA adds its partial block into a
+//   zeroed fp32 state slice with fire-and-forget atomics, then moves on.
+// * epilogue (exl3_gv_epilogue_kernel): one warp per (problem, 128-column block,
+//   row) reads the summed partials and re-zeroes them, runs H128 over the block,
+//   * 1/sqrt(128) * svh, and then stores (fp16 / bf16 / fp32), or adds
+//   weight * y into a routed fp32 output row (MoE combine), or - for (gate, up)
+//   problem pairs - applies the clipped SwiGLU and writes the rotated input of the
+//   down projection (the reference's had_hf_r_128_guad_inner and p2b_moe phase 3,
+//   csrc/quant/hadamard_inner.cuh:283-413, csrc/p2b_moe.cu:300-336).
+#include <algorithm>
+
 #include "exl3_common.cuh"
 #include "exl3_capi_internal.h"
+#include "exl3_grouped.cuh"
 
 namespace exl3b200 {
 
@@ -45,74 +49,85 @@ constexpr int kGvThreads = 256;
 constexpr int kGvWarps = kGvThreads / 32;
 constexpr int kRedStride = 132;  // padded row stride of the shared reduction block
 
-struct GemvParams {
-    const uint32_t* xd;      // [M, k] rotated input as duplicated fp16 pairs {h, h}
-    const uint32_t* trellis; // [k/16, n/16, 16K] as uint32 words
-    const __half* svh;       // [n]
-    const float* sblk;       // [M, k/128] block sums of xh (cb 2 only)
-    void* out;               // [M, out_stride]
-    float* ws_acc;           // [n/128, 16, 128] zeroed fp32 partial sums
-    long long out_stride;
-    int out_dtype;
-    int m;
-    int k;
-    int n;
-};
-
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ const GvProblem& gv_prob(const GvArgs& a, int i)
+{
+    const int j = i * a.stride + a.offset;
+    return a.dev ? a.dev[j] : a.inl[j];
+}
+
+struct GvTotals {
+    int nprob, units, in_tasks, out_tasks;
+};
+
+__device__ __forceinline__ GvTotals gv_totals(const GvArgs& a)
+{
+    GvTotals t;
+    if (a.dev_totals) {
+        t.nprob = __ldcg(a.dev_totals + 0);
+        t.units = __ldcg(a.dev_totals + 1);
+        t.in_tasks = __ldcg(a.dev_totals + 2);
+        t.out_tasks = __ldcg(a.dev_totals + 3);
+    } else {
+        t.nprob = a.nprob;
+        t.units = a.units;
+        t.in_tasks = a.in_tasks;
+        t.out_tasks = a.out_tasks;
+    }
+    if (a.uniform_units > 0) t.units = t.nprob * a.uniform_units;
+    return t;
+}
+
+// largest problem index whose task range starts at or before task
+template <int WHICH>
+__device__ __forceinline__ int gv_find(const GvArgs& a, int nprob, int task)
+{
+    int lo = 0, hi = nprob - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        const GvProblem& p = gv_prob(a, mid);
+        const int begin = WHICH == 0 ? p.in_task_begin : WHICH == 1 ? p.out_task_begin : p.unit_begin;
+        if (begin <= task) lo = mid;
+        else hi = mid - 1;
+    }
+    return lo;
+}
 
 // ---------------------------------------------------------------------------
 // input stage
 // ---------------------------------------------------------------------------
 
-// One warp per (row, 128-block): h = fp16(H128(fp16(x * suh)) / sqrt(128)).
-// Writes h to xh (if non-null, fp16 [m][xh_stride]) and/or the duplicated pairs
-// {h, h} to xd (if non-null, uint32 [m][k]) - the B fragments of the folded MMA.
-__global__ __launch_bounds__(256) void exl3_input_kernel(
-    const __half* __restrict__ x, long long x_stride, const __half* __restrict__ suh,
-    __half* __restrict__ xh, long long xh_stride, uint32_t* __restrict__ xd, float* __restrict__ sblk,
-    int m, int k, int rotate)
+__global__ __launch_bounds__(256) void exl3_gv_input_kernel(const __grid_constant__ GvArgs a)
 {
     griddep_launch();
+    griddep_wait();  // inputs may be produced by the previous kernel (no-op otherwise)
+    const GvTotals tot = gv_totals(a);
     const int lane = threadIdx.x & 31;
-    const int nblk = k >> 7;
-    const int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (task >= m * nblk) return;
-    const int row = task / nblk;
-    const int b = task - row * nblk;
-    const __half* src = x + row * x_stride + b * 128;
-    float v[4];
-    __half h[4];
-    if (rotate) {
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < tot.in_tasks; task += warps) {
+        const int pi = gv_find<0>(a, tot.nprob, task);
+        const GvProblem& p = gv_prob(a, pi);
+        const int nblk = p.k >> 7;
+        const int local = task - p.in_task_begin;
+        const int r = local / nblk;
+        const int b = local - r * nblk;
+        const int row = p.x_rows ? p.x_rows[r] : r;
+        __half h[4];
+        rotate_block(p.x + (size_t) row * p.x_stride + b * 128, p.suh ? p.suh + b * 128 : nullptr, lane, h);
+        float s = 0.f;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            const float xv = __half2float(src[lane + 32 * i]);
-            v[i] = suh ? __half2float(__float2half_rn(__fmul_rn(xv, __half2float(suh[b * 128 + lane + 32 * i]))))
-                       : xv;
-        }
-        warp_fwht128(v, lane);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) h[i] = __float2half_rn(__fmul_rn(v[i], kHadScale));
-    } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) h[i] = src[lane + 32 * i];
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const size_t col = (size_t) b * 128 + lane + 32 * i;
-        if (xh) xh[(size_t) row * xh_stride + col] = h[i];
-        if (xd) {
             const uint32_t u = __half_as_ushort(h[i]);
-            xd[(size_t) row * k + col] = u | (u << 16);
+            p.xd[(size_t) r * p.k + b * 128 + lane + 32 * i] = u | (u << 16);
+            s += __half2float(h[i]);
         }
-        v[i] = __half2float(h[i]);
-    }
-    if (sblk) {
-        float s = (v[0] + v[1]) + (v[2] + v[3]);
+        if (p.sblk) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) sblk[(size_t) row * nblk + b] = s;
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == 0) p.sblk[(size_t) r * nblk + b] = s;
+        }
     }
 }
 
@@ -120,9 +135,8 @@ __global__ __launch_bounds__(256) void exl3_input_kernel(
 // matmul
 // ---------------------------------------------------------------------------
 
-// Loads per k-slice per lane for the 8 tiles of a block: tiles are 8K words;
-// K = 1, 2, 4 pack 32/(8K) tiles into one 32-lane load, K = 3 loads one tile per
-// load on 24 lanes.
+// Loads per k-slice per lane for a warp's NT tiles: tiles are 8K words; K = 1, 2, 4
+// pack 32/(8K) tiles into one 32-lane load, K = 3 loads one tile per load on 24 lanes.
 template <int K, int NT>
 struct SliceLoad {
     static constexpr int TW = 8 * K;
@@ -132,13 +146,13 @@ struct SliceLoad {
 // K bits, codebook CB, TG groups of 8 rows, NT tiles per warp per k-slice (8 or 4:
 // with 4, two warps share a slice's 8-tile block), P-deep trellis register ring.
 template <int K, int CB, int TG, int NT, int P, int MINB>
-__global__ __launch_bounds__(kGvThreads, MINB) void exl3_gemv_kernel(const GemvParams p)
+__global__ __launch_bounds__(kGvThreads, MINB) void exl3_gv_matmul_kernel(const __grid_constant__ GvArgs a)
 {
     griddep_launch();  // let the epilogue kernel get scheduled early; it waits for this grid
     constexpr int TW = SliceLoad<K, NT>::TW;
     constexpr int LOADS = SliceLoad<K, NT>::LOADS;
-    constexpr int TGRP = 8 / NT;            // warps sharing one slice
-    constexpr int SG = kGvWarps / TGRP;     // slice groups
+    constexpr int TGRP = 8 / NT;         // warps sharing one slice
+    constexpr int SG = kGvWarps / TGRP;  // slice groups
 
     __shared__ float red[TG * 8][kRedStride];
 
@@ -147,25 +161,37 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gemv_kernel(const GemvP
     const int g = lane >> 2;
     const int c = lane & 3;
     const LaneWords lw = lane_words<K>(lane);
+    const bool load_lane = (K != 3) || lane < 24;  // K = 3: 24 of 32 lanes carry a tile's words
 
-    const int kt_total = p.k >> 4;
-    const int n_tiles = p.n >> 4;
-    const int nblocks = p.n >> 7;
-    const long long units = (long long) nblocks * kt_total;
+    bool waited = false;
+    if (a.dev_totals) {  // the totals are produced by an earlier kernel
+        griddep_wait();
+        waited = true;
+    }
+    const GvTotals tot = gv_totals(a);
+    const long long units = tot.units;
     const long long G = gridDim.x;
     const long long u_begin = (long long) blockIdx.x * units / G;
     const long long u_end = (long long) (blockIdx.x + 1) * units / G;
 
-    // K = 3: 24 of 32 lanes carry a tile's words
-    const bool load_lane = (K != 3) || lane < 24;
-    const size_t slice_words = (size_t) n_tiles * TW;  // words per k-slice row of the matrix
-
-    bool waited = false;
-
+    int pi = -1;
+    long long pu0 = 0, pu1 = 0;  // unit range of the current problem
     for (long long u = u_begin; u < u_end;) {
-        const int nb = (int) (u / kt_total);
-        const int kr0 = (int) (u - (long long) nb * kt_total);
+        if (u >= pu1) {
+            pi = a.uniform_units > 0 ? (int) (u / a.uniform_units) : gv_find<2>(a, tot.nprob, (int) u);
+            const GvProblem& pp = gv_prob(a, pi);
+            pu0 = a.uniform_units > 0 ? (long long) pi * a.uniform_units : pp.unit_begin;
+            pu1 = pu0 + (long long) (pp.n >> 7) * (pp.k >> 4);
+        }
+        const GvProblem& p = gv_prob(a, pi);
+        const int kt_total = p.k >> 4;
+        const int n_tiles = p.n >> 4;
+        const long long lu = u - pu0;
+        const int nb = (int) (lu / kt_total);
+        const int kr0 = (int) (lu - (long long) nb * kt_total);
         const int len = (int) min((long long) (kt_total - kr0), u_end - u);
+        const int m = p.m;
+        const size_t slice_words = (size_t) n_tiles * TW;  // words per k-slice row of the matrix
 
         for (int i = threadIdx.x; i < TG * 8 * kRedStride; i += kGvThreads) (&red[0][0])[i] = 0.f;
 
@@ -190,7 +216,7 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gemv_kernel(const GemvP
 #pragma unroll
         for (int q = 0; q < TG; ++q) {
             const int row = 8 * q + g;
-            xrow[q] = row < p.m;
+            xrow[q] = row < m;
             xptr[q] = reinterpret_cast<const uint2*>(p.xd + (size_t) (xrow[q] ? row : 0) * p.k +
                                                      (size_t) (kr0 + sg) * 16 + 2 * c);
         }
@@ -294,11 +320,11 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gemv_kernel(const GemvP
 #pragma unroll
             for (int t = 0; t < NT; ++t) {
                 const int n0 = 16 * (th * NT + t) + g;
-                if (r0 < p.m) {
+                if (r0 < m) {
                     atomicAdd(&red[r0][n0], acc[t][q][0]);
                     atomicAdd(&red[r0][n0 + 8], acc[t][q][2]);
                 }
-                if (r0 + 1 < p.m) {
+                if (r0 + 1 < m) {
                     atomicAdd(&red[r0 + 1][n0], acc[t][q][1]);
                     atomicAdd(&red[r0 + 1][n0 + 8], acc[t][q][3]);
                 }
@@ -308,8 +334,8 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gemv_kernel(const GemvP
 
         // fire-and-forget: add this CTA's partial block into the zeroed state; the
         // epilogue kernel (a programmatic dependent of this grid) finishes it
-        float* wsb = p.ws_acc + (size_t) nb * 16 * 128;
-        for (int e = threadIdx.x; e < p.m * 128; e += kGvThreads) {
+        float* wsb = p.acc + (size_t) nb * p.acc_nb_stride;
+        for (int e = threadIdx.x; e < m * 128; e += kGvThreads) {
             const int r = e >> 7, col = e & 127;
             atomicAdd(wsb + r * 128 + col, red[r][col]);
         }
@@ -320,24 +346,15 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gemv_kernel(const GemvP
 }
 
 // ---------------------------------------------------------------------------
-// epilogue: one warp per (128-column block, row): read the summed partials and
-// re-zero them, H128 over the block, * 1/sqrt(128) * svh, one rounding, store.
-// Launched as a programmatic dependent of the matmul grid.
+// epilogue
 // ---------------------------------------------------------------------------
+
+// Finish one (problem, block, row): read and re-zero the summed partials, mul1
+// correction, H128, * 1/sqrt(128) * svh.  Lane holds columns lane + 32 i.
 template <int CB>
-__global__ __launch_bounds__(256) void exl3_gemv_epilogue_kernel(
-    float* __restrict__ ws_acc, const __half* __restrict__ svh, const float* __restrict__ sblk, void* out,
-    long long out_stride, int out_dtype, int m, int k, int n)
+__device__ __forceinline__ void gv_finish(const GvProblem& p, int nb, int r, int lane, float (&v)[4])
 {
-    const int lane = threadIdx.x & 31;
-    const int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int nblocks = n >> 7;
-    griddep_wait();
-    if (task >= nblocks * m) return;
-    const int nb = task % nblocks;
-    const int r = task / nblocks;
-    float* src = ws_acc + ((size_t) nb * 16 + r) * 128;
-    float v[4];
+    float* src = p.acc + (size_t) nb * p.acc_nb_stride + (size_t) r * 128;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
         v[e] = __ldcg(src + lane + 32 * e);
@@ -346,9 +363,9 @@ __global__ __launch_bounds__(256) void exl3_gemv_epilogue_kernel(
     if constexpr (CB == 2) {
         const float k_inv = __half2float(__ushort_as_half(kMul1InvBits));
         const float k_bias = __half2float(__ushort_as_half(kMul1BiasBits));
-        const int nblk = k >> 7;
+        const int nblk = p.k >> 7;
         float sum = 0.f;
-        for (int b = lane; b < nblk; b += 32) sum += __ldcg(sblk + (size_t) r * nblk + b);
+        for (int b = lane; b < nblk; b += 32) sum += __ldcg(p.sblk + (size_t) r * nblk + b);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
 #pragma unroll
@@ -356,9 +373,75 @@ __global__ __launch_bounds__(256) void exl3_gemv_epilogue_kernel(
     }
     warp_fwht128(v, lane);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        const int col = nb * 128 + lane + 32 * e;
-        store_out(out, (size_t) r * out_stride + col, v[e] * kHadScale * __half2float(svh[col]), out_dtype);
+    for (int e = 0; e < 4; ++e) v[e] = v[e] * kHadScale * __half2float(p.svh[nb * 128 + lane + 32 * e]);
+}
+
+template <int CB, int MODE>
+__global__ __launch_bounds__(256) void exl3_gv_epilogue_kernel(const __grid_constant__ GvArgs a)
+{
+    griddep_launch();
+    griddep_wait();
+    const GvTotals tot = gv_totals(a);
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < tot.out_tasks; task += warps) {
+        const int pi = gv_find<1>(a, tot.nprob, task);
+        const GvProblem& p = gv_prob(a, pi);
+        const int nblocks = p.n >> 7;
+        const int local = task - p.out_task_begin;
+        const int r = local / nblocks;
+        const int nb = local - r * nblocks;
+        float v[4];
+        gv_finish<CB>(p, nb, r, lane, v);
+        if constexpr (MODE == kEpiStore) {
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                store_out(p.out, (size_t) r * p.out_stride + nb * 128 + lane + 32 * e, v[e], a.out_dtype);
+        } else if constexpr (MODE == kEpiCombine) {
+            const int orow = p.out_rows ? p.out_rows[r] : r;
+            const float w = p.out_scale ? p.out_scale[r] : 1.f;
+            float* o = reinterpret_cast<float*>(p.out) + (size_t) orow * p.out_stride + nb * 128;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) atomicAdd(o + lane + 32 * e, w * v[e]);
+        } else {
+            // (gate, up) pair: table entries j and j+1 (stride 2 view)
+            const GvProblem& pu = a.dev ? a.dev[pi * a.stride + a.offset + 1] : a.inl[pi * a.stride + a.offset + 1];
+            float u[4];
+            gv_finish<CB>(pu, nb, r, lane, u);
+            const float lim = a.swiglu_limit;
+            const bool clip = lim > 0.f && lim < 3.0e38f;
+            float act[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float gv = v[e], uv = u[e];
+                if (clip) {
+                    gv = fminf(gv, lim);
+                    uv = fminf(fmaxf(uv, -lim), lim);
+                }
+                const float s = gv / (1.0f + expf(-gv));
+                act[e] = __half2float(__float2half_rn(s * uv));
+            }
+            // rotated input of the down projection for this 128-block of the intermediate
+            const __half* suh_d = p.out_suh + nb * 128;
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                act[e] = __half2float(__float2half_rn(__fmul_rn(act[e], __half2float(suh_d[lane + 32 * e]))));
+            warp_fwht128(act, lane);
+            uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + (size_t) r * p.out_stride + nb * 128;
+            float bsum = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const __half hh = __float2half_rn(__fmul_rn(act[e], kHadScale));
+                const uint32_t h = __half_as_ushort(hh);
+                dst[lane + 32 * e] = h | (h << 16);
+                bsum += __half2float(hh);
+            }
+            if (p.out_sblk) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
+                if (lane == 0) p.out_sblk[(size_t) r * (p.n >> 7) + nb] = bsum;
+            }
+        }
     }
 }
 
@@ -366,7 +449,7 @@ __global__ __launch_bounds__(256) void exl3_gemv_epilogue_kernel(
 // host side
 // ---------------------------------------------------------------------------
 
-static int sm_count()
+int gv_sm_count()
 {
     static int cache[64] = {0};
     int dev = 0;
@@ -382,31 +465,15 @@ static int sm_count()
 
 static inline size_t align256(size_t v) { return (v + 255) & ~(size_t) 255; }
 
-// state: [n/128][16][128] fp32 partial sums; zero when allocated, left zero by
-// every call (the epilogue kernel re-zeroes what the matmul kernel added).
-static size_t gemv_state_bytes(int n)
-{
-    const size_t nblocks = (size_t) n / 128;
-    return align256(nblocks * 16 * 128 * sizeof(float));
-}
+size_t gv_state_bytes_per_problem(int n) { return align256((size_t) (n / 128) * 16 * 128 * sizeof(float)); }
+size_t gv_xd_bytes(int m, int k) { return align256((size_t) m * k * sizeof(uint32_t)); }
+size_t gv_sblk_bytes(int m, int k) { return align256((size_t) m * (k / 128) * sizeof(float)); }
 
-// scratch: [m][k] rotated input as duplicated fp16 pairs, then [m][k/128] fp32 block sums.
-static size_t gemv_scratch_bytes(int m, int k)
+template <typename Kern>
+static int launch_ex(Kern kern, int grid, bool pdl, cudaStream_t stream, const GvArgs& a)
 {
-    return align256((size_t) m * k * sizeof(uint32_t)) + align256((size_t) m * (k / 128) * sizeof(float));
-}
-
-// Tiling variants (the kernel-shape map picks one per call):
-//   0: 8 tiles per warp, 2 CTAs/SM    1: 4 tiles per warp, 3 CTAs/SM
-//   2: 4 tiles per warp, 4 CTAs/SM
-template <int K, int CB, int TG, int NT, int MINB>
-static int launch_gemv_kernel(const GemvParams& prm, int sms, cudaStream_t stream)
-{
-    constexpr int P = 3;
-    const long long units = (long long) (prm.n / 128) * (prm.k / 16);
-    const int grid = (int) std::min<long long>(units, (long long) MINB * sms);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
+    cfg.gridDim = dim3(std::max(grid, 1));
     cfg.blockDim = dim3(kGvThreads);
     cfg.dynamicSmemBytes = 0;
     cfg.stream = stream;
@@ -414,51 +481,105 @@ static int launch_gemv_kernel(const GemvParams& prm, int sms, cudaStream_t strea
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, exl3_gemv_kernel<K, CB, TG, NT, P, MINB>, prm);
-    return e == cudaSuccess ? kOk : kErrLaunch;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess ? kOk : kErrLaunch;
+}
+
+int gv_launch_input(const GvArgs& a, int max_in_tasks, bool pdl, cudaStream_t stream)
+{
+    const int warps_per_cta = kGvThreads / 32;
+    const int grid = std::min((max_in_tasks + warps_per_cta - 1) / warps_per_cta, 8 * gv_sm_count());
+    return launch_ex(exl3_gv_input_kernel, grid, pdl, stream, a);
+}
+
+// Tiling variants (the kernel-shape map picks one per call):
+//   0: 8 tiles per warp, 2 CTAs/SM    1: 4 tiles per warp, 3 CTAs/SM
+template <int K, int CB, int TG, int NT, int MINB>
+static int launch_matmul_t(const GvArgs& a, bool pdl, cudaStream_t stream)
+{
+    constexpr int P = 3;
+    int grid = MINB * gv_sm_count();
+    if (!a.dev_totals) {
+        const long long units = a.uniform_units > 0 ? (long long) a.nprob * a.uniform_units : a.units;
+        grid = (int) std::min<long long>(units, grid);
+    }
+    return launch_ex(exl3_gv_matmul_kernel<K, CB, TG, NT, P, MINB>, grid, pdl, stream, a);
 }
 
 template <int K, int CB>
-static int dispatch_tg(const GemvParams& prm, int sms, int variant, cudaStream_t stream)
+static int launch_matmul_tg(const GvArgs& a, int max_rows, int variant, bool pdl, cudaStream_t stream)
 {
-    if (prm.m <= 8) {
-        if (variant == 1) return launch_gemv_kernel<K, CB, 1, 4, 3>(prm, sms, stream);
-        if (variant == 2) return launch_gemv_kernel<K, CB, 1, 4, 4>(prm, sms, stream);
-        return launch_gemv_kernel<K, CB, 1, 8, 2>(prm, sms, stream);
+    if (max_rows <= 8) {
+        if (variant == 1) return launch_matmul_t<K, CB, 1, 4, 3>(a, pdl, stream);
+        return launch_matmul_t<K, CB, 1, 8, 2>(a, pdl, stream);
     }
-    if (variant == 2) return launch_gemv_kernel<K, CB, 2, 4, 3>(prm, sms, stream);
-    return launch_gemv_kernel<K, CB, 2, 4, 2>(prm, sms, stream);
+    return launch_matmul_t<K, CB, 2, 4, 2>(a, pdl, stream);
 }
 
 template <int K>
-static int dispatch_cb(int cb, const GemvParams& prm, int sms, int variant, cudaStream_t stream)
+static int launch_matmul_cb(const GvArgs& a, int cb, int max_rows, int variant, bool pdl, cudaStream_t stream)
 {
-    if (cb == 0) return dispatch_tg<K, 0>(prm, sms, variant, stream);
-    if (cb == 1) return dispatch_tg<K, 1>(prm, sms, variant, stream);
-    return dispatch_tg<K, 2>(prm, sms, variant, stream);
+    if (cb == 0) return launch_matmul_tg<K, 0>(a, max_rows, variant, pdl, stream);
+    if (cb == 1) return launch_matmul_tg<K, 1>(a, max_rows, variant, pdl, stream);
+    return launch_matmul_tg<K, 2>(a, max_rows, variant, pdl, stream);
 }
 
-static int launch_epilogue(int cb, float* ws_acc, const __half* svh, const float* sblk, void* out,
-                           long long out_stride, int out_dtype, int m, int k, int n, cudaStream_t stream)
+int gv_launch_matmul(const GvArgs& a, int K, int cb, int max_rows, int variant, bool pdl, cudaStream_t stream)
 {
-    const int tasks = (n / 128) * m;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((tasks + 7) / 8);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = 0;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t e;
-    if (cb == 2)
-        e = cudaLaunchKernelEx(&cfg, exl3_gemv_epilogue_kernel<2>, ws_acc, svh, sblk, out, out_stride, out_dtype, m, k, n);
-    else
-        e = cudaLaunchKernelEx(&cfg, exl3_gemv_epilogue_kernel<0>, ws_acc, svh, sblk, out, out_stride, out_dtype, m, k, n);
-    return e == cudaSuccess ? kOk : kErrLaunch;
+    switch (K) {
+        case 2: return launch_matmul_cb<2>(a, cb, max_rows, variant, pdl, stream);
+        case 3: return launch_matmul_cb<3>(a, cb, max_rows, variant, pdl, stream);
+        case 4: return launch_matmul_cb<4>(a, cb, max_rows, variant, pdl, stream);
+        default: return kErrBadBits;
+    }
+}
+
+int gv_launch_epilogue(const GvArgs& a, int cb, int max_out_tasks, bool pdl, cudaStream_t stream)
+{
+    const int warps_per_cta = kGvThreads / 32;
+    const int grid = std::min((max_out_tasks + warps_per_cta - 1) / warps_per_cta, 8 * gv_sm_count());
+    const bool mul1 = cb == 2;
+    switch (a.epi_mode) {
+        case kEpiStore:
+            return mul1 ? launch_ex(exl3_gv_epilogue_kernel<2, kEpiStore>, grid, pdl, stream, a)
+                        : launch_ex(exl3_gv_epilogue_kernel<0, kEpiStore>, grid, pdl, stream, a);
+        case kEpiCombine:
+            return mul1 ? launch_ex(exl3_gv_epilogue_kernel<2, kEpiCombine>, grid, pdl, stream, a)
+                        : launch_ex(exl3_gv_epilogue_kernel<0, kEpiCombine>, grid, pdl, stream, a);
+        case kEpiSwiglu:
+            return mul1 ? launch_ex(exl3_gv_epilogue_kernel<2, kEpiSwiglu>, grid, pdl, stream, a)
+                        : launch_ex(exl3_gv_epilogue_kernel<0, kEpiSwiglu>, grid, pdl, stream, a);
+        default: return kErrBadArgument;
+    }
+}
+
+// Host-built table of up to kGvInline dense problems (one input matrix, several
+// linears sharing K and codebook): fill prefixes and launch the three kernels.
+static int run_inline(GvArgs& a, int K, int cb, int max_rows, int variant, cudaStream_t stream)
+{
+    int units = 0, in_tasks = 0, out_tasks = 0;
+    for (int i = 0; i < a.nprob; ++i) {
+        GvProblem& p = a.inl[i];
+        p.unit_begin = units;
+        p.in_task_begin = in_tasks;
+        p.out_task_begin = out_tasks;
+        units += (p.n / 128) * (p.k / 16);
+        in_tasks += p.m * (p.k / 128);
+        out_tasks += p.m * (p.n / 128);
+    }
+    a.units = units;
+    a.in_tasks = in_tasks;
+    a.out_tasks = out_tasks;
+    a.dev = nullptr;
+    a.dev_totals = nullptr;
+    a.stride = 1;
+    a.offset = 0;
+    a.uniform_units = 0;
+    int rc = gv_launch_input(a, in_tasks, false, stream);
+    if (rc != kOk) return rc;
+    rc = gv_launch_matmul(a, K, cb, max_rows, variant, true, stream);
+    if (rc != kOk) return rc;
+    return gv_launch_epilogue(a, cb, out_tasks, true, stream);
 }
 
 }  // namespace exl3b200
@@ -468,13 +589,24 @@ using namespace exl3b200;
 extern "C" size_t exl3b200_gemv_state_size(int n)
 {
     if (n <= 0 || n % 128) return 0;
-    return gemv_state_bytes(n);
+    return gv_state_bytes_per_problem(n);
 }
 
 extern "C" size_t exl3b200_gemv_scratch_size(int m, int k)
 {
     if (m <= 0 || k <= 0 || k % 128) return 0;
-    return gemv_scratch_bytes(m, k);
+    return gv_xd_bytes(m, k) + gv_sblk_bytes(m, k);
+}
+
+static int check_linear_args(const void* trellis, const void* svh, int m, int k, int n, int K, int cb)
+{
+    if (!trellis || !svh) return kErrNullPointer;
+    if (K < 2 || K > 4) return kErrBadBits;
+    if (cb < 0 || cb > 2) return kErrBadCodebook;
+    if (m < 1 || m > EXL3B200_GEMV_MAX_M) return kErrBadShape;
+    if (k <= 0 || n <= 0 || (k % 128) || (n % 128)) return kErrBadShape;
+    if ((uintptr_t) trellis & 3) return kErrUnaligned;
+    return kOk;
 }
 
 extern "C" int exl3b200_gemv(const void* x, long long x_stride, int m, int k, const void* trellis, int n, int K,
@@ -482,67 +614,126 @@ extern "C" int exl3b200_gemv(const void* x, long long x_stride, int m, int k, co
                              int out_dtype, int flags, void* state, size_t state_bytes, void* scratch,
                              size_t scratch_bytes, void* stream)
 {
-    if (!x || !trellis || !svh || !out || !state || !scratch) return kErrNullPointer;
-    if (K < 2 || K > 4) return kErrBadBits;
-    if (cb < 0 || cb > 2) return kErrBadCodebook;
-    if (m < 1 || m > EXL3B200_GEMV_MAX_M) return kErrBadShape;
-    if (k <= 0 || n <= 0 || (k % 128) || (n % 128)) return kErrBadShape;
+    if (!x || !out || !state || !scratch) return kErrNullPointer;
+    int rc = check_linear_args(trellis, svh, m, k, n, K, cb);
+    if (rc != kOk) return rc;
     if (out_dtype < 0 || out_dtype > 2) return kErrBadArgument;
     if (x_stride < k || out_stride < n) return kErrBadShape;
     const bool pre_rotated = (flags & EXL3B200_FLAG_INPUT_ROTATED) != 0;
     if (!pre_rotated && !suh) return kErrNullPointer;
-    if (((uintptr_t) trellis & 3) || ((uintptr_t) x & 3) || (x_stride & 1)) return kErrUnaligned;
+    if (((uintptr_t) x & 3) || (x_stride & 1)) return kErrUnaligned;
     if (((uintptr_t) state & 255) || ((uintptr_t) scratch & 255)) return kErrUnaligned;
-    if (state_bytes < gemv_state_bytes(n) || scratch_bytes < gemv_scratch_bytes(m, k)) return kErrWorkspace;
+    if (state_bytes < gv_state_bytes_per_problem(n) || scratch_bytes < gv_xd_bytes(m, k) + gv_sblk_bytes(m, k))
+        return kErrWorkspace;
 
-    char* st_base = reinterpret_cast<char*>(state);
-    char* sc_base = reinterpret_cast<char*>(scratch);
-    float* ws_acc = reinterpret_cast<float*>(st_base);
-    uint32_t* xd = reinterpret_cast<uint32_t*>(sc_base);
-    float* sblk = reinterpret_cast<float*>(sc_base + align256((size_t) m * k * sizeof(uint32_t)));
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-
-    const int tasks = m * (k / 128);
-    exl3_input_kernel<<<(tasks + 7) / 8, 256, 0, st>>>(
-        reinterpret_cast<const __half*>(x), x_stride, reinterpret_cast<const __half*>(suh), nullptr, 0, xd,
-        cb == 2 ? sblk : nullptr, m, k, pre_rotated ? 0 : 1);
-    if (cudaGetLastError() != cudaSuccess) return kErrLaunch;
-
-    GemvParams prm;
-    prm.xd = xd;
-    prm.trellis = reinterpret_cast<const uint32_t*>(trellis);
-    prm.svh = reinterpret_cast<const __half*>(svh);
-    prm.sblk = sblk;
-    prm.out = out;
-    prm.ws_acc = ws_acc;
-    prm.out_stride = out_stride;
-    prm.out_dtype = out_dtype;
-    prm.m = m;
-    prm.k = k;
-    prm.n = n;
-
-    const int variant = (flags >> 8) & 3;
-    const int sms = sm_count();
-    int rc;
-    switch (K) {
-        case 2: rc = dispatch_cb<2>(cb, prm, sms, variant, st); break;
-        case 3: rc = dispatch_cb<3>(cb, prm, sms, variant, st); break;
-        default: rc = dispatch_cb<4>(cb, prm, sms, variant, st); break;
-    }
-    if (rc != kOk) return rc;
-    return launch_epilogue(cb, ws_acc, reinterpret_cast<const __half*>(svh), sblk, out, out_stride, out_dtype, m, k,
-                           n, st);
+    GvArgs a = {};
+    a.nprob = 1;
+    a.out_dtype = out_dtype;
+    a.epi_mode = kEpiStore;
+    GvProblem& p = a.inl[0];
+    p.trellis = reinterpret_cast<const uint32_t*>(trellis);
+    p.suh = pre_rotated ? nullptr : reinterpret_cast<const __half*>(suh);
+    p.svh = reinterpret_cast<const __half*>(svh);
+    p.x = reinterpret_cast<const __half*>(x);
+    p.x_stride = x_stride;
+    p.xd = reinterpret_cast<uint32_t*>(scratch);
+    p.sblk = cb == 2 ? reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + gv_xd_bytes(m, k)) : nullptr;
+    p.acc = reinterpret_cast<float*>(state);
+    p.acc_nb_stride = 16 * 128;
+    p.out = out;
+    p.out_stride = out_stride;
+    p.k = k;
+    p.n = n;
+    p.m = m;
+    return run_inline(a, K, cb, m, (flags >> 8) & 3, reinterpret_cast<cudaStream_t>(stream));
 }
 
-extern "C" int exl3b200_hadamard_in(const void* x, long long x_stride, int m, int k, const void* suh, void* out,
-                                    long long out_stride, void* stream)
+extern "C" int exl3b200_gemv_multi(int count, const void* x, long long x_stride, int m, int k, int K, int cb,
+                                   const void* const* trellis, const int* n, const void* const* suh,
+                                   const void* const* svh, void* const* out, const long long* out_stride,
+                                   int out_dtype, int flags, void* state, size_t state_bytes, void* scratch,
+                                   size_t scratch_bytes, void* stream)
 {
-    if (!x || !out) return kErrNullPointer;
-    if (m < 1 || k <= 0 || (k % 128) || x_stride < k || out_stride < k) return kErrBadShape;
-    if (((uintptr_t) x & 1) || ((uintptr_t) out & 1)) return kErrUnaligned;
-    const int tasks = m * (k / 128);
-    exl3_input_kernel<<<(tasks + 7) / 8, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        reinterpret_cast<const __half*>(x), x_stride, reinterpret_cast<const __half*>(suh),
-        reinterpret_cast<__half*>(out), out_stride, nullptr, nullptr, m, k, 1);
-    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
+    if (count < 1 || count > EXL3B200_MULTI_MAX) return kErrBadArgument;
+    if (!x || !trellis || !n || !suh || !svh || !out || !out_stride || !state || !scratch) return kErrNullPointer;
+    if (out_dtype < 0 || out_dtype > 2) return kErrBadArgument;
+    if (x_stride < k || ((uintptr_t) x & 3) || (x_stride & 1)) return kErrUnaligned;
+    if (((uintptr_t) state & 255) || ((uintptr_t) scratch & 255)) return kErrUnaligned;
+    size_t need_state = 0, need_scratch = 0;
+    for (int i = 0; i < count; ++i) {
+        int rc = check_linear_args(trellis[i], svh[i], m, k, n[i], K, cb);
+        if (rc != kOk) return rc;
+        if (!suh[i] || !out[i]) return kErrNullPointer;
+        if (out_stride[i] < n[i]) return kErrBadShape;
+        need_state += gv_state_bytes_per_problem(n[i]);
+        need_scratch += gv_xd_bytes(m, k) + gv_sblk_bytes(m, k);
+    }
+    if (state_bytes < need_state || scratch_bytes < need_scratch) return kErrWorkspace;
+
+    GvArgs a = {};
+    a.nprob = count;
+    a.out_dtype = out_dtype;
+    a.epi_mode = kEpiStore;
+    char* st = reinterpret_cast<char*>(state);
+    char* sc = reinterpret_cast<char*>(scratch);
+    for (int i = 0; i < count; ++i) {
+        GvProblem& p = a.inl[i];
+        p.trellis = reinterpret_cast<const uint32_t*>(trellis[i]);
+        p.suh = reinterpret_cast<const __half*>(suh[i]);
+        p.svh = reinterpret_cast<const __half*>(svh[i]);
+        p.x = reinterpret_cast<const __half*>(x);
+        p.x_stride = x_stride;
+        p.xd = reinterpret_cast<uint32_t*>(sc);
+        sc += gv_xd_bytes(m, k);
+        p.sblk = cb == 2 ? reinterpret_cast<float*>(sc) : nullptr;
+        sc += gv_sblk_bytes(m, k);
+        p.acc = reinterpret_cast<float*>(st);
+        p.acc_nb_stride = 16 * 128;
+        st += gv_state_bytes_per_problem(n[i]);
+        p.out = out[i];
+        p.out_stride = out_stride[i];
+        p.k = k;
+        p.n = n[i];
+        p.m = m;
+    }
+    return run_inline(a, K, cb, m, (flags >> 8) & 3, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int exl3b200_gemv_combine(const void* x, long long x_stride, int m, int k, const void* trellis, int n,
+                                     int K, int cb, const void* suh, const void* svh, float* out,
+                                     long long out_stride, const int* out_rows, const float* out_scale, int flags,
+                                     void* state, size_t state_bytes, void* scratch, size_t scratch_bytes,
+                                     void* stream)
+{
+    if (!x || !out || !out_rows || !state || !scratch) return kErrNullPointer;
+    int rc = check_linear_args(trellis, svh, m, k, n, K, cb);
+    if (rc != kOk) return rc;
+    if (x_stride < k || out_stride < n) return kErrBadShape;
+    const bool pre_rotated = (flags & EXL3B200_FLAG_INPUT_ROTATED) != 0;
+    if (!pre_rotated && !suh) return kErrNullPointer;
+    if (((uintptr_t) x & 3) || (x_stride & 1)) return kErrUnaligned;
+    if (((uintptr_t) state & 255) || ((uintptr_t) scratch & 255)) return kErrUnaligned;
+    if (state_bytes < gv_state_bytes_per_problem(n) || scratch_bytes < gv_xd_bytes(m, k) + gv_sblk_bytes(m, k))
+        return kErrWorkspace;
+    GvArgs a = {};
+    a.nprob = 1;
+    a.epi_mode = kEpiCombine;
+    GvProblem& p = a.inl[0];
+    p.trellis = reinterpret_cast<const uint32_t*>(trellis);
+    p.suh = pre_rotated ? nullptr : reinterpret_cast<const __half*>(suh);
+    p.svh = reinterpret_cast<const __half*>(svh);
+    p.x = reinterpret_cast<const __half*>(x);
+    p.x_stride = x_stride;
+    p.xd = reinterpret_cast<uint32_t*>(scratch);
+    p.sblk = cb == 2 ? reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + gv_xd_bytes(m, k)) : nullptr;
+    p.acc = reinterpret_cast<float*>(state);
+    p.acc_nb_stride = 16 * 128;
+    p.out = out;
+    p.out_stride = out_stride;
+    p.out_rows = out_rows;
+    p.out_scale = out_scale;
+    p.k = k;
+    p.n = n;
+    p.m = m;
+    return run_inline(a, K, cb, m, (flags >> 8) & 3, reinterpret_cast<cudaStream_t>(stream));
 }

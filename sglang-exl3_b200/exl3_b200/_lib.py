@@ -44,7 +44,20 @@ SIGNATURES = {
     "exl3b200_gemv_scratch_size": (_sz, [_i, _i]),
     "exl3b200_gemv": (_i, [_vp, _ll, _i, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _ll, _i, _i, _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_hadamard_in": (_i, [_vp, _ll, _i, _i, _vp, _vp, _ll, _vp]),
+    "exl3b200_gemv_multi": (_i, [_i, _vp, _ll, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _sz, _vp,
+                                 _sz, _vp]),
+    "exl3b200_gemv_combine": (_i, [_vp, _ll, _i, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _ll, _vp, _vp, _i, _vp, _sz,
+                                   _vp, _sz, _vp]),
+    "exl3b200_batched_state_size": (_sz, [_i, _i, _i]),
+    "exl3b200_batched_scratch_size": (_sz, [_i, _i, _i]),
+    "exl3b200_batched_gemv": (_i, [_vp, _i, _ll, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _vp, _i, _vp, _sz,
+                                   _vp, _sz, _vp]),
+    "exl3b200_moe_state_size": (_sz, [_i, _i, _i, _i]),
+    "exl3b200_moe_scratch_size": (_sz, [_i, _i, _i, _i]),
+    "exl3b200_moe": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
+                          _i, _i, _i, ctypes.c_float, _vp, _ll, _i, _i, _vp, _sz, _vp, _sz, _vp]),
 }
+MULTI_MAX = 8
 
 _lib = None
 _lock = threading.Lock()

@@ -237,3 +237,93 @@ def exl3_gemm(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: to
     """``sglang_exl3_c.exl3_gemm`` (``csrc/exl3_gemm.cu:9-31``): fp16 ``[m, n]``."""
     x2 = x.contiguous().view(x.numel() // x.size(-1), x.size(-1))
     return matmul(x2, trellis, suh, svh, int(K), legacy_codebook(mcg, cb))
+
+
+def _ptr_array(vals) -> "ctypes.Array":
+    import ctypes
+
+    arr = (ctypes.c_void_p * len(vals))()
+    for i, v in enumerate(vals):
+        arr[i] = v
+    return arr
+
+
+def matmul_multi(x: torch.Tensor, linears, K: int, cb: int, outs=None,
+                 out_dtype: torch.dtype = torch.float16, variant: Optional[int] = None):
+    """Several linears ``(trellis, suh, svh)`` over one input in one launch sequence
+    (fused q/k/v or gate/up; replaces the upstream ``exl3_mgemm`` pair GEMM the
+    reference calls, ``src/sglang_exl3/dense.py:91-119``).  Returns the list of
+    outputs (or writes into ``outs``: 2D row-strided views, e.g. column slices of one
+    fused output)."""
+    import ctypes
+
+    count = len(linears)
+    if not 1 <= count <= _lib.MULTI_MAX:
+        raise RuntimeError(f"matmul_multi takes 1..{_lib.MULTI_MAX} linears")
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1 or (x2.stride(0) % 2):
+        x2 = x2.contiguous()
+    for tr, su, sv in linears:
+        _check_linear(x2, tr, su, sv, K)
+    dev = _require_cuda(x2, *[t for lin in linears for t in lin])
+    m, k = x2.shape
+    ns = [tr.size(1) * 16 for tr, _, _ in linears]
+    if outs is None:
+        outs = [torch.empty((m, n), dtype=out_dtype, device=dev) for n in ns]
+    for o, n in zip(outs, ns):
+        if o.dim() != 2 or o.shape != (m, n) or o.stride(-1) != 1:
+            raise RuntimeError("matmul_multi outputs must be [m, n] with unit column stride")
+        if o.dtype != outs[0].dtype:
+            raise RuntimeError("matmul_multi outputs must share a dtype")
+    L = _lib.lib()
+    flags = 0 if variant is None else (int(variant) & 3) << 8
+    for r0 in range(0, m, _lib.GEMV_MAX_M):
+        r1 = min(m, r0 + _lib.GEMV_MAX_M)
+        mc = r1 - r0
+        state_n = sum(L.exl3b200_gemv_state_size(n) for n in ns)
+        scratch_n = count * L.exl3b200_gemv_scratch_size(mc, k)
+        with torch.cuda.device(dev):
+            state = workspace.state_buffer(dev, state_n)
+            scratch = workspace.scratch_buffer(dev, scratch_n)
+            oc = [o[r0:r1] for o in outs]
+            st = L.exl3b200_gemv_multi(
+                count, x2[r0:r1].data_ptr(), x2.stride(0), mc, k, K, cb,
+                _ptr_array([lin[0].data_ptr() for lin in linears]), (ctypes.c_int * count)(*ns),
+                _ptr_array([lin[1].data_ptr() for lin in linears]), _ptr_array([lin[2].data_ptr() for lin in linears]),
+                _ptr_array([o.data_ptr() for o in oc]), (ctypes.c_longlong * count)(*[o.stride(0) for o in oc]),
+                _OUT_DTYPES[outs[0].dtype], flags, state.data_ptr(), state.numel(), scratch.data_ptr(),
+                scratch.numel(), _stream_ptr(dev))
+        _lib.check(st, "exl3b200_gemv_multi")
+    return outs
+
+
+def matmul_combine(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], svh: torch.Tensor,
+                   K: int, cb: int, out: torch.Tensor, rows: torch.Tensor, scale: Optional[torch.Tensor] = None,
+                   input_rotated: bool = False) -> torch.Tensor:
+    """``out[rows[r]] += scale[r] * (x[r] @ W)`` (fp32 out; rows int32, scale fp32;
+    rows of one 16-row chunk must be distinct)."""
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1 or (x2.stride(0) % 2):
+        x2 = x2.contiguous()
+    _check_linear(x2, trellis, suh, svh, K)
+    dev = _require_cuda(x2, trellis, svh, out, rows)
+    if out.dtype != torch.float32 or out.dim() != 2 or out.stride(-1) != 1:
+        raise RuntimeError("out must be a float32 [rows, N] tensor")
+    rows = rows.to(torch.int32).contiguous()
+    scale = None if scale is None else scale.to(torch.float32).contiguous()
+    m, k = x2.shape
+    n = trellis.size(1) * 16
+    L = _lib.lib()
+    flags = _lib.FLAG_INPUT_ROTATED if input_rotated else 0
+    for r0 in range(0, m, _lib.GEMV_MAX_M):
+        r1 = min(m, r0 + _lib.GEMV_MAX_M)
+        with torch.cuda.device(dev):
+            state = workspace.state_buffer(dev, L.exl3b200_gemv_state_size(n))
+            scratch = workspace.scratch_buffer(dev, L.exl3b200_gemv_scratch_size(r1 - r0, k))
+            st = L.exl3b200_gemv_combine(
+                x2[r0:r1].data_ptr(), x2.stride(0), r1 - r0, k, trellis.data_ptr(), n, K, cb,
+                suh.data_ptr() if suh is not None else None, svh.data_ptr(), out.data_ptr(), out.stride(0),
+                rows[r0:r1].data_ptr(), scale[r0:r1].data_ptr() if scale is not None else None, flags,
+                state.data_ptr(), state.numel(), scratch.data_ptr(), scratch.numel(), _stream_ptr(dev))
+        _lib.check(st, "exl3b200_gemv_combine")
+    return out
