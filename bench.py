@@ -3,7 +3,14 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload W]
 
 Workloads (synthetic, seeded):
-* ``linears`` (default): the EXL3 linear layers of one decode step of the
+* ``decode`` (default): greedy decode of the Llama-70B-shaped model (config 4:
+  80 layers, hidden 8192, 64/8 heads x 128, SwiGLU 28672, vocab 128256, all
+  linears EXL3 4 bpw 3INST on this backend; bf16 embeddings, lm_head and KV
+  cache) at ``--batch`` sequences with a 2048-token context (KV cache filled with
+  random values instead of running the random prompt) - one CUDA graph per step.
+  Under torchrun the model is tensor-parallel over the N GPUs (NCCL all-reduce
+  after o and down, vocab-sharded lm_head).  ``value`` is generated tokens/s.
+* ``linears``: the EXL3 linear layers of one decode step of the
   Llama-70B-shaped model (config 4: 80 layers, hidden 8192, 64/8 heads x 128,
   SwiGLU 28672, all linears 4 bpw 3INST) at batch 1: q/k/v/o/gate/up/down = 560
   matmuls over 34.23 GB of trellis codes per step.  Inputs exceed L2, so no flush
@@ -339,6 +346,9 @@ def run_ours(args, world, rank, local):
                 "clocks": clk.summary()}
         return finish(line, args, world)
 
+    if args.workload == "decode":
+        return run_decode(args, world, rank, local, device)
+
     layers, bufs, step_bytes, dims = build_linear_stack(world, rank, device, batch)
     torch.cuda.synchronize()
     s = torch.cuda.Stream(device)
@@ -403,6 +413,85 @@ def run_ours(args, world, rank, local):
     return finish(line, args, world)
 
 
+def run_decode(args, world, rank, local, device):
+    from exl3_b200 import ops
+    from exl3_b200.harness import LLAMA_70B, DecodeModel, exl3_weight_bytes
+
+    hbm_peak, tc_peak, peak_kind = peaks()
+    cfg = LLAMA_70B
+    batch = args.batch
+    new_tokens = 512
+    group = torch.distributed.group.WORLD if world > 1 else None
+    model = DecodeModel(cfg, batch, args.ctx + new_tokens, device, world, rank, group)
+    model.fill_random_kv(args.ctx)
+    model.capture()
+    steps = min(args.steps, new_tokens - args.warmup - 8)
+    model.pos.fill_(args.ctx)
+    model.decode(args.warmup)
+    torch.cuda.synchronize()
+    barrier(world)
+    with ClockSampler(local) as clk:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(model.stream)
+        model.decode(steps)
+        e1.record(model.stream)
+        e1.synchronize()
+    ms = max_over_ranks(world, e0.elapsed_time(e1) / steps)
+    tok_s = batch / (ms * 1e-3)
+    step_bytes = exl3_weight_bytes(cfg, world)
+
+    # end to end through the public API: host prompt token in, each step's token out
+    e2e_n = 8
+    model.pos.fill_(args.ctx)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    model.generate(torch.zeros(batch, dtype=torch.long), e2e_n)
+    e2e_ms = max_over_ranks(world, (time.perf_counter() - t0) / e2e_n * 1e3)
+
+    # dominant kernel in isolation: the fused gate/up launch of each layer
+    gu = [L["gu"] for L in model.layers]
+    x = torch.randn(batch, cfg.hidden, dtype=torch.float16, device=device)
+    outs = [torch.empty(batch, model.i_loc, dtype=torch.float16, device=device) for _ in range(2)]
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        for pair in gu[:3]:
+            ops.matmul_multi(x, pair, cfg.K, cfg.cb, outs=outs)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for pair in gu:
+                ops.matmul_multi(x, pair, cfg.K, cfg.cb, outs=outs)
+        g.replay()
+        kt = time_graph(g, 3, s) / len(gu)
+    torch.cuda.current_stream(device).wait_stream(s)
+    kbytes = 2 * (cfg.hidden * model.i_loc * cfg.K // 8) + 2 * batch * (cfg.hidden + 2 * model.i_loc)
+    k_gbs = kbytes / (kt * 1e-3) / 1e9
+    del g
+    model.release()
+
+    line = {
+        "metric": METRIC, "value": tok_s, "unit": "tok/s", "ms_per_step": ms,
+        "config": {"workload": "llama70b-shape decode (config 4), greedy, one CUDA graph per step",
+                   "model": "llama-70b-shape (random init)", "layers": cfg.layers, "global_batch": batch,
+                   "seq_len": args.ctx, "new_tokens_timed": steps, "parallelism": f"tp{world}", "bpw": cfg.K,
+                   "codebook": "3INST", "kv_cache": "bf16, random contents for the 2048-token prompt",
+                   "l2": "no flush needed: 34.2 GB / tp of codes per step >> 126 MB L2",
+                   "exl3_bytes_per_step_per_rank": step_bytes},
+        "exl3_gbs_per_rank": step_bytes / (ms * 1e-3) / 1e9,
+        "roofline": {"bound": "hbm", "achieved": k_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": k_gbs / hbm_peak,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "kernel": f"fused gate+up EXL3 matmul 8192x2x{model.i_loc} 4bpw M={batch} (3 kernels)"},
+        "e2e": {"value": batch / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": 8 * batch, "d2h_bytes_per_step": 8 * batch,
+                "path": "DecodeModel.generate: host token in, per-step token out, stream sync each step"},
+        "gpu_launches": steps * cfg.layers * 12,
+        "clocks": clk.summary(),
+    }
+    return finish(line, args, world)
+
+
 def finish(line, args, world):
     base = {"n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "fp16 x 4-bit trellis -> fp32 acc",
@@ -432,7 +521,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="linears", choices=["linears", "gemv-c1"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "linears", "gemv-c1"])
+    ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
