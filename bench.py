@@ -16,8 +16,9 @@ Workloads (synthetic, seeded):
   matmuls over 34.23 GB of trellis codes per step.  Inputs exceed L2, so no flush
   is needed.  Under torchrun the step is tensor-parallel over N GPUs:
   q/k/v/gate/up column-sharded, o/down row-sharded with an NCCL all-reduce.
-* ``gemv-c1``: config 1, one 4096x4096 4-bpw 3INST linear at M=1, rotating 40
-  weight copies (> 2x L2) between calls.
+* ``linear``: one ``--k`` x ``--n`` ``--bits``-bpw 3INST linear at ``--batch`` rows
+  (default 4096x4096 4 bpw M=1: config 1), rotating weight copies (> 2x L2)
+  between calls; value in GB/s of trellis + activations.
 
 ``--impl reference`` times the reference's own CPU path for the same workload on
 the host cores: its compiled ``dequant_trellis`` + ``at::mm``
@@ -122,10 +123,13 @@ def dist_setup(n_gpus: int):
 
         import torch.distributed as dist
 
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
-    else:
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+    elif torch.cuda.is_available():
         torch.cuda.set_device(0)
     return world, rank, local
 
@@ -296,7 +300,7 @@ def run_reference(args, world, rank):
         return
     sec, weights, threads = sample
     c = L70
-    if args.workload == "gemv-c1":
+    if args.workload == "linear":
         value, unit = (4096 * 4096 * 0.5) / sec / 1e9, "GB/s"
         ms = sec * 1e3
     else:
@@ -319,30 +323,38 @@ def run_reference(args, world, rank):
 
 def run_ours(args, world, rank, local):
     device = torch.device("cuda", local)
-    from exl3_b200 import ops
+    from exl3_b200 import ops  # noqa: F401
 
     hbm_peak, tc_peak, peak_kind = peaks()
     c = L70
     K, cb = c["K"], c["cb"]
     batch = args.batch
     group = None
-    if args.workload == "gemv-c1":
+    if args.workload == "linear":
         if world > 1:
-            raise SystemExit("gemv-c1 is a single-GPU workload (replicas only)")
+            raise SystemExit("linear is a single-GPU workload (replicas only)")
         gen = torch.Generator(device=device)
         gen.manual_seed(0)
-        copies = [make_linear(gen, 4096, 4096, 4, device) for _ in range(40)]
-        trs, sus, svs = zip(*copies)
+        k_in, n_out, bits = args.k, args.n, args.bits
+        wbytes = k_in * n_out * bits // 8
+        copies = max(1, min(40, (336 << 20) // wbytes + 1))  # rotate > 2x L2 worth of codes
+        lins = [make_linear(gen, k_in, n_out, bits, device) for _ in range(copies)]
+        trs, sus, svs = zip(*lins)
         for _ in range(args.warmup):
-            isolated_kernel_time(trs, sus, svs, 4, 0, batch, 2, device)
+            isolated_kernel_time(trs, sus, svs, bits, 0, batch, 1, device)
         with ClockSampler(local) as clk:
-            ms = isolated_kernel_time(trs, sus, svs, 4, 0, batch, args.steps, device)
-        byts = linear_bytes(4096, 4096, 4, batch)
+            ms = isolated_kernel_time(trs, sus, svs, bits, 0, batch, args.steps, device)
+        byts = linear_bytes(k_in, n_out, bits, batch)
         gbs = byts / (ms * 1e-3) / 1e9
         line = {"metric": METRIC, "value": gbs, "unit": "GB/s", "ms_per_step": ms,
-                "config": {"workload": "gemv-c1", "m": batch, "l2": "40 rotating weight copies (336 MB > 2x L2)"},
+                "config": {"workload": f"linear {k_in}x{n_out} {bits}bpw 3INST m={batch}"
+                                       + (" (config 1)" if (k_in, n_out, bits) == (4096, 4096, 4) else ""),
+                           "m": batch, "copies": copies,
+                           "l2": f"{copies} rotating weight copies ({copies * wbytes >> 20} MB) between calls"},
                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
-                             "frac": gbs / hbm_peak, "traffic": None, "peak_kind": peak_kind},
+                             "frac": gbs / hbm_peak, "traffic": None, "peak_kind": peak_kind,
+                             "kernel": "exl3_gv_matmul_kernel (+ input and epilogue kernels)"},
+                "gpu_launches": 3 * copies * args.steps,
                 "clocks": clk.summary()}
         return finish(line, args, world)
 
@@ -433,10 +445,12 @@ def run_decode(args, world, rank, local, device):
     with ClockSampler(local) as clk:
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.nvtx.range_push("timed")
         e0.record(model.stream)
         model.decode(steps)
         e1.record(model.stream)
         e1.synchronize()
+        torch.cuda.nvtx.range_pop()
     ms = max_over_ranks(world, e0.elapsed_time(e1) / steps)
     tok_s = batch / (ms * 1e-3)
     step_bytes = exl3_weight_bytes(cfg, world)
@@ -521,7 +535,10 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "linears", "gemv-c1"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "linears", "linear"])
+    ap.add_argument("--k", type=int, default=4096)
+    ap.add_argument("--n", type=int, default=4096)
+    ap.add_argument("--bits", type=int, default=4)
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
