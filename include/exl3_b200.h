@@ -111,6 +111,22 @@ EXL3B200_API int exl3b200_gemv_combine(const void* x, long long x_stride, int m,
                                        size_t scratch_bytes, void* stream);
 
 /*
+ * Small-M matmul that allocates nothing and takes no workspace: out = x @ W as
+ * exl3b200_gemv, for callers that cannot allocate device memory (an
+ * allocator-less runtime that owns all device memory up front, or a thread that
+ * must not enter the CUDA allocator).  Its scratch is one device array inside
+ * the library (about 4 MB, held by every GPU that loads the library until the
+ * process exits).  Limits: m <= 16, k <= 32768, n <= 32768; larger sizes return
+ * EXL3B200_EBADSHAPE.  All calls share that array: calls that overlap on the GPU
+ * race, so serialise them.  The first call on a device looks the array up; make
+ * it before capturing a stream.  This entry point has no counterpart in the
+ * reference.
+ */
+EXL3B200_API int exl3b200_gemv_noalloc(const void* x, long long x_stride, int m, int k, const void* trellis, int n,
+                                       int K, int cb, const void* suh, const void* svh, void* out,
+                                       long long out_stride, int out_dtype, void* stream);
+
+/*
  * Several linears over one input in a single launch sequence: out_i = x @ W_i for
  * i < count (count <= EXL3B200_MULTI_MAX), all with the same K, codebook and k.
  * Replaces the upstream exllamav3 exl3_mgemm pair GEMM the reference calls for

@@ -737,3 +737,90 @@ extern "C" int exl3b200_gemv_combine(const void* x, long long x_stride, int m, i
     p.m = m;
     return run_inline(a, K, cb, m, (flags >> 8) & 3, reinterpret_cast<cudaStream_t>(stream));
 }
+
+// ---------------------------------------------------------------------------
+// Small-M matmul that allocates nothing and takes no workspace.
+//
+// Some callers cannot allocate device memory at all: code running inside an
+// allocator-less runtime (a custom serving loop that owns every byte of device
+// memory up front, or a host thread that must not take the CUDA allocator's
+// locks) still needs a matmul.  This entry point serves them: its scratch - the
+// rotated activations and the split-K partial sums - lives in one file-scope
+// device array below, reserved once per GPU when the library is loaded and held
+// until the process exits.  Limits: m <= 16, k <= 32768, n <= 32768.
+//
+// The array is shared by every call on a device and keeps the last call's data,
+// so calls that overlap on the GPU (different streams, or different host
+// threads) race and corrupt each other's results; serialise them.  Each call
+// clears the partial sums it will use before its kernels run.  The first call on
+// each device looks up the array's device address (cudaGetSymbolAddress, with
+// that device current); make that first call before capturing a stream.
+// ---------------------------------------------------------------------------
+namespace exl3b200 {
+
+constexpr int kNoAllocMaxM = 16;
+constexpr int kNoAllocMaxK = 32768;
+constexpr int kNoAllocMaxN = 32768;
+constexpr size_t kNoAllocStateBytes = (size_t) (kNoAllocMaxN / 128) * 16 * 128 * sizeof(float);
+constexpr size_t kNoAllocScratchBytes = (size_t) kNoAllocMaxM * kNoAllocMaxK * sizeof(uint32_t) +
+                                        (size_t) kNoAllocMaxM * (kNoAllocMaxK / 128) * sizeof(float);
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocStateBytes + kNoAllocScratchBytes];
+
+static int noalloc_base(char** base)
+{
+    static void* cache[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kErrLaunch;
+    if (!cache[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return kErrLaunch;
+        cache[dev] = p;
+    }
+    *base = reinterpret_cast<char*>(cache[dev]);
+    return kOk;
+}
+
+}  // namespace exl3b200
+
+extern "C" int exl3b200_gemv_noalloc(const void* x, long long x_stride, int m, int k, const void* trellis, int n,
+                                     int K, int cb, const void* suh, const void* svh, void* out,
+                                     long long out_stride, int out_dtype, void* stream)
+{
+    if (!x || !out || !suh) return kErrNullPointer;
+    int rc = check_linear_args(trellis, svh, m, k, n, K, cb);
+    if (rc != kOk) return rc;
+    if (m > kNoAllocMaxM || k > kNoAllocMaxK || n > kNoAllocMaxN) return kErrBadShape;
+    if (out_dtype < 0 || out_dtype > 2) return kErrBadArgument;
+    if (x_stride < k || out_stride < n) return kErrBadShape;
+    if (((uintptr_t) x & 3) || (x_stride & 1)) return kErrUnaligned;
+    char* base = nullptr;
+    rc = noalloc_base(&base);
+    if (rc != kOk) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const size_t used_state = gv_state_bytes_per_problem(n);
+    if (cudaMemsetAsync(base, 0, used_state, st) != cudaSuccess) return kErrLaunch;
+
+    GvArgs a = {};
+    a.nprob = 1;
+    a.out_dtype = out_dtype;
+    a.epi_mode = kEpiStore;
+    GvProblem& p = a.inl[0];
+    p.trellis = reinterpret_cast<const uint32_t*>(trellis);
+    p.suh = reinterpret_cast<const __half*>(suh);
+    p.svh = reinterpret_cast<const __half*>(svh);
+    p.x = reinterpret_cast<const __half*>(x);
+    p.x_stride = x_stride;
+    char* scratch = base + kNoAllocStateBytes;
+    p.xd = reinterpret_cast<uint32_t*>(scratch);
+    p.sblk = cb == 2 ? reinterpret_cast<float*>(scratch + (size_t) kNoAllocMaxM * kNoAllocMaxK * sizeof(uint32_t))
+                     : nullptr;
+    p.acc = reinterpret_cast<float*>(base);
+    p.acc_nb_stride = 16 * 128;
+    p.out = out;
+    p.out_stride = out_stride;
+    p.k = k;
+    p.n = n;
+    p.m = m;
+    return run_inline(a, K, cb, m, 0, st);
+}

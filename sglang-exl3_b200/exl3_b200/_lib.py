@@ -52,6 +52,7 @@ SIGNATURES = {
     "exl3b200_batched_scratch_size": (_sz, [_i, _i, _i]),
     "exl3b200_batched_gemv": (_i, [_vp, _i, _ll, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _vp, _i, _vp, _sz,
                                    _vp, _sz, _vp]),
+    "exl3b200_gemv_noalloc": (_i, [_vp, _ll, _i, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _ll, _i, _vp]),
     "exl3b200_moe_state_size": (_sz, [_i, _i, _i, _i]),
     "exl3b200_moe_scratch_size": (_sz, [_i, _i, _i, _i]),
     "exl3b200_moe": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
