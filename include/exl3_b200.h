@@ -193,6 +193,40 @@ EXL3B200_API int exl3b200_moe(const void* x, long long x_stride, int tokens, int
 EXL3B200_API int exl3b200_hadamard_in(const void* x, long long x_stride, int m, int k, const void* suh,
                                       void* out, long long out_stride, void* stream);
 
+/*
+ * Large-M matmul on the tensor cores (tcgen05 MMA, TMEM accumulators):
+ * out[m, n] = x[m, k] @ W for any m >= 1, one pass over the codes per 256 rows.
+ * Replaces sglang_exl3_c.exl3_gemm for M > 8 (reference csrc/bindings.cpp:102-132,
+ * csrc/exl3_gemm.cu:9-31; op src/sglang_exl3/ops.py:77-95) and the dense GEMM of
+ * exl3_fat_gemm (csrc/exl3_fat_gemm.cu:65-305; pass EXL3B200_FLAG_INPUT_ROTATED and
+ * an fp32 out).  K in 2..4, k and n multiples of 128, trellis 16-byte aligned.
+ *
+ * state:   exl3b200_gemm_state_size() bytes (a partial-sum slot per SM for the
+ *          output tiles that two CTAs share), 16-byte aligned, ZEROED once when
+ *          allocated; every call leaves it zeroed.  One per concurrent stream; it
+ *          may be the same buffer as the small-M matmul's state on that stream.
+ * scratch: exl3b200_gemm_scratch_size(m, k) bytes, 16-byte aligned, no
+ *          initialisation, one per concurrently running stream (the rotated
+ *          input, laid out as the tensor cores' shared-memory tiles).
+ * svh must be 16-byte aligned.  A device-side wait that gives up (after 1 s)
+ * ends the kernel early and records EXL3B200_ETIMEOUT in the library's device
+ * status (exl3b200_device_status).
+ */
+EXL3B200_API size_t exl3b200_gemm_state_size(void);
+EXL3B200_API size_t exl3b200_gemm_scratch_size(int m, int k);
+EXL3B200_API int exl3b200_gemm(const void* x, long long x_stride, int m, int k, const void* trellis, int n, int K,
+                               int cb, const void* suh, const void* svh, void* out, long long out_stride,
+                               int out_dtype, int flags, void* state, size_t state_bytes, void* scratch,
+                               size_t scratch_bytes, void* stream);
+
+/*
+ * Enqueue on stream a copy of the library's sticky device status (0 or the first
+ * device-side error code, e.g. EXL3B200_ETIMEOUT) into *host_status, and reset it
+ * when reset != 0.  *host_status is valid after the stream has synchronised.
+ * No counterpart in the reference, whose kernels have no device-side waits.
+ */
+EXL3B200_API int exl3b200_device_status(int* host_status, int reset, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,922 @@
+// Large-M EXL3 matmul on the 5th-generation tensor cores (tcgen05 MMA with TMEM
+// accumulators): y = H128(H128(x * suh) @ W_raw) * svh / 128 for m rows at once.
+//
+// Replaces the reference's exl3_gemm for M > 8 (csrc/exl3_gemm.cu:9-31, which
+// runs the upstream exllamav3 smem-decode GEMM) and the dense part of its fat
+// GEMM (csrc/exl3_fat_gemm.cu:65-305).  Three kernels, chained by programmatic
+// dependent launch:
+//
+// * exl3_tc_input_kernel: one warp per (row, 128-block) computes the fp16
+//   x_had = H128(x * suh) / sqrt(128) with the reference's roundings (the same
+//   rotate_block as the small-M path) and writes it straight into the shared
+//   memory image the MMA reads: 128-row x 64-column blocks of 16 KB, rows of 128
+//   bytes whose 16-byte chunks are XOR-swizzled by (row % 8) (the canonical
+//   K-major SWIZZLE_128B layout).  Padding rows up to a multiple of 128 are zero.
+// * exl3_tc_gemm_kernel: persistent, one CTA per SM, stream-K: the output is cut
+//   into 256x256 tiles (rows fastest, so CTAs working on one column block's codes
+//   run together and share them in L2), every tile into k/64 iterations, and the
+//   concatenated iteration list into one contiguous range per CTA.  A CTA's range
+//   is a sequence of segments (a tile's iterations [kc0, kc1)).  Warp roles
+//   (warp w runs on SM sub-partition w % 4):
+//     warp 0    allocates 512 TMEM columns; lane 0 streams the activation blocks
+//               with bulk copies (cp.async.bulk) into a 3-stage ring;
+//     warp 1    lane 0 issues tcgen05.mma (M=128, N=256, K=16, fp16 x fp16 -> fp32)
+//               for each of the two 128-row accumulators and releases ring slots
+//               with tcgen05.commit;
+//     warp 2    lane 0 streams the trellis codes of the tile (4 k-tiles x 16
+//               n-tiles per stage) with bulk copies into a 4-stage ring;
+//     warps 3-23 with w % 4 != 1 (16 warps) decode the codes from shared memory
+//               (window extraction, codebook, final fp16 add / fma; one 16-column
+//               tile x 4 k-tiles per warp and stage) into the B operand (256
+//               output columns x 64 k, K-major, 128-byte swizzle, 3-stage ring);
+//     warps 5, 9, .., 21 share the MMA issuer's sub-partition and only run the
+//               epilogue of TMEM lanes 32..63: a decoder there took issue slots
+//               from the MMA issuer (measured: MMA issue time halved without it).
+//   At the end of a segment each thread of the epilogue owns one TMEM lane
+//   (= output row); H128 over a 128-column block is a 32-point transform per
+//   quarter in registers, written back to TMEM, then the stride-32 and stride-64
+//   butterflies on 8-column slices; scale by svh / sqrt(128).  A segment that is a
+//   whole tile stores the output; a part of a tile split between CTAs adds its
+//   fp32 partial into the tile's slot of a zeroed state buffer (the transform is
+//   linear).
+// * exl3_tc_finish_kernel: converts the split tiles' slots to the output dtype
+//   and re-zeroes them.
+// Every wait on an mbarrier is bounded (1 s of %globaltimer); a wait that runs
+// out raises the CTA's abort flag and the library's sticky device status; every
+// role then leaves its loop, waits (bounded) for its own copies and MMAs in
+// flight, and the CTA frees its TMEM and exits.
+#include <algorithm>
+
+#include "exl3_common.cuh"
+#include "exl3_capi_internal.h"
+
+namespace exl3b200 {
+
+// Warp roles (warp w runs on SM sub-partition w % 4): 0 activation producer,
+// 1 MMA issuer, 2 code producer; of warps 3..23, those with w % 4 == 1 share the
+// MMA issuer's sub-partition and only run the epilogue of TMEM lanes 32..63 (so
+// no decoder competes with the MMA issuer for issue slots); the other 16 decode.
+constexpr int kTcWarps = 24;
+constexpr int kTcDecWarps = 16;
+constexpr int kTcThreads = 32 * kTcWarps;  // 768
+constexpr int kTcRows = 256;          // rows per tile: two M=128 accumulators
+constexpr int kTcCols = 256;          // output columns per tile
+constexpr int kTcStageA = 3;
+constexpr int kTcStageB = 3;
+constexpr int kTcStageT = 4;
+constexpr int kTcABlock = 128 * 64 * 2;        // one 128-row x 64-k fp16 block (16 KB)
+constexpr int kTcBStage = kTcCols * 64 * 2;    // 32 KB
+constexpr int kTcBars = 2 * kTcStageA + 2 * kTcStageT + 2 * kTcStageB + 2;
+constexpr int kTcSlotFloats = kTcRows * kTcCols;  // one split tile's fp32 partial sums
+constexpr unsigned long long kTcTimeoutNs = 1000000000ull;
+
+__device__ int g_exl3_device_status = 0;  // sticky: first device-side error code
+
+template <int K>
+struct TcSmem {
+    static constexpr uint32_t kTChunk = 4u * 16u * 32u * K;  // codes of one stage at 256 columns
+    static constexpr uint32_t kA = 0;
+    static constexpr uint32_t kB = kA + kTcStageA * 2 * kTcABlock;
+    static constexpr uint32_t kT = kB + kTcStageB * kTcBStage;
+    static constexpr uint32_t kBar = kT + kTcStageT * kTChunk;
+    static constexpr uint32_t kMisc = kBar + 8 * kTcBars;
+    static constexpr uint32_t kBytes = kMisc + 16;
+    static constexpr uint32_t kLaunchBytes = kBytes + 1024;  // room to align the base to 1024
+};
+
+struct TcArgs {
+    const uint8_t* xt;        // swizzled rotated input blocks [m128 tiles][k/64][16 KB]
+    const uint8_t* trellis;   // [k/16][n/16][32K bytes]
+    const __half* svh;        // [n], 16-byte aligned
+    void* out;
+    float* slots;             // zeroed [grid][256][256] fp32: partial sums of split tiles
+    long long out_stride;     // elements
+    long long iters;          // tiles * k/64
+    int m, k, n;
+    int mtiles, tiles, nkc;
+    int out_dtype;            // 0 fp16, 1 bf16, 2 fp32
+    int vec_store;            // rows of out are 16-byte aligned
+};
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tc_griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void tc_griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t) __cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count)
+{
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
+{
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ unsigned long long global_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Slow path of a bounded wait: false once the CTA's abort flag is up
+// (check_abort) or the deadline passes (then raises the flag and the status).
+__device__ __forceinline__ bool mbar_test_sleep(uint32_t bar, uint32_t parity)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 200000;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag, bool check_abort)
+{
+    const unsigned long long t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_test_sleep(bar, parity)) return true;
+        if ((it & 63u) == 0) {
+            if (check_abort && *abort_flag) return false;
+            if (global_ns() - t0 > kTcTimeoutNs) {
+                *abort_flag = 1;
+                atomicCAS(&g_exl3_device_status, 0, (int) kErrTimeout);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, bool check_abort)
+{
+    if (mbar_test(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, abort_flag, check_abort);
+}
+
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar)
+{
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (fp16 inputs, fp32 accumulate)
+__device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32])
+{
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32])
+{
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+        "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+        "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+        "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+        "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+        "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+        "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+        "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+        "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+        "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+        "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8])
+{
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Shared memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024
+// bytes apart (SBO), leading offset unused for swizzled K-major (1), version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
+{
+    const uint32_t lo = ((saddr >> 4) & 0x3FFFu) | (1u << 16);
+    const uint32_t hi = (1024u >> 4) | (1u << 14) | (2u << 29);
+    return ((uint64_t) hi << 32) | lo;
+}
+
+// Instruction descriptor, kind::f16: fp32 D, fp16 A and B, both K-major, M = 128.
+__device__ __forceinline__ uint32_t tc_idesc(int n)
+{
+    return (1u << 4) | ((uint32_t) (n >> 3) << 17) | ((uint32_t) (128 >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b)
+{
+    uint32_t r;
+    asm("add.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c)
+{
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+// The 8 fp16 weights of a lane in one tile, packed as the k pairs (j, j+1):
+// h2[0] = (k0, k0+1) at n0, h2[1] = (k0+8, k0+9) at n0, h2[2], h2[3] the same at
+// n0 + 8, with k0 = 2 (lane % 4), n0 = lane / 4.  Round to nearest, exactly as
+// codebook_value_rn (one fp16 rounding of an exact sum / fma).
+template <int K, int CB>
+__device__ __forceinline__ void tc_decode_lane(uint32_t wa, uint32_t wb, int shift7, uint32_t (&h2)[4])
+{
+    uint32_t w[8];
+    lane_windows<K>(wa, wb, shift7, w);
+    uint32_t p[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) p[j] = codebook_pre<CB>(w[j]);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const uint32_t lo = prmt(p[2 * q], p[2 * q + 1], 0x5410);
+        if constexpr (CB == 2) {
+            h2[q] = hfma2_u32(lo, (uint32_t) kMul1InvBits * 0x10001u, (uint32_t) kMul1BiasBits * 0x10001u);
+        } else {
+            const uint32_t hi = prmt(p[2 * q], p[2 * q + 1], 0x7632);
+            h2[q] = hadd2_u32(lo, hi);
+        }
+    }
+}
+
+// One warp's share of a stage: NB16 = 16 n-tiles (256 columns): n-tile dw, k-tiles
+// 0..3; NB16 = 8 (128 columns): n-tile dw % 8, k-tiles 2 (dw / 8) + {0, 1}.
+template <int K, int CB, int NB16>
+__device__ __forceinline__ void tc_decode_stage(const uint8_t* __restrict__ tch, uint8_t* __restrict__ bst, int dw,
+                                                int lane, const LaneWords& lw)
+{
+    constexpr int T = NB16 / 4;
+    const int ntl = NB16 == 16 ? dw : (dw & 7);
+    const int kt0 = NB16 == 16 ? 0 : 2 * (dw >> 3);
+    const uint32_t* tw = reinterpret_cast<const uint32_t*>(tch + (kt0 * NB16 + ntl) * 32 * K);
+    uint32_t wa[T], wb[T];
+#pragma unroll
+    for (int i = 0; i < T; ++i) {
+        wa[i] = tw[i * NB16 * 8 * K + lw.wa];
+        wb[i] = tw[i * NB16 * 8 * K + lw.wb];
+    }
+    const int sw = lane >> 2;
+    uint8_t* rowp = bst + ntl * 16 * 128 + (lane >> 2) * 128 + 4 * (lane & 3);
+#pragma unroll
+    for (int i = 0; i < T; ++i) {
+        uint32_t h2[4];
+        tc_decode_lane<K, CB>(wa[i], wb[i], lw.shift7, h2);
+        const int kt = kt0 + i;
+        const int c_lo = ((2 * kt) ^ sw) << 4, c_hi = ((2 * kt + 1) ^ sw) << 4;
+        *reinterpret_cast<uint32_t*>(rowp + c_lo) = h2[0];
+        *reinterpret_cast<uint32_t*>(rowp + c_hi) = h2[1];
+        *reinterpret_cast<uint32_t*>(rowp + 1024 + c_lo) = h2[2];
+        *reinterpret_cast<uint32_t*>(rowp + 1024 + c_hi) = h2[3];
+    }
+}
+
+// ---------------------------------------------------------------------------
+// input stage
+// ---------------------------------------------------------------------------
+__global__ __launch_bounds__(256) void exl3_tc_input_kernel(const __half* __restrict__ x, long long x_stride,
+                                                            const __half* __restrict__ suh, int m, int mpad, int k,
+                                                            uint8_t* __restrict__ xt)
+{
+    tc_griddep_launch();
+    tc_griddep_wait();
+    const int lane = threadIdx.x & 31;
+    const int nblk = k >> 7;
+    const int nkc = k >> 6;
+    const int tasks = mpad * nblk;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < tasks; task += warps) {
+        const int r = task / nblk;
+        const int b = task - r * nblk;
+        __half h[4];
+        if (r < m) {
+            rotate_block(x + (size_t) r * x_stride + b * 128, suh ? suh + b * 128 : nullptr, lane, h);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) h[i] = __ushort_as_half(0);
+        }
+        const int rr = r & 127;
+        uint8_t* tile_row = xt + ((size_t) (r >> 7) * nkc << 14) + rr * 128;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int kc = 2 * b + (i >> 1);
+            const int kk = lane + 32 * (i & 1);
+            *reinterpret_cast<__half*>(tile_row + ((size_t) kc << 14) + (((kk >> 3) ^ (rr & 7)) << 4) + (kk & 7) * 2) =
+                h[i];
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// epilogue
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void fwht32_local(float (&v)[32])
+{
+#pragma unroll
+    for (int s = 1; s < 32; s <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if ((i & s) == 0) {
+                const float a = v[i], b = v[i + s];
+                v[i] = __fadd_rn(a, b);
+                v[i + s] = __fsub_rn(a, b);
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void store8(const TcArgs& a, int row, int col, const float (&v)[8])
+{
+    if (a.out_dtype == 2) {
+        float* dst = reinterpret_cast<float*>(a.out) + (size_t) row * a.out_stride + col;
+        if (a.vec_store) {
+            reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+            reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = v[i];
+        }
+        return;
+    }
+    uint32_t pk[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        if (a.out_dtype == 0) {
+            const __half2 h = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+        } else {
+            const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+        }
+    }
+    uint16_t* dst = reinterpret_cast<uint16_t*>(a.out) + (size_t) row * a.out_stride + col;
+    if (a.vec_store) {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            dst[2 * i] = (uint16_t) (pk[i] & 0xffffu);
+            dst[2 * i + 1] = (uint16_t) (pk[i] >> 16);
+        }
+    }
+}
+
+// One 128-column block of one 128-row accumulator, this warp's 32 rows.  TMEM
+// lanes = rows; the block's columns are overwritten (the transform runs in place).
+__device__ __forceinline__ void tc_epilogue_block(const TcArgs& a, uint32_t taddr, int row, int col0, bool whole,
+                                                  float* __restrict__ slot_row)
+{
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+        float v[32];
+        tmem_ld32(taddr + 32 * j, v);
+        tmem_ld_wait();
+        fwht32_local(v);
+        tmem_st32(taddr + 32 * j, v);
+    }
+    tmem_st_wait();
+    const uint4* sv4 = reinterpret_cast<const uint4*>(a.svh + col0);
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+        float u[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tmem_ld8(taddr + 32 * j + 8 * c, u[j]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float b0 = __fadd_rn(u[0][i], u[1][i]), b1 = __fsub_rn(u[0][i], u[1][i]);
+            const float b2 = __fadd_rn(u[2][i], u[3][i]), b3 = __fsub_rn(u[2][i], u[3][i]);
+            u[0][i] = __fadd_rn(b0, b2);
+            u[2][i] = __fsub_rn(b0, b2);
+            u[1][i] = __fadd_rn(b1, b3);
+            u[3][i] = __fsub_rn(b1, b3);
+        }
+        if (row >= a.m) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint4 s = __ldg(sv4 + 4 * j + c);
+            const __half* sh = reinterpret_cast<const __half*>(&s);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) u[j][i] = u[j][i] * kHadScale * __half2float(sh[i]);
+            const int col = 32 * j + 8 * c;
+            if (whole) {
+                store8(a, row, col0 + col, u[j]);
+            } else {
+                float4* dst = reinterpret_cast<float4*>(slot_row + col);
+                atomicAdd(dst, make_float4(u[j][0], u[j][1], u[j][2], u[j][3]));
+                atomicAdd(dst + 1, make_float4(u[j][4], u[j][5], u[j][6], u[j][7]));
+            }
+        }
+    }
+}
+
+// first iteration of CTA c, and the CTA that runs iteration it
+__device__ __forceinline__ long long tc_range_start(long long iters, int grid, int c)
+{
+    return iters * c / grid;
+}
+
+__device__ __forceinline__ int tc_cta_of(long long iters, int grid, long long it)
+{
+    return (int) (((it + 1) * grid - 1) / iters);
+}
+
+// ---------------------------------------------------------------------------
+// matmul
+// ---------------------------------------------------------------------------
+template <int K, int CB>
+__global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __grid_constant__ TcArgs a)
+{
+    using L = TcSmem<K>;
+    extern __shared__ uint8_t tc_smem_raw[];
+    const uint32_t raw = smem_u32(tc_smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* gbase = tc_smem_raw + (base - raw);
+    const uint32_t sA = base + L::kA, sB = base + L::kB, sT = base + L::kT, sBar = base + L::kBar;
+    const uint32_t full_a = sBar, empty_a = full_a + 8 * kTcStageA;
+    const uint32_t full_t = empty_a + 8 * kTcStageA, empty_t = full_t + 8 * kTcStageT;
+    const uint32_t full_b = empty_t + 8 * kTcStageT, empty_b = full_b + 8 * kTcStageB;
+    const uint32_t acc_full = empty_b + 8 * kTcStageB, acc_empty = acc_full + 8;
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + L::kMisc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kMisc + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int grid = gridDim.x;
+    const long long it_begin = tc_range_start(a.iters, grid, blockIdx.x);
+    const long long it_end = tc_range_start(a.iters, grid, blockIdx.x + 1);
+    const int nkc = a.nkc;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTcStageA; ++s) {
+            mbar_init(full_a + 8 * s, 1);
+            mbar_init(empty_a + 8 * s, 1);
+        }
+        for (int s = 0; s < kTcStageT; ++s) {
+            mbar_init(full_t + 8 * s, 1);
+            mbar_init(empty_t + 8 * s, kTcDecWarps);
+        }
+        for (int s = 0; s < kTcStageB; ++s) {
+            mbar_init(full_b + 8 * s, kTcDecWarps);
+            mbar_init(empty_b + 8 * s, 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, kTcWarps - 3);  // every decoder and epilogue-only warp
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        tmem_alloc(base + L::kMisc, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    tc_griddep_launch();
+
+    if (warp == 0) {
+        // activation producer
+        tc_griddep_wait();  // the input stage of this call wrote xt
+        if (lane == 0) {
+            uint32_t s = 0, ph = 0, used = 0, par = 0;  // ring slot, phase; per-slot issued / parity bits
+            bool ok = true;
+            for (long long it = it_begin; it < it_end && ok;) {
+                const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
+                const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
+                const int mt = tile % a.mtiles;
+                const int nacc = a.m - mt * kTcRows > 128 ? 2 : 1;
+                const uint8_t* src0 = a.xt + (((size_t) (2 * mt) * nkc + kc0) << 14);
+                const size_t acc_step = (size_t) nkc << 14;
+                for (int kc = kc0; kc < kc1; ++kc, src0 += kTcABlock) {
+                    if (!mbar_wait(empty_a + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
+                    mbar_expect_tx(full_a + 8 * s, (uint32_t) (nacc * kTcABlock));
+                    bulk_g2s(sA + (s * 2) * kTcABlock, src0, kTcABlock, full_a + 8 * s);
+                    if (nacc == 2) bulk_g2s(sA + (s * 2 + 1) * kTcABlock, src0 + acc_step, kTcABlock, full_a + 8 * s);
+                    used |= 1u << s;
+                    par = (par & ~(1u << s)) | (ph << s);
+                    if (++s == kTcStageA) { s = 0; ph ^= 1; }
+                }
+                it += kc1 - kc0;
+            }
+            // own copies in flight (all consumed already unless the CTA aborted)
+            for (uint32_t j = 0; j < kTcStageA; ++j)
+                if (used >> j & 1) mbar_wait(full_a + 8 * j, par >> j & 1, abort_flag, false);
+        }
+    } else if (warp == 2) {
+        // code producer
+        if (lane == 0) {
+            const size_t row_bytes = (size_t) (a.n >> 4) * 32 * K;
+            uint32_t s = 0, ph = 0, used = 0, par = 0;
+            bool ok = true;
+            for (long long it = it_begin; it < it_end && ok;) {
+                const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
+                const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
+                const int nt = tile / a.mtiles;
+                const int bn = min(kTcCols, a.n - nt * kTcCols);
+                const uint32_t seg = (uint32_t) (bn >> 4) * 32 * K;
+                const uint8_t* src = a.trellis + (size_t) kc0 * 4 * row_bytes + (size_t) nt * 16 * 32 * K;
+                for (int kc = kc0; kc < kc1; ++kc, src += 4 * row_bytes) {
+                    if (!mbar_wait(empty_t + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
+                    mbar_expect_tx(full_t + 8 * s, 4 * seg);
+                    const uint32_t dst = sT + s * L::kTChunk;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) bulk_g2s(dst + i * seg, src + i * row_bytes, seg, full_t + 8 * s);
+                    used |= 1u << s;
+                    par = (par & ~(1u << s)) | (ph << s);
+                    if (++s == kTcStageT) { s = 0; ph ^= 1; }
+                }
+                it += kc1 - kc0;
+            }
+            for (uint32_t j = 0; j < kTcStageT; ++j)
+                if (used >> j & 1) mbar_wait(full_t + 8 * j, par >> j & 1, abort_flag, false);
+        }
+    } else if (warp == 1) {
+        // MMA issuer
+        if (lane == 0) {
+            uint32_t sa = 0, pa = 0, sb = 0, pb = 0;
+            int seg_i = 0;
+            bool ok = true;
+            const uint64_t a_desc0 = sw128_desc(sA), b_desc0 = sw128_desc(sB);
+            for (long long it = it_begin; it < it_end && ok; ++seg_i) {
+                const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
+                const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
+                const int mt = tile % a.mtiles, nt = tile / a.mtiles;
+                const int nacc = a.m - mt * kTcRows > 128 ? 2 : 1;
+                const uint32_t idesc = tc_idesc(min(kTcCols, a.n - nt * kTcCols));
+                // the epilogue of the previous segment has read the accumulators
+                if (!mbar_wait(acc_empty, (uint32_t) (seg_i & 1) ^ 1, abort_flag, true)) break;
+                tc_fence_after();
+                for (int kc = kc0; kc < kc1; ++kc) {
+                    if (!mbar_wait(full_a + 8 * sa, pa, abort_flag, true) ||
+                        !mbar_wait(full_b + 8 * sb, pb, abort_flag, true)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    // descriptor start addresses advance in 16-byte units: 32 bytes per k-step
+                    const uint64_t ad = a_desc0 + sa * (2 * kTcABlock >> 4);
+                    const uint64_t bd = b_desc0 + sb * (kTcBStage >> 4);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) {
+                        const uint32_t acc_flag = (kc != kc0 || ks != 0) ? 1u : 0u;
+                        tc_mma(tmem, ad + 2 * ks, bd + 2 * ks, idesc, acc_flag);
+                        if (nacc == 2) tc_mma(tmem + 256, ad + (kTcABlock >> 4) + 2 * ks, bd + 2 * ks, idesc, acc_flag);
+                    }
+                    tc_commit(empty_a + 8 * sa);
+                    tc_commit(empty_b + 8 * sb);
+                    if (++sa == kTcStageA) { sa = 0; pa ^= 1; }
+                    if (++sb == kTcStageB) { sb = 0; pb ^= 1; }
+                }
+                tc_commit(acc_full);
+                it += kc1 - kc0;
+            }
+            // every MMA issued by this thread has completed before the CTA frees TMEM
+            // (a commit tracks all of the thread's earlier tcgen05 operations)
+            if (seg_i > 0) mbar_wait(acc_full, (uint32_t) ((seg_i - 1) & 1), abort_flag, false);
+        }
+    } else {
+        // decoders (and the epilogue of their TMEM lane quarter) or epilogue-only
+        // warps of lane quarter 1
+        const int q = warp & 3;                               // TMEM lane quarter this warp may access
+        const int hq = q == 3 ? warp >> 2 : (warp >> 2) - 1;  // its index among the quarter's warps
+        const bool decoder = q != 1;
+        const int dw = (warp - 3) - (warp - 2) / 4;           // decoder index 0..15
+        tc_griddep_wait();
+        const LaneWords lw = lane_words<K>(lane);
+        uint32_t st = 0, pt = 0, sb = 0, pb = 0;
+        int seg_i = 0;
+        bool ok = true;
+        for (long long it = it_begin; it < it_end && ok; ++seg_i) {
+            const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
+            const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
+            const int mt = tile % a.mtiles, nt = tile / a.mtiles;
+            const int bn = min(kTcCols, a.n - nt * kTcCols);
+            if (decoder) {
+                for (int kc = kc0; kc < kc1; ++kc) {
+                    if (!mbar_wait(full_t + 8 * st, pt, abort_flag, true) ||
+                        !mbar_wait(empty_b + 8 * sb, pb ^ 1, abort_flag, true)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint8_t* tch = gbase + L::kT + st * L::kTChunk;
+                    uint8_t* bst = gbase + L::kB + sb * kTcBStage;
+                    if (bn == kTcCols) tc_decode_stage<K, CB, 16>(tch, bst, dw, lane, lw);
+                    else tc_decode_stage<K, CB, 8>(tch, bst, dw, lane, lw);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(full_b + 8 * sb);
+                        mbar_arrive(empty_t + 8 * st);
+                    }
+                    if (++st == kTcStageT) { st = 0; pt ^= 1; }
+                    if (++sb == kTcStageB) { sb = 0; pb ^= 1; }
+                }
+            }
+            if (!ok || !mbar_wait(acc_full, (uint32_t) (seg_i & 1), abort_flag, true)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int nacc = a.m - mt * kTcRows > 128 ? 2 : 1;
+            const int nblk = bn >> 7;
+            if (hq < nacc * nblk) {
+                const int acc = hq / nblk, cb = hq - acc * nblk;
+                const int row = mt * kTcRows + acc * 128 + q * 32 + lane;
+                const bool whole = kc0 == 0 && kc1 == nkc;
+                float* slot_row = nullptr;
+                if (!whole) {
+                    const int slot = tc_cta_of(a.iters, grid, (long long) tile * nkc);
+                    slot_row = a.slots + (size_t) slot * kTcSlotFloats + (size_t) (acc * 128 + q * 32 + lane) * kTcCols +
+                               cb * 128;
+                }
+                tc_epilogue_block(a, tmem + ((uint32_t) (q * 32) << 16) + acc * 256 + cb * 128, row,
+                                  nt * kTcCols + cb * 128, whole, slot_row);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty);
+            it += kc1 - kc0;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+// Split tiles: the slot of CTA c holds the tile that contains c's range end,
+// when that tile starts inside c's range.  One CTA per slot.
+__global__ __launch_bounds__(256) void exl3_tc_finish_kernel(const __grid_constant__ TcArgs a, int grid)
+{
+    tc_griddep_wait();
+    const int c = blockIdx.x;
+    const long long start = tc_range_start(a.iters, grid, c);
+    const long long end = tc_range_start(a.iters, grid, c + 1);
+    if (end >= a.iters || end % a.nkc == 0) return;
+    const int tile = (int) (end / a.nkc);
+    if ((long long) tile * a.nkc < start) return;
+    const int mt = tile % a.mtiles, nt = tile / a.mtiles;
+    const int rows = min(kTcRows, a.m - mt * kTcRows);
+    const int cols = min(kTcCols, a.n - nt * kTcCols);
+    float* slot = a.slots + (size_t) c * kTcSlotFloats;
+    const int cols8 = cols >> 3;
+    for (int e = threadIdx.x; e < rows * cols8; e += blockDim.x) {
+        const int r = e / cols8, c8 = (e - r * cols8) * 8;
+        float4* src = reinterpret_cast<float4*>(slot + (size_t) r * kTcCols + c8);
+        const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
+        __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
+        __stcg(src + 1, make_float4(0.f, 0.f, 0.f, 0.f));
+        const float v[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        store8(a, mt * kTcRows + r, nt * kTcCols + c8, v);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static int tc_sm_count()
+{
+    static int count[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (!count[dev]) {
+        int c = 0;
+        if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) c = 148;
+        count[dev] = c;
+    }
+    return count[dev];
+}
+
+static cudaError_t tc_launch(const void* kern, int grid, int block, size_t smem, cudaStream_t stream, void** args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) grid);
+    cfg.blockDim = dim3((unsigned) block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, kern, args);
+}
+
+template <int K, int CB>
+static int tc_launch_gemm(const TcArgs& a, int grid, cudaStream_t stream)
+{
+    using L = TcSmem<K>;
+    static bool configured[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kErrLaunch;
+    if (!configured[dev]) {
+        if (cudaFuncSetAttribute(exl3_tc_gemm_kernel<K, CB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int) L::kLaunchBytes) != cudaSuccess)
+            return kErrLaunch;
+        configured[dev] = true;
+    }
+    TcArgs arg = a;
+    void* args[] = {&arg};
+    return tc_launch((const void*) exl3_tc_gemm_kernel<K, CB>, grid, kTcThreads, L::kLaunchBytes, stream, args) ==
+                   cudaSuccess
+               ? kOk
+               : kErrLaunch;
+}
+
+template <int K>
+static int tc_launch_cb(const TcArgs& a, int cb, int grid, cudaStream_t stream)
+{
+    if (cb == 0) return tc_launch_gemm<K, 0>(a, grid, stream);
+    if (cb == 1) return tc_launch_gemm<K, 1>(a, grid, stream);
+    return tc_launch_gemm<K, 2>(a, grid, stream);
+}
+
+static size_t tc_xt_bytes(int m, int k) { return (size_t) ((m + 127) / 128) * 128 * (size_t) k * 2; }
+
+static size_t tc_state_bytes() { return (size_t) tc_sm_count() * kTcSlotFloats * sizeof(float); }
+
+}  // namespace exl3b200
+
+using namespace exl3b200;
+
+extern "C" size_t exl3b200_gemm_scratch_size(int m, int k)
+{
+    if (m <= 0 || k <= 0 || k % 128) return 0;
+    return tc_xt_bytes(m, k);
+}
+
+extern "C" size_t exl3b200_gemm_state_size(void) { return tc_state_bytes(); }
+
+extern "C" int exl3b200_gemm(const void* x, long long x_stride, int m, int k, const void* trellis, int n, int K, int cb,
+                             const void* suh, const void* svh, void* out, long long out_stride, int out_dtype,
+                             int flags, void* state, size_t state_bytes, void* scratch, size_t scratch_bytes,
+                             void* stream)
+{
+    if (!x || !out || !trellis || !svh || !scratch || !state) return kErrNullPointer;
+    if (K < 2 || K > 4) return kErrBadBits;
+    if (cb < 0 || cb > 2) return kErrBadCodebook;
+    if (out_dtype < 0 || out_dtype > 2) return kErrBadArgument;
+    if (m < 1 || k <= 0 || n <= 0 || (k % 128) || (n % 128)) return kErrBadShape;
+    if (x_stride < k || out_stride < n) return kErrBadShape;
+    const bool pre_rotated = (flags & EXL3B200_FLAG_INPUT_ROTATED) != 0;
+    if (!pre_rotated && !suh) return kErrNullPointer;
+    if (((uintptr_t) x & 1) || ((uintptr_t) out & 3)) return kErrUnaligned;
+    if (((uintptr_t) trellis & 15) || ((uintptr_t) scratch & 15) || ((uintptr_t) svh & 15)) return kErrUnaligned;
+    if ((uintptr_t) state & 15) return kErrUnaligned;
+    if (scratch_bytes < tc_xt_bytes(m, k) || state_bytes < tc_state_bytes()) return kErrWorkspace;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+
+    const int mtiles = (m + kTcRows - 1) / kTcRows;
+    const int ntiles = (n + kTcCols - 1) / kTcCols;
+    const long long tiles = (long long) mtiles * ntiles;
+    if (tiles > 0x7fffffffLL) return kErrBadShape;
+    const int nkc = k / 64;
+    const long long iters = tiles * nkc;
+    const int grid = (int) std::min<long long>(tc_sm_count(), iters);
+
+    const int mpad = (m + 127) / 128 * 128;
+    const int in_tasks = mpad * (k / 128);
+    const int in_grid = std::min((in_tasks + 7) / 8, 8 * tc_sm_count());
+    exl3_tc_input_kernel<<<in_grid, 256, 0, st>>>(reinterpret_cast<const __half*>(x), x_stride,
+                                                   pre_rotated ? nullptr : reinterpret_cast<const __half*>(suh), m,
+                                                   mpad, k, reinterpret_cast<uint8_t*>(scratch));
+    if (cudaPeekAtLastError() != cudaSuccess) return kErrLaunch;
+
+    TcArgs a = {};
+    a.xt = reinterpret_cast<const uint8_t*>(scratch);
+    a.trellis = reinterpret_cast<const uint8_t*>(trellis);
+    a.svh = reinterpret_cast<const __half*>(svh);
+    a.out = out;
+    a.slots = reinterpret_cast<float*>(state);
+    a.out_stride = out_stride;
+    a.iters = iters;
+    a.m = m;
+    a.k = k;
+    a.n = n;
+    a.mtiles = mtiles;
+    a.tiles = (int) tiles;
+    a.nkc = nkc;
+    a.out_dtype = out_dtype;
+    const int esz = out_dtype == 2 ? 4 : 2;
+    a.vec_store = ((uintptr_t) out % 16 == 0) && ((out_stride * esz) % 16 == 0);
+    int rc;
+    switch (K) {
+        case 2: rc = tc_launch_cb<2>(a, cb, grid, st); break;
+        case 3: rc = tc_launch_cb<3>(a, cb, grid, st); break;
+        default: rc = tc_launch_cb<4>(a, cb, grid, st); break;
+    }
+    if (rc != kOk) return rc;
+    if (grid > 1) {
+        int g = grid;
+        void* args[] = {&a, &g};
+        if (tc_launch((const void*) exl3_tc_finish_kernel, grid, 256, 0, st, args) != cudaSuccess) return kErrLaunch;
+    }
+    return kOk;
+}
+
+extern "C" int exl3b200_device_status(int* host_status, int reset, void* stream)
+{
+    if (!host_status) return kErrNullPointer;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaMemcpyFromSymbolAsync(host_status, g_exl3_device_status, sizeof(int), 0, cudaMemcpyDeviceToHost, st) !=
+        cudaSuccess)
+        return kErrLaunch;
+    if (reset) {
+        static const int zero = 0;
+        if (cudaMemcpyToSymbolAsync(g_exl3_device_status, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) !=
+            cudaSuccess)
+            return kErrLaunch;
+    }
+    return kOk;
+}

@@ -26,6 +26,8 @@ STATUS_NAMES = {
     9: "EXL3B200_ETIMEOUT",
 }
 
+EBADSHAPE, EBADBITS, EBADCODEBOOK, EUNALIGNED, ELAUNCH, EWORKSPACE, ENULL, EBADARG, ETIMEOUT = range(1, 10)
+
 DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 FLAG_INPUT_ROTATED = 1
 GEMV_MAX_M = 16
@@ -53,6 +55,10 @@ SIGNATURES = {
     "exl3b200_batched_gemv": (_i, [_vp, _i, _ll, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp, _i, _vp, _i, _vp, _sz,
                                    _vp, _sz, _vp]),
     "exl3b200_gemv_noalloc": (_i, [_vp, _ll, _i, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _ll, _i, _vp]),
+    "exl3b200_gemm_state_size": (_sz, []),
+    "exl3b200_gemm_scratch_size": (_sz, [_i, _i]),
+    "exl3b200_gemm": (_i, [_vp, _ll, _i, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _ll, _i, _i, _vp, _sz, _vp, _sz, _vp]),
+    "exl3b200_device_status": (_i, [_vp, _i, _vp]),
     "exl3b200_moe_state_size": (_sz, [_i, _i, _i, _i]),
     "exl3b200_moe_scratch_size": (_sz, [_i, _i, _i, _i]),
     "exl3b200_moe": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,

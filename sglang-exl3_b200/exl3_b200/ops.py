@@ -164,14 +164,53 @@ def _check_linear(x2: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, sv
         raise RuntimeError("suh K dimension does not match trellis")
 
 
+# Row count from which ``matmul`` uses the tensor-core kernel instead of 16-row
+# chunks of the small-M kernel.
+TC_MIN_ROWS = 32
+
+
+def _gemm_into(x2: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], svh: torch.Tensor,
+               K: int, cb: int, out: torch.Tensor, flags: int) -> None:
+    m, k = x2.shape
+    n = trellis.size(1) * 16
+    dev = x2.device
+    L = _lib.lib()
+    if svh.data_ptr() % 16:
+        svh = svh.clone()
+    with torch.cuda.device(dev):
+        state = workspace.state_buffer(dev, L.exl3b200_gemm_state_size())
+        scratch = workspace.scratch_buffer(dev, L.exl3b200_gemm_scratch_size(m, k))
+        st = L.exl3b200_gemm(x2.data_ptr(), x2.stride(0), m, k, trellis.data_ptr(), n, K, cb,
+                             suh.data_ptr() if suh is not None else None, svh.data_ptr(),
+                             out.data_ptr(), out.stride(0), _OUT_DTYPES[out.dtype], flags,
+                             state.data_ptr(), state.numel(), scratch.data_ptr(), scratch.numel(),
+                             _stream_ptr(dev))
+    _lib.check(st, "exl3b200_gemm")
+
+
+def device_status(device: Optional[torch.device] = None, reset: bool = True) -> int:
+    """The library's sticky device-side status (0, or e.g. ``ETIMEOUT`` when a
+    tensor-core kernel's bounded wait gave up); synchronises the current stream."""
+    import ctypes
+
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    host = torch.zeros(1, dtype=torch.int32).pin_memory()
+    with torch.cuda.device(dev):
+        st = _lib.lib().exl3b200_device_status(ctypes.c_void_p(host.data_ptr()), int(reset), _stream_ptr(dev))
+        _lib.check(st, "exl3b200_device_status")
+        torch.cuda.current_stream(dev).synchronize()
+    return int(host.item())
+
+
 def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], svh: torch.Tensor,
            K: Optional[int] = None, cb: int = 0, out_dtype: torch.dtype = torch.float16,
            out: Optional[torch.Tensor] = None, input_rotated: bool = False,
-           variant: Optional[int] = None) -> torch.Tensor:
+           variant: Optional[int] = None, path: Optional[str] = None) -> torch.Tensor:
     """``y = x @ W`` for any number of rows: ``x [..., k]`` fp16 -> ``[..., n]``.
 
-    Rows go to the small-M kernel in chunks of at most 16 (replaces
-    ``exl3_gemm_cuda``'s chunks of 8, ``csrc/exl3_gemm.cu:20-29``).  ``out`` may be a
+    From ``TC_MIN_ROWS`` rows on (or ``path="tc"``), one tensor-core GEMM over all
+    rows; below, the small-M kernel in chunks of at most 16 rows (``path="gemv"``).
+    Replaces ``exl3_gemm_cuda`` (``csrc/exl3_gemm.cu:9-31``).  ``out`` may be a
     row-strided 2D view (e.g. a column slice of a fused qkv output)."""
     if K is None:
         K = bits_of(trellis)
@@ -194,9 +233,15 @@ def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], 
     flags = _lib.FLAG_INPUT_ROTATED if input_rotated else 0
     if variant is not None:
         flags |= (int(variant) & 3) << 8
-    for r0 in range(0, m, _lib.GEMV_MAX_M):
-        r1 = min(m, r0 + _lib.GEMV_MAX_M)
-        _gemv_into(x2[r0:r1], trellis, suh, svh, K, cb, out2[r0:r1], flags)
+    if path not in (None, "tc", "gemv"):
+        raise RuntimeError("path must be None, 'tc' or 'gemv'")
+    use_tc = path == "tc" or (path is None and m >= TC_MIN_ROWS and trellis.data_ptr() % 16 == 0)
+    if use_tc:
+        _gemm_into(x2, trellis.contiguous(), suh, svh, K, cb, out2, flags)
+    else:
+        for r0 in range(0, m, _lib.GEMV_MAX_M):
+            r1 = min(m, r0 + _lib.GEMV_MAX_M)
+            _gemv_into(x2[r0:r1], trellis, suh, svh, K, cb, out2[r0:r1], flags)
     if out is not None:
         return out
     return out2.view(*lead, n)

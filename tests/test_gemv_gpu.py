@@ -80,7 +80,8 @@ def test_gemv_strided_output_slice(cuda_device):
 
 def test_gemv_rows_above_16_are_chunked(cuda_device):
     x, tr, su, sv = _case(13, 37, 256, 256, 2)
-    y = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), 2, 0)
+    y = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), 2, 0,
+                   path="gemv")
     assert O.normwise_rel_err(y.float().cpu().numpy(), O.gemv_ref(x, tr, su, sv, 2, 0)) < TOL_F32_ACC
 
 

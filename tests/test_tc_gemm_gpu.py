@@ -1,0 +1,138 @@
+"""Tensor-core (tcgen05) EXL3 matmul on the GPU against the oracle.
+
+Tolerance as for the small-M kernel: fp32 accumulation, so normwise relative
+error (max|y - y_ref| / max|y_ref|) below 2e-3 against an fp32 matmul on the
+round-to-nearest dequantised weights; bf16 outputs 4e-3.  Row counts cover one
+and two 128-row accumulators, partial tiles and tiles of 128 output columns.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import exl3_oracle as O
+from exl3_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+TOL_F32_ACC = 2e-3
+TOL_BF16_OUT = 4e-3
+
+
+def _t(a, dev):
+    return torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+
+
+def _case(seed, m, k, n, K):
+    rng = np.random.default_rng(seed)
+    tr = O.random_trellis(rng, k, n, K)
+    su = O.random_signs(rng, k)
+    sv = O.random_signs(rng, n)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    return x, tr, su, sv
+
+
+def _run(dev, x, tr, su, sv, K, cb, **kw):
+    return ops.matmul(_t(x, dev), _t(tr, dev), _t(su, dev), _t(sv, dev), K, cb, path="tc", **kw)
+
+
+@pytest.mark.parametrize("K", [2, 3, 4])
+@pytest.mark.parametrize("cb", [0, 1, 2])
+def test_tc_parity(cuda_device, K, cb):
+    x, tr, su, sv = _case(3000 + 10 * K + cb, 300, 512, 384, K)
+    y = _run(cuda_device, x, tr, su, sv, K, cb)
+    assert y.shape == (300, 384) and y.dtype == torch.float16
+    assert O.normwise_rel_err(y.float().cpu().numpy(), O.gemv_ref(x, tr, su, sv, K, cb)) < TOL_F32_ACC
+    assert ops.device_status(cuda_device) == 0
+
+
+@pytest.mark.parametrize("m", [1, 17, 128, 129, 256, 257, 513])
+def test_tc_row_edges(cuda_device, m):
+    x, tr, su, sv = _case(3100 + m, m, 256, 640, 4)
+    y = _run(cuda_device, x, tr, su, sv, 4, 0)
+    assert O.normwise_rel_err(y.float().cpu().numpy(), O.gemv_ref(x, tr, su, sv, 4, 0)) < TOL_F32_ACC
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, TOL_F32_ACC), (torch.bfloat16, TOL_BF16_OUT)])
+def test_tc_out_dtypes(cuda_device, dtype, tol):
+    x, tr, su, sv = _case(3200, 200, 384, 256, 3)
+    y = _run(cuda_device, x, tr, su, sv, 3, 1, out_dtype=dtype)
+    assert y.dtype == dtype
+    assert O.normwise_rel_err(y.float().cpu().numpy(), O.gemv_ref(x, tr, su, sv, 3, 1)) < tol
+
+
+def test_tc_strided_output_slice(cuda_device):
+    """Column slice of a wider output whose row pitch is not a multiple of 8."""
+    x, tr, su, sv = _case(3300, 70, 256, 128, 4)
+    wide = torch.full((70, 388), 7.0, dtype=torch.float16, device=cuda_device)
+    _run(cuda_device, x, tr, su, sv, 4, 0, out=wide[:, 130:258])
+    w = wide.float().cpu().numpy()
+    assert np.all(w[:, :130] == 7.0) and np.all(w[:, 258:] == 7.0)
+    assert O.normwise_rel_err(w[:, 130:258], O.gemv_ref(x, tr, su, sv, 4, 0)) < TOL_F32_ACC
+
+
+def test_tc_input_rotated_fp32_out(cuda_device):
+    """The fat-GEMM form: pre-rotated input, fp32 output (csrc/exl3_fat_gemm.cu)."""
+    x, tr, su, sv = _case(3400, 96, 512, 256, 3)
+    xh = O.input_transform(x, su)
+    y = ops.matmul(_t(xh, cuda_device), _t(tr, cuda_device), None, _t(sv, cuda_device), 3, 0,
+                   out_dtype=torch.float32, input_rotated=True, path="tc")
+    assert O.normwise_rel_err(y.cpu().numpy(), O.gemv_ref(x, tr, su, sv, 3, 0)) < TOL_F32_ACC
+
+
+def test_tc_config2_down_shape(cuda_device):
+    """Config 2's down projection shape (k = 25600 -> n = 5120 in the benchmark;
+    here k = 5120, n = 2560 to keep the oracle fast), MCG 4 bpw, 256 rows."""
+    x, tr, su, sv = _case(1, 256, 5120, 2560, 4)
+    y = _run(cuda_device, x, tr, su, sv, 4, 1)
+    assert O.normwise_rel_err(y.float().cpu().numpy(), O.gemv_ref(x, tr, su, sv, 4, 1)) < TOL_F32_ACC
+
+
+def test_tc_matches_gemv_path(cuda_device):
+    x, tr, su, sv = _case(3500, 48, 1024, 512, 3)
+    args = [_t(a, cuda_device) for a in (x, tr, su, sv)]
+    y_tc = ops.matmul(*args, 3, 2, path="tc").float().cpu().numpy()
+    y_gv = ops.matmul(*args, 3, 2, path="gemv").float().cpu().numpy()
+    ref = O.gemv_ref(x, tr, su, sv, 3, 2)
+    assert O.normwise_rel_err(y_tc, ref) < TOL_F32_ACC
+    assert O.normwise_rel_err(y_gv, ref) < TOL_F32_ACC
+
+
+def test_tc_cuda_graph_replay(cuda_device):
+    x, tr, su, sv = _case(3600, 160, 512, 512, 4)
+    xd, trd, sud, svd = (_t(a, cuda_device) for a in (x, tr, su, sv))
+    s = torch.cuda.Stream(cuda_device)
+    s.wait_stream(torch.cuda.current_stream(cuda_device))
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            ops.matmul(xd, trd, sud, svd, 4, 0, path="tc")
+    torch.cuda.current_stream(cuda_device).wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        y = ops.matmul(xd, trd, sud, svd, 4, 0, path="tc")
+    x2 = np.random.default_rng(98).standard_normal((160, 512)).astype(np.float16)
+    xd.copy_(_t(x2, cuda_device))
+    g.replay()
+    torch.cuda.synchronize()
+    assert O.normwise_rel_err(y.float().cpu().numpy(), O.gemv_ref(x2, tr, su, sv, 4, 0)) < TOL_F32_ACC
+    del g
+
+
+def test_tc_rejects_bad_input(cuda_device):
+    from exl3_b200 import _lib
+
+    L = _lib.lib()
+    x = torch.zeros((64, 256), dtype=torch.float16, device=cuda_device)
+    tr = torch.zeros((16, 8, 64), dtype=torch.int16, device=cuda_device)
+    s = torch.ones(256, dtype=torch.float16, device=cuda_device)
+    out = torch.empty((64, 128), dtype=torch.float16, device=cuda_device)
+    scr = torch.empty(1 << 20, dtype=torch.uint8, device=cuda_device)
+    state = torch.zeros(L.exl3b200_gemm_state_size(), dtype=torch.uint8, device=cuda_device)
+    stream = torch.cuda.current_stream(cuda_device).cuda_stream
+    args = lambda K, n, tr_ptr, scr_n: (x.data_ptr(), 256, 64, 256, tr_ptr, n, K, 0, s.data_ptr(), s.data_ptr(),
+                                        out.data_ptr(), 128, 0, 0, state.data_ptr(), state.numel(), scr.data_ptr(),
+                                        scr_n, stream)
+    assert L.exl3b200_gemm(*args(5, 128, tr.data_ptr(), scr.numel())) == _lib.EBADBITS
+    assert L.exl3b200_gemm(*args(4, 100, tr.data_ptr(), scr.numel())) == _lib.EBADSHAPE
+    assert L.exl3b200_gemm(*args(4, 128, tr.data_ptr() + 4, scr.numel())) == _lib.EUNALIGNED
+    assert L.exl3b200_gemm(*args(4, 128, tr.data_ptr(), 16)) == _lib.EWORKSPACE
