@@ -19,6 +19,16 @@ Workloads (synthetic, seeded):
 * ``linear``: one ``--k`` x ``--n`` ``--bits``-bpw 3INST linear at ``--batch`` rows
   (default 4096x4096 4 bpw M=1: config 1), rotating weight copies (> 2x L2)
   between calls; value in GB/s of trellis + activations.
+* ``mlp``: config 2, the dense SwiGLU MLP block (hidden 5120, intermediate 25600;
+  fused gate+up one 3-bpw 3INST trellis of N = 2 x 25600, SiLU*mul, down 4 bpw MCG;
+  seed 1) at ``--batch`` = M rows; small-M kernels below 32 rows, the tensor-core
+  GEMM from 32.  Under torchrun: tensor parallel (gate/up column shards, down row
+  shards, NCCL all-reduce).  Value in tokens (rows)/s; roofline in TFLOP/s.
+* ``moe``: config 3, a routed MoE layer (288 experts top-8, hidden 2048, expert
+  intermediate 1024, 3 bpw 3INST; one 4-bpw shared expert; router logits fp32
+  N(0,1) -> softmax -> renormalised top-8; seed 2) at ``--batch`` = T tokens.  Under
+  torchrun: expert parallel (288/N experts per rank, all-to-all dispatch and
+  combine, ``exl3_b200.ep``); value in tokens/s.
 
 ``--impl reference`` times the reference's own CPU path for the same workload on
 the host cores: its compiled ``dequant_trellis`` + ``at::mm``
@@ -286,6 +296,24 @@ def cpu_baseline_sample(steps_hint: int = 1):
     return float(np.median(ts)), 4096 * 4096, torch.get_num_threads()
 
 
+def workload_scale(args):
+    """(weights decoded per step, units per step, unit) of a workload, to scale the
+    reference CPU sample (its cost is the per-weight dequant; at::mm is minor)."""
+    c = L70
+    if args.workload == "linear":
+        return args.k * args.n, args.k * args.n * args.bits / 8 / 1e9, "GB/s"
+    if args.workload == "mlp":
+        H, I = 5120, 25600
+        return H * 2 * I + I * H, args.batch, "rows/s"
+    if args.workload == "moe":
+        E, topk, H, I = 288, 8, 2048, 1024
+        touched = E * (1.0 - (1.0 - topk / E) ** args.batch)  # expected distinct experts under uniform routing
+        return touched * 3 * H * I + 3 * H * I, args.batch, "tok/s"
+    model_weights = c["layers"] * (2 * c["hidden"] ** 2 + 2 * c["hidden"] * c["kv_heads"] * c["head_dim"]
+                                   + 3 * c["hidden"] * c["inter"])
+    return model_weights, args.batch, "tok/s"
+
+
 # ---------------------------------------------------------------------------
 # arms
 # ---------------------------------------------------------------------------
@@ -299,21 +327,16 @@ def run_reference(args, world, rank):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (python oracle/build_ref.py)"}))
         return
     sec, weights, threads = sample
-    c = L70
-    if args.workload == "linear":
-        value, unit = (4096 * 4096 * 0.5) / sec / 1e9, "GB/s"
-        ms = sec * 1e3
-    else:
-        model_weights = c["layers"] * (2 * c["hidden"] ** 2 + 2 * c["hidden"] * c["kv_heads"] * c["head_dim"]
-                                       + 3 * c["hidden"] * c["inter"])
-        step_s = sec * model_weights / weights
-        value, unit = 1.0 / step_s, "tok/s"
-        ms = step_s * 1e3
+    step_weights, units, unit = workload_scale(args)
+    step_s = sec * step_weights / weights
+    value = units / step_s
+    ms = step_s * 1e3
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "fp32 (reference CPU dequant + at::mm)", "data": "synthetic (seeded)",
-        "config": {"workload": args.workload, "sample": "one 4096x4096 4-bpw MCG linear per step, scaled by weight count"},
+        "config": {"workload": args.workload, "batch": args.batch,
+                   "sample": "one 4096x4096 4-bpw MCG linear per step, scaled by the workload's weight count"},
         "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "reference",
                          "sample": "reference dequant_trellis + at::mm on one 4096x4096 linear (MCG: the binding cannot select 3INST)"},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -360,6 +383,10 @@ def run_ours(args, world, rank, local):
 
     if args.workload == "decode":
         return run_decode(args, world, rank, local, device)
+    if args.workload == "mlp":
+        return run_mlp(args, world, rank, local, device)
+    if args.workload == "moe":
+        return run_moe(args, world, rank, local, device)
 
     layers, bufs, step_bytes, dims = build_linear_stack(world, rank, device, batch)
     torch.cuda.synchronize()
@@ -422,6 +449,196 @@ def run_ours(args, world, rank, local):
         "clocks": clk.summary(),
     }
     del g
+    return finish(line, args, world)
+
+
+def run_mlp(args, world, rank, local, device):
+    """Config 2: dense SwiGLU MLP block at M = --batch rows (TP over the ranks)."""
+    from exl3_b200 import ops
+
+    hbm_peak, tc_peak, peak_kind = peaks()
+    H, I = 5120, 25600
+    if I % (128 * world):
+        raise SystemExit("intermediate size does not shard over this many ranks")
+    i_loc = I // world
+    m = args.batch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1 + 1000 * rank)
+    gu = make_linear(gen, H, 2 * i_loc, 3, device)       # [gate_r | up_r], 3 bpw 3INST
+    down = make_linear(gen, i_loc, H, 4, device)         # 4 bpw MCG
+    x = torch.randn(m, H, dtype=torch.float16, device=device, generator=gen)
+    gu_out = torch.empty(m, 2 * i_loc, dtype=torch.float16, device=device)
+    act = torch.empty(m, i_loc, dtype=torch.float16, device=device)
+    out = torch.empty(m, H, dtype=torch.float16, device=device)
+    group = torch.distributed.group.WORLD if world > 1 else None
+
+    def step():
+        ops.matmul(x, *gu, 3, 0, out=gu_out)
+        torch.mul(torch.nn.functional.silu(gu_out[:, :i_loc]), gu_out[:, i_loc:], out=act)
+        ops.matmul(act, *down, 4, 1, out=out)
+        if world > 1:
+            torch.distributed.all_reduce(out, group=group)
+
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        step()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            step()
+        for _ in range(args.warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        with ClockSampler(local) as clk:
+            ms = time_graph(g, args.steps, s)
+        ms = max_over_ranks(world, ms)
+    torch.cuda.current_stream(device).wait_stream(s)
+    flops = 2.0 * m * (H * 2 * I + I * H)
+    wbytes = (H * 2 * I * 3 + I * H * 4) // 8
+    tflops = flops / (ms * 1e-3) / 1e12
+    gbs = wbytes / world / (ms * 1e-3) / 1e9
+    tensor_bound = m >= 64
+    roof = ({"bound": "tensor", "achieved": tflops / world, "peak": tc_peak, "unit": "TFLOP/s",
+             "frac": tflops / world / tc_peak} if tensor_bound else
+            {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak})
+    roof.update({"traffic": None, "peak_kind": peak_kind, "per": "rank",
+                 "kernel": "whole MLP block (gate+up, SiLU*mul, down) per rank"})
+
+    # end to end: host x in, host y out, eager calls
+    px = torch.randn(m, H, dtype=torch.float16).pin_memory()
+    py = torch.empty(m, H, dtype=torch.float16).pin_memory()
+    torch.cuda.synchronize()
+    barrier(world)
+    n_e2e = max(1, min(args.steps, 5))
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        x.copy_(px, non_blocking=True)
+        step()
+        py.copy_(out, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(world, (time.perf_counter() - t0) / n_e2e * 1e3)
+    del g
+    line = {"metric": "C2 SwiGLU MLP block rows/s", "value": m / (ms * 1e-3), "unit": "rows/s", "ms_per_step": ms,
+            "config": {"workload": f"config 2 SwiGLU MLP block, M={m}", "hidden": H, "intermediate": I,
+                       "gate_up": "3 bpw 3INST fused N=2x25600", "down": "4 bpw MCG", "parallelism": f"tp{world}",
+                       "l2": f"{wbytes >> 20} MB of codes per step (> 126 MB L2), no flush",
+                       "path": "tensor-core GEMM" if m >= 32 else "small-M kernels"},
+            "tflops": tflops, "exl3_gbs_per_rank": gbs,
+            "roofline": roof,
+            "e2e": {"value": m / (e2e_ms * 1e-3), "unit": "rows/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": px.numel() * 2, "d2h_bytes_per_step": py.numel() * 2},
+            "gpu_launches": args.steps * (6 if m >= 32 else 2 * 3 * ((m + 15) // 16)),
+            "clocks": clk.summary()}
+    return finish(line, args, world)
+
+
+def run_moe(args, world, rank, local, device):
+    """Config 3: routed MoE layer (288 experts top-8) + shared expert at T = --batch tokens."""
+    from exl3_b200 import moe as M
+    from exl3_b200 import ops
+    from exl3_b200.ep import ExpertParallelMoE, exl3_local_experts
+
+    hbm_peak, tc_peak, peak_kind = peaks()
+    E, topk, H, I, K = 288, 8, 2048, 1024, 3
+    if E % world:
+        raise SystemExit("288 experts do not split over this many ranks")
+    el = E // world
+    T = args.batch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(2 + 1000 * rank)
+    w13 = torch.randint(-32768, 32768, (el, 2, H // 16, I // 16, 16 * K), dtype=torch.int16, device=device, generator=gen)
+    w2 = torch.randint(-32768, 32768, (el, I // 16, H // 16, 16 * K), dtype=torch.int16, device=device, generator=gen)
+
+    def signs(*shape):
+        return ((torch.randint(0, 2, shape, device=device, generator=gen) * 2 - 1).half()
+                * (torch.rand(shape, device=device, generator=gen) + 0.5).half())
+
+    w13_suh, w13_svh, w2_suh, w2_svh = signs(el, 2, H), signs(el, 2, I), signs(el, I), signs(el, H)
+
+    def ptrs(t):
+        return torch.tensor([int(t[e].data_ptr()) for e in range(el)], dtype=torch.int64, device=device)
+
+    tables = {"gate_trellis": ptrs(w13[:, 0]), "gate_suh": ptrs(w13_suh[:, 0]), "gate_svh": ptrs(w13_svh[:, 0]),
+              "up_trellis": ptrs(w13[:, 1]), "up_suh": ptrs(w13_suh[:, 1]), "up_svh": ptrs(w13_svh[:, 1]),
+              "down_trellis": ptrs(w2), "down_suh": ptrs(w2_suh), "down_svh": ptrs(w2_svh)}
+    shared_gen = torch.Generator(device=device)
+    shared_gen.manual_seed(2)  # the shared expert is replicated
+    sh_gate = make_linear(shared_gen, H, I, 4, device)
+    sh_up = make_linear(shared_gen, H, I, 4, device)
+    sh_down = make_linear(shared_gen, I, H, 4, device)
+    rgen = torch.Generator(device=device)
+    rgen.manual_seed(2)
+    x = torch.randn(T, H, dtype=torch.float16, device=device, generator=rgen)
+    logits = torch.randn(T, E, dtype=torch.float32, device=device, generator=rgen)
+    local_fn = exl3_local_experts(tables, K, K, K, 0, I)
+    ep = ExpertParallelMoE(E, world, rank, torch.distributed.group.WORLD) if world > 1 else None
+    sh_gu = [torch.empty(T, I, dtype=torch.float16, device=device) for _ in range(2)]
+    sh_act = torch.empty(T, I, dtype=torch.float16, device=device)
+    sh_out = torch.empty(T, H, dtype=torch.float16, device=device)
+
+    def step():
+        p = torch.softmax(logits, dim=-1)
+        w, ids = torch.topk(p, topk, dim=-1)
+        w = w / w.sum(-1, keepdim=True)
+        if ep is None:
+            out = local_fn(x, ids.to(torch.int32), w)
+        else:
+            out = ep(x, ids, w, local_fn)
+        ops.matmul_multi(x, [sh_gate, sh_up], 4, 0, outs=sh_gu)
+        torch.mul(torch.nn.functional.silu(sh_gu[0]), sh_gu[1], out=sh_act)
+        ops.matmul(sh_act, *sh_down, 4, 0, out=sh_out)
+        out += sh_out.float()
+        return out
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    with ClockSampler(local) as clk:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        e1.synchronize()
+    ms = max_over_ranks(world, e0.elapsed_time(e1) / args.steps)
+    # distinct experts touched and their code bytes (the HBM roofline of the step)
+    with torch.no_grad():
+        ids_all = torch.topk(torch.softmax(logits, -1), topk, dim=-1)[1]
+        touched = int(torch.unique(ids_all).numel())
+    expert_bytes = (2 * H * I + I * H) * K // 8
+    step_bytes = touched * expert_bytes / world + 3 * H * I * 4 // 8
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+
+    px = torch.randn(T, H, dtype=torch.float16).pin_memory()
+    py = torch.empty(T, H, dtype=torch.float32).pin_memory()
+    torch.cuda.synchronize()
+    barrier(world)
+    n_e2e = max(1, min(args.steps, 5))
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        x.copy_(px, non_blocking=True)
+        y = step()
+        py.copy_(y, non_blocking=True)
+        torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(world, (time.perf_counter() - t0) / n_e2e * 1e3)
+    line = {"metric": "C3 routed MoE layer tokens/s", "value": T / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms,
+            "config": {"workload": f"config 3 MoE layer, T={T}", "experts": E, "topk": topk, "hidden": H,
+                       "intermediate": I, "bpw": K, "codebook": "3INST", "shared_expert": "4 bpw",
+                       "parallelism": f"ep{world}" if world > 1 else "single GPU",
+                       "experts_touched": touched,
+                       "l2": "expert codes 2.36 MB each; time includes routing (softmax/top-k) and the shared expert"},
+            "exl3_gbs_per_rank": gbs,
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                         "traffic": None, "peak_kind": peak_kind,
+                         "kernel": "whole MoE layer per rank (touched experts' codes / step time)"},
+            "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
+                    "h2d_bytes_per_step": px.numel() * 2, "d2h_bytes_per_step": py.numel() * 4},
+            "gpu_launches": args.steps * (5 * ((T * topk + 2047) // 2048) + 6),
+            "clocks": clk.summary()}
     return finish(line, args, world)
 
 
@@ -516,13 +733,8 @@ def finish(line, args, world):
             sample = cpu_baseline_sample(1)
             if sample is not None:
                 sec, weights, threads = sample
-                if base.get("unit") == "GB/s":
-                    v, u = weights * 0.5 / sec / 1e9, "GB/s"
-                else:
-                    c = L70
-                    model_weights = c["layers"] * (2 * c["hidden"] ** 2 + 2 * c["hidden"] * c["kv_heads"] * c["head_dim"]
-                                                   + 3 * c["hidden"] * c["inter"])
-                    v, u = 1.0 / (sec * model_weights / weights), "tok/s"
+                step_weights, units, u = workload_scale(args)
+                v = units / (sec * step_weights / weights)
                 base["cpu_baseline"] = {"value": v, "unit": u, "cores": threads, "kind": "reference",
                                         "sample": "reference dequant_trellis + at::mm, one 4096x4096 4-bpw MCG linear"}
         print(json.dumps(base))
@@ -535,7 +747,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "linears", "linear"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "linears", "linear", "mlp", "moe"])
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--bits", type=int, default=4)
