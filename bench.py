@@ -704,7 +704,8 @@ def run_decode(args, world, rank, local, device):
 
     line = {
         "metric": METRIC, "value": tok_s, "unit": "tok/s", "ms_per_step": ms,
-        "config": {"workload": "llama70b-shape decode (config 4), greedy, one CUDA graph per step",
+        "config": {"workload": "llama70b-shape decode (config 4), greedy, one CUDA graph per step"
+                               + (", fused decode layers" if model.fused else ", unfused torch glue"),
                    "model": "llama-70b-shape (random init)", "layers": cfg.layers, "global_batch": batch,
                    "seq_len": args.ctx, "new_tokens_timed": steps, "parallelism": f"tp{world}", "bpw": cfg.K,
                    "codebook": "3INST", "kv_cache": "bf16, random contents for the 2048-token prompt",
@@ -717,7 +718,8 @@ def run_decode(args, world, rank, local, device):
         "e2e": {"value": batch / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": 8 * batch, "d2h_bytes_per_step": 8 * batch,
                 "path": "DecodeModel.generate: host token in, per-step token out, stream sync each step"},
-        "gpu_launches": steps * cfg.layers * 12,
+        # fused: per layer 7 (attention) + 5 (MLP) launches, + 2 residual kernels per layer under TP
+        "gpu_launches": steps * cfg.layers * ((12 + (2 if world > 1 else 0)) if model.fused else 12),
         "clocks": clk.summary(),
     }
     return finish(line, args, world)

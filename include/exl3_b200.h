@@ -227,6 +227,58 @@ EXL3B200_API int exl3b200_gemm(const void* x, long long x_stride, int m, int k, 
  */
 EXL3B200_API int exl3b200_device_status(int* host_status, int reset, void* stream);
 
+/*
+ * One EXL3 linear as the decode-layer entry points take it.
+ */
+typedef struct exl3b200_linear {
+    const void* trellis; /* int16 [k/16][n/16][16K], 4-byte aligned */
+    const void* suh;     /* fp16 [k] */
+    const void* svh;     /* fp16 [n] */
+    int k, n;
+} exl3b200_linear;
+
+/*
+ * Fused decode sub-layers of a Llama-style decoder for batch <= 16 sequences,
+ * head_dim 128, query heads per kv head <= 8.  No counterpart in the reference,
+ * whose layers call SGLang's norm / attention / activation kernels around the
+ * EXL3 ops (dense.py:317-371); each step follows the unfused model (RMSNorm,
+ * RoPE rotate-half, softmax attention over the bf16 cache, SwiGLU, residual).
+ *
+ * State is the residual stream h (fp32 [batch][hidden], row stride h_stride) and
+ * two alternating per-row sum-of-squares buffers: a sub-layer reads ss_in
+ * (sum of h^2 per row, for its RMSNorm), zeroes ss_out and - when y_out is NULL -
+ * adds its output into h and the new sum of squares into ss_out.  With y_out
+ * (tensor parallelism) it stores its fp32 partial output in y_out instead; after
+ * the all-reduce, exl3b200_residual_add(h, y, ss_out) completes the sub-layer.
+ *
+ * Attention: k_cache / v_cache are this layer's bf16 [batch][kv_heads][max_ctx][128];
+ * *pos (device) is the new token's position, the cache holds 0..pos-1 and the
+ * call appends position pos; inv_freq is fp32 [64] (RoPE, rotate-half).
+ * MLP: swiglu_limit 0 or infinite = no clamp.
+ * state (zeroed once, left zeroed) and scratch sizes: the *_workspace functions;
+ * 256-byte aligned; per concurrently running stream.
+ */
+EXL3B200_API int exl3b200_decode_attention_workspace(int batch, int hidden, int q_heads, int kv_heads, int max_ctx,
+                                                     size_t* state_bytes, size_t* scratch_bytes);
+EXL3B200_API int exl3b200_decode_mlp_workspace(int batch, int hidden, int inter, size_t* state_bytes,
+                                               size_t* scratch_bytes);
+EXL3B200_API int exl3b200_decode_attention(int batch, int hidden, int q_heads, int kv_heads, int K, int cb, float* h,
+                                           long long h_stride, const float* ss_in, float* ss_out,
+                                           const void* norm_w, float eps, const exl3b200_linear* q,
+                                           const exl3b200_linear* k, const exl3b200_linear* v,
+                                           const exl3b200_linear* o, void* k_cache, void* v_cache, int max_ctx,
+                                           const long long* pos, const float* inv_freq, float* y_out,
+                                           long long y_stride, void* state, size_t state_bytes, void* scratch,
+                                           size_t scratch_bytes, void* stream);
+EXL3B200_API int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int cb, float* h, long long h_stride,
+                                     const float* ss_in, float* ss_out, const void* norm_w, float eps,
+                                     const exl3b200_linear* gate, const exl3b200_linear* up,
+                                     const exl3b200_linear* down, float swiglu_limit, float* y_out,
+                                     long long y_stride, void* state, size_t state_bytes, void* scratch,
+                                     size_t scratch_bytes, void* stream);
+EXL3B200_API int exl3b200_residual_add(int batch, int hidden, float* h, long long h_stride, const float* y,
+                                       long long y_stride, float* ss_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,635 @@
+// Fused decode layer around the EXL3 small-M matmul: the glue of a Llama-style
+// decoder layer (RMSNorm, RoPE, KV-cache append, attention, residual adds,
+// SwiGLU) moved into the matmul pipeline's own input stages and epilogues, so a
+// decode step runs about a dozen kernels per layer instead of ~75.
+//
+// Attention sub-layer (exl3b200_decode_attention), all launches chained by
+// programmatic dependent launch:
+//   1. input stage, norm mode: x = fp16(h * rsqrt(ss/hidden + eps) * w) (ss = the
+//      row's sum of squares, accumulated by the previous residual epilogue), then
+//      the usual fp16 x*suh, H128, /sqrt(128) for each of q, k, v; zeroes the
+//      sum-of-squares buffer the next residual epilogue accumulates into;
+//   2. grouped matmul over q, k, v;
+//   3. epilogue, RoPE/KV mode: each (row, head) block of q and k is rotated
+//      (rotate-half pairs (d, d+64) sit in one lane of the warp-wide H128 layout),
+//      q is stored scaled by 1/sqrt(head_dim), k and v are appended to the bf16
+//      cache at the current position;
+//   4. split-K attention: one CTA per (row, kv head, 64-position chunk), one warp
+//      per query head of the group: scores, chunk softmax (max, sum) and the
+//      weighted sum of V, written as partials;
+//   5. input stage, attention mode: merges a head's chunk partials (log-sum-exp
+//      rescale), normalises, fp16, then x*suh, H128 for the o projection;
+//   6. matmul (o);
+//   7. epilogue, residual mode: h += y and the row's new sum of squares (or, with
+//      tensor parallelism, an fp32 store of the partial y for the all-reduce).
+// MLP sub-layer (exl3b200_decode_mlp): norm input stage for gate and up, their
+// grouped matmul, the SwiGLU epilogue that writes the down projection's rotated
+// input, the down matmul and the residual epilogue.
+//
+// The reference has no decode-layer fusion (its layers call SGLang's norm,
+// attention and activation kernels around the EXL3 ops); the arithmetic of each
+// step follows the unfused model in exl3_b200/harness.py.
+#include <algorithm>
+
+#include "exl3_common.cuh"
+#include "exl3_capi_internal.h"
+#include "exl3_grouped.cuh"
+#include "exl3_grouped_dev.cuh"
+
+namespace exl3b200 {
+
+constexpr int kDecChunk = 64;   // attention positions per CTA
+constexpr int kHeadDim = 128;
+
+enum DecInMode : int { kInNorm = 0, kInAttn = 1 };
+enum DecEpiMode : int { kEpiRopeKV = 10, kEpiResidual = 11 };
+
+struct DecAux {
+    // norm input stage
+    const float* h;
+    long long h_stride;
+    const float* ss_in;
+    float* ss_out;           // zeroed by the norm input stage (rows zero_rows)
+    int zero_rows;
+    const __nv_bfloat16* norm_w;
+    float eps;
+    float inv_hidden;
+    // RoPE / KV append / attention
+    const long long* pos;    // position of the new token (= tokens already cached)
+    const float* inv_freq;   // [head_dim / 2]
+    float* qbuf;             // [batch][q_heads][128], scaled by 1/sqrt(128)
+    __nv_bfloat16* k_cache;  // [batch][kv_heads][max_ctx][128]
+    __nv_bfloat16* v_cache;
+    long long cache_b_stride, cache_h_stride;
+    int max_ctx, q_heads, kv_heads, max_chunks;
+    float* attn_o;           // [batch][q_heads][max_chunks][128] unnormalised partial outputs
+    float* attn_ml;          // [batch][q_heads][max_chunks][2] (chunk max, chunk sum)
+    // residual epilogue
+    float* resid;
+    long long resid_stride;
+    float* ss_acc;
+};
+
+// fp16 values (already rounded) of one 128-block -> rotated input of a problem
+// (the GEMV input stage's layout: duplicated fp16 pairs, block sums for mul1).
+__device__ __forceinline__ void dec_store_rotated(const GvProblem& p, int r, int b, int lane, float (&xv)[4])
+{
+    float v[4];
+    if (p.suh) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            v[i] = __half2float(__float2half_rn(__fmul_rn(xv[i], __half2float(p.suh[b * 128 + lane + 32 * i]))));
+        warp_fwht128(v, lane);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], kHadScale);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = xv[i];
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half hh = __float2half_rn(v[i]);
+        const uint32_t u = __half_as_ushort(hh);
+        p.xd[(size_t) r * p.k + b * 128 + lane + 32 * i] = u | (u << 16);
+        s += __half2float(hh);
+    }
+    if (p.sblk) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) p.sblk[(size_t) r * (p.k >> 7) + b] = s;
+    }
+}
+
+template <int MODE>
+__global__ __launch_bounds__(256) void exl3_dec_input_kernel(const __grid_constant__ GvArgs a,
+                                                             const __grid_constant__ DecAux x)
+{
+    griddep_launch();
+    griddep_wait();
+    const int lane = threadIdx.x & 31;
+    if (MODE == kInNorm && x.ss_out && blockIdx.x == 0)
+        for (int i = threadIdx.x; i < x.zero_rows; i += blockDim.x) x.ss_out[i] = 0.f;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < a.in_tasks; task += warps) {
+        const int pi = gv_find<0>(a, a.nprob, task);
+        const GvProblem& p = gv_prob(a, pi);
+        const int nblk = p.k >> 7;
+        const int local = task - p.in_task_begin;
+        const int r = local / nblk;
+        const int b = local - r * nblk;
+        float xv[4];
+        if constexpr (MODE == kInNorm) {
+            const float rs = rsqrtf(x.ss_in[r] * x.inv_hidden + x.eps);
+            const float* hr = x.h + (size_t) r * x.h_stride + b * 128;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int c = lane + 32 * i;
+                xv[i] = __half2float(__float2half_rn(hr[c] * rs * __bfloat162float(x.norm_w[b * 128 + c])));
+            }
+        } else {
+            // block b of the o-projection input = query head b
+            const int L = (int) (*x.pos) + 1;
+            const int nch = (L + kDecChunk - 1) / kDecChunk;
+            const size_t hb = (size_t) r * x.q_heads + b;
+            const float* ml = x.attn_ml + hb * x.max_chunks * 2;
+            const float* po = x.attn_o + hb * x.max_chunks * kHeadDim;
+            float mx = -INFINITY;
+            for (int c = 0; c < nch; ++c) mx = fmaxf(mx, ml[2 * c]);
+            float l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int c = 0; c < nch; ++c) {
+                const float f = __expf(ml[2 * c] - mx);
+                l += f * ml[2 * c + 1];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] += f * po[(size_t) c * kHeadDim + lane + 32 * i];
+            }
+            const float inv = 1.f / l;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xv[i] = __half2float(__float2half_rn(o[i] * inv));
+        }
+        dec_store_rotated(p, r, b, lane, xv);
+    }
+}
+
+template <int CB, int MODE>
+__global__ __launch_bounds__(256) void exl3_dec_epilogue_kernel(const __grid_constant__ GvArgs a,
+                                                                const __grid_constant__ DecAux x)
+{
+    griddep_launch();
+    griddep_wait();
+    const int lane = threadIdx.x & 31;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < a.out_tasks; task += warps) {
+        const int pi = gv_find<1>(a, a.nprob, task);
+        const GvProblem& p = gv_prob(a, pi);
+        const int nblocks = p.n >> 7;
+        const int local = task - p.out_task_begin;
+        const int r = local / nblocks;
+        const int nb = local - r * nblocks;
+        float v[4];
+        gv_finish<CB>(p, nb, r, lane, v);
+        if constexpr (MODE == kEpiRopeKV) {
+            // problems 0, 1, 2 = q, k, v; block nb = head nb; lane holds dims lane + 32e
+            const long long pos = *x.pos;
+            if (pi < 2) {
+                const float fpos = (float) pos;
+                float s0, c0, s1, c1;
+                sincosf(fpos * x.inv_freq[lane], &s0, &c0);
+                sincosf(fpos * x.inv_freq[lane + 32], &s1, &c1);
+                const float n0 = v[0] * c0 - v[2] * s0, n2 = v[2] * c0 + v[0] * s0;
+                const float n1 = v[1] * c1 - v[3] * s1, n3 = v[3] * c1 + v[1] * s1;
+                v[0] = n0;
+                v[1] = n1;
+                v[2] = n2;
+                v[3] = n3;
+            }
+            if (pi == 0) {
+                float* q = x.qbuf + ((size_t) r * x.q_heads + nb) * kHeadDim;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) q[lane + 32 * e] = v[e] * kHadScale;  // 1/sqrt(head_dim), head_dim = 128
+            } else {
+                __nv_bfloat16* c = (pi == 1 ? x.k_cache : x.v_cache) + (size_t) r * x.cache_b_stride +
+                                   (size_t) nb * x.cache_h_stride + (size_t) pos * kHeadDim;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) c[lane + 32 * e] = __float2bfloat16_rn(v[e]);
+            }
+        } else {
+            float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
+            float sq = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float nv = hr[lane + 32 * e] + v[e];
+                hr[lane + 32 * e] = nv;
+                sq += nv * nv;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            if (lane == 0) atomicAdd(x.ss_acc + r, sq);
+        }
+    }
+}
+
+// Split-K decode attention over the bf16 cache (positions 0..pos inclusive).
+__global__ __launch_bounds__(256) void exl3_dec_attn_kernel(const __grid_constant__ DecAux x)
+{
+    griddep_launch();
+    griddep_wait();
+    __shared__ __align__(16) __nv_bfloat16 ks[kDecChunk][kHeadDim];
+    __shared__ __align__(16) __nv_bfloat16 vs[kDecChunk][kHeadDim];
+    const int chunk = blockIdx.x % x.max_chunks;
+    const int t = blockIdx.x / x.max_chunks;
+    const int kvh = t % x.kv_heads;
+    const int b = t / x.kv_heads;
+    const int L = (int) (*x.pos) + 1;
+    const int p0 = chunk * kDecChunk;
+    if (p0 >= L) return;  // uniform over the CTA
+    const int np = min(kDecChunk, L - p0);
+    const size_t base = (size_t) b * x.cache_b_stride + (size_t) kvh * x.cache_h_stride + (size_t) p0 * kHeadDim;
+    const uint4* kg = reinterpret_cast<const uint4*>(x.k_cache + base);
+    const uint4* vg = reinterpret_cast<const uint4*>(x.v_cache + base);
+    uint4* ksv = reinterpret_cast<uint4*>(&ks[0][0]);
+    uint4* vsv = reinterpret_cast<uint4*>(&vs[0][0]);
+    const int n16 = np * (kHeadDim / 8);  // 16-byte pieces of the chunk
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) {
+        ksv[i] = kg[i];
+        vsv[i] = vg[i];
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int group = x.q_heads / x.kv_heads;
+    if (warp >= group) return;
+    const int qh = kvh * group + warp;
+    const float4 q = *reinterpret_cast<const float4*>(x.qbuf + ((size_t) b * x.q_heads + qh) * kHeadDim + 4 * lane);
+    float s_lo = -INFINITY, s_hi = -INFINITY;
+    for (int p = 0; p < np; ++p) {
+        const uint2 kr = *reinterpret_cast<const uint2*>(&ks[p][4 * lane]);
+        const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kr.x));
+        const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kr.y));
+        float d = q.x * k01.x + q.y * k01.y + q.z * k23.x + q.w * k23.y;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+        if (lane == (p & 31)) {
+            if (p < 32) s_lo = d;
+            else s_hi = d;
+        }
+    }
+    float m = fmaxf(s_lo, s_hi);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float e_lo = s_lo == -INFINITY ? 0.f : __expf(s_lo - m);
+    const float e_hi = s_hi == -INFINITY ? 0.f : __expf(s_hi - m);
+    float l = e_lo + e_hi;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < np; ++p) {
+        const float e = __shfl_sync(0xffffffffu, p < 32 ? e_lo : e_hi, p & 31);
+        const uint2 vr = *reinterpret_cast<const uint2*>(&vs[p][4 * lane]);
+        const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr.x));
+        const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr.y));
+        acc.x += e * v01.x;
+        acc.y += e * v01.y;
+        acc.z += e * v23.x;
+        acc.w += e * v23.y;
+    }
+    const size_t hc = ((size_t) b * x.q_heads + qh) * x.max_chunks + chunk;
+    *reinterpret_cast<float4*>(x.attn_o + hc * kHeadDim + 4 * lane) = acc;
+    if (lane == 0) {
+        x.attn_ml[2 * hc] = m;
+        x.attn_ml[2 * hc + 1] = l;
+    }
+}
+
+// h += y and the row's sum of squares (tensor-parallel path, after the all-reduce)
+__global__ __launch_bounds__(256) void exl3_dec_residual_kernel(float* __restrict__ h, long long h_stride,
+                                                                const float* __restrict__ y, long long y_stride,
+                                                                float* __restrict__ ss, int batch, int hidden)
+{
+    griddep_launch();
+    griddep_wait();
+    const int lane = threadIdx.x & 31;
+    const int nblk = hidden >> 7;
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < batch * nblk; task += warps) {
+        const int r = task / nblk, b = task - r * nblk;
+        float* hr = h + (size_t) r * h_stride + b * 128;
+        const float* yr = y + (size_t) r * y_stride + b * 128;
+        float sq = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float nv = hr[lane + 32 * e] + yr[lane + 32 * e];
+            hr[lane + 32 * e] = nv;
+            sq += nv * nv;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if (lane == 0) atomicAdd(ss + r, sq);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+template <typename Kern, typename... Args>
+static int dec_launch(Kern kern, int grid, int block, cudaStream_t stream, Args... args)
+{
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) std::max(grid, 1));
+    cfg.blockDim = dim3((unsigned) block);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? kOk : kErrLaunch;
+}
+
+static int dec_grid(int tasks) { return std::min((tasks + 7) / 8, 8 * gv_sm_count()); }
+
+template <int MODE>
+static int dec_launch_epilogue(const GvArgs& a, const DecAux& x, int cb, cudaStream_t st)
+{
+    const int g = dec_grid(a.out_tasks);
+    return cb == 2 ? dec_launch(exl3_dec_epilogue_kernel<2, MODE>, g, 256, st, a, x)
+                   : dec_launch(exl3_dec_epilogue_kernel<0, MODE>, g, 256, st, a, x);
+}
+
+static size_t al256(size_t v) { return (v + 255) & ~(size_t) 255; }
+
+static bool dec_linear_ok(const exl3b200_linear* l, int k, int n)
+{
+    return l && l->trellis && l->suh && l->svh && l->k == k && l->n == n && !((uintptr_t) l->trellis & 3);
+}
+
+static void dec_problem(GvProblem& p, const exl3b200_linear* l, int m, uint32_t* xd, float* sblk, float* acc)
+{
+    p = GvProblem{};
+    p.trellis = reinterpret_cast<const uint32_t*>(l->trellis);
+    p.suh = reinterpret_cast<const __half*>(l->suh);
+    p.svh = reinterpret_cast<const __half*>(l->svh);
+    p.xd = xd;
+    p.sblk = sblk;
+    p.acc = acc;
+    p.acc_nb_stride = 16 * 128;
+    p.k = l->k;
+    p.n = l->n;
+    p.m = m;
+}
+
+// Workspace layout of the attention sub-layer.
+struct DecAttnLayout {
+    size_t st_q, st_k, st_v, st_o, state_bytes;
+    size_t xd_q, xd_k, xd_v, sb_q, sb_k, sb_v, qbuf, attn_o, attn_ml, xd_o, sb_o, scratch_bytes;
+};
+
+static DecAttnLayout dec_attn_layout(int batch, int hidden, int q_heads, int kv_heads, int max_ctx)
+{
+    DecAttnLayout L = {};
+    const int nq = q_heads * kHeadDim, nkv = kv_heads * kHeadDim;
+    const int max_chunks = (max_ctx + kDecChunk - 1) / kDecChunk;
+    size_t o = 0;
+    L.st_q = o; o += gv_state_bytes_per_problem(nq);
+    L.st_k = o; o += gv_state_bytes_per_problem(nkv);
+    L.st_v = o; o += gv_state_bytes_per_problem(nkv);
+    L.st_o = o; o += gv_state_bytes_per_problem(hidden);
+    L.state_bytes = o;
+    o = 0;
+    L.xd_q = o; o += gv_xd_bytes(batch, hidden);
+    L.xd_k = o; o += gv_xd_bytes(batch, hidden);
+    L.xd_v = o; o += gv_xd_bytes(batch, hidden);
+    L.sb_q = o; o += gv_sblk_bytes(batch, hidden);
+    L.sb_k = o; o += gv_sblk_bytes(batch, hidden);
+    L.sb_v = o; o += gv_sblk_bytes(batch, hidden);
+    L.qbuf = o; o += al256((size_t) batch * nq * sizeof(float));
+    L.attn_o = o; o += al256((size_t) batch * q_heads * max_chunks * kHeadDim * sizeof(float));
+    L.attn_ml = o; o += al256((size_t) batch * q_heads * max_chunks * 2 * sizeof(float));
+    L.xd_o = o; o += gv_xd_bytes(batch, nq);
+    L.sb_o = o; o += gv_sblk_bytes(batch, nq);
+    L.scratch_bytes = o;
+    return L;
+}
+
+struct DecMlpLayout {
+    size_t st_g, st_u, st_d, state_bytes;
+    size_t xd_g, xd_u, sb_g, sb_u, xd_d, sb_d, scratch_bytes;
+};
+
+static DecMlpLayout dec_mlp_layout(int batch, int hidden, int inter)
+{
+    DecMlpLayout L = {};
+    size_t o = 0;
+    L.st_g = o; o += gv_state_bytes_per_problem(inter);
+    L.st_u = o; o += gv_state_bytes_per_problem(inter);
+    L.st_d = o; o += gv_state_bytes_per_problem(hidden);
+    L.state_bytes = o;
+    o = 0;
+    L.xd_g = o; o += gv_xd_bytes(batch, hidden);
+    L.xd_u = o; o += gv_xd_bytes(batch, hidden);
+    L.sb_g = o; o += gv_sblk_bytes(batch, hidden);
+    L.sb_u = o; o += gv_sblk_bytes(batch, hidden);
+    L.xd_d = o; o += gv_xd_bytes(batch, inter);
+    L.sb_d = o; o += gv_sblk_bytes(batch, inter);
+    L.scratch_bytes = o;
+    return L;
+}
+
+// Final epilogue of a sub-layer: residual add into h (+ sum of squares), or an
+// fp32 store of the partial for a tensor-parallel all-reduce.
+static int dec_finish(GvArgs& a, DecAux& x, int cb, float* h, long long h_stride, float* ss_out, float* y_out,
+                      long long y_stride, cudaStream_t st)
+{
+    if (y_out) {
+        a.inl[0].out = y_out;
+        a.inl[0].out_stride = y_stride;
+        a.out_dtype = 2;
+        a.epi_mode = kEpiStore;
+        return gv_launch_epilogue(a, cb, a.out_tasks, true, st);
+    }
+    x.resid = h;
+    x.resid_stride = h_stride;
+    x.ss_acc = ss_out;
+    return dec_launch_epilogue<kEpiResidual>(a, x, cb, st);
+}
+
+static int dec_common_checks(int batch, int hidden, int K, int cb, const float* h, long long h_stride,
+                             const float* ss_in, const float* ss_out, const void* norm_w, const void* state,
+                             const void* scratch)
+{
+    if (!h || !ss_in || !ss_out || !norm_w || !state || !scratch) return kErrNullPointer;
+    if (batch < 1 || batch > EXL3B200_GEMV_MAX_M || hidden <= 0 || hidden % 128 || h_stride < hidden)
+        return kErrBadShape;
+    if (K < 2 || K > 4) return kErrBadBits;
+    if (cb < 0 || cb > 2) return kErrBadCodebook;
+    if (((uintptr_t) state & 255) || ((uintptr_t) scratch & 255)) return kErrUnaligned;
+    return kOk;
+}
+
+}  // namespace exl3b200
+
+using namespace exl3b200;
+
+extern "C" int exl3b200_decode_attention_workspace(int batch, int hidden, int q_heads, int kv_heads, int max_ctx,
+                                                   size_t* state_bytes, size_t* scratch_bytes)
+{
+    if (!state_bytes || !scratch_bytes) return kErrNullPointer;
+    if (batch < 1 || batch > EXL3B200_GEMV_MAX_M || hidden <= 0 || hidden % 128 || q_heads < 1 || kv_heads < 1 ||
+        q_heads % kv_heads || q_heads / kv_heads > 8 || max_ctx < 1)
+        return kErrBadShape;
+    const DecAttnLayout L = dec_attn_layout(batch, hidden, q_heads, kv_heads, max_ctx);
+    *state_bytes = L.state_bytes;
+    *scratch_bytes = L.scratch_bytes;
+    return kOk;
+}
+
+extern "C" int exl3b200_decode_mlp_workspace(int batch, int hidden, int inter, size_t* state_bytes,
+                                             size_t* scratch_bytes)
+{
+    if (!state_bytes || !scratch_bytes) return kErrNullPointer;
+    if (batch < 1 || batch > EXL3B200_GEMV_MAX_M || hidden <= 0 || hidden % 128 || inter <= 0 || inter % 128)
+        return kErrBadShape;
+    const DecMlpLayout L = dec_mlp_layout(batch, hidden, inter);
+    *state_bytes = L.state_bytes;
+    *scratch_bytes = L.scratch_bytes;
+    return kOk;
+}
+
+extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int kv_heads, int K, int cb, float* h,
+                                         long long h_stride, const float* ss_in, float* ss_out, const void* norm_w,
+                                         float eps, const exl3b200_linear* q, const exl3b200_linear* k,
+                                         const exl3b200_linear* v, const exl3b200_linear* o, void* k_cache,
+                                         void* v_cache, int max_ctx, const long long* pos, const float* inv_freq,
+                                         float* y_out, long long y_stride, void* state, size_t state_bytes,
+                                         void* scratch, size_t scratch_bytes, void* stream)
+{
+    int rc = dec_common_checks(batch, hidden, K, cb, h, h_stride, ss_in, ss_out, norm_w, state, scratch);
+    if (rc != kOk) return rc;
+    if (!k_cache || !v_cache || !pos || !inv_freq) return kErrNullPointer;
+    if (q_heads < 1 || kv_heads < 1 || q_heads % kv_heads || q_heads / kv_heads > 8 || max_ctx < 1)
+        return kErrBadShape;
+    const int nq = q_heads * kHeadDim, nkv = kv_heads * kHeadDim;
+    if (!dec_linear_ok(q, hidden, nq) || !dec_linear_ok(k, hidden, nkv) || !dec_linear_ok(v, hidden, nkv) ||
+        !dec_linear_ok(o, nq, hidden))
+        return kErrBadShape;
+    if (y_out && y_stride < hidden) return kErrBadShape;
+    if (((uintptr_t) k_cache & 15) || ((uintptr_t) v_cache & 15)) return kErrUnaligned;
+    const DecAttnLayout L = dec_attn_layout(batch, hidden, q_heads, kv_heads, max_ctx);
+    if (state_bytes < L.state_bytes || scratch_bytes < L.scratch_bytes) return kErrWorkspace;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    char* S = reinterpret_cast<char*>(state);
+    char* W = reinterpret_cast<char*>(scratch);
+    const bool mul1 = cb == 2;
+
+    DecAux x = {};
+    x.h = h;
+    x.h_stride = h_stride;
+    x.ss_in = ss_in;
+    x.ss_out = ss_out;
+    x.zero_rows = batch;
+    x.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
+    x.eps = eps;
+    x.inv_hidden = 1.f / (float) hidden;
+    x.pos = pos;
+    x.inv_freq = inv_freq;
+    x.qbuf = reinterpret_cast<float*>(W + L.qbuf);
+    x.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache);
+    x.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache);
+    x.cache_h_stride = (long long) max_ctx * kHeadDim;
+    x.cache_b_stride = (long long) kv_heads * x.cache_h_stride;
+    x.max_ctx = max_ctx;
+    x.q_heads = q_heads;
+    x.kv_heads = kv_heads;
+    x.max_chunks = (max_ctx + kDecChunk - 1) / kDecChunk;
+    x.attn_o = reinterpret_cast<float*>(W + L.attn_o);
+    x.attn_ml = reinterpret_cast<float*>(W + L.attn_ml);
+
+    // 1-3: norm input stage, q/k/v matmul, RoPE + KV append epilogue
+    GvArgs a = {};
+    a.nprob = 3;
+    dec_problem(a.inl[0], q, batch, reinterpret_cast<uint32_t*>(W + L.xd_q),
+                mul1 ? reinterpret_cast<float*>(W + L.sb_q) : nullptr, reinterpret_cast<float*>(S + L.st_q));
+    dec_problem(a.inl[1], k, batch, reinterpret_cast<uint32_t*>(W + L.xd_k),
+                mul1 ? reinterpret_cast<float*>(W + L.sb_k) : nullptr, reinterpret_cast<float*>(S + L.st_k));
+    dec_problem(a.inl[2], v, batch, reinterpret_cast<uint32_t*>(W + L.xd_v),
+                mul1 ? reinterpret_cast<float*>(W + L.sb_v) : nullptr, reinterpret_cast<float*>(S + L.st_v));
+    gv_prefix_inline(a);
+    rc = dec_launch(exl3_dec_input_kernel<kInNorm>, dec_grid(a.in_tasks), 256, st, a, x);
+    if (rc != kOk) return rc;
+    rc = gv_launch_matmul(a, K, cb, batch, 0, true, st);
+    if (rc != kOk) return rc;
+    rc = dec_launch_epilogue<kEpiRopeKV>(a, x, cb, st);
+    if (rc != kOk) return rc;
+
+    // 4: attention partials
+    rc = dec_launch(exl3_dec_attn_kernel, batch * kv_heads * x.max_chunks, 32 * (q_heads / kv_heads), st, x);
+    if (rc != kOk) return rc;
+
+    // 5-7: merge + rotate, o matmul, residual (or fp32 partial for the all-reduce)
+    GvArgs b = {};
+    b.nprob = 1;
+    dec_problem(b.inl[0], o, batch, reinterpret_cast<uint32_t*>(W + L.xd_o),
+                mul1 ? reinterpret_cast<float*>(W + L.sb_o) : nullptr, reinterpret_cast<float*>(S + L.st_o));
+    gv_prefix_inline(b);
+    rc = dec_launch(exl3_dec_input_kernel<kInAttn>, dec_grid(b.in_tasks), 256, st, b, x);
+    if (rc != kOk) return rc;
+    rc = gv_launch_matmul(b, K, cb, batch, 0, true, st);
+    if (rc != kOk) return rc;
+    return dec_finish(b, x, cb, h, h_stride, ss_out, y_out, y_stride, st);
+}
+
+extern "C" int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int cb, float* h, long long h_stride,
+                                   const float* ss_in, float* ss_out, const void* norm_w, float eps,
+                                   const exl3b200_linear* gate, const exl3b200_linear* up,
+                                   const exl3b200_linear* down, float swiglu_limit, float* y_out, long long y_stride,
+                                   void* state, size_t state_bytes, void* scratch, size_t scratch_bytes,
+                                   void* stream)
+{
+    int rc = dec_common_checks(batch, hidden, K, cb, h, h_stride, ss_in, ss_out, norm_w, state, scratch);
+    if (rc != kOk) return rc;
+    if (inter <= 0 || inter % 128) return kErrBadShape;
+    if (!dec_linear_ok(gate, hidden, inter) || !dec_linear_ok(up, hidden, inter) || !dec_linear_ok(down, inter, hidden))
+        return kErrBadShape;
+    if (y_out && y_stride < hidden) return kErrBadShape;
+    const DecMlpLayout L = dec_mlp_layout(batch, hidden, inter);
+    if (state_bytes < L.state_bytes || scratch_bytes < L.scratch_bytes) return kErrWorkspace;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    char* S = reinterpret_cast<char*>(state);
+    char* W = reinterpret_cast<char*>(scratch);
+    const bool mul1 = cb == 2;
+
+    DecAux x = {};
+    x.h = h;
+    x.h_stride = h_stride;
+    x.ss_in = ss_in;
+    x.ss_out = ss_out;
+    x.zero_rows = batch;
+    x.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
+    x.eps = eps;
+    x.inv_hidden = 1.f / (float) hidden;
+
+    GvArgs a = {};
+    a.nprob = 2;
+    dec_problem(a.inl[0], gate, batch, reinterpret_cast<uint32_t*>(W + L.xd_g),
+                mul1 ? reinterpret_cast<float*>(W + L.sb_g) : nullptr, reinterpret_cast<float*>(S + L.st_g));
+    dec_problem(a.inl[1], up, batch, reinterpret_cast<uint32_t*>(W + L.xd_u),
+                mul1 ? reinterpret_cast<float*>(W + L.sb_u) : nullptr, reinterpret_cast<float*>(S + L.st_u));
+    // the SwiGLU epilogue of gate writes the rotated input of down
+    a.inl[0].out = W + L.xd_d;
+    a.inl[0].out_stride = inter;
+    a.inl[0].out_suh = reinterpret_cast<const __half*>(down->suh);
+    a.inl[0].out_sblk = mul1 ? reinterpret_cast<float*>(W + L.sb_d) : nullptr;
+    gv_prefix_inline(a);
+    rc = dec_launch(exl3_dec_input_kernel<kInNorm>, dec_grid(a.in_tasks), 256, st, a, x);
+    if (rc != kOk) return rc;
+    rc = gv_launch_matmul(a, K, cb, batch, 0, true, st);
+    if (rc != kOk) return rc;
+
+    GvArgs e = a;
+    e.stride = 2;
+    e.offset = 0;
+    e.nprob = 1;
+    e.out_tasks = batch * (inter / 128);
+    e.epi_mode = kEpiSwiglu;
+    e.swiglu_limit = swiglu_limit;
+    rc = gv_launch_epilogue(e, cb, e.out_tasks, true, st);
+    if (rc != kOk) return rc;
+
+    GvArgs d = {};
+    d.nprob = 1;
+    dec_problem(d.inl[0], down, batch, reinterpret_cast<uint32_t*>(W + L.xd_d),
+                mul1 ? reinterpret_cast<float*>(W + L.sb_d) : nullptr, reinterpret_cast<float*>(S + L.st_d));
+    gv_prefix_inline(d);
+    rc = gv_launch_matmul(d, K, cb, batch, 0, true, st);
+    if (rc != kOk) return rc;
+    return dec_finish(d, x, cb, h, h_stride, ss_out, y_out, y_stride, st);
+}
+
+extern "C" int exl3b200_residual_add(int batch, int hidden, float* h, long long h_stride, const float* y,
+                                     long long y_stride, float* ss_out, void* stream)
+{
+    if (!h || !y || !ss_out) return kErrNullPointer;
+    if (batch < 1 || hidden <= 0 || hidden % 128 || h_stride < hidden || y_stride < hidden) return kErrBadShape;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    return dec_launch(exl3_dec_residual_kernel, dec_grid(batch * (hidden / 128)), 256, st, h, h_stride, y, y_stride,
+                      ss_out, batch, hidden);
+}

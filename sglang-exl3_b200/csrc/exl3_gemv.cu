@@ -42,58 +42,13 @@
 #include "exl3_common.cuh"
 #include "exl3_capi_internal.h"
 #include "exl3_grouped.cuh"
+#include "exl3_grouped_dev.cuh"
 
 namespace exl3b200 {
 
 constexpr int kGvThreads = 256;
 constexpr int kGvWarps = kGvThreads / 32;
 constexpr int kRedStride = 132;  // padded row stride of the shared reduction block
-
-__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
-__device__ __forceinline__ const GvProblem& gv_prob(const GvArgs& a, int i)
-{
-    const int j = i * a.stride + a.offset;
-    return a.dev ? a.dev[j] : a.inl[j];
-}
-
-struct GvTotals {
-    int nprob, units, in_tasks, out_tasks;
-};
-
-__device__ __forceinline__ GvTotals gv_totals(const GvArgs& a)
-{
-    GvTotals t;
-    if (a.dev_totals) {
-        t.nprob = __ldcg(a.dev_totals + 0);
-        t.units = __ldcg(a.dev_totals + 1);
-        t.in_tasks = __ldcg(a.dev_totals + 2);
-        t.out_tasks = __ldcg(a.dev_totals + 3);
-    } else {
-        t.nprob = a.nprob;
-        t.units = a.units;
-        t.in_tasks = a.in_tasks;
-        t.out_tasks = a.out_tasks;
-    }
-    if (a.uniform_units > 0) t.units = t.nprob * a.uniform_units;
-    return t;
-}
-
-// largest problem index whose task range starts at or before task
-template <int WHICH>
-__device__ __forceinline__ int gv_find(const GvArgs& a, int nprob, int task)
-{
-    int lo = 0, hi = nprob - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        const GvProblem& p = gv_prob(a, mid);
-        const int begin = WHICH == 0 ? p.in_task_begin : WHICH == 1 ? p.out_task_begin : p.unit_begin;
-        if (begin <= task) lo = mid;
-        else hi = mid - 1;
-    }
-    return lo;
-}
 
 // ---------------------------------------------------------------------------
 // input stage
@@ -351,31 +306,6 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gv_matmul_kernel(const 
 
 // Finish one (problem, block, row): read and re-zero the summed partials, mul1
 // correction, H128, * 1/sqrt(128) * svh.  Lane holds columns lane + 32 i.
-template <int CB>
-__device__ __forceinline__ void gv_finish(const GvProblem& p, int nb, int r, int lane, float (&v)[4])
-{
-    float* src = p.acc + (size_t) nb * p.acc_nb_stride + (size_t) r * 128;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        v[e] = __ldcg(src + lane + 32 * e);
-        __stcg(src + lane + 32 * e, 0.f);
-    }
-    if constexpr (CB == 2) {
-        const float k_inv = __half2float(__ushort_as_half(kMul1InvBits));
-        const float k_bias = __half2float(__ushort_as_half(kMul1BiasBits));
-        const int nblk = p.k >> 7;
-        float sum = 0.f;
-        for (int b = lane; b < nblk; b += 32) sum += __ldcg(p.sblk + (size_t) r * nblk + b);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] = fmaf(k_inv, v[e], k_bias * sum);
-    }
-    warp_fwht128(v, lane);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = v[e] * kHadScale * __half2float(p.svh[nb * 128 + lane + 32 * e]);
-}
-
 template <int CB, int MODE>
 __global__ __launch_bounds__(256) void exl3_gv_epilogue_kernel(const __grid_constant__ GvArgs a)
 {
@@ -553,9 +483,7 @@ int gv_launch_epilogue(const GvArgs& a, int cb, int max_out_tasks, bool pdl, cud
     }
 }
 
-// Host-built table of up to kGvInline dense problems (one input matrix, several
-// linears sharing K and codebook): fill prefixes and launch the three kernels.
-static int run_inline(GvArgs& a, int K, int cb, int max_rows, int variant, cudaStream_t stream)
+void gv_prefix_inline(GvArgs& a)
 {
     int units = 0, in_tasks = 0, out_tasks = 0;
     for (int i = 0; i < a.nprob; ++i) {
@@ -575,11 +503,18 @@ static int run_inline(GvArgs& a, int K, int cb, int max_rows, int variant, cudaS
     a.stride = 1;
     a.offset = 0;
     a.uniform_units = 0;
-    int rc = gv_launch_input(a, in_tasks, false, stream);
+}
+
+// Host-built table of up to kGvInline dense problems (one input matrix, several
+// linears sharing K and codebook): fill prefixes and launch the three kernels.
+static int run_inline(GvArgs& a, int K, int cb, int max_rows, int variant, cudaStream_t stream)
+{
+    gv_prefix_inline(a);
+    int rc = gv_launch_input(a, a.in_tasks, false, stream);
     if (rc != kOk) return rc;
     rc = gv_launch_matmul(a, K, cb, max_rows, variant, true, stream);
     if (rc != kOk) return rc;
-    return gv_launch_epilogue(a, cb, out_tasks, true, stream);
+    return gv_launch_epilogue(a, cb, a.out_tasks, true, stream);
 }
 
 }  // namespace exl3b200

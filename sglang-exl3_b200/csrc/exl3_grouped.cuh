@@ -71,6 +71,9 @@ int gv_launch_input(const GvArgs& a, int max_in_tasks, bool pdl, cudaStream_t st
 int gv_launch_matmul(const GvArgs& a, int K, int cb, int max_rows, int variant, bool pdl, cudaStream_t stream);
 int gv_launch_epilogue(const GvArgs& a, int cb, int max_out_tasks, bool pdl, cudaStream_t stream);
 
+// Fill the task prefixes of an inline (host-built) table.
+void gv_prefix_inline(GvArgs& a);
+
 size_t gv_state_bytes_per_problem(int n);
 size_t gv_xd_bytes(int m, int k);
 size_t gv_sblk_bytes(int m, int k);

@@ -37,6 +37,16 @@ _i = ctypes.c_int
 _ll = ctypes.c_longlong
 _sz = ctypes.c_size_t
 
+
+
+class Linear(ctypes.Structure):
+    """``exl3b200_linear``: one EXL3 linear for the decode-layer entry points."""
+
+    _fields_ = [("trellis", _vp), ("suh", _vp), ("svh", _vp), ("k", _i), ("n", _i)]
+
+
+_f = ctypes.c_float
+
 # name -> (restype, argtypes); one entry per declaration in include/exl3_b200.h
 SIGNATURES = {
     "exl3b200_abi_version": (_i, []),
@@ -59,6 +69,13 @@ SIGNATURES = {
     "exl3b200_gemm_scratch_size": (_sz, [_i, _i]),
     "exl3b200_gemm": (_i, [_vp, _ll, _i, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _ll, _i, _i, _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_device_status": (_i, [_vp, _i, _vp]),
+    "exl3b200_decode_attention_workspace": (_i, [_i, _i, _i, _i, _i, _vp, _vp]),
+    "exl3b200_decode_mlp_workspace": (_i, [_i, _i, _i, _vp, _vp]),
+    "exl3b200_decode_attention": (_i, [_i, _i, _i, _i, _i, _i, _vp, _ll, _vp, _vp, _vp, _f, _vp, _vp, _vp, _vp,
+                                       _vp, _vp, _i, _vp, _vp, _vp, _ll, _vp, _sz, _vp, _sz, _vp]),
+    "exl3b200_decode_mlp": (_i, [_i, _i, _i, _i, _i, _vp, _ll, _vp, _vp, _vp, _f, _vp, _vp, _vp, _f, _vp, _ll, _vp,
+                                 _sz, _vp, _sz, _vp]),
+    "exl3b200_residual_add": (_i, [_i, _i, _vp, _ll, _vp, _ll, _vp, _vp]),
     "exl3b200_moe_state_size": (_sz, [_i, _i, _i, _i]),
     "exl3b200_moe_scratch_size": (_sz, [_i, _i, _i, _i]),
     "exl3b200_moe": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,

@@ -1,0 +1,111 @@
+"""Fused decode sub-layers (RMSNorm -> q/k/v -> RoPE + KV append -> attention -> o
+-> residual, and RMSNorm -> gate/up -> SwiGLU -> down -> residual) over the C ABI.
+
+The residual stream ``h`` is fp32 ``[batch, hidden]``; ``ss`` holds two per-row
+sum-of-squares buffers that the sub-layers alternate between: a sub-layer reads
+``ss_in`` for its RMSNorm, zeroes ``ss_out`` and accumulates the new sum of
+squares into it with its residual add.  With tensor parallelism the sub-layer
+stores its partial output in ``y`` instead; after the all-reduce,
+``residual_add`` completes it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from . import workspace
+
+
+def linear_desc(trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor) -> _lib.Linear:
+    if trellis.dtype != torch.int16 or trellis.dim() != 3 or not trellis.is_contiguous():
+        raise RuntimeError("trellis must be a contiguous int16 [k/16, n/16, 16K] tensor")
+    return _lib.Linear(trellis.data_ptr(), suh.data_ptr(), svh.data_ptr(), trellis.size(0) * 16, trellis.size(1) * 16)
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ws(dev: torch.device, state_n: int, scratch_n: int):
+    return workspace.state_buffer(dev, state_n), workspace.scratch_buffer(dev, scratch_n)
+
+
+def _check_state(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor, norm_w: torch.Tensor):
+    if h.dtype != torch.float32 or h.dim() != 2 or h.stride(1) != 1:
+        raise RuntimeError("h must be fp32 [batch, hidden] with unit column stride")
+    for s in (ss_in, ss_out):
+        if s.dtype != torch.float32 or s.numel() < h.size(0) or not s.is_contiguous():
+            raise RuntimeError("sum-of-squares buffers must be contiguous fp32 [batch]")
+    if norm_w.dtype != torch.bfloat16 or norm_w.numel() != h.size(1) or not norm_w.is_contiguous():
+        raise RuntimeError("norm weight must be contiguous bf16 [hidden]")
+
+
+def decode_attention(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor, norm_w: torch.Tensor, eps: float,
+                     qkv: Sequence, o: Sequence, K: int, cb: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     pos: torch.Tensor, inv_freq: torch.Tensor, y: Optional[torch.Tensor] = None) -> None:
+    """Attention sub-layer for one new token per row of ``h``.  ``qkv`` = three
+    (trellis, suh, svh) linears, ``o`` one; caches bf16 [batch, kv_heads, max_ctx, 128]."""
+    _check_state(h, ss_in, ss_out, norm_w)
+    B, H = h.shape
+    if k_cache.dtype != torch.bfloat16 or k_cache.dim() != 4 or k_cache.size(-1) != 128 or not k_cache.is_contiguous():
+        raise RuntimeError("caches must be contiguous bf16 [batch, kv_heads, max_ctx, 128]")
+    if v_cache.shape != k_cache.shape or not v_cache.is_contiguous() or k_cache.size(0) != B:
+        raise RuntimeError("k and v caches must match and have one row per sequence")
+    if pos.dtype != torch.int64 or inv_freq.dtype != torch.float32 or inv_freq.numel() != 64:
+        raise RuntimeError("pos must be int64 and inv_freq fp32 [64]")
+    kv_heads, max_ctx = k_cache.size(1), k_cache.size(2)
+    q_heads = qkv[0][0].size(1) * 16 // 128
+    dev = h.device
+    L = _lib.lib()
+    st_n, sc_n = ctypes.c_size_t(), ctypes.c_size_t()
+    _lib.check(L.exl3b200_decode_attention_workspace(B, H, q_heads, kv_heads, max_ctx, ctypes.byref(st_n),
+                                                     ctypes.byref(sc_n)), "exl3b200_decode_attention_workspace")
+    lq, lk, lv = (linear_desc(*lin) for lin in qkv)
+    lo = linear_desc(*o)
+    with torch.cuda.device(dev):
+        state, scratch = _ws(dev, st_n.value, sc_n.value)
+        rc = L.exl3b200_decode_attention(
+            B, H, q_heads, kv_heads, int(K), int(cb), h.data_ptr(), h.stride(0), ss_in.data_ptr(), ss_out.data_ptr(),
+            norm_w.data_ptr(), float(eps), ctypes.byref(lq), ctypes.byref(lk), ctypes.byref(lv), ctypes.byref(lo),
+            k_cache.data_ptr(), v_cache.data_ptr(), max_ctx, pos.data_ptr(), inv_freq.data_ptr(),
+            y.data_ptr() if y is not None else None, y.stride(0) if y is not None else 0,
+            state.data_ptr(), state.numel(), scratch.data_ptr(), scratch.numel(), _stream(dev))
+    _lib.check(rc, "exl3b200_decode_attention")
+
+
+def decode_mlp(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor, norm_w: torch.Tensor, eps: float,
+               gate: Sequence, up: Sequence, down: Sequence, K: int, cb: int, swiglu_limit: float = 0.0,
+               y: Optional[torch.Tensor] = None) -> None:
+    """SwiGLU MLP sub-layer."""
+    _check_state(h, ss_in, ss_out, norm_w)
+    B, H = h.shape
+    inter = gate[0].size(1) * 16
+    dev = h.device
+    L = _lib.lib()
+    st_n, sc_n = ctypes.c_size_t(), ctypes.c_size_t()
+    _lib.check(L.exl3b200_decode_mlp_workspace(B, H, inter, ctypes.byref(st_n), ctypes.byref(sc_n)),
+               "exl3b200_decode_mlp_workspace")
+    lg, lu, ld = linear_desc(*gate), linear_desc(*up), linear_desc(*down)
+    with torch.cuda.device(dev):
+        state, scratch = _ws(dev, st_n.value, sc_n.value)
+        rc = L.exl3b200_decode_mlp(
+            B, H, inter, int(K), int(cb), h.data_ptr(), h.stride(0), ss_in.data_ptr(), ss_out.data_ptr(),
+            norm_w.data_ptr(), float(eps), ctypes.byref(lg), ctypes.byref(lu), ctypes.byref(ld), float(swiglu_limit),
+            y.data_ptr() if y is not None else None, y.stride(0) if y is not None else 0,
+            state.data_ptr(), state.numel(), scratch.data_ptr(), scratch.numel(), _stream(dev))
+    _lib.check(rc, "exl3b200_decode_mlp")
+
+
+def residual_add(h: torch.Tensor, y: torch.Tensor, ss_out: torch.Tensor) -> None:
+    """``h += y`` and the new per-row sum of squares into (zeroed) ``ss_out``."""
+    if y.dtype != torch.float32 or y.shape != h.shape:
+        raise RuntimeError("y must be fp32 shaped like h")
+    dev = h.device
+    with torch.cuda.device(dev):
+        rc = _lib.lib().exl3b200_residual_add(h.size(0), h.size(1), h.data_ptr(), h.stride(0), y.data_ptr(),
+                                              y.stride(0), ss_out.data_ptr(), _stream(dev))
+    _lib.check(rc, "exl3b200_residual_add")

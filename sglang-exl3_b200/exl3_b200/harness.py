@@ -1,10 +1,16 @@
 """Decode harness for the Llama-70B-shaped benchmark model (config 4).
 
 A random-initialised Llama-architecture decoder whose every linear is an EXL3
-4-bpw 3INST layer run by this backend: per layer one grouped launch for q/k/v,
-one for o, one grouped launch for gate/up (SiLU*mul in torch), one for down.
-Embeddings, lm_head and the KV cache are bf16; RMSNorm, RoPE and attention are
-plain torch (attention: ``scaled_dot_product_attention`` over the cache).  Under
+4-bpw 3INST layer run by this backend.  Embeddings, lm_head and the KV cache are
+bf16.  Two step implementations:
+
+* fused (default for batch <= 16): per layer the two fused sub-layers of
+  ``exl3_b200.decode`` - RMSNorm in the matmul input stage, RoPE + KV append in
+  the q/k/v epilogue, split-K attention, residual add in the o / down epilogues,
+  SwiGLU in the gate/up epilogue - about a dozen kernels per layer;
+* unfused: one grouped launch for q/k/v, one for o, one for gate/up, one for
+  down, with RMSNorm, RoPE, KV append, SiLU*mul and attention
+  (``scaled_dot_product_attention``) in plain torch.  Under
 tensor parallelism (one process per GPU) q/k/v/gate/up are column shards, o/down
 row shards followed by an NCCL all-reduce, and lm_head is sharded by vocabulary
 with an all-gather of the logits.  A decode step (one token per sequence) is
@@ -64,7 +70,7 @@ def exl3_weight_bytes(cfg: DecoderConfig, world: int = 1) -> int:
 
 class DecodeModel:
     def __init__(self, cfg: DecoderConfig, batch: int, max_ctx: int, device: torch.device, world: int = 1,
-                 rank: int = 0, group=None, seed: int = 3):
+                 rank: int = 0, group=None, seed: int = 3, fused: Optional[bool] = None):
         if cfg.heads % world or cfg.kv_heads % world or cfg.inter % (128 * world) or cfg.vocab % world:
             raise ValueError(f"config does not shard over tp={world}")
         self.cfg, self.batch, self.max_ctx, self.device = cfg, batch, max_ctx, device
@@ -91,8 +97,10 @@ class DecodeModel:
         self.lm_head = (torch.randn(self.v_loc, H, generator=gen, device=device) * 0.02).to(torch.bfloat16)
         self.ln_f = torch.ones(H, dtype=torch.bfloat16, device=device)
         # KV cache: [layer][B, kv_heads_local, max_ctx, head_dim] bf16
-        self.k_cache = torch.empty((cfg.layers, batch, self.hkv, max_ctx, hd), dtype=torch.bfloat16, device=device)
-        self.v_cache = torch.empty_like(self.k_cache)
+        # zero-filled: the unfused step attends over the whole cache with a mask, and a
+        # masked position holding NaN garbage would still poison the softmax sum
+        self.k_cache = torch.zeros((cfg.layers, batch, self.hkv, max_ctx, hd), dtype=torch.bfloat16, device=device)
+        self.v_cache = torch.zeros_like(self.k_cache)
         inv = 1.0 / (cfg.rope_theta ** (torch.arange(0, hd, 2, device=device, dtype=torch.float32) / hd))
         self.inv_freq = inv
         # static step buffers
@@ -105,6 +113,12 @@ class DecodeModel:
         self.down = torch.empty((batch, H), dtype=torch.float16, device=device)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.ctx = 0
+        self.fused = (batch <= 16) if fused is None else bool(fused)
+        if self.fused and batch > 16:
+            raise ValueError("the fused decode layer takes at most 16 sequences")
+        self.h = torch.zeros((batch, H), dtype=torch.float32, device=device)       # residual stream
+        self.ss = torch.zeros((2, batch), dtype=torch.float32, device=device)      # per-row sum of squares
+        self.y = torch.zeros((batch, H), dtype=torch.float32, device=device)       # TP partial outputs
 
     def fill_random_kv(self, ctx: int, seed: int = 11):
         g = torch.Generator(device=self.device)
@@ -133,6 +147,43 @@ class DecodeModel:
     def step(self):
         """One decode step for the batch: reads self.tokens and self.pos, writes
         self.next_tokens (greedy) and appends to the KV cache."""
+        if self.fused:
+            return self._step_fused()
+        return self._step_unfused()
+
+    def _step_fused(self):
+        from . import decode as D
+
+        cfg = self.cfg
+        h, ss = self.h, self.ss
+        h.copy_(self.embed[self.tokens].float())
+        torch.sum(h * h, dim=-1, out=ss[0])
+        y = self.y if self.world > 1 else None
+        for li, L in enumerate(self.layers):
+            D.decode_attention(h, ss[0], ss[1], L["ln1"], cfg.eps, L["qkv"], L["o"], cfg.K, cfg.cb,
+                               self.k_cache[li], self.v_cache[li], self.pos, self.inv_freq, y=y)
+            if y is not None:
+                self._allreduce(y)
+                D.residual_add(h, y, ss[1])
+            D.decode_mlp(h, ss[1], ss[0], L["ln2"], cfg.eps, L["gu"][0], L["gu"][1], L["down"], cfg.K, cfg.cb, y=y)
+            if y is not None:
+                self._allreduce(y)
+                D.residual_add(h, y, ss[0])
+        self._finish(h)
+
+    def _finish(self, h: torch.Tensor):
+        hf = self._rms(h, self.ln_f).to(torch.bfloat16)
+        logits = hf @ self.lm_head.t()
+        if self.world > 1:
+            parts = [torch.empty_like(logits) for _ in range(self.world)]
+            torch.distributed.all_gather(parts, logits, group=self.group)
+            logits = torch.cat(parts, dim=-1)
+        self.last_logits = logits
+        self.next_tokens.copy_(logits.argmax(-1))
+        self.tokens.copy_(self.next_tokens)
+        self.pos.add_(1)
+
+    def _step_unfused(self):
         cfg = self.cfg
         B, hd = self.batch, cfg.head_dim
         h = self.embed[self.tokens].float()
@@ -159,15 +210,8 @@ class DecodeModel:
             ops.matmul(act, *L["down"], cfg.K, cfg.cb, out=self.down)
             self._allreduce(self.down)
             h = h + self.down.float()
-        hf = self._rms(h, self.ln_f).to(torch.bfloat16)
-        logits = hf @ self.lm_head.t()
-        if self.world > 1:
-            parts = [torch.empty_like(logits) for _ in range(self.world)]
-            torch.distributed.all_gather(parts, logits, group=self.group)
-            logits = torch.cat(parts, dim=-1)
-        self.next_tokens.copy_(logits.argmax(-1))
-        self.tokens.copy_(self.next_tokens)
-        self.pos.add_(1)
+        self.h.copy_(h)
+        self._finish(h)
 
     def capture(self, stream: Optional[torch.cuda.Stream] = None):
         """Warm up on a side stream and capture one decode step in a CUDA graph."""
