@@ -700,7 +700,7 @@ def run_decode(args, world, rank, local, device):
     kbytes = 2 * (cfg.hidden * model.i_loc * cfg.K // 8) + 2 * batch * (cfg.hidden + 2 * model.i_loc)
     k_gbs = kbytes / (kt * 1e-3) / 1e9
     del g
-    model.release()
+    model.close()
 
     line = {
         "metric": METRIC, "value": tok_s, "unit": "tok/s", "ms_per_step": ms,

@@ -238,6 +238,26 @@ typedef struct exl3b200_linear {
 } exl3b200_linear;
 
 /*
+ * Peer buffers for tensor parallelism without NCCL in the decode sub-layers: one per
+ * rank, allocated by its owner (the only allocating calls of the library, made once
+ * at setup), mapped into every other rank's process through its 64-byte CUDA IPC
+ * handle.  Each rank's buffer receives every rank's fp32 partial of a sub-layer and
+ * the flags that say it has arrived.
+ */
+typedef struct exl3b200_peers {
+    void* buffers[8];   /* every rank's buffer as mapped in this process; [rank] = own */
+    int world, rank;    /* world <= 8 */
+    int max_rows;       /* capacity the buffers were sized for (exl3b200_peer_buffer_size) */
+    int hidden;
+} exl3b200_peers;
+
+EXL3B200_API size_t exl3b200_peer_buffer_size(int max_rows, int hidden);
+EXL3B200_API int exl3b200_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+EXL3B200_API int exl3b200_peer_buffer_open(const void* ipc_handle, void** ptr);
+EXL3B200_API int exl3b200_peer_buffer_close(void* ptr);
+EXL3B200_API int exl3b200_peer_buffer_free(void* ptr);
+
+/*
  * Fused decode sub-layers of a Llama-style decoder for batch <= 16 sequences,
  * head_dim 128, query heads per kv head <= 8.  No counterpart in the reference,
  * whose layers call SGLang's norm / attention / activation kernels around the
@@ -250,6 +270,10 @@ typedef struct exl3b200_linear {
  * adds its output into h and the new sum of squares into ss_out.  With y_out
  * (tensor parallelism) it stores its fp32 partial output in y_out instead; after
  * the all-reduce, exl3b200_residual_add(h, y, ss_out) completes the sub-layer.
+ * With peers (non-NULL; y_out ignored) the sub-layer exchanges the partials itself
+ * through the peer buffers (stores over NVLink, a flag per rank, a bounded wait of
+ * 2 s that records EXL3B200_ETIMEOUT in the device status when it gives up) and adds
+ * their sum into h; every rank must make the same sequence of calls.
  *
  * Attention: k_cache / v_cache are this layer's bf16 [batch][kv_heads][max_ctx][128];
  * *pos (device) is the new token's position, the cache holds 0..pos-1 and the
@@ -268,14 +292,14 @@ EXL3B200_API int exl3b200_decode_attention(int batch, int hidden, int q_heads, i
                                            const exl3b200_linear* k, const exl3b200_linear* v,
                                            const exl3b200_linear* o, void* k_cache, void* v_cache, int max_ctx,
                                            const long long* pos, const float* inv_freq, float* y_out,
-                                           long long y_stride, void* state, size_t state_bytes, void* scratch,
-                                           size_t scratch_bytes, void* stream);
+                                           long long y_stride, const exl3b200_peers* peers, void* state,
+                                           size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream);
 EXL3B200_API int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int cb, float* h, long long h_stride,
                                      const float* ss_in, float* ss_out, const void* norm_w, float eps,
                                      const exl3b200_linear* gate, const exl3b200_linear* up,
                                      const exl3b200_linear* down, float swiglu_limit, float* y_out,
-                                     long long y_stride, void* state, size_t state_bytes, void* scratch,
-                                     size_t scratch_bytes, void* stream);
+                                     long long y_stride, const exl3b200_peers* peers, void* state,
+                                     size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream);
 EXL3B200_API int exl3b200_residual_add(int batch, int hidden, float* h, long long h_stride, const float* y,
                                        long long y_stride, float* ss_out, void* stream);
 

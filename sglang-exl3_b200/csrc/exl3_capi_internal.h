@@ -8,3 +8,8 @@
 #include <cuda_runtime.h>
 
 #include "exl3_b200.h"
+
+namespace exl3b200 {
+// device address of the library's sticky device status (exl3_tc.cu); null on error
+int* exl3_status_dev_ptr();
+}  // namespace exl3b200

@@ -26,10 +26,19 @@
 // grouped matmul, the SwiGLU epilogue that writes the down projection's rotated
 // input, the down matmul and the residual epilogue.
 //
+// Tensor parallelism without NCCL (peers != NULL): the o / down epilogue writes its
+// fp32 partial straight into a slot of every rank's peer buffer (CUDA IPC mapping,
+// plain stores over NVLink), then a reduce kernel raises this rank's flag in every
+// buffer, waits (bounded, 2 s) until all ranks' flags for this call are up in its
+// own buffer, sums the slots into h and accumulates the sum of squares.  Slots and
+// flags alternate between two parities by call; a rank cannot reach call k+2 before
+// every peer has finished reading call k (it waits for their call k+1 flags first).
+//
 // The reference has no decode-layer fusion (its layers call SGLang's norm,
 // attention and activation kernels around the EXL3 ops); the arithmetic of each
 // step follows the unfused model in exl3_b200/harness.py.
 #include <algorithm>
+#include <cstring>
 
 #include "exl3_common.cuh"
 #include "exl3_capi_internal.h"
@@ -42,7 +51,19 @@ constexpr int kDecChunk = 64;   // attention positions per CTA
 constexpr int kHeadDim = 128;
 
 enum DecInMode : int { kInNorm = 0, kInAttn = 1 };
-enum DecEpiMode : int { kEpiRopeKV = 10, kEpiResidual = 11 };
+enum DecEpiMode : int { kEpiRopeKV = 10, kEpiResidual = 11, kEpiPeerStore = 12 };
+
+// peer buffer: [control 128 B][flags: 2 parities x 8 ranks x u32, padded to 128 B]
+//              [data: 2 parities x 8 ranks x max_rows x hidden fp32]
+constexpr int kPeerMaxRanks = 8;
+constexpr size_t kPeerFlags = 128;
+constexpr size_t kPeerData = 256;
+constexpr unsigned long long kPeerTimeoutNs = 2000000000ull;
+
+struct PeerCtl {
+    unsigned int epoch;  // calls completed
+    unsigned int done;   // CTAs of the running reduce that finished
+};
 
 struct DecAux {
     // norm input stage
@@ -68,7 +89,41 @@ struct DecAux {
     float* resid;
     long long resid_stride;
     float* ss_acc;
+    // tensor-parallel partial exchange
+    char* peer[kPeerMaxRanks];
+    int peer_world, peer_rank, peer_rows, peer_hidden;
+    int* status;
 };
+
+__device__ __forceinline__ float* peer_slot(const DecAux& x, int q, unsigned int parity, int src, int row)
+{
+    return reinterpret_cast<float*>(x.peer[q] + kPeerData) +
+           (((size_t) parity * kPeerMaxRanks + src) * x.peer_rows + row) * x.peer_hidden;
+}
+
+__device__ __forceinline__ unsigned int* peer_flag(const DecAux& x, int q, unsigned int parity, int src)
+{
+    return reinterpret_cast<unsigned int*>(x.peer[q] + kPeerFlags) + parity * kPeerMaxRanks + src;
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p)
+{
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // fp16 values (already rounded) of one 128-block -> rotated input of a problem
 // (the GEMV input stage's layout: duplicated fp16 pairs, block sums for mul1).
@@ -128,24 +183,40 @@ __global__ __launch_bounds__(256) void exl3_dec_input_kernel(const __grid_consta
                 xv[i] = __half2float(__float2half_rn(hr[c] * rs * __bfloat162float(x.norm_w[b * 128 + c])));
             }
         } else {
-            // block b of the o-projection input = query head b
+            // block b of the o-projection input = query head b; chunk statistics
+            // across lanes, partial outputs 8 chunks at a time (independent loads)
             const int L = (int) (*x.pos) + 1;
             const int nch = (L + kDecChunk - 1) / kDecChunk;
             const size_t hb = (size_t) r * x.q_heads + b;
             const float* ml = x.attn_ml + hb * x.max_chunks * 2;
             const float* po = x.attn_o + hb * x.max_chunks * kHeadDim;
             float mx = -INFINITY;
-            for (int c = 0; c < nch; ++c) mx = fmaxf(mx, ml[2 * c]);
-            float l = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int c = 0; c < nch; ++c) {
-                const float f = __expf(ml[2 * c] - mx);
-                l += f * ml[2 * c + 1];
+            for (int c = lane; c < nch; c += 32) mx = fmaxf(mx, ml[2 * c]);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) o[i] += f * po[(size_t) c * kHeadDim + lane + 32 * i];
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            float l = 0.f;
+            for (int c = lane; c < nch; c += 32) l += __expf(ml[2 * c] - mx) * ml[2 * c + 1];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            float o4[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int c0 = 0; c0 < nch; c0 += 8) {
+                float f[8], pv[8][4];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int c = c0 + j;
+                    const bool ok = c < nch;
+                    f[j] = ok ? __expf(ml[2 * c] - mx) : 0.f;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) pv[j][i] = ok ? po[(size_t) c * kHeadDim + lane + 32 * i] : 0.f;
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) o4[i] += f[j] * pv[j][i];
             }
             const float inv = 1.f / l;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) xv[i] = __half2float(__float2half_rn(o[i] * inv));
+            for (int i = 0; i < 4; ++i) xv[i] = __half2float(__float2half_rn(o4[i] * inv));
         }
         dec_store_rotated(p, r, b, lane, xv);
     }
@@ -193,6 +264,15 @@ __global__ __launch_bounds__(256) void exl3_dec_epilogue_kernel(const __grid_con
 #pragma unroll
                 for (int e = 0; e < 4; ++e) c[lane + 32 * e] = __float2bfloat16_rn(v[e]);
             }
+        } else if constexpr (MODE == kEpiPeerStore) {
+            const PeerCtl* ctl = reinterpret_cast<const PeerCtl*>(x.peer[x.peer_rank]);
+            const unsigned int parity = (*reinterpret_cast<const volatile unsigned int*>(&ctl->epoch) + 1u) & 1u;
+            for (int q = 0; q < x.peer_world; ++q) {
+                float* dst = peer_slot(x, q, parity, x.peer_rank, r) + nb * 128;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dst[lane + 32 * e] = v[e];
+            }
+            __threadfence_system();
         } else {
             float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
             float sq = 0.f;
@@ -234,23 +314,40 @@ __global__ __launch_bounds__(256) void exl3_dec_attn_kernel(const __grid_constan
         ksv[i] = kg[i];
         vsv[i] = vg[i];
     }
+    // rows past the end of the context are zero: the 4-wide loops read them with weight 0
+    for (int i = n16 + threadIdx.x; i < kDecChunk * (kHeadDim / 8); i += blockDim.x) {
+        ksv[i] = make_uint4(0u, 0u, 0u, 0u);
+        vsv[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int group = x.q_heads / x.kv_heads;
     if (warp >= group) return;
     const int qh = kvh * group + warp;
     const float4 q = *reinterpret_cast<const float4*>(x.qbuf + ((size_t) b * x.q_heads + qh) * kHeadDim + 4 * lane);
+    // scores, 4 positions per step with independent warp reductions (the scores of
+    // the zero rows >= np are discarded)
     float s_lo = -INFINITY, s_hi = -INFINITY;
-    for (int p = 0; p < np; ++p) {
-        const uint2 kr = *reinterpret_cast<const uint2*>(&ks[p][4 * lane]);
-        const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kr.x));
-        const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kr.y));
-        float d = q.x * k01.x + q.y * k01.y + q.z * k23.x + q.w * k23.y;
+    for (int p = 0; p < np; p += 4) {
+        float d[4];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
-        if (lane == (p & 31)) {
-            if (p < 32) s_lo = d;
-            else s_hi = d;
+        for (int j = 0; j < 4; ++j) {
+            const uint2 kr = *reinterpret_cast<const uint2*>(&ks[p + j][4 * lane]);
+            const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kr.x));
+            const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kr.y));
+            d[j] = q.x * k01.x + q.y * k01.y + q.z * k23.x + q.w * k23.y;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) d[j] += __shfl_xor_sync(0xffffffffu, d[j], o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int pp = p + j;
+            if (pp < np && lane == (pp & 31)) {
+                if (pp < 32) s_lo = d[j];
+                else s_hi = d[j];
+            }
         }
     }
     float m = fmaxf(s_lo, s_hi);
@@ -261,19 +358,28 @@ __global__ __launch_bounds__(256) void exl3_dec_attn_kernel(const __grid_constan
     float l = e_lo + e_hi;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p = 0; p < np; ++p) {
-        const float e = __shfl_sync(0xffffffffu, p < 32 ? e_lo : e_hi, p & 31);
-        const uint2 vr = *reinterpret_cast<const uint2*>(&vs[p][4 * lane]);
-        const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr.x));
-        const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr.y));
-        acc.x += e * v01.x;
-        acc.y += e * v01.y;
-        acc.z += e * v23.x;
-        acc.w += e * v23.y;
+    float4 acc[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int p = 0; p < np; p += 4) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int pp = p + j;
+            float e = __shfl_sync(0xffffffffu, pp < 32 ? e_lo : e_hi, pp & 31);
+            if (pp >= np) e = 0.f;
+            const uint2 vr = *reinterpret_cast<const uint2*>(&vs[pp][4 * lane]);
+            const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr.x));
+            const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr.y));
+            acc[j].x += e * v01.x;
+            acc[j].y += e * v01.y;
+            acc[j].z += e * v23.x;
+            acc[j].w += e * v23.y;
+        }
     }
+    const float4 o4 = make_float4(acc[0].x + acc[1].x + acc[2].x + acc[3].x, acc[0].y + acc[1].y + acc[2].y + acc[3].y,
+                                  acc[0].z + acc[1].z + acc[2].z + acc[3].z, acc[0].w + acc[1].w + acc[2].w + acc[3].w);
     const size_t hc = ((size_t) b * x.q_heads + qh) * x.max_chunks + chunk;
-    *reinterpret_cast<float4*>(x.attn_o + hc * kHeadDim + 4 * lane) = acc;
+    *reinterpret_cast<float4*>(x.attn_o + hc * kHeadDim + 4 * lane) = o4;
     if (lane == 0) {
         x.attn_ml[2 * hc] = m;
         x.attn_ml[2 * hc + 1] = l;
@@ -304,6 +410,74 @@ __global__ __launch_bounds__(256) void exl3_dec_residual_kernel(float* __restric
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
         if (lane == 0) atomicAdd(ss + r, sq);
+    }
+}
+
+// Tensor-parallel exchange: signal, bounded wait for every rank's partial of this
+// call, h += sum of the partials, sum of squares.  The last CTA advances the epoch.
+__global__ __launch_bounds__(256) void exl3_dec_peer_reduce_kernel(const __grid_constant__ DecAux x, int batch,
+                                                                   int hidden)
+{
+    griddep_launch();
+    griddep_wait();  // this rank's partials (previous kernel) are stored
+    __shared__ int ok;
+    PeerCtl* ctl = reinterpret_cast<PeerCtl*>(x.peer[x.peer_rank]);
+    const unsigned int epoch = *reinterpret_cast<volatile unsigned int*>(&ctl->epoch) + 1u;
+    const unsigned int parity = epoch & 1u;
+    if (blockIdx.x == 0 && threadIdx.x < x.peer_world) {
+        __threadfence_system();
+        st_release_sys(peer_flag(x, threadIdx.x, parity, x.peer_rank), epoch);
+    }
+    if (threadIdx.x == 0) {
+        int good = 1;
+        const unsigned long long t0 = globaltimer_ns();
+        for (int q = 0; q < x.peer_world && good; ++q) {
+            const unsigned int* f = peer_flag(x, x.peer_rank, parity, q);
+            while (ld_acquire_sys(f) != epoch) {
+                if (globaltimer_ns() - t0 > kPeerTimeoutNs) {
+                    good = 0;
+                    if (x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        ok = good;
+    }
+    __syncthreads();
+    if (ok) {
+        const int lane = threadIdx.x & 31;
+        const int nblk = hidden >> 7;
+        const int warps = gridDim.x * (blockDim.x >> 5);
+        for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < batch * nblk; task += warps) {
+            const int r = task / nblk, b = task - r * nblk;
+            float sum[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int q = 0; q < x.peer_world; ++q) {
+                const float* src = peer_slot(x, x.peer_rank, parity, q, r) + b * 128;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) sum[e] += __ldcv(src + lane + 32 * e);
+            }
+            float* hr = x.resid + (size_t) r * x.resid_stride + b * 128;
+            float sq = 0.f;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float nv = hr[lane + 32 * e] + sum[e];
+                hr[lane + 32 * e] = nv;
+                sq += nv * nv;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+            if (lane == 0) atomicAdd(x.ss_acc + r, sq);
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&ctl->done, 1u) == gridDim.x - 1) {
+            ctl->done = 0u;
+            __threadfence();
+            *reinterpret_cast<volatile unsigned int*>(&ctl->epoch) = epoch;
+        }
     }
 }
 
@@ -417,8 +591,23 @@ static DecMlpLayout dec_mlp_layout(int batch, int hidden, int inter)
 // Final epilogue of a sub-layer: residual add into h (+ sum of squares), or an
 // fp32 store of the partial for a tensor-parallel all-reduce.
 static int dec_finish(GvArgs& a, DecAux& x, int cb, float* h, long long h_stride, float* ss_out, float* y_out,
-                      long long y_stride, cudaStream_t st)
+                      long long y_stride, const exl3b200_peers* peers, int batch, int hidden, cudaStream_t st)
 {
+    if (peers) {
+        for (int q = 0; q < kPeerMaxRanks; ++q) x.peer[q] = q < peers->world ? (char*) peers->buffers[q] : nullptr;
+        x.peer_world = peers->world;
+        x.peer_rank = peers->rank;
+        x.peer_rows = peers->max_rows;
+        x.peer_hidden = peers->hidden;
+        x.status = exl3_status_dev_ptr();
+        x.resid = h;
+        x.resid_stride = h_stride;
+        x.ss_acc = ss_out;
+        int rc = dec_launch_epilogue<kEpiPeerStore>(a, x, cb, st);
+        if (rc != kOk) return rc;
+        return dec_launch(exl3_dec_peer_reduce_kernel, std::min(dec_grid(batch * (hidden / 128)), 2 * gv_sm_count()),
+                          256, st, x, batch, hidden);
+    }
     if (y_out) {
         a.inl[0].out = y_out;
         a.inl[0].out_stride = y_stride;
@@ -445,9 +634,64 @@ static int dec_common_checks(int batch, int hidden, int K, int cb, const float* 
     return kOk;
 }
 
+static int dec_peers_check(const exl3b200_peers* peers, int batch, int hidden)
+{
+    if (!peers) return kOk;
+    if (peers->world < 1 || peers->world > kPeerMaxRanks || peers->rank < 0 || peers->rank >= peers->world)
+        return kErrBadArgument;
+    if (peers->max_rows < batch || peers->hidden != hidden) return kErrBadShape;
+    for (int q = 0; q < peers->world; ++q) {
+        if (!peers->buffers[q]) return kErrNullPointer;
+        if ((uintptr_t) peers->buffers[q] & 255) return kErrUnaligned;
+    }
+    return kOk;
+}
+
 }  // namespace exl3b200
 
 using namespace exl3b200;
+
+extern "C" size_t exl3b200_peer_buffer_size(int max_rows, int hidden)
+{
+    if (max_rows < 1 || hidden <= 0 || hidden % 128) return 0;
+    return kPeerData + (size_t) 2 * kPeerMaxRanks * max_rows * hidden * sizeof(float);
+}
+
+extern "C" int exl3b200_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle)
+{
+    if (!ptr || !ipc_handle) return kErrNullPointer;
+    if (bytes < kPeerData) return kErrBadShape;
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return kErrLaunch;
+    cudaIpcMemHandle_t h;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+        cudaFree(p);
+        return kErrLaunch;
+    }
+    memcpy(ipc_handle, &h, sizeof(h));
+    *ptr = p;
+    return kOk;
+}
+
+extern "C" int exl3b200_peer_buffer_open(const void* ipc_handle, void** ptr)
+{
+    if (!ptr || !ipc_handle) return kErrNullPointer;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, ipc_handle, sizeof(h));
+    return cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? kOk : kErrLaunch;
+}
+
+extern "C" int exl3b200_peer_buffer_close(void* ptr)
+{
+    if (!ptr) return kErrNullPointer;
+    return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? kOk : kErrLaunch;
+}
+
+extern "C" int exl3b200_peer_buffer_free(void* ptr)
+{
+    if (!ptr) return kErrNullPointer;
+    return cudaFree(ptr) == cudaSuccess ? kOk : kErrLaunch;
+}
 
 extern "C" int exl3b200_decode_attention_workspace(int batch, int hidden, int q_heads, int kv_heads, int max_ctx,
                                                    size_t* state_bytes, size_t* scratch_bytes)
@@ -479,10 +723,12 @@ extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int
                                          float eps, const exl3b200_linear* q, const exl3b200_linear* k,
                                          const exl3b200_linear* v, const exl3b200_linear* o, void* k_cache,
                                          void* v_cache, int max_ctx, const long long* pos, const float* inv_freq,
-                                         float* y_out, long long y_stride, void* state, size_t state_bytes,
-                                         void* scratch, size_t scratch_bytes, void* stream)
+                                         float* y_out, long long y_stride, const exl3b200_peers* peers, void* state,
+                                         size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream)
 {
     int rc = dec_common_checks(batch, hidden, K, cb, h, h_stride, ss_in, ss_out, norm_w, state, scratch);
+    if (rc != kOk) return rc;
+    rc = dec_peers_check(peers, batch, hidden);
     if (rc != kOk) return rc;
     if (!k_cache || !v_cache || !pos || !inv_freq) return kErrNullPointer;
     if (q_heads < 1 || kv_heads < 1 || q_heads % kv_heads || q_heads / kv_heads > 8 || max_ctx < 1)
@@ -554,17 +800,19 @@ extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int
     if (rc != kOk) return rc;
     rc = gv_launch_matmul(b, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
-    return dec_finish(b, x, cb, h, h_stride, ss_out, y_out, y_stride, st);
+    return dec_finish(b, x, cb, h, h_stride, ss_out, y_out, y_stride, peers, batch, hidden, st);
 }
 
 extern "C" int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int cb, float* h, long long h_stride,
                                    const float* ss_in, float* ss_out, const void* norm_w, float eps,
                                    const exl3b200_linear* gate, const exl3b200_linear* up,
                                    const exl3b200_linear* down, float swiglu_limit, float* y_out, long long y_stride,
-                                   void* state, size_t state_bytes, void* scratch, size_t scratch_bytes,
-                                   void* stream)
+                                   const exl3b200_peers* peers, void* state, size_t state_bytes, void* scratch,
+                                   size_t scratch_bytes, void* stream)
 {
     int rc = dec_common_checks(batch, hidden, K, cb, h, h_stride, ss_in, ss_out, norm_w, state, scratch);
+    if (rc != kOk) return rc;
+    rc = dec_peers_check(peers, batch, hidden);
     if (rc != kOk) return rc;
     if (inter <= 0 || inter % 128) return kErrBadShape;
     if (!dec_linear_ok(gate, hidden, inter) || !dec_linear_ok(up, hidden, inter) || !dec_linear_ok(down, inter, hidden))
@@ -621,7 +869,7 @@ extern "C" int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int 
     gv_prefix_inline(d);
     rc = gv_launch_matmul(d, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
-    return dec_finish(d, x, cb, h, h_stride, ss_out, y_out, y_stride, st);
+    return dec_finish(d, x, cb, h, h_stride, ss_out, y_out, y_stride, peers, batch, hidden, st);
 }
 
 extern "C" int exl3b200_residual_add(int batch, int hidden, float* h, long long h_stride, const float* y,

@@ -905,6 +905,22 @@ extern "C" int exl3b200_gemm(const void* x, long long x_stride, int m, int k, co
     return kOk;
 }
 
+namespace exl3b200 {
+// Device address of the sticky status, for the kernels of other translation units.
+int* exl3_status_dev_ptr()
+{
+    static int* cache[64] = {nullptr};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!cache[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_exl3_device_status) != cudaSuccess) return nullptr;
+        cache[dev] = reinterpret_cast<int*>(p);
+    }
+    return cache[dev];
+}
+}  // namespace exl3b200
+
 extern "C" int exl3b200_device_status(int* host_status, int reset, void* stream)
 {
     if (!host_status) return kErrNullPointer;

@@ -45,6 +45,12 @@ class Linear(ctypes.Structure):
     _fields_ = [("trellis", _vp), ("suh", _vp), ("svh", _vp), ("k", _i), ("n", _i)]
 
 
+class Peers(ctypes.Structure):
+    """``exl3b200_peers``: every rank's peer buffer as mapped in this process."""
+
+    _fields_ = [("buffers", _vp * 8), ("world", _i), ("rank", _i), ("max_rows", _i), ("hidden", _i)]
+
+
 _f = ctypes.c_float
 
 # name -> (restype, argtypes); one entry per declaration in include/exl3_b200.h
@@ -72,9 +78,14 @@ SIGNATURES = {
     "exl3b200_decode_attention_workspace": (_i, [_i, _i, _i, _i, _i, _vp, _vp]),
     "exl3b200_decode_mlp_workspace": (_i, [_i, _i, _i, _vp, _vp]),
     "exl3b200_decode_attention": (_i, [_i, _i, _i, _i, _i, _i, _vp, _ll, _vp, _vp, _vp, _f, _vp, _vp, _vp, _vp,
-                                       _vp, _vp, _i, _vp, _vp, _vp, _ll, _vp, _sz, _vp, _sz, _vp]),
+                                       _vp, _vp, _i, _vp, _vp, _vp, _ll, _vp, _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_decode_mlp": (_i, [_i, _i, _i, _i, _i, _vp, _ll, _vp, _vp, _vp, _f, _vp, _vp, _vp, _f, _vp, _ll, _vp,
-                                 _sz, _vp, _sz, _vp]),
+                                 _vp, _sz, _vp, _sz, _vp]),
+    "exl3b200_peer_buffer_size": (_sz, [_i, _i]),
+    "exl3b200_peer_buffer_alloc": (_i, [_sz, _vp, _vp]),
+    "exl3b200_peer_buffer_open": (_i, [_vp, _vp]),
+    "exl3b200_peer_buffer_close": (_i, [_vp]),
+    "exl3b200_peer_buffer_free": (_i, [_vp]),
     "exl3b200_residual_add": (_i, [_i, _i, _vp, _ll, _vp, _ll, _vp, _vp]),
     "exl3b200_moe_state_size": (_sz, [_i, _i, _i, _i]),
     "exl3b200_moe_scratch_size": (_sz, [_i, _i, _i, _i]),

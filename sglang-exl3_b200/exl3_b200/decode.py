@@ -4,9 +4,10 @@
 The residual stream ``h`` is fp32 ``[batch, hidden]``; ``ss`` holds two per-row
 sum-of-squares buffers that the sub-layers alternate between: a sub-layer reads
 ``ss_in`` for its RMSNorm, zeroes ``ss_out`` and accumulates the new sum of
-squares into it with its residual add.  With tensor parallelism the sub-layer
-stores its partial output in ``y`` instead; after the all-reduce,
-``residual_add`` completes it.
+squares into it with its residual add.  With tensor parallelism either the
+sub-layer stores its partial output in ``y`` and, after an NCCL all-reduce,
+``residual_add`` completes it, or (``peers``: a ``PeerExchange``) the sub-layer
+exchanges the partials itself over NVLink and adds their sum.
 """
 
 from __future__ import annotations
@@ -44,9 +45,14 @@ def _check_state(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor, nor
         raise RuntimeError("norm weight must be contiguous bf16 [hidden]")
 
 
+def _peers_arg(peers):
+    return ctypes.byref(peers.struct) if peers is not None else None
+
+
 def decode_attention(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor, norm_w: torch.Tensor, eps: float,
                      qkv: Sequence, o: Sequence, K: int, cb: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
-                     pos: torch.Tensor, inv_freq: torch.Tensor, y: Optional[torch.Tensor] = None) -> None:
+                     pos: torch.Tensor, inv_freq: torch.Tensor, y: Optional[torch.Tensor] = None,
+                     peers=None) -> None:
     """Attention sub-layer for one new token per row of ``h``.  ``qkv`` = three
     (trellis, suh, svh) linears, ``o`` one; caches bf16 [batch, kv_heads, max_ctx, 128]."""
     _check_state(h, ss_in, ss_out, norm_w)
@@ -72,14 +78,14 @@ def decode_attention(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor,
             B, H, q_heads, kv_heads, int(K), int(cb), h.data_ptr(), h.stride(0), ss_in.data_ptr(), ss_out.data_ptr(),
             norm_w.data_ptr(), float(eps), ctypes.byref(lq), ctypes.byref(lk), ctypes.byref(lv), ctypes.byref(lo),
             k_cache.data_ptr(), v_cache.data_ptr(), max_ctx, pos.data_ptr(), inv_freq.data_ptr(),
-            y.data_ptr() if y is not None else None, y.stride(0) if y is not None else 0,
+            y.data_ptr() if y is not None else None, y.stride(0) if y is not None else 0, _peers_arg(peers),
             state.data_ptr(), state.numel(), scratch.data_ptr(), scratch.numel(), _stream(dev))
     _lib.check(rc, "exl3b200_decode_attention")
 
 
 def decode_mlp(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor, norm_w: torch.Tensor, eps: float,
                gate: Sequence, up: Sequence, down: Sequence, K: int, cb: int, swiglu_limit: float = 0.0,
-               y: Optional[torch.Tensor] = None) -> None:
+               y: Optional[torch.Tensor] = None, peers=None) -> None:
     """SwiGLU MLP sub-layer."""
     _check_state(h, ss_in, ss_out, norm_w)
     B, H = h.shape
@@ -95,7 +101,7 @@ def decode_mlp(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor, norm_
         rc = L.exl3b200_decode_mlp(
             B, H, inter, int(K), int(cb), h.data_ptr(), h.stride(0), ss_in.data_ptr(), ss_out.data_ptr(),
             norm_w.data_ptr(), float(eps), ctypes.byref(lg), ctypes.byref(lu), ctypes.byref(ld), float(swiglu_limit),
-            y.data_ptr() if y is not None else None, y.stride(0) if y is not None else 0,
+            y.data_ptr() if y is not None else None, y.stride(0) if y is not None else 0, _peers_arg(peers),
             state.data_ptr(), state.numel(), scratch.data_ptr(), scratch.numel(), _stream(dev))
     _lib.check(rc, "exl3b200_decode_mlp")
 
@@ -109,3 +115,58 @@ def residual_add(h: torch.Tensor, y: torch.Tensor, ss_out: torch.Tensor) -> None
         rc = _lib.lib().exl3b200_residual_add(h.size(0), h.size(1), h.data_ptr(), h.stride(0), y.data_ptr(),
                                               y.stride(0), ss_out.data_ptr(), _stream(dev))
     _lib.check(rc, "exl3b200_residual_add")
+
+
+class PeerExchange:
+    """Peer buffers of one tensor-parallel group for the fused decode sub-layers:
+    each rank allocates its buffer, the 64-byte CUDA IPC handles are exchanged with
+    ``all_gather_object`` and every rank maps the others' buffers.  ``close`` (all
+    ranks, before the process group goes away) unmaps and frees them."""
+
+    def __init__(self, max_rows: int, hidden: int, group=None):
+        import torch.distributed as dist
+
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise RuntimeError("peer exchange supports at most 8 ranks")
+        L = _lib.lib()
+        size = L.exl3b200_peer_buffer_size(max_rows, hidden)
+        if size == 0:
+            raise RuntimeError("bad peer buffer shape")
+        handle = (ctypes.c_char * 64)()
+        own = ctypes.c_void_p()
+        _lib.check(L.exl3b200_peer_buffer_alloc(size, ctypes.byref(own), handle), "exl3b200_peer_buffer_alloc")
+        self._own = own.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        ptrs = []
+        for q in range(self.world):
+            if q == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            buf = (ctypes.c_char * 64).from_buffer_copy(handles[q])
+            _lib.check(L.exl3b200_peer_buffer_open(buf, ctypes.byref(p)), "exl3b200_peer_buffer_open")
+            self._opened.append(p.value)
+            ptrs.append(p.value)
+        self.struct = _lib.Peers((ctypes.c_void_p * 8)(*(ptrs + [None] * (8 - len(ptrs)))), self.world, self.rank,
+                                 max_rows, hidden)
+        dist.barrier(group)
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
+        L = _lib.lib()
+        for p in self._opened:
+            L.exl3b200_peer_buffer_close(p)
+        self._opened = []
+        dist.barrier(self.group)
+        L.exl3b200_peer_buffer_free(self._own)
+        self._own = None

@@ -70,7 +70,7 @@ def exl3_weight_bytes(cfg: DecoderConfig, world: int = 1) -> int:
 
 class DecodeModel:
     def __init__(self, cfg: DecoderConfig, batch: int, max_ctx: int, device: torch.device, world: int = 1,
-                 rank: int = 0, group=None, seed: int = 3, fused: Optional[bool] = None):
+                 rank: int = 0, group=None, seed: int = 3, fused: Optional[bool] = None, peer: bool = True):
         if cfg.heads % world or cfg.kv_heads % world or cfg.inter % (128 * world) or cfg.vocab % world:
             raise ValueError(f"config does not shard over tp={world}")
         self.cfg, self.batch, self.max_ctx, self.device = cfg, batch, max_ctx, device
@@ -119,6 +119,11 @@ class DecodeModel:
         self.h = torch.zeros((batch, H), dtype=torch.float32, device=device)       # residual stream
         self.ss = torch.zeros((2, batch), dtype=torch.float32, device=device)      # per-row sum of squares
         self.y = torch.zeros((batch, H), dtype=torch.float32, device=device)       # TP partial outputs
+        self.peers = None
+        if self.fused and world > 1 and peer:
+            from .decode import PeerExchange
+
+            self.peers = PeerExchange(batch, H, group)  # partial sums over NVLink, no NCCL in the layers
 
     def fill_random_kv(self, ctx: int, seed: int = 11):
         g = torch.Generator(device=self.device)
@@ -158,14 +163,16 @@ class DecodeModel:
         h, ss = self.h, self.ss
         h.copy_(self.embed[self.tokens].float())
         torch.sum(h * h, dim=-1, out=ss[0])
-        y = self.y if self.world > 1 else None
+        pe = self.peers
+        y = self.y if (self.world > 1 and pe is None) else None
         for li, L in enumerate(self.layers):
             D.decode_attention(h, ss[0], ss[1], L["ln1"], cfg.eps, L["qkv"], L["o"], cfg.K, cfg.cb,
-                               self.k_cache[li], self.v_cache[li], self.pos, self.inv_freq, y=y)
+                               self.k_cache[li], self.v_cache[li], self.pos, self.inv_freq, y=y, peers=pe)
             if y is not None:
                 self._allreduce(y)
                 D.residual_add(h, y, ss[1])
-            D.decode_mlp(h, ss[1], ss[0], L["ln2"], cfg.eps, L["gu"][0], L["gu"][1], L["down"], cfg.K, cfg.cb, y=y)
+            D.decode_mlp(h, ss[1], ss[0], L["ln2"], cfg.eps, L["gu"][0], L["gu"][1], L["down"], cfg.K, cfg.cb, y=y,
+                         peers=pe)
             if y is not None:
                 self._allreduce(y)
                 D.residual_add(h, y, ss[0])
@@ -237,6 +244,14 @@ class DecodeModel:
 
     def release(self):
         self.graph = None
+
+    def close(self):
+        """Release the graph and the peer buffers (every rank, before the process
+        group is destroyed)."""
+        self.release()
+        if self.peers is not None:
+            self.peers.close()
+            self.peers = None
 
     def generate(self, prompt_tokens: torch.Tensor, n: int) -> torch.Tensor:
         """Public API: greedy-decode n tokens after ``prompt_tokens`` (host [B] last

@@ -98,7 +98,7 @@ def test_tensor_parallel_partial_path(cuda_device):
         torch.cuda.synchronize()
         outs.append((h.clone(), ss[0].clone()))
     assert _rel(outs[1][0], outs[0][0]) < 2e-3
-    torch.testing.assert_close(outs[0][1], outs[1][1], rtol=1e-5, atol=0)
+    torch.testing.assert_close(outs[0][1], outs[1][1], rtol=1e-3, atol=0)
     torch.testing.assert_close(outs[1][1], (outs[1][0] ** 2).sum(-1), rtol=1e-4, atol=0)
 
 
