@@ -646,8 +646,10 @@ def run_decode(args, world, rank, local, device):
     from exl3_b200 import ops
     from exl3_b200.harness import LLAMA_70B, DecodeModel, exl3_weight_bytes
 
+    import dataclasses
+
     hbm_peak, tc_peak, peak_kind = peaks()
-    cfg = LLAMA_70B
+    cfg = LLAMA_70B if args.layers == LLAMA_70B.layers else dataclasses.replace(LLAMA_70B, layers=args.layers)
     batch = args.batch
     new_tokens = 512
     group = torch.distributed.group.WORLD if world > 1 else None
@@ -755,6 +757,7 @@ def main():
     ap.add_argument("--bits", type=int, default=4)
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=80, help="decode: decoder layers (80 = config 4; fewer for profiling)")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
