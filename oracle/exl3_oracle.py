@@ -276,16 +276,17 @@ def moe_ref(x: np.ndarray, experts: list, ids: np.ndarray, weights: np.ndarray,
     x = np.asarray(x, dtype=np.float16)
     T = x.shape[0]
     out = np.zeros((T, x.shape[1]), dtype=np.float64)
-    for t in range(T):
-        for j in range(ids.shape[1]):
-            e = int(ids[t, j])
-            if e < 0 or e >= len(experts):
-                continue
-            xt = x[t:t + 1]
-            g = linear_device_ref(xt, *experts[e]["gate"])
-            u = linear_device_ref(xt, *experts[e]["up"])
-            a = swiglu(g, u, limit).astype(np.float16)
-            out[t] += float(weights[t, j]) * linear_device_ref(a, *experts[e]["down"])[0]
+    ids = np.asarray(ids)
+    for e in range(len(experts)):
+        ts, js = np.nonzero(ids == e)  # every (token, slot) routed to expert e; rows are independent
+        if ts.size == 0:
+            continue
+        xt = x[ts]
+        g = linear_device_ref(xt, *experts[e]["gate"])
+        u = linear_device_ref(xt, *experts[e]["up"])
+        a = swiglu(g, u, limit).astype(np.float16)
+        d = linear_device_ref(a, *experts[e]["down"]).astype(np.float64)
+        np.add.at(out, ts, np.asarray(weights, dtype=np.float64)[ts, js][:, None] * d)
     return out.astype(np.float32)
 
 

@@ -30,7 +30,7 @@ namespace exl3b200 {
 
 constexpr int kRouteThreads = 1024;
 constexpr int kMaxLocalExperts = 2048;
-constexpr int kMaxPairs = 2048;
+constexpr int kMaxPairs = 8192;
 constexpr int kExpertsPerThread = kMaxLocalExperts / kRouteThreads;
 
 static inline size_t al256(size_t v) { return (v + 255) & ~(size_t) 255; }
@@ -84,8 +84,7 @@ __global__ __launch_bounds__(kRouteThreads) void exl3_moe_route_kernel(const Moe
     __shared__ int s_count[kMaxLocalExperts];
     __shared__ int s_slot[kMaxLocalExperts];   // exclusive prefix of rows
     __shared__ int s_prob[kMaxLocalExperts];   // exclusive prefix of problems
-    __shared__ int s_pair_e[kMaxPairs];
-    __shared__ int s_pair_rank[kMaxPairs];
+    __shared__ unsigned short s_pair_rank[kMaxPairs];  // rank of a pair within its expert (< kMaxPairs)
     __shared__ int s_warp[32][2];
 
     const int tid = threadIdx.x;
@@ -95,8 +94,7 @@ __global__ __launch_bounds__(kRouteThreads) void exl3_moe_route_kernel(const Moe
     for (int p = tid; p < P; p += kRouteThreads) {
         const int e = t.ids[p];
         const bool ok = e >= 0 && e < t.experts;
-        s_pair_e[p] = ok ? e : -1;
-        s_pair_rank[p] = ok ? atomicAdd(&s_count[e], 1) : 0;
+        s_pair_rank[p] = ok ? (unsigned short) atomicAdd(&s_count[e], 1) : 0;
     }
     __syncthreads();
 
@@ -162,8 +160,8 @@ __global__ __launch_bounds__(kRouteThreads) void exl3_moe_route_kernel(const Moe
     int* token = reinterpret_cast<int*>(t.scratch + L.token);
     float* weight = reinterpret_cast<float*>(t.scratch + L.weight);
     for (int p = tid; p < P; p += kRouteThreads) {
-        const int e = s_pair_e[p];
-        if (e < 0) continue;
+        const int e = t.ids[p];
+        if (e < 0 || e >= t.experts) continue;
         const int slot = s_slot[e] + s_pair_rank[p];
         token[slot] = p / t.topk;
         weight[slot] = t.weights[p];

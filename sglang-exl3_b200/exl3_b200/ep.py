@@ -113,11 +113,12 @@ def exl3_local_experts(tables: dict, K_gate: int, K_up: int, K_down: int, cb: in
         xr = xr.to(torch.float16).contiguous()
         rows, k = ids.shape
         chunk = max(1, _moe.MOE_MAX_PAIRS // k)
+        cap = _moe.workspace_tokens(rows, chunk)
         out = torch.empty((rows, xr.size(1)), dtype=torch.float32, device=xr.device)
         for r0 in range(0, rows, chunk):
             r1 = min(rows, r0 + chunk)
             _moe.moe_forward(xr[r0:r1], ids[r0:r1], w[r0:r1], tables, K_gate, K_up, K_down, cb,
-                             intermediate_size, swiglu_limit, out=out[r0:r1], max_tokens=chunk)
+                             intermediate_size, swiglu_limit, out=out[r0:r1], max_tokens=cap)
         return out
 
     return fn

@@ -483,11 +483,12 @@ def apply_exl3_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: to
     lim = 0.0 if (limit is None or not math.isfinite(float(limit))) else float(limit)
     topk = ids.shape[1]
     chunk = max(1, _moe.MOE_MAX_PAIRS // topk)
+    cap = _moe.workspace_tokens(tokens, chunk)
     out = torch.empty((tokens, hidden), dtype=torch.float32, device=x2d.device)
     for t0 in range(0, tokens, chunk):
         t1 = min(tokens, t0 + chunk)
         _moe.moe_forward(xh[t0:t1], ids[t0:t1], w[t0:t1], ptrs, layer._exl3_k_gate, layer._exl3_k_up,
                          layer._exl3_k_down, layer._exl3_cb, int(layer._exl3_intermediate_local), lim,
-                         out=out[t0:t1], max_tokens=chunk)
+                         out=out[t0:t1], max_tokens=cap)
     layer._exl3_last_apply = "b200"
     return out.to(dtype=x.dtype)

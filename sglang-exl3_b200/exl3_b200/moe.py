@@ -17,7 +17,7 @@ import torch
 from . import _lib, workspace
 from .ops import (_OUT_DTYPES, _require_cuda, _stream_ptr, codebook_id, legacy_codebook, matmul, matmul_combine)
 
-MOE_MAX_PAIRS = 2048
+MOE_MAX_PAIRS = 8192
 MOE_MAX_EXPERTS = 2048
 
 
@@ -70,6 +70,16 @@ def p2b_gemv_batched(x: torch.Tensor, trellis_ptrs: torch.Tensor, suh_ptrs: torc
                                      scratch.numel(), _stream_ptr(dev))
     _lib.check(st, "exl3b200_batched_gemv")
     return out
+
+
+def workspace_tokens(tokens: int, chunk: int) -> int:
+    """Token capacity to size the MoE workspaces for: the next power of two of the
+    tokens of one launch (so a captured graph keeps its buffers while batch sizes
+    vary below it), at most one chunk."""
+    cap = 1
+    while cap < min(tokens, chunk):
+        cap <<= 1
+    return min(cap, chunk)
 
 
 def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, tables: dict,

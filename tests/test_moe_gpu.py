@@ -82,7 +82,7 @@ def test_p2b_gemv_batched(cuda_device, cb, per_expert):
         assert O.normwise_rel_err(out[j].float().cpu().numpy(), O.gemv_ref(xe, tr, su, sv, K, cb)) < TOL
 
 
-@pytest.mark.parametrize("T,topk,E", [(1, 8, 16), (5, 4, 8), (16, 8, 12), (40, 2, 6)])
+@pytest.mark.parametrize("T,topk,E", [(1, 8, 16), (5, 4, 8), (16, 8, 12), (40, 2, 6), (600, 8, 16)])
 @pytest.mark.parametrize("cb", [0, 1])
 def test_moe_forward(cuda_device, T, topk, E, cb):
     rng = np.random.default_rng(1000 * T + 10 * topk + cb)
