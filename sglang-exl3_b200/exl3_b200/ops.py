@@ -322,6 +322,11 @@ def matmul_multi(x: torch.Tensor, linears, K: int, cb: int, outs=None,
             raise RuntimeError("matmul_multi outputs must share a dtype")
     L = _lib.lib()
     flags = 0 if variant is None else (int(variant) & 3) << 8
+    if m >= TC_MIN_ROWS and all(lin[0].data_ptr() % 16 == 0 for lin in linears):
+        # one tensor-core GEMM per linear: codes streamed once per 256 rows
+        for (tr, su, sv), o in zip(linears, outs):
+            _gemm_into(x2, tr.contiguous(), su, sv, K, cb, o, 0)
+        return outs
     for r0 in range(0, m, _lib.GEMV_MAX_M):
         r1 = min(m, r0 + _lib.GEMV_MAX_M)
         mc = r1 - r0

@@ -25,13 +25,14 @@ def _lin(rng, k, n, K):
     return O.random_trellis(rng, k, n, K), O.random_signs(rng, k), O.random_signs(rng, n)
 
 
+@pytest.mark.parametrize("m", [5, 40])  # 40 rows: one tensor-core GEMM per linear
 @pytest.mark.parametrize("K,cb", [(4, 0), (3, 1), (2, 2)])
-def test_matmul_multi_qkv(cuda_device, K, cb):
+def test_matmul_multi_qkv(cuda_device, K, cb, m):
     rng = np.random.default_rng(31 + K)
     lins = [_lin(rng, 512, n, K) for n in (512, 128, 128)]
-    x = rng.standard_normal((5, 512)).astype(np.float16)
+    x = rng.standard_normal((m, 512)).astype(np.float16)
     dev_lins = [tuple(_t(a, cuda_device) for a in lin) for lin in lins]
-    fused = torch.zeros((5, 768), dtype=torch.float16, device=cuda_device)
+    fused = torch.zeros((m, 768), dtype=torch.float16, device=cuda_device)
     outs = [fused[:, 0:512], fused[:, 512:640], fused[:, 640:768]]
     ops.matmul_multi(_t(x, cuda_device), dev_lins, K, cb, outs=outs)
     for (tr, su, sv), o in zip(lins, outs):
