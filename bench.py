@@ -306,6 +306,10 @@ def workload_scale(args):
         H, I = 5120, 25600
         return H * 2 * I + I * H, args.batch, "rows/s"
     if args.workload == "moe":
+        if getattr(args, "moe", "c3") == "c5":
+            E, topk, H, I, T = 128, 8, 4096, 1536, 5 * args.batch
+            touched = E * (1.0 - (1.0 - topk / E) ** T)
+            return touched * 3 * H * I, T, "tok/s"
         E, topk, H, I = 288, 8, 2048, 1024
         touched = E * (1.0 - (1.0 - topk / E) ** args.batch)  # expected distinct experts under uniform routing
         return touched * 3 * H * I + 3 * H * I, args.batch, "tok/s"
@@ -541,13 +545,15 @@ def run_moe(args, world, rank, local, device):
     from exl3_b200.ep import ExpertParallelMoE, exl3_local_experts
 
     hbm_peak, tc_peak, peak_kind = peaks()
-    E, topk, H, I, K = 288, 8, 2048, 1024, 3
+    c5 = args.moe == "c5"
+    E, topk, H, I, K = (128, 8, 4096, 1536, 3) if c5 else (288, 8, 2048, 1024, 3)
     if E % world:
-        raise SystemExit("288 experts do not split over this many ranks")
+        raise SystemExit(f"{E} experts do not split over this many ranks")
     el = E // world
-    T = args.batch
+    T = 5 * args.batch if c5 else args.batch  # config 5 verifies 4 draft tokens + 1 per sequence
+    seed = 4 if c5 else 2
     gen = torch.Generator(device=device)
-    gen.manual_seed(2 + 1000 * rank)
+    gen.manual_seed(seed + 1000 * rank)
     w13 = torch.randint(-32768, 32768, (el, 2, H // 16, I // 16, 16 * K), dtype=torch.int16, device=device, generator=gen)
     w2 = torch.randint(-32768, 32768, (el, I // 16, H // 16, 16 * K), dtype=torch.int16, device=device, generator=gen)
 
@@ -569,7 +575,7 @@ def run_moe(args, world, rank, local, device):
     sh_up = make_linear(shared_gen, H, I, 4, device)
     sh_down = make_linear(shared_gen, I, H, 4, device)
     rgen = torch.Generator(device=device)
-    rgen.manual_seed(2)
+    rgen.manual_seed(seed)
     x = torch.randn(T, H, dtype=torch.float16, device=device, generator=rgen)
     logits = torch.randn(T, E, dtype=torch.float32, device=device, generator=rgen)
     local_fn = exl3_local_experts(tables, K, K, K, 0, I)
@@ -586,10 +592,11 @@ def run_moe(args, world, rank, local, device):
             out = local_fn(x, ids.to(torch.int32), w)
         else:
             out = ep(x, ids, w, local_fn)
-        ops.matmul_multi(x, [sh_gate, sh_up], 4, 0, outs=sh_gu)
-        torch.mul(torch.nn.functional.silu(sh_gu[0]), sh_gu[1], out=sh_act)
-        ops.matmul(sh_act, *sh_down, 4, 0, out=sh_out)
-        out += sh_out.float()
+        if not c5:  # config 3's shared expert (config 5 has none)
+            ops.matmul_multi(x, [sh_gate, sh_up], 4, 0, outs=sh_gu)
+            torch.mul(torch.nn.functional.silu(sh_gu[0]), sh_gu[1], out=sh_act)
+            ops.matmul(sh_act, *sh_down, 4, 0, out=sh_out)
+            out += sh_out.float()
         return out
 
     for _ in range(args.warmup):
@@ -610,7 +617,7 @@ def run_moe(args, world, rank, local, device):
         ids_all = torch.topk(torch.softmax(logits, -1), topk, dim=-1)[1]
         touched = int(torch.unique(ids_all).numel())
     expert_bytes = (2 * H * I + I * H) * K // 8
-    step_bytes = touched * expert_bytes / world + 3 * H * I * 4 // 8
+    step_bytes = touched * expert_bytes / world + (0 if c5 else 3 * H * I * 4 // 8)
     gbs = step_bytes / (ms * 1e-3) / 1e9
 
     px = torch.randn(T, H, dtype=torch.float16).pin_memory()
@@ -625,9 +632,12 @@ def run_moe(args, world, rank, local, device):
         py.copy_(y, non_blocking=True)
         torch.cuda.synchronize()
     e2e_ms = max_over_ranks(world, (time.perf_counter() - t0) / n_e2e * 1e3)
-    line = {"metric": "C3 routed MoE layer tokens/s", "value": T / (ms * 1e-3), "unit": "tok/s", "ms_per_step": ms,
-            "config": {"workload": f"config 3 MoE layer, T={T}", "experts": E, "topk": topk, "hidden": H,
-                       "intermediate": I, "bpw": K, "codebook": "3INST", "shared_expert": "4 bpw",
+    name = (f"config 5 MoE layer, speculative verify of {args.batch} sequences x 5 tokens (T={T})" if c5
+            else f"config 3 MoE layer, T={T}")
+    line = {"metric": ("C5" if c5 else "C3") + " routed MoE layer tokens/s", "value": T / (ms * 1e-3), "unit": "tok/s",
+            "ms_per_step": ms,
+            "config": {"workload": name, "experts": E, "topk": topk, "hidden": H,
+                       "intermediate": I, "bpw": K, "codebook": "3INST", "shared_expert": "none" if c5 else "4 bpw",
                        "parallelism": f"ep{world}" if world > 1 else "single GPU",
                        "experts_touched": touched,
                        "l2": "expert codes 2.36 MB each; time includes routing (softmax/top-k) and the shared expert"},
@@ -758,6 +768,9 @@ def main():
     ap.add_argument("--ctx", type=int, default=2048)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=80, help="decode: decoder layers (80 = config 4; fewer for profiling)")
+    ap.add_argument("--moe", default="c3", choices=["c3", "c5"],
+                    help="moe workload: c3 = 288 experts, hidden 2048 (+ shared expert); c5 = the MoE layer of "
+                         "config 5's speculative verify: 128 experts, hidden 4096, 5 rows per sequence")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
