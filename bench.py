@@ -730,8 +730,8 @@ def run_decode(args, world, rank, local, device):
         "e2e": {"value": batch / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": 8 * batch, "d2h_bytes_per_step": 8 * batch,
                 "path": "DecodeModel.generate: host token in, per-step token out, stream sync each step"},
-        # fused: per layer 7 (attention) + 5 (MLP) launches, + 2 residual kernels per layer under TP
-        "gpu_launches": steps * cfg.layers * ((12 + (2 if world > 1 else 0)) if model.fused else 12),
+        # fused: per layer 6 (attention) + 5 (MLP) launches, + 2 peer-reduce kernels per layer under TP
+        "gpu_launches": steps * cfg.layers * ((11 + (2 if world > 1 else 0)) if model.fused else 12),
         "clocks": clk.summary(),
     }
     return finish(line, args, world)

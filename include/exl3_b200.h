@@ -259,7 +259,7 @@ EXL3B200_API int exl3b200_peer_buffer_free(void* ptr);
 
 /*
  * Fused decode sub-layers of a Llama-style decoder for batch <= 16 sequences,
- * head_dim 128, query heads per kv head <= 8.  No counterpart in the reference,
+ * head_dim 128, query heads per kv head <= 16.  No counterpart in the reference,
  * whose layers call SGLang's norm / attention / activation kernels around the
  * EXL3 ops (dense.py:317-371); each step follows the unfused model (RMSNorm,
  * RoPE rotate-half, softmax attention over the bf16 cache, SwiGLU, residual).

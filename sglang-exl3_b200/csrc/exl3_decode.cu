@@ -1,7 +1,7 @@
 // Fused decode layer around the EXL3 small-M matmul: the glue of a Llama-style
 // decoder layer (RMSNorm, RoPE, KV-cache append, attention, residual adds,
 // SwiGLU) moved into the matmul pipeline's own input stages and epilogues, so a
-// decode step runs about a dozen kernels per layer instead of ~75.
+// decode step runs about ten kernels per layer instead of ~75.
 //
 // Attention sub-layer (exl3b200_decode_attention), all launches chained by
 // programmatic dependent launch:
@@ -14,13 +14,18 @@
 //      (rotate-half pairs (d, d+64) sit in one lane of the warp-wide H128 layout),
 //      q is stored scaled by 1/sqrt(head_dim), k and v are appended to the bf16
 //      cache at the current position;
-//   4. split-K attention: one CTA per (row, kv head, 64-position chunk), one warp
-//      per query head of the group: scores, chunk softmax (max, sum) and the
-//      weighted sum of V, written as partials;
-//   5. input stage, attention mode: merges a head's chunk partials (log-sum-exp
-//      rescale), normalises, fp16, then x*suh, H128 for the o projection;
-//   6. matmul (o);
-//   7. epilogue, residual mode: h += y and the row's new sum of squares (or, with
+//   4. split-K attention on the tensor cores: one CTA per (row, kv head,
+//      64-position chunk), four warps of 16 positions each.  The query heads of the
+//      GQA group (up to 16, zero-padded) are the M rows of mma.m16n8k16 (bf16,
+//      fp32 accumulate; q and the softmax weights enter as bf16 hi + lo pairs, two MMAs
+//      each): S = Q K^T, the chunk softmax with one CTA-wide row max, then P V with
+//      the score accumulators reused as the A fragments.  Each CTA
+//      writes its chunk partial (unnormalised O, max, sum); the last CTA of a
+//      (row, kv head) to finish - an arrival ticket, no waiting - merges the
+//      chunks (log-sum-exp rescale), normalises, rounds to fp16 and writes the o
+//      projection's rotated input (x*suh, H128) for the group's heads;
+//   5. matmul (o);
+//   6. epilogue, residual mode: h += y and the row's new sum of squares (or, with
 //      tensor parallelism, an fp32 store of the partial y for the all-reduce).
 // MLP sub-layer (exl3b200_decode_mlp): norm input stage for gate and up, their
 // grouped matmul, the SwiGLU epilogue that writes the down projection's rotated
@@ -50,7 +55,6 @@ namespace exl3b200 {
 constexpr int kDecChunk = 64;   // attention positions per CTA
 constexpr int kHeadDim = 128;
 
-enum DecInMode : int { kInNorm = 0, kInAttn = 1 };
 enum DecEpiMode : int { kEpiRopeKV = 10, kEpiResidual = 11, kEpiPeerStore = 12 };
 
 // peer buffer: [control 128 B][flags: 2 parities x 8 ranks x u32, padded to 128 B]
@@ -85,6 +89,7 @@ struct DecAux {
     int max_ctx, q_heads, kv_heads, max_chunks;
     float* attn_o;           // [batch][q_heads][max_chunks][128] unnormalised partial outputs
     float* attn_ml;          // [batch][q_heads][max_chunks][2] (chunk max, chunk sum)
+    unsigned int* attn_cnt;  // [batch][kv_heads] chunk arrival tickets (state: zero between calls)
     // residual epilogue
     float* resid;
     long long resid_stride;
@@ -156,14 +161,13 @@ __device__ __forceinline__ void dec_store_rotated(const GvProblem& p, int r, int
     }
 }
 
-template <int MODE>
 __global__ __launch_bounds__(256) void exl3_dec_input_kernel(const __grid_constant__ GvArgs a,
                                                              const __grid_constant__ DecAux x)
 {
     griddep_launch();
     griddep_wait();
     const int lane = threadIdx.x & 31;
-    if (MODE == kInNorm && x.ss_out && blockIdx.x == 0)
+    if (x.ss_out && blockIdx.x == 0)
         for (int i = threadIdx.x; i < x.zero_rows; i += blockDim.x) x.ss_out[i] = 0.f;
     const int warps = gridDim.x * (blockDim.x >> 5);
     for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < a.in_tasks; task += warps) {
@@ -174,7 +178,7 @@ __global__ __launch_bounds__(256) void exl3_dec_input_kernel(const __grid_consta
         const int r = local / nblk;
         const int b = local - r * nblk;
         float xv[4];
-        if constexpr (MODE == kInNorm) {
+        {
             const float rs = rsqrtf(x.ss_in[r] * x.inv_hidden + x.eps);
             const float* hr = x.h + (size_t) r * x.h_stride + b * 128;
 #pragma unroll
@@ -182,41 +186,6 @@ __global__ __launch_bounds__(256) void exl3_dec_input_kernel(const __grid_consta
                 const int c = lane + 32 * i;
                 xv[i] = __half2float(__float2half_rn(hr[c] * rs * __bfloat162float(x.norm_w[b * 128 + c])));
             }
-        } else {
-            // block b of the o-projection input = query head b; chunk statistics
-            // across lanes, partial outputs 8 chunks at a time (independent loads)
-            const int L = (int) (*x.pos) + 1;
-            const int nch = (L + kDecChunk - 1) / kDecChunk;
-            const size_t hb = (size_t) r * x.q_heads + b;
-            const float* ml = x.attn_ml + hb * x.max_chunks * 2;
-            const float* po = x.attn_o + hb * x.max_chunks * kHeadDim;
-            float mx = -INFINITY;
-            for (int c = lane; c < nch; c += 32) mx = fmaxf(mx, ml[2 * c]);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-            float l = 0.f;
-            for (int c = lane; c < nch; c += 32) l += __expf(ml[2 * c] - mx) * ml[2 * c + 1];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-            float o4[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int c0 = 0; c0 < nch; c0 += 8) {
-                float f[8], pv[8][4];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int c = c0 + j;
-                    const bool ok = c < nch;
-                    f[j] = ok ? __expf(ml[2 * c] - mx) : 0.f;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) pv[j][i] = ok ? po[(size_t) c * kHeadDim + lane + 32 * i] : 0.f;
-                }
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) o4[i] += f[j] * pv[j][i];
-            }
-            const float inv = 1.f / l;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) xv[i] = __half2float(__float2half_rn(o4[i] * inv));
         }
         dec_store_rotated(p, r, b, lane, xv);
     }
@@ -242,6 +211,10 @@ __global__ __launch_bounds__(256) void exl3_dec_epilogue_kernel(const __grid_con
         if constexpr (MODE == kEpiRopeKV) {
             // problems 0, 1, 2 = q, k, v; block nb = head nb; lane holds dims lane + 32e
             const long long pos = *x.pos;
+            if (pos < 0 || pos >= x.max_ctx) {  // the cache has no row for this position
+                if (x.status && lane == 0) atomicCAS(x.status, 0, (int) kErrBadShape);
+                continue;
+            }
             if (pi < 2) {
                 const float fpos = (float) pos;
                 float s0, c0, s1, c1;
@@ -289,100 +262,283 @@ __global__ __launch_bounds__(256) void exl3_dec_epilogue_kernel(const __grid_con
     }
 }
 
-// Split-K decode attention over the bf16 cache (positions 0..pos inclusive).
-__global__ __launch_bounds__(256) void exl3_dec_attn_kernel(const __grid_constant__ DecAux x)
+// ---------------------------------------------------------------------------
+// split-K decode attention on the tensor cores
+// ---------------------------------------------------------------------------
+
+constexpr int kAttnWarps = kDecChunk / 16;  // 16 positions per warp
+constexpr int kAttnThreads = 32 * kAttnWarps;
+constexpr int kAttnMaxGroup = 16;           // query heads per kv head (the M rows of the MMA)
+constexpr int kKvPitch = kHeadDim + 8;      // bf16 per staged K/V row: 272 B, ldmatrix rows on distinct banks
+constexpr int kOPitch = kHeadDim + 8;       // fp32 per row of a warp's partial O
+
+struct AttnSmem {
+    __nv_bfloat16 k[kDecChunk][kKvPitch];
+    __nv_bfloat16 v[kDecChunk][kKvPitch];
+    float o[kAttnWarps][kAttnMaxGroup][kOPitch];  // per-warp partial O
+    float red_m[kAttnWarps][kAttnMaxGroup];
+    float red_l[kAttnWarps][kAttnMaxGroup];
+    unsigned int ticket;
+};
+
+__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, int src_bytes)
+{
+    const unsigned s = (unsigned) __cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(src_bytes) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem)
+{
+    const unsigned s = (unsigned) __cvta_generic_to_shared(smem);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(s));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* smem)
+{
+    const unsigned s = (unsigned) __cvta_generic_to_shared(smem);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(s));
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+                 "{%8, %9}, {%0, %1, %2, %3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// (a, b) -> bf16x2 hi = rn(a, b) and lo = rn(a - hi_a, b - hi_b): hi + lo carries
+// about 16 significant bits, so bf16 MMAs on both parts act like fp32 inputs
+__device__ __forceinline__ void split_bf16(float a, float b, uint32_t& hi, uint32_t& lo)
+{
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// One CTA per (row b, kv head, chunk of 64 cached positions; positions 0..pos
+// inclusive are attended).  Warp w owns positions 16w..16w+15 of the chunk.  MMA
+// fragments (lane = 4g + c): A rows g / g+8 = query heads of the group, B / C
+// columns = positions (S) or head dims (O).  Grid: batch * kv_heads * max_chunks;
+// `ob` holds the o projection (problem 0) whose rotated input the finisher writes.
+__global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __grid_constant__ GvArgs ob,
+                                                                     const __grid_constant__ DecAux x)
 {
     griddep_launch();
-    griddep_wait();
-    __shared__ __align__(16) __nv_bfloat16 ks[kDecChunk][kHeadDim];
-    __shared__ __align__(16) __nv_bfloat16 vs[kDecChunk][kHeadDim];
+    griddep_wait();  // q (scaled) and the new K/V row come from the RoPE epilogue
+    extern __shared__ __align__(128) unsigned char attn_smem_raw[];
+    AttnSmem& sm = *reinterpret_cast<AttnSmem*>(attn_smem_raw);
     const int chunk = blockIdx.x % x.max_chunks;
     const int t = blockIdx.x / x.max_chunks;
     const int kvh = t % x.kv_heads;
     const int b = t / x.kv_heads;
-    const int L = (int) (*x.pos) + 1;
+    const long long pos = *x.pos;
+    if (pos < 0 || pos >= x.max_ctx) return;  // recorded in the device status by the RoPE epilogue
+    const int L = (int) pos + 1;
+    const int nch = (L + kDecChunk - 1) / kDecChunk;
+    if (chunk >= nch) return;  // uniform over the CTA
     const int p0 = chunk * kDecChunk;
-    if (p0 >= L) return;  // uniform over the CTA
     const int np = min(kDecChunk, L - p0);
-    const size_t base = (size_t) b * x.cache_b_stride + (size_t) kvh * x.cache_h_stride + (size_t) p0 * kHeadDim;
-    const uint4* kg = reinterpret_cast<const uint4*>(x.k_cache + base);
-    const uint4* vg = reinterpret_cast<const uint4*>(x.v_cache + base);
-    uint4* ksv = reinterpret_cast<uint4*>(&ks[0][0]);
-    uint4* vsv = reinterpret_cast<uint4*>(&vs[0][0]);
-    const int n16 = np * (kHeadDim / 8);  // 16-byte pieces of the chunk
-    for (int i = threadIdx.x; i < n16; i += blockDim.x) {
-        ksv[i] = kg[i];
-        vsv[i] = vg[i];
+    const int group = x.q_heads / x.kv_heads;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int g = lane >> 2, c = lane & 3;
+
+    // stage the chunk's K and V rows (16 x 16 B each); rows >= np are zero-filled
+    {
+        const size_t base = (size_t) b * x.cache_b_stride + (size_t) kvh * x.cache_h_stride + (size_t) p0 * kHeadDim;
+        const __nv_bfloat16* kg = x.k_cache + base;
+        const __nv_bfloat16* vg = x.v_cache + base;
+        for (int i = tid; i < kDecChunk * 16; i += kAttnThreads) {
+            const int row = i >> 4, seg = (i & 15) * 8;
+            const bool ok = row < np;
+            const size_t off = ok ? (size_t) row * kHeadDim + seg : 0;
+            cp_async16_zfill(&sm.k[row][seg], kg + off, ok ? 16 : 0);
+            cp_async16_zfill(&sm.v[row][seg], vg + off, ok ? 16 : 0);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    // rows past the end of the context are zero: the 4-wide loops read them with weight 0
-    for (int i = n16 + threadIdx.x; i < kDecChunk * (kHeadDim / 8); i += blockDim.x) {
-        ksv[i] = make_uint4(0u, 0u, 0u, 0u);
-        vsv[i] = make_uint4(0u, 0u, 0u, 0u);
+
+    // Q fragments of the group's heads (rows >= group are zero) as bf16 pairs
+    // hi + lo (hi = bf16(q), lo = bf16(q - hi)): two MMAs give the scores to ~16 bits
+    uint32_t qa[kHeadDim / 16][4], ql[kHeadDim / 16][4];
+    {
+        const float* qb = x.qbuf + ((size_t) b * x.q_heads + (size_t) kvh * group) * kHeadDim;
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int row = g + 8 * hf;
+                float2 f0 = make_float2(0.f, 0.f), f1 = make_float2(0.f, 0.f);
+                if (row < group) {
+                    f0 = *reinterpret_cast<const float2*>(qb + row * kHeadDim + 16 * kk + 2 * c);
+                    f1 = *reinterpret_cast<const float2*>(qb + row * kHeadDim + 16 * kk + 2 * c + 8);
+                }
+                split_bf16(f0.x, f0.y, qa[kk][hf], ql[kk][hf]);
+                split_bf16(f1.x, f1.y, qa[kk][2 + hf], ql[kk][2 + hf]);
+            }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+
+    // S = Q K^T over this warp's two 8-position tiles
+    const int mi = lane >> 3, mr = lane & 7;  // ldmatrix: matrix and row this lane addresses
+    float s[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[j][e] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+        uint32_t kb[4];
+        ldsm_x4(kb, &sm.k[16 * warp + 8 * (mi >> 1) + mr][16 * kk + 8 * (mi & 1)]);
+        mma_bf16_16816(s[0], qa[kk], kb[0], kb[1]);
+        mma_bf16_16816(s[1], qa[kk], kb[2], kb[3]);
+        mma_bf16_16816(s[0], ql[kk], kb[0], kb[1]);
+        mma_bf16_16816(s[1], ql[kk], kb[2], kb[3]);
+    }
+    // mask positions past the context, row maxima (rows g, g+8) over the CTA
+    float mg = -INFINITY, mh = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const bool ok = 16 * warp + 8 * j + 2 * c + e < np;
+            s[j][e] = ok ? s[j][e] : -INFINITY;
+            s[j][2 + e] = ok ? s[j][2 + e] : -INFINITY;
+            mg = fmaxf(mg, s[j][e]);
+            mh = fmaxf(mh, s[j][2 + e]);
+        }
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+        mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, o));
+        mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
+    }
+    if (c == 0) {
+        sm.red_m[warp][g] = mg;
+        sm.red_m[warp][g + 8] = mh;
     }
     __syncthreads();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int group = x.q_heads / x.kv_heads;
-    if (warp >= group) return;
-    const int qh = kvh * group + warp;
-    const float4 q = *reinterpret_cast<const float4*>(x.qbuf + ((size_t) b * x.q_heads + qh) * kHeadDim + 4 * lane);
-    // scores, 4 positions per step with independent warp reductions (the scores of
-    // the zero rows >= np are discarded)
-    float s_lo = -INFINITY, s_hi = -INFINITY;
-    for (int p = 0; p < np; p += 4) {
-        float d[4];
+    mg = sm.red_m[0][g];
+    mh = sm.red_m[0][g + 8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const uint2 kr = *reinterpret_cast<const uint2*>(&ks[p + j][4 * lane]);
-            const float2 k01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kr.x));
-            const float2 k23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&kr.y));
-            d[j] = q.x * k01.x + q.y * k01.y + q.z * k23.x + q.w * k23.y;
-        }
+    for (int w = 1; w < kAttnWarps; ++w) {
+        mg = fmaxf(mg, sm.red_m[w][g]);
+        mh = fmaxf(mh, sm.red_m[w][g + 8]);
+    }
+    // P = exp(S - max) in fp32, fed to the MMA as bf16 pairs hi + lo
+    uint32_t pa[4], pl[4];
+    float lg = 0.f, lh = 0.f;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
+    for (int j = 0; j < 2; ++j) {
+        const float e0 = __expf(s[j][0] - mg), e1 = __expf(s[j][1] - mg);
+        const float e2 = __expf(s[j][2] - mh), e3 = __expf(s[j][3] - mh);
+        lg += e0 + e1;
+        lh += e2 + e3;
+        split_bf16(e0, e1, pa[2 * j], pl[2 * j]);
+        split_bf16(e2, e3, pa[2 * j + 1], pl[2 * j + 1]);
+    }
 #pragma unroll
-            for (int j = 0; j < 4; ++j) d[j] += __shfl_xor_sync(0xffffffffu, d[j], o);
+    for (int o = 1; o < 4; o <<= 1) {
+        lg += __shfl_xor_sync(0xffffffffu, lg, o);
+        lh += __shfl_xor_sync(0xffffffffu, lh, o);
+    }
+    if (c == 0) {
+        sm.red_l[warp][g] = lg;
+        sm.red_l[warp][g + 8] = lh;
+    }
+    // O_w = P V over the warp's 16 positions, 16 tiles of 8 head dims
+    float acc[kHeadDim / 8][4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int pp = p + j;
-            if (pp < np && lane == (pp & 31)) {
-                if (pp < 32) s_lo = d[j];
-                else s_hi = d[j];
+    for (int n = 0; n < kHeadDim / 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+#pragma unroll
+    for (int q = 0; q < kHeadDim / 16; ++q) {
+        uint32_t vb[4];
+        ldsm_x4_t(vb, &sm.v[16 * warp + 8 * (mi & 1) + mr][16 * q + 8 * (mi >> 1)]);
+        mma_bf16_16816(acc[2 * q], pa, vb[0], vb[1]);
+        mma_bf16_16816(acc[2 * q + 1], pa, vb[2], vb[3]);
+        mma_bf16_16816(acc[2 * q], pl, vb[0], vb[1]);
+        mma_bf16_16816(acc[2 * q + 1], pl, vb[2], vb[3]);
+    }
+#pragma unroll
+    for (int n = 0; n < kHeadDim / 8; ++n) {
+        if (g < group) *reinterpret_cast<float2*>(&sm.o[warp][g][8 * n + 2 * c]) = make_float2(acc[n][0], acc[n][1]);
+        if (g + 8 < group)
+            *reinterpret_cast<float2*>(&sm.o[warp][g + 8][8 * n + 2 * c]) = make_float2(acc[n][2], acc[n][3]);
+    }
+    __syncthreads();
+
+    // chunk partial: O summed over the warps (shared row max), max and sum per head
+    const size_t hc0 = ((size_t) b * x.q_heads + (size_t) kvh * group) * x.max_chunks + chunk;
+    for (int hh = 0; hh < group; ++hh) {
+        float v = sm.o[0][hh][tid];
+#pragma unroll
+        for (int w = 1; w < kAttnWarps; ++w) v += sm.o[w][hh][tid];
+        x.attn_o[(hc0 + (size_t) hh * x.max_chunks) * kHeadDim + tid] = v;
+    }
+    if (tid < group) {
+        float l = 0.f, m = sm.red_m[0][tid];
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) l += sm.red_l[w][tid];
+#pragma unroll
+        for (int w = 1; w < kAttnWarps; ++w) m = fmaxf(m, sm.red_m[w][tid]);
+        x.attn_ml[2 * (hc0 + (size_t) tid * x.max_chunks)] = m;
+        x.attn_ml[2 * (hc0 + (size_t) tid * x.max_chunks) + 1] = l;
+    }
+
+    // arrival ticket: the last chunk CTA of (b, kv head) merges
+    __threadfence();
+    __syncthreads();
+    unsigned int* cnt = x.attn_cnt + (size_t) b * x.kv_heads + kvh;
+    if (tid == 0) sm.ticket = atomicAdd(cnt, 1u);
+    __syncthreads();
+    if (sm.ticket != (unsigned int) (nch - 1)) return;
+    __threadfence();
+    if (tid == 0) *cnt = 0u;  // every chunk CTA of this call has arrived
+
+    // merge: warp per head; lanes split the chunks for the statistics, then hold
+    // head dims lane + 32i for the weighted sum (partials read from L2)
+    const GvProblem& po = gv_prob(ob, 0);
+    for (int hh = warp; hh < group; hh += kAttnWarps) {
+        const size_t hb = ((size_t) b * x.q_heads + (size_t) kvh * group + hh) * x.max_chunks;
+        const float* ml = x.attn_ml + 2 * hb;
+        const float* po_c = x.attn_o + hb * kHeadDim;
+        float mx = -INFINITY;
+        for (int cc = lane; cc < nch; cc += 32) mx = fmaxf(mx, __ldcg(ml + 2 * cc));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float l = 0.f;
+        for (int cc = lane; cc < nch; cc += 32) l += __expf(__ldcg(ml + 2 * cc) - mx) * __ldcg(ml + 2 * cc + 1);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        float o4[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c0 = 0; c0 < nch; c0 += 8) {
+            float f[8], pv[8][4];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int cc = c0 + j;
+                const bool ok = cc < nch;
+                f[j] = ok ? __expf(__ldcg(ml + 2 * cc) - mx) : 0.f;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) pv[j][i] = ok ? __ldcg(po_c + (size_t) cc * kHeadDim + lane + 32 * i) : 0.f;
             }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o4[i] += f[j] * pv[j][i];
         }
-    }
-    float m = fmaxf(s_lo, s_hi);
+        const float inv = 1.f / l;
+        float xv[4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    const float e_lo = s_lo == -INFINITY ? 0.f : __expf(s_lo - m);
-    const float e_hi = s_hi == -INFINITY ? 0.f : __expf(s_hi - m);
-    float l = e_lo + e_hi;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    float4 acc[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int p = 0; p < np; p += 4) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int pp = p + j;
-            float e = __shfl_sync(0xffffffffu, pp < 32 ? e_lo : e_hi, pp & 31);
-            if (pp >= np) e = 0.f;
-            const uint2 vr = *reinterpret_cast<const uint2*>(&vs[pp][4 * lane]);
-            const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr.x));
-            const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vr.y));
-            acc[j].x += e * v01.x;
-            acc[j].y += e * v01.y;
-            acc[j].z += e * v23.x;
-            acc[j].w += e * v23.y;
-        }
-    }
-    const float4 o4 = make_float4(acc[0].x + acc[1].x + acc[2].x + acc[3].x, acc[0].y + acc[1].y + acc[2].y + acc[3].y,
-                                  acc[0].z + acc[1].z + acc[2].z + acc[3].z, acc[0].w + acc[1].w + acc[2].w + acc[3].w);
-    const size_t hc = ((size_t) b * x.q_heads + qh) * x.max_chunks + chunk;
-    *reinterpret_cast<float4*>(x.attn_o + hc * kHeadDim + 4 * lane) = o4;
-    if (lane == 0) {
-        x.attn_ml[2 * hc] = m;
-        x.attn_ml[2 * hc + 1] = l;
+        for (int i = 0; i < 4; ++i) xv[i] = __half2float(__float2half_rn(o4[i] * inv));
+        dec_store_rotated(po, b, kvh * group + hh, lane, xv);
     }
 }
 
@@ -499,6 +655,39 @@ static int dec_launch(Kern kern, int grid, int block, cudaStream_t stream, Args.
     return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? kOk : kErrLaunch;
 }
 
+// The attention kernel's shared memory (K and V chunk, per-warp partials) exceeds
+// the 48 KB default: raise the limit once per device.
+static int dec_attn_smem_setup()
+{
+    static int done[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kErrLaunch;
+    if (!done[dev]) {
+        if (cudaFuncSetAttribute(exl3_dec_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int) sizeof(AttnSmem)) != cudaSuccess)
+            return kErrLaunch;
+        done[dev] = 1;
+    }
+    return kOk;
+}
+
+static int dec_launch_attn(const GvArgs& ob, const DecAux& x, int grid, cudaStream_t stream)
+{
+    const int rc = dec_attn_smem_setup();
+    if (rc != kOk) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) std::max(grid, 1));
+    cfg.blockDim = dim3((unsigned) kAttnThreads);
+    cfg.dynamicSmemBytes = sizeof(AttnSmem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, exl3_dec_attn_kernel, ob, x) == cudaSuccess ? kOk : kErrLaunch;
+}
+
 static int dec_grid(int tasks) { return std::min((tasks + 7) / 8, 8 * gv_sm_count()); }
 
 template <int MODE>
@@ -533,7 +722,7 @@ static void dec_problem(GvProblem& p, const exl3b200_linear* l, int m, uint32_t*
 
 // Workspace layout of the attention sub-layer.
 struct DecAttnLayout {
-    size_t st_q, st_k, st_v, st_o, state_bytes;
+    size_t st_q, st_k, st_v, st_o, st_cnt, state_bytes;
     size_t xd_q, xd_k, xd_v, sb_q, sb_k, sb_v, qbuf, attn_o, attn_ml, xd_o, sb_o, scratch_bytes;
 };
 
@@ -547,6 +736,7 @@ static DecAttnLayout dec_attn_layout(int batch, int hidden, int q_heads, int kv_
     L.st_k = o; o += gv_state_bytes_per_problem(nkv);
     L.st_v = o; o += gv_state_bytes_per_problem(nkv);
     L.st_o = o; o += gv_state_bytes_per_problem(hidden);
+    L.st_cnt = o; o += al256((size_t) batch * kv_heads * sizeof(unsigned int));
     L.state_bytes = o;
     o = 0;
     L.xd_q = o; o += gv_xd_bytes(batch, hidden);
@@ -698,7 +888,7 @@ extern "C" int exl3b200_decode_attention_workspace(int batch, int hidden, int q_
 {
     if (!state_bytes || !scratch_bytes) return kErrNullPointer;
     if (batch < 1 || batch > EXL3B200_GEMV_MAX_M || hidden <= 0 || hidden % 128 || q_heads < 1 || kv_heads < 1 ||
-        q_heads % kv_heads || q_heads / kv_heads > 8 || max_ctx < 1)
+        q_heads % kv_heads || q_heads / kv_heads > kAttnMaxGroup || max_ctx < 1)
         return kErrBadShape;
     const DecAttnLayout L = dec_attn_layout(batch, hidden, q_heads, kv_heads, max_ctx);
     *state_bytes = L.state_bytes;
@@ -731,7 +921,7 @@ extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int
     rc = dec_peers_check(peers, batch, hidden);
     if (rc != kOk) return rc;
     if (!k_cache || !v_cache || !pos || !inv_freq) return kErrNullPointer;
-    if (q_heads < 1 || kv_heads < 1 || q_heads % kv_heads || q_heads / kv_heads > 8 || max_ctx < 1)
+    if (q_heads < 1 || kv_heads < 1 || q_heads % kv_heads || q_heads / kv_heads > kAttnMaxGroup || max_ctx < 1)
         return kErrBadShape;
     const int nq = q_heads * kHeadDim, nkv = kv_heads * kHeadDim;
     if (!dec_linear_ok(q, hidden, nq) || !dec_linear_ok(k, hidden, nkv) || !dec_linear_ok(v, hidden, nkv) ||
@@ -757,6 +947,7 @@ extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int
     x.inv_hidden = 1.f / (float) hidden;
     x.pos = pos;
     x.inv_freq = inv_freq;
+    x.status = exl3_status_dev_ptr();
     x.qbuf = reinterpret_cast<float*>(W + L.qbuf);
     x.k_cache = reinterpret_cast<__nv_bfloat16*>(k_cache);
     x.v_cache = reinterpret_cast<__nv_bfloat16*>(v_cache);
@@ -768,6 +959,7 @@ extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int
     x.max_chunks = (max_ctx + kDecChunk - 1) / kDecChunk;
     x.attn_o = reinterpret_cast<float*>(W + L.attn_o);
     x.attn_ml = reinterpret_cast<float*>(W + L.attn_ml);
+    x.attn_cnt = reinterpret_cast<unsigned int*>(S + L.st_cnt);
 
     // 1-3: norm input stage, q/k/v matmul, RoPE + KV append epilogue
     GvArgs a = {};
@@ -779,25 +971,23 @@ extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int
     dec_problem(a.inl[2], v, batch, reinterpret_cast<uint32_t*>(W + L.xd_v),
                 mul1 ? reinterpret_cast<float*>(W + L.sb_v) : nullptr, reinterpret_cast<float*>(S + L.st_v));
     gv_prefix_inline(a);
-    rc = dec_launch(exl3_dec_input_kernel<kInNorm>, dec_grid(a.in_tasks), 256, st, a, x);
+    rc = dec_launch(exl3_dec_input_kernel, dec_grid(a.in_tasks), 256, st, a, x);
     if (rc != kOk) return rc;
     rc = gv_launch_matmul(a, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
     rc = dec_launch_epilogue<kEpiRopeKV>(a, x, cb, st);
     if (rc != kOk) return rc;
 
-    // 4: attention partials
-    rc = dec_launch(exl3_dec_attn_kernel, batch * kv_heads * x.max_chunks, 32 * (q_heads / kv_heads), st, x);
-    if (rc != kOk) return rc;
-
-    // 5-7: merge + rotate, o matmul, residual (or fp32 partial for the all-reduce)
+    // 4: attention (chunk partials, merged by the last chunk CTA into the o input)
     GvArgs b = {};
     b.nprob = 1;
     dec_problem(b.inl[0], o, batch, reinterpret_cast<uint32_t*>(W + L.xd_o),
                 mul1 ? reinterpret_cast<float*>(W + L.sb_o) : nullptr, reinterpret_cast<float*>(S + L.st_o));
     gv_prefix_inline(b);
-    rc = dec_launch(exl3_dec_input_kernel<kInAttn>, dec_grid(b.in_tasks), 256, st, b, x);
+    rc = dec_launch_attn(b, x, batch * kv_heads * x.max_chunks, st);
     if (rc != kOk) return rc;
+
+    // 5-6: o matmul, residual (or fp32 partial for the all-reduce)
     rc = gv_launch_matmul(b, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
     return dec_finish(b, x, cb, h, h_stride, ss_out, y_out, y_stride, peers, batch, hidden, st);
@@ -847,7 +1037,7 @@ extern "C" int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int 
     a.inl[0].out_suh = reinterpret_cast<const __half*>(down->suh);
     a.inl[0].out_sblk = mul1 ? reinterpret_cast<float*>(W + L.sb_d) : nullptr;
     gv_prefix_inline(a);
-    rc = dec_launch(exl3_dec_input_kernel<kInNorm>, dec_grid(a.in_tasks), 256, st, a, x);
+    rc = dec_launch(exl3_dec_input_kernel, dec_grid(a.in_tasks), 256, st, a, x);
     if (rc != kOk) return rc;
     rc = gv_launch_matmul(a, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;

@@ -2,10 +2,14 @@
 
 Both steps use the same EXL3 kernels for the matmuls; the fused one moves
 RMSNorm, RoPE, the KV append, attention, SiLU*mul and the residual adds into the
-matmul pipeline.  The unfused step rounds q and the attention output to bf16
-(scaled_dot_product_attention on bf16), the fused one keeps them in fp32, so the
-residual stream is held to a normwise relative error of 1e-2 and the KV entries
-it appends to 2e-2 (bf16 rounding of slightly different fp32 values).
+matmul pipeline.  The unfused step rounds q to bf16, runs
+scaled_dot_product_attention on bf16 and rounds its output to bf16; the fused one
+keeps q and the softmax weights to ~16 bits (bf16 hi + lo pairs on the tensor
+cores, fp32 sums) and the merged output in fp32, so the residual stream is held to a
+relative error of 1e-2 (max abs difference over max abs value) and the KV
+entries it appends to 2e-2 (bf16 rounding of slightly different fp32 values).
+The shapes cover GQA groups of 1 to 16 query heads and contexts of one to
+seventeen 64-position chunks (the chunk merge of the attention kernel).
 """
 
 import pytest
@@ -43,12 +47,14 @@ def _pair(cfg, batch, max_ctx, ctx, dev, tokens):
     return ms
 
 
-@pytest.mark.parametrize("heads,kv_heads,batch,ctx", [(4, 2, 1, 10), (16, 2, 3, 70), (8, 8, 2, 64), (8, 1, 1, 127)])
-def test_fused_step_matches_unfused(cuda_device, heads, kv_heads, batch, ctx):
+@pytest.mark.parametrize("heads,kv_heads,batch,ctx,max_ctx", [
+    (4, 2, 1, 10, 160), (16, 2, 3, 70, 160), (8, 8, 2, 64, 160), (8, 1, 1, 127, 160),
+    (16, 1, 1, 300, 320), (32, 4, 2, 1050, 1100), (8, 1, 1, 0, 64)])
+def test_fused_step_matches_unfused(cuda_device, heads, kv_heads, batch, ctx, max_ctx):
     cfg = DecoderConfig(layers=2, hidden=512, heads=heads, kv_heads=kv_heads, head_dim=128, inter=1024, vocab=1024,
                         K=4, cb=0)
     tokens = torch.arange(batch, device=cuda_device) * 7 + 3
-    ref, fus = _pair(cfg, batch, 160, ctx, cuda_device, tokens)
+    ref, fus = _pair(cfg, batch, max_ctx, ctx, cuda_device, tokens)
     for step in range(2):
         pos = int(ref.pos.item())
         ref.step()
@@ -135,3 +141,21 @@ def test_decode_rejects_bad_state(cuda_device):
                            m.v_cache[0], m.pos, m.inv_freq)
     with pytest.raises(RuntimeError):
         D.decode_mlp(m.h, m.ss[0], m.ss[1], L["ln2"].float(), cfg.eps, L["gu"][0], L["gu"][1], L["down"], 4, 0)
+
+
+def test_position_past_cache_sets_status(cuda_device):
+    """A device-side position with no cache row (pos >= max_ctx) is not written:
+    the sub-layer records EBADSHAPE in the sticky device status and the call
+    returns without touching the cache."""
+    from exl3_b200 import _lib, ops
+
+    cfg = DecoderConfig(layers=1, hidden=256, heads=2, kv_heads=1, head_dim=128, inter=512, vocab=256, K=4, cb=0)
+    m = DecodeModel(cfg, batch=1, max_ctx=64, device=cuda_device, fused=True)
+    m.fill_random_kv(64)  # pos = 64 = max_ctx
+    assert ops.device_status(cuda_device) == 0
+    k0 = m.k_cache.clone()
+    m.step()
+    torch.cuda.synchronize()
+    assert ops.device_status(cuda_device) == _lib.EBADSHAPE
+    assert ops.device_status(cuda_device) == 0  # read-and-reset
+    assert torch.equal(m.k_cache, k0)
