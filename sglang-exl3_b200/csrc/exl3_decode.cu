@@ -49,86 +49,11 @@
 #include "exl3_capi_internal.h"
 #include "exl3_grouped.cuh"
 #include "exl3_grouped_dev.cuh"
+#include "exl3_epilogue.cuh"
 
 namespace exl3b200 {
 
 constexpr int kDecChunk = 64;   // attention positions per CTA
-constexpr int kHeadDim = 128;
-
-enum DecEpiMode : int { kEpiRopeKV = 10, kEpiResidual = 11, kEpiPeerStore = 12 };
-
-// peer buffer: [control 128 B][flags: 2 parities x 8 ranks x u32, padded to 128 B]
-//              [data: 2 parities x 8 ranks x max_rows x hidden fp32]
-constexpr int kPeerMaxRanks = 8;
-constexpr size_t kPeerFlags = 128;
-constexpr size_t kPeerData = 256;
-constexpr unsigned long long kPeerTimeoutNs = 2000000000ull;
-
-struct PeerCtl {
-    unsigned int epoch;  // calls completed
-    unsigned int done;   // CTAs of the running reduce that finished
-};
-
-struct DecAux {
-    // norm input stage
-    const float* h;
-    long long h_stride;
-    const float* ss_in;
-    float* ss_out;           // zeroed by the norm input stage (rows zero_rows)
-    int zero_rows;
-    const __nv_bfloat16* norm_w;
-    float eps;
-    float inv_hidden;
-    // RoPE / KV append / attention
-    const long long* pos;    // position of the new token (= tokens already cached)
-    const float* inv_freq;   // [head_dim / 2]
-    float* qbuf;             // [batch][q_heads][128], scaled by 1/sqrt(128)
-    __nv_bfloat16* k_cache;  // [batch][kv_heads][max_ctx][128]
-    __nv_bfloat16* v_cache;
-    long long cache_b_stride, cache_h_stride;
-    int max_ctx, q_heads, kv_heads, max_chunks;
-    float* attn_o;           // [batch][q_heads][max_chunks][128] unnormalised partial outputs
-    float* attn_ml;          // [batch][q_heads][max_chunks][2] (chunk max, chunk sum)
-    unsigned int* attn_cnt;  // [batch][kv_heads] chunk arrival tickets (state: zero between calls)
-    // residual epilogue
-    float* resid;
-    long long resid_stride;
-    float* ss_acc;
-    // tensor-parallel partial exchange
-    char* peer[kPeerMaxRanks];
-    int peer_world, peer_rank, peer_rows, peer_hidden;
-    int* status;
-};
-
-__device__ __forceinline__ float* peer_slot(const DecAux& x, int q, unsigned int parity, int src, int row)
-{
-    return reinterpret_cast<float*>(x.peer[q] + kPeerData) +
-           (((size_t) parity * kPeerMaxRanks + src) * x.peer_rows + row) * x.peer_hidden;
-}
-
-__device__ __forceinline__ unsigned int* peer_flag(const DecAux& x, int q, unsigned int parity, int src)
-{
-    return reinterpret_cast<unsigned int*>(x.peer[q] + kPeerFlags) + parity * kPeerMaxRanks + src;
-}
-
-__device__ __forceinline__ unsigned long long globaltimer_ns()
-{
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p)
-{
-    unsigned int v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v)
-{
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 // fp16 values (already rounded) of one 128-block -> rotated input of a problem
 // (the GEMV input stage's layout: duplicated fp16 pairs, block sums for mul1).
@@ -206,59 +131,7 @@ __global__ __launch_bounds__(256) void exl3_dec_epilogue_kernel(const __grid_con
         const int local = task - p.out_task_begin;
         const int r = local / nblocks;
         const int nb = local - r * nblocks;
-        float v[4];
-        gv_finish<CB>(p, nb, r, lane, v);
-        if constexpr (MODE == kEpiRopeKV) {
-            // problems 0, 1, 2 = q, k, v; block nb = head nb; lane holds dims lane + 32e
-            const long long pos = *x.pos;
-            if (pos < 0 || pos >= x.max_ctx) {  // the cache has no row for this position
-                if (x.status && lane == 0) atomicCAS(x.status, 0, (int) kErrBadShape);
-                continue;
-            }
-            if (pi < 2) {
-                const float fpos = (float) pos;
-                float s0, c0, s1, c1;
-                sincosf(fpos * x.inv_freq[lane], &s0, &c0);
-                sincosf(fpos * x.inv_freq[lane + 32], &s1, &c1);
-                const float n0 = v[0] * c0 - v[2] * s0, n2 = v[2] * c0 + v[0] * s0;
-                const float n1 = v[1] * c1 - v[3] * s1, n3 = v[3] * c1 + v[1] * s1;
-                v[0] = n0;
-                v[1] = n1;
-                v[2] = n2;
-                v[3] = n3;
-            }
-            if (pi == 0) {
-                float* q = x.qbuf + ((size_t) r * x.q_heads + nb) * kHeadDim;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) q[lane + 32 * e] = v[e] * kHadScale;  // 1/sqrt(head_dim), head_dim = 128
-            } else {
-                __nv_bfloat16* c = (pi == 1 ? x.k_cache : x.v_cache) + (size_t) r * x.cache_b_stride +
-                                   (size_t) nb * x.cache_h_stride + (size_t) pos * kHeadDim;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) c[lane + 32 * e] = __float2bfloat16_rn(v[e]);
-            }
-        } else if constexpr (MODE == kEpiPeerStore) {
-            const PeerCtl* ctl = reinterpret_cast<const PeerCtl*>(x.peer[x.peer_rank]);
-            const unsigned int parity = (*reinterpret_cast<const volatile unsigned int*>(&ctl->epoch) + 1u) & 1u;
-            for (int q = 0; q < x.peer_world; ++q) {
-                float* dst = peer_slot(x, q, parity, x.peer_rank, r) + nb * 128;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) dst[lane + 32 * e] = v[e];
-            }
-            __threadfence_system();
-        } else {
-            float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
-            float sq = 0.f;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float nv = hr[lane + 32 * e] + v[e];
-                hr[lane + 32 * e] = nv;
-                sq += nv * nv;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-            if (lane == 0) atomicAdd(x.ss_acc + r, sq);
-        }
+        epi_block_row<CB>(a, x, MODE, pi, p, nullptr, nb, r, lane);
     }
 }
 
@@ -503,41 +376,66 @@ __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __gri
     __threadfence();
     if (tid == 0) *cnt = 0u;  // every chunk CTA of this call has arrived
 
-    // merge: warp per head; lanes split the chunks for the statistics, then hold
-    // head dims lane + 32i for the weighted sum (partials read from L2)
-    const GvProblem& po = gv_prob(ob, 0);
-    for (int hh = warp; hh < group; hh += kAttnWarps) {
+    // merge with a running max, 8 chunks of loads in flight per step: 16 threads per
+    // head, 8 head dims each; the normalised, fp16-rounded output goes through
+    // shared memory to the warp-per-head rotation of the o projection's input
+    float* merged = &sm.o[0][0][0];  // [kAttnMaxGroup][kOPitch]; the warps' partials are consumed
+    for (int hh = tid >> 4; hh < group; hh += kAttnThreads / 16) {
+        const int d = (tid & 15) * 8;
         const size_t hb = ((size_t) b * x.q_heads + (size_t) kvh * group + hh) * x.max_chunks;
         const float* ml = x.attn_ml + 2 * hb;
-        const float* po_c = x.attn_o + hb * kHeadDim;
-        float mx = -INFINITY;
-        for (int cc = lane; cc < nch; cc += 32) mx = fmaxf(mx, __ldcg(ml + 2 * cc));
+        const float* po_c = x.attn_o + hb * kHeadDim + d;
+        float m_run = -INFINITY, l_run = 0.f, o[8];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        float l = 0.f;
-        for (int cc = lane; cc < nch; cc += 32) l += __expf(__ldcg(ml + 2 * cc) - mx) * __ldcg(ml + 2 * cc + 1);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        float o4[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int i = 0; i < 8; ++i) o[i] = 0.f;
         for (int c0 = 0; c0 < nch; c0 += 8) {
-            float f[8], pv[8][4];
+            float2 st[8];
+            float4 oa[8], ob[8];
 #pragma unroll
             for (int j = 0; j < 8; ++j) {
                 const int cc = c0 + j;
-                const bool ok = cc < nch;
-                f[j] = ok ? __expf(__ldcg(ml + 2 * cc) - mx) : 0.f;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) pv[j][i] = ok ? __ldcg(po_c + (size_t) cc * kHeadDim + lane + 32 * i) : 0.f;
+                if (cc < nch) {
+                    st[j] = __ldcg(reinterpret_cast<const float2*>(ml + 2 * cc));
+                    oa[j] = __ldcg(reinterpret_cast<const float4*>(po_c + (size_t) cc * kHeadDim));
+                    ob[j] = __ldcg(reinterpret_cast<const float4*>(po_c + (size_t) cc * kHeadDim + 4));
+                } else {
+                    st[j] = make_float2(-INFINITY, 0.f);
+                    oa[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    ob[j] = oa[j];
+                }
             }
+            float mn = m_run;
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
+            for (int j = 0; j < 8; ++j) mn = fmaxf(mn, st[j].x);
+            const float sc = __expf(m_run - mn);  // 0 on the first step (m_run = -inf)
+            l_run *= sc;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) o4[i] += f[j] * pv[j][i];
+            for (int i = 0; i < 8; ++i) o[i] *= sc;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float f = __expf(st[j].x - mn);
+                l_run += f * st[j].y;
+                o[0] += f * oa[j].x;
+                o[1] += f * oa[j].y;
+                o[2] += f * oa[j].z;
+                o[3] += f * oa[j].w;
+                o[4] += f * ob[j].x;
+                o[5] += f * ob[j].y;
+                o[6] += f * ob[j].z;
+                o[7] += f * ob[j].w;
+            }
+            m_run = mn;
         }
-        const float inv = 1.f / l;
+        const float inv = 1.f / l_run;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) merged[hh * kOPitch + d + i] = __half2float(__float2half_rn(o[i] * inv));
+    }
+    __syncthreads();
+    const GvProblem& po = gv_prob(ob, 0);
+    for (int hh = warp; hh < group; hh += kAttnWarps) {
         float xv[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) xv[i] = __half2float(__float2half_rn(o4[i] * inv));
+        for (int i = 0; i < 4; ++i) xv[i] = merged[hh * kOPitch + lane + 32 * i];
         dec_store_rotated(po, b, kvh * group + hh, lane, xv);
     }
 }

@@ -1,0 +1,206 @@
+// Epilogue of one (problem, 128-column block, row) of the grouped small-M matmul,
+// shared by the epilogue kernels of exl3_gemv.cu and exl3_decode.cu: read and
+// re-zero the block's summed partials (gv_finish), then one of
+//   kEpiStore     out = y (fp16 / bf16 / fp32)
+//   kEpiCombine   fp32 out[out_rows[r]] += out_scale[r] * y (routed MoE combine)
+//   kEpiSwiglu    (gate, up) pair -> clipped SwiGLU -> the down projection's rotated
+//                 input (csrc/quant/hadamard_inner.cuh:283-413, csrc/p2b_moe.cu:300-336
+//                 of the reference)
+//   kEpiRopeKV    decode q/k/v: RoPE (rotate-half), q scaled into the attention
+//                 buffer, k and v appended to the bf16 cache
+//   kEpiResidual  decode: h += y and the row's sum of squares
+//   kEpiPeerStore decode, tensor parallel: the fp32 partial into every rank's peer
+//                 buffer over NVLink
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "exl3_common.cuh"
+#include "exl3_grouped.cuh"
+#include "exl3_grouped_dev.cuh"
+
+namespace exl3b200 {
+
+constexpr int kHeadDim = 128;
+
+enum DecEpiMode : int { kEpiRopeKV = 10, kEpiResidual = 11, kEpiPeerStore = 12 };
+
+// peer buffer: [control 128 B][flags: 2 parities x 8 ranks x u32, padded to 128 B]
+//              [data: 2 parities x 8 ranks x max_rows x hidden fp32]
+constexpr int kPeerMaxRanks = 8;
+constexpr size_t kPeerFlags = 128;
+constexpr size_t kPeerData = 256;
+constexpr unsigned long long kPeerTimeoutNs = 2000000000ull;
+
+struct PeerCtl {
+    unsigned int epoch;  // calls completed
+    unsigned int done;   // CTAs of the running reduce that finished
+};
+
+struct DecAux {
+    // norm input stage
+    const float* h;
+    long long h_stride;
+    const float* ss_in;
+    float* ss_out;           // zeroed by the norm input stage (rows zero_rows)
+    int zero_rows;
+    const __nv_bfloat16* norm_w;
+    float eps;
+    float inv_hidden;
+    // RoPE / KV append / attention
+    const long long* pos;    // position of the new token (= tokens already cached)
+    const float* inv_freq;   // [head_dim / 2]
+    float* qbuf;             // [batch][q_heads][128], scaled by 1/sqrt(128)
+    __nv_bfloat16* k_cache;  // [batch][kv_heads][max_ctx][128]
+    __nv_bfloat16* v_cache;
+    long long cache_b_stride, cache_h_stride;
+    int max_ctx, q_heads, kv_heads, max_chunks;
+    float* attn_o;           // [batch][q_heads][max_chunks][128] unnormalised partial outputs
+    float* attn_ml;          // [batch][q_heads][max_chunks][2] (chunk max, chunk sum)
+    unsigned int* attn_cnt;  // [batch][kv_heads] chunk arrival tickets (state: zero between calls)
+    // residual epilogue
+    float* resid;
+    long long resid_stride;
+    float* ss_acc;
+    // tensor-parallel partial exchange
+    char* peer[kPeerMaxRanks];
+    int peer_world, peer_rank, peer_rows, peer_hidden;
+    int* status;
+};
+
+__device__ __forceinline__ float* peer_slot(const DecAux& x, int q, unsigned int parity, int src, int row)
+{
+    return reinterpret_cast<float*>(x.peer[q] + kPeerData) +
+           (((size_t) parity * kPeerMaxRanks + src) * x.peer_rows + row) * x.peer_hidden;
+}
+
+__device__ __forceinline__ unsigned int* peer_flag(const DecAux& x, int q, unsigned int parity, int src)
+{
+    return reinterpret_cast<unsigned int*>(x.peer[q] + kPeerFlags) + parity * kPeerMaxRanks + src;
+}
+
+__device__ __forceinline__ unsigned long long globaltimer_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p)
+{
+    unsigned int v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v)
+{
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+template <int CB>
+__device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, int mode, int pi, const GvProblem& p,
+                                              const GvProblem* up, int nb, int r, int lane)
+{
+    float v[4];
+    gv_finish<CB>(p, nb, r, lane, v);
+    if (mode == kEpiStore) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            store_out(p.out, (size_t) r * p.out_stride + nb * 128 + lane + 32 * e, v[e], a.out_dtype);
+    } else if (mode == kEpiCombine) {
+        const int orow = p.out_rows ? p.out_rows[r] : r;
+        const float w = p.out_scale ? p.out_scale[r] : 1.f;
+        float* o = reinterpret_cast<float*>(p.out) + (size_t) orow * p.out_stride + nb * 128;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) atomicAdd(o + lane + 32 * e, w * v[e]);
+    } else if (mode == kEpiSwiglu) {
+        float u[4];
+        gv_finish<CB>(*up, nb, r, lane, u);
+        const float lim = a.swiglu_limit;
+        const bool clip = lim > 0.f && lim < 3.0e38f;
+        float act[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float gv = v[e], uv = u[e];
+            if (clip) {
+                gv = fminf(gv, lim);
+                uv = fminf(fmaxf(uv, -lim), lim);
+            }
+            const float s = gv / (1.0f + expf(-gv));
+            act[e] = __half2float(__float2half_rn(s * uv));
+        }
+        // rotated input of the down projection for this 128-block of the intermediate
+        const __half* suh_d = p.out_suh + nb * 128;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            act[e] = __half2float(__float2half_rn(__fmul_rn(act[e], __half2float(suh_d[lane + 32 * e]))));
+        warp_fwht128(act, lane);
+        uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + (size_t) r * p.out_stride + nb * 128;
+        float bsum = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const __half hh = __float2half_rn(__fmul_rn(act[e], kHadScale));
+            const uint32_t h = __half_as_ushort(hh);
+            dst[lane + 32 * e] = h | (h << 16);
+            bsum += __half2float(hh);
+        }
+        if (p.out_sblk) {
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
+            if (lane == 0) p.out_sblk[(size_t) r * (p.n >> 7) + nb] = bsum;
+        }
+    } else if (mode == kEpiRopeKV) {
+        // problems 0, 1, 2 = q, k, v; block nb = head nb; lane holds dims lane + 32e
+        const long long pos = *x.pos;
+        if (pos < 0 || pos >= x.max_ctx) {  // the cache has no row for this position
+            if (x.status && lane == 0) atomicCAS(x.status, 0, (int) kErrBadShape);
+            return;
+        }
+        if (pi < 2) {
+            const float fpos = (float) pos;
+            float s0, c0, s1, c1;
+            sincosf(fpos * x.inv_freq[lane], &s0, &c0);
+            sincosf(fpos * x.inv_freq[lane + 32], &s1, &c1);
+            const float n0 = v[0] * c0 - v[2] * s0, n2 = v[2] * c0 + v[0] * s0;
+            const float n1 = v[1] * c1 - v[3] * s1, n3 = v[3] * c1 + v[1] * s1;
+            v[0] = n0;
+            v[1] = n1;
+            v[2] = n2;
+            v[3] = n3;
+        }
+        if (pi == 0) {
+            float* q = x.qbuf + ((size_t) r * x.q_heads + nb) * kHeadDim;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) q[lane + 32 * e] = v[e] * kHadScale;  // 1/sqrt(head_dim), head_dim = 128
+        } else {
+            __nv_bfloat16* c = (pi == 1 ? x.k_cache : x.v_cache) + (size_t) r * x.cache_b_stride +
+                               (size_t) nb * x.cache_h_stride + (size_t) pos * kHeadDim;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) c[lane + 32 * e] = __float2bfloat16_rn(v[e]);
+        }
+    } else if (mode == kEpiPeerStore) {
+        const PeerCtl* ctl = reinterpret_cast<const PeerCtl*>(x.peer[x.peer_rank]);
+        const unsigned int parity = (*reinterpret_cast<const volatile unsigned int*>(&ctl->epoch) + 1u) & 1u;
+        for (int q = 0; q < x.peer_world; ++q) {
+            float* dst = peer_slot(x, q, parity, x.peer_rank, r) + nb * 128;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[lane + 32 * e] = v[e];
+        }
+        __threadfence_system();
+    } else {  // kEpiResidual
+        float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
+        float sq = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float nv = hr[lane + 32 * e] + v[e];
+            hr[lane + 32 * e] = nv;
+            sq += nv * nv;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if (lane == 0) atomicAdd(x.ss_acc + r, sq);
+    }
+}
+
+}  // namespace exl3b200

@@ -43,6 +43,7 @@
 #include "exl3_capi_internal.h"
 #include "exl3_grouped.cuh"
 #include "exl3_grouped_dev.cuh"
+#include "exl3_epilogue.cuh"
 
 namespace exl3b200 {
 
@@ -126,8 +127,18 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gv_matmul_kernel(const 
     const GvTotals tot = gv_totals(a);
     const long long units = tot.units;
     const long long G = gridDim.x;
-    const long long u_begin = (long long) blockIdx.x * units / G;
-    const long long u_end = (long long) (blockIdx.x + 1) * units / G;
+    long long u_begin, u_end;
+    if (a.cta_per_block > 0) {
+        // block-aligned split: cta_per_block CTAs share each 128-column block's k
+        // range (every problem has a.block_units k-slices), no CTA crosses a block
+        const long long blk = blockIdx.x / a.cta_per_block;
+        const int j = blockIdx.x - (int) blk * a.cta_per_block;
+        u_begin = blk * a.block_units + (long long) j * a.block_units / a.cta_per_block;
+        u_end = blk * a.block_units + (long long) (j + 1) * a.block_units / a.cta_per_block;
+    } else {
+        u_begin = (long long) blockIdx.x * units / G;
+        u_end = (long long) (blockIdx.x + 1) * units / G;
+    }
 
     int pi = -1;
     long long pu0 = 0, pu1 = 0;  // unit range of the current problem
@@ -321,56 +332,12 @@ __global__ __launch_bounds__(256) void exl3_gv_epilogue_kernel(const __grid_cons
         const int local = task - p.out_task_begin;
         const int r = local / nblocks;
         const int nb = local - r * nblocks;
-        float v[4];
-        gv_finish<CB>(p, nb, r, lane, v);
-        if constexpr (MODE == kEpiStore) {
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                store_out(p.out, (size_t) r * p.out_stride + nb * 128 + lane + 32 * e, v[e], a.out_dtype);
-        } else if constexpr (MODE == kEpiCombine) {
-            const int orow = p.out_rows ? p.out_rows[r] : r;
-            const float w = p.out_scale ? p.out_scale[r] : 1.f;
-            float* o = reinterpret_cast<float*>(p.out) + (size_t) orow * p.out_stride + nb * 128;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) atomicAdd(o + lane + 32 * e, w * v[e]);
-        } else {
+        if constexpr (MODE == kEpiSwiglu) {
             // (gate, up) pair: table entries j and j+1 (stride 2 view)
             const GvProblem& pu = a.dev ? a.dev[pi * a.stride + a.offset + 1] : a.inl[pi * a.stride + a.offset + 1];
-            float u[4];
-            gv_finish<CB>(pu, nb, r, lane, u);
-            const float lim = a.swiglu_limit;
-            const bool clip = lim > 0.f && lim < 3.0e38f;
-            float act[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                float gv = v[e], uv = u[e];
-                if (clip) {
-                    gv = fminf(gv, lim);
-                    uv = fminf(fmaxf(uv, -lim), lim);
-                }
-                const float s = gv / (1.0f + expf(-gv));
-                act[e] = __half2float(__float2half_rn(s * uv));
-            }
-            // rotated input of the down projection for this 128-block of the intermediate
-            const __half* suh_d = p.out_suh + nb * 128;
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-                act[e] = __half2float(__float2half_rn(__fmul_rn(act[e], __half2float(suh_d[lane + 32 * e]))));
-            warp_fwht128(act, lane);
-            uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + (size_t) r * p.out_stride + nb * 128;
-            float bsum = 0.f;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const __half hh = __float2half_rn(__fmul_rn(act[e], kHadScale));
-                const uint32_t h = __half_as_ushort(hh);
-                dst[lane + 32 * e] = h | (h << 16);
-                bsum += __half2float(hh);
-            }
-            if (p.out_sblk) {
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) bsum += __shfl_xor_sync(0xffffffffu, bsum, o);
-                if (lane == 0) p.out_sblk[(size_t) r * (p.n >> 7) + nb] = bsum;
-            }
+            epi_block_row<CB>(a, DecAux{}, MODE, pi, p, &pu, nb, r, lane);
+        } else {
+            epi_block_row<CB>(a, DecAux{}, MODE, pi, p, nullptr, nb, r, lane);
         }
     }
 }
@@ -424,14 +391,45 @@ int gv_launch_input(const GvArgs& a, int max_in_tasks, bool pdl, cudaStream_t st
 
 // Tiling variants (the kernel-shape map picks one per call):
 //   0: 8 tiles per warp, 2 CTAs/SM    1: 4 tiles per warp, 3 CTAs/SM
+// A CTA whose unit range crosses into another 128-column block pays a second
+// reduction and a cold start of its trellis loads (~3 us, about 20 units of
+// streaming at this grid).  For a host-built table whose problems share k, when
+// few blocks share the grid, splitting each block's k range over a whole number
+// of CTAs removes the crossings; the host takes it when its per-CTA units do not
+// exceed stream-K's plus that penalty.
+constexpr int kCrossPenaltyUnits = 20;
+
+static int block_aligned_split(GvArgs& a, int grid)
+{
+    if (a.dev || a.dev_totals || a.uniform_units > 0 || a.stride != 1 || a.offset != 0 || a.nprob < 1) return grid;
+    const int k = a.inl[0].k;
+    long long blocks = 0;
+    for (int i = 0; i < a.nprob; ++i) {
+        if (a.inl[i].k != k) return grid;
+        blocks += a.inl[i].n / 128;
+    }
+    const int kt = k / 16;
+    if (blocks < 1 || blocks > grid) return grid;
+    const int cpb = std::min<long long>(grid / blocks, kt);
+    const long long aligned = (kt + cpb - 1) / cpb;
+    const long long stream_k = (a.units + grid - 1) / grid + kCrossPenaltyUnits;
+    if (aligned > stream_k) return grid;
+    a.cta_per_block = cpb;
+    a.block_units = kt;
+    return (int) (blocks * cpb);
+}
+
 template <int K, int CB, int TG, int NT, int MINB>
-static int launch_matmul_t(const GvArgs& a, bool pdl, cudaStream_t stream)
+static int launch_matmul_t(const GvArgs& a_in, bool pdl, cudaStream_t stream)
 {
     constexpr int P = 3;
+    GvArgs a = a_in;
+    a.cta_per_block = 0;
     int grid = MINB * gv_sm_count();
     if (!a.dev_totals) {
         const long long units = a.uniform_units > 0 ? (long long) a.nprob * a.uniform_units : a.units;
         grid = (int) std::min<long long>(units, grid);
+        grid = block_aligned_split(a, grid);
     }
     return launch_ex(exl3_gv_matmul_kernel<K, CB, TG, NT, P, MINB>, grid, pdl, stream, a);
 }

@@ -60,6 +60,8 @@ struct GvArgs {
     int nprob, units, in_tasks, out_tasks;
     int stride, offset;       // problem i of this launch is table entry i*stride + offset
     int uniform_units;        // > 0: every problem has this many units (unit_begin unused)
+    int cta_per_block;        // > 0: matmul CTAs per 128-column block (block-aligned split; set by the launcher)
+    int block_units;          // k-slices of every block when cta_per_block > 0
     int out_dtype;            // 0 fp16, 1 bf16, 2 fp32 (store mode)
     int epi_mode;
     float swiglu_limit;       // swiglu: 0 or infinite = no clip
