@@ -1,7 +1,7 @@
 // Fused decode layer around the EXL3 small-M matmul: the glue of a Llama-style
 // decoder layer (RMSNorm, RoPE, KV-cache append, attention, residual adds,
 // SwiGLU) moved into the matmul pipeline's own input stages and epilogues, so a
-// decode step runs about ten kernels per layer instead of ~75.
+// decode step runs eleven kernels per layer instead of ~75.
 //
 // Attention sub-layer (exl3b200_decode_attention), all launches chained by
 // programmatic dependent launch:
@@ -14,16 +14,18 @@
 //      (rotate-half pairs (d, d+64) sit in one lane of the warp-wide H128 layout),
 //      q is stored scaled by 1/sqrt(head_dim), k and v are appended to the bf16
 //      cache at the current position;
-//   4. split-K attention on the tensor cores: one CTA per (row, kv head,
-//      64-position chunk), four warps of 16 positions each.  The query heads of the
-//      GQA group (up to 16, zero-padded) are the M rows of mma.m16n8k16 (bf16,
-//      fp32 accumulate; q and the softmax weights enter as bf16 hi + lo pairs, two MMAs
-//      each): S = Q K^T, the chunk softmax with one CTA-wide row max, then P V with
-//      the score accumulators reused as the A fragments.  Each CTA
-//      writes its chunk partial (unnormalised O, max, sum); the last CTA of a
-//      (row, kv head) to finish - an arrival ticket, no waiting - merges the
-//      chunks (log-sum-exp rescale), normalises, rounds to fp16 and writes the o
-//      projection's rotated input (x*suh, H128) for the group's heads;
+//   4. split-K attention on the tensor cores: one thread-block cluster of up to
+//      16 CTAs per (row, kv head); each CTA takes every 16th 64-position chunk
+//      through a three-buffer cp.async ring whose first fill is requested before
+//      the dependency wait (only q and the new row come from step 3), four warps
+//      of 16 positions each.  The query heads of the GQA group (up to 16,
+//      zero-padded) are the M rows of mma.m16n8k16 (bf16, fp32 accumulate; q and
+//      the softmax weights enter as bf16 hi + lo pairs, two MMAs each): S = Q K^T,
+//      a running softmax per warp, then P V with the score accumulators reused as
+//      the A fragments.  The CTAs exchange their partials (unnormalised O, max,
+//      sum) through distributed shared memory; rank r merges heads r, r + 16, ...
+//      (log-sum-exp rescale), normalises, rounds to fp16 and writes the o
+//      projection's rotated input (x*suh, H128);
 //   5. matmul (o);
 //   6. epilogue, residual mode: h += y and the row's new sum of squares (or, with
 //      tensor parallelism, an fp32 store of the partial y for the all-reduce).
@@ -45,6 +47,8 @@
 #include <algorithm>
 #include <cstring>
 
+#include <cooperative_groups.h>
+
 #include "exl3_common.cuh"
 #include "exl3_capi_internal.h"
 #include "exl3_grouped.cuh"
@@ -52,6 +56,8 @@
 #include "exl3_epilogue.cuh"
 
 namespace exl3b200 {
+
+namespace cg = cooperative_groups;
 
 constexpr int kDecChunk = 64;   // attention positions per CTA
 
@@ -90,8 +96,18 @@ __global__ __launch_bounds__(256) void exl3_dec_input_kernel(const __grid_consta
                                                              const __grid_constant__ DecAux x)
 {
     griddep_launch();
-    griddep_wait();
     const int lane = threadIdx.x & 31;
+    {
+        // before the wait: the first task's norm weights and input scales into L2
+        const int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        if (task < a.in_tasks) {
+            const GvProblem& p = gv_prob(a, gv_find<0>(a, a.nprob, task));
+            const int b = (task - p.in_task_begin) % (p.k >> 7);
+            prefetch_l2_256(x.norm_w + b * 128, lane);
+            if (p.suh) prefetch_l2_256(p.suh + b * 128, lane);
+        }
+    }
+    griddep_wait();
     if (x.ss_out && blockIdx.x == 0)
         for (int i = threadIdx.x; i < x.zero_rows; i += blockDim.x) x.ss_out[i] = 0.f;
     const int warps = gridDim.x * (blockDim.x >> 5);
@@ -121,8 +137,9 @@ __global__ __launch_bounds__(256) void exl3_dec_epilogue_kernel(const __grid_con
                                                                 const __grid_constant__ DecAux x)
 {
     griddep_launch();
-    griddep_wait();
     const int lane = threadIdx.x & 31;
+    gv_prefetch_epilogue(a, lane);
+    griddep_wait();
     const int warps = gridDim.x * (blockDim.x >> 5);
     for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < a.out_tasks; task += warps) {
         const int pi = gv_find<1>(a, a.nprob, task);
@@ -136,22 +153,29 @@ __global__ __launch_bounds__(256) void exl3_dec_epilogue_kernel(const __grid_con
 }
 
 // ---------------------------------------------------------------------------
-// split-K decode attention on the tensor cores
+// split-K decode attention on the tensor cores: one thread-block cluster per
+// (row, kv head), partials merged through distributed shared memory
 // ---------------------------------------------------------------------------
 
-constexpr int kAttnWarps = kDecChunk / 16;  // 16 positions per warp
+constexpr int kAttnWarps = kDecChunk / 16;  // 16 positions of a chunk per warp
 constexpr int kAttnThreads = 32 * kAttnWarps;
 constexpr int kAttnMaxGroup = 16;           // query heads per kv head (the M rows of the MMA)
+constexpr int kAttnMaxCluster = 16;         // CTAs per (row, kv head)
 constexpr int kKvPitch = kHeadDim + 8;      // bf16 per staged K/V row: 272 B, ldmatrix rows on distinct banks
 constexpr int kOPitch = kHeadDim + 8;       // fp32 per row of a warp's partial O
 
+constexpr int kAttnBufs = 3;                // K/V chunk ring; all three requested before the dependency wait
+
 struct AttnSmem {
-    __nv_bfloat16 k[kDecChunk][kKvPitch];
-    __nv_bfloat16 v[kDecChunk][kKvPitch];
-    float o[kAttnWarps][kAttnMaxGroup][kOPitch];  // per-warp partial O
+    union {
+        __nv_bfloat16 kv[kAttnBufs][2][kDecChunk][kKvPitch];  // [buffer][K, V][position][dim]
+        float o[kAttnWarps][kAttnMaxGroup][kOPitch];  // after the chunks: per-warp partial O, then the merged heads
+    };
+    float part_o[kAttnMaxGroup][kHeadDim];        // this CTA's partial (unnormalised O), read by the cluster
+    float part_m[kAttnMaxGroup];                  // its row max (-inf: no chunk)
+    float part_l[kAttnMaxGroup];                  // its softmax sum
     float red_m[kAttnWarps][kAttnMaxGroup];
     float red_l[kAttnWarps][kAttnMaxGroup];
-    unsigned int ticket;
 };
 
 __device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, int src_bytes)
@@ -195,47 +219,76 @@ __device__ __forceinline__ void split_bf16(float a, float b, uint32_t& hi, uint3
     lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
-// One CTA per (row b, kv head, chunk of 64 cached positions; positions 0..pos
-// inclusive are attended).  Warp w owns positions 16w..16w+15 of the chunk.  MMA
-// fragments (lane = 4g + c): A rows g / g+8 = query heads of the group, B / C
-// columns = positions (S) or head dims (O).  Grid: batch * kv_heads * max_chunks;
-// `ob` holds the o projection (problem 0) whose rotated input the finisher writes.
+// Cluster of csize CTAs per (row b, kv head); rank r takes the 64-position chunks
+// r, r + csize, ... of positions 0..pos through a ring of kAttnBufs cp.async
+// buffers whose first fill is requested before the dependency wait; one running
+// max per warp and row, combined per CTA at the end.  Warp w owns positions 16w..16w+15 of a chunk.
+// MMA fragments (lane = 4g + c): A rows g / g+8 = query heads of the group, B / C
+// columns = positions (S) or head dims (O).  After the first cluster barrier rank
+// r merges heads r, r + csize, ... from every rank's partial (distributed shared
+// memory), normalises, rounds to fp16 and writes the o projection's rotated input
+// (`ob` problem 0); the second barrier keeps every partial alive until then.
+// Every CTA reaches both barriers (the only early exit is grid-uniform).
 __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __grid_constant__ GvArgs ob,
-                                                                     const __grid_constant__ DecAux x)
+                                                                     const __grid_constant__ DecAux x, int csize)
 {
     griddep_launch();
-    griddep_wait();  // q (scaled) and the new K/V row come from the RoPE epilogue
     extern __shared__ __align__(128) unsigned char attn_smem_raw[];
     AttnSmem& sm = *reinterpret_cast<AttnSmem*>(attn_smem_raw);
-    const int chunk = blockIdx.x % x.max_chunks;
-    const int t = blockIdx.x / x.max_chunks;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = (int) cluster.block_rank();
+    const int t = blockIdx.x / csize;
     const int kvh = t % x.kv_heads;
     const int b = t / x.kv_heads;
+    // pos and the cache rows before it were written before this step's kernels
+    // (graph replays are separated by ordinary launches); only q and the new row at
+    // pos come from the RoPE epilogue this kernel depends on
     const long long pos = *x.pos;
-    if (pos < 0 || pos >= x.max_ctx) return;  // recorded in the device status by the RoPE epilogue
+    if (pos < 0 || pos >= x.max_ctx) return;  // grid-uniform; recorded in the device status by the RoPE epilogue
     const int L = (int) pos + 1;
     const int nch = (L + kDecChunk - 1) / kDecChunk;
-    if (chunk >= nch) return;  // uniform over the CTA
-    const int p0 = chunk * kDecChunk;
-    const int np = min(kDecChunk, L - p0);
+    const int nloc = rank < nch ? (nch - 1 - rank) / csize + 1 : 0;
     const int group = x.q_heads / x.kv_heads;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, c = lane & 3;
+    const GvProblem& po = gv_prob(ob, 0);
+    if (tid < 2 * group && (tid >> 1) % csize == rank && po.suh)  // into L2: the o input scales of this rank's heads
+        prefetch_l2_256(po.suh + (size_t) (kvh * group + (tid >> 1)) * 128, tid & 1);
 
-    // stage the chunk's K and V rows (16 x 16 B each); rows >= np are zero-filled
-    {
-        const size_t base = (size_t) b * x.cache_b_stride + (size_t) kvh * x.cache_h_stride + (size_t) p0 * kHeadDim;
-        const __nv_bfloat16* kg = x.k_cache + base;
-        const __nv_bfloat16* vg = x.v_cache + base;
-        for (int i = tid; i < kDecChunk * 16; i += kAttnThreads) {
-            const int row = i >> 4, seg = (i & 15) * 8;
+    const size_t hbase = (size_t) b * x.cache_b_stride + (size_t) kvh * x.cache_h_stride;
+    // local chunk i -> buffer; rows >= its length are zero-filled; with skip_new the
+    // row at pos is left out (returned) for a load after the wait
+    auto stage = [&](int i, int buf, bool skip_new) -> int {
+        const int p0 = (rank + i * csize) * kDecChunk;
+        const int np = min(kDecChunk, L - p0);
+        const __nv_bfloat16* kg = x.k_cache + hbase + (size_t) p0 * kHeadDim;
+        const __nv_bfloat16* vg = x.v_cache + hbase + (size_t) p0 * kHeadDim;
+        const int new_row = (skip_new && p0 + np - 1 == (int) pos) ? np - 1 : kDecChunk;
+        for (int e = tid; e < kDecChunk * 16; e += kAttnThreads) {
+            const int row = e >> 4, seg = (e & 15) * 8;
+            if (row == new_row) continue;
             const bool ok = row < np;
             const size_t off = ok ? (size_t) row * kHeadDim + seg : 0;
-            cp_async16_zfill(&sm.k[row][seg], kg + off, ok ? 16 : 0);
-            cp_async16_zfill(&sm.v[row][seg], vg + off, ok ? 16 : 0);
+            cp_async16_zfill(&sm.kv[buf][0][row][seg], kg + off, ok ? 16 : 0);
+            cp_async16_zfill(&sm.kv[buf][1][row][seg], vg + off, ok ? 16 : 0);
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
+        return new_row;
+    };
+    // first fill of the ring: rows written by earlier steps; the new row (position
+    // pos, in the rank's local chunk jn if it owns the last chunk) after the wait
+    const int jn = (rank < nch && (nch - 1 - rank) % csize == 0) ? (nch - 1 - rank) / csize : -1;
+    int new_row = kDecChunk;
+    for (int i = 0; i < min(nloc, kAttnBufs); ++i) {
+        const int nr = stage(i, i, true);
+        if (i == jn) new_row = nr;
     }
+    griddep_wait();  // q (scaled) and the new K/V row come from the RoPE epilogue
+    if (new_row < kDecChunk && tid < 16) {
+        const size_t off = hbase + (size_t) pos * kHeadDim + tid * 8;
+        cp_async16_zfill(&sm.kv[jn][0][new_row][tid * 8], x.k_cache + off, 16);
+        cp_async16_zfill(&sm.kv[jn][1][new_row][tid * 8], x.v_cache + off, 16);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
 
     // Q fragments of the group's heads (rows >= group are zero) as bf16 pairs
     // hi + lo (hi = bf16(q), lo = bf16(q - hi)): two MMAs give the scores to ~16 bits
@@ -256,89 +309,104 @@ __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __gri
                 split_bf16(f1.x, f1.y, qa[kk][2 + hf], ql[kk][2 + hf]);
             }
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
 
-    // S = Q K^T over this warp's two 8-position tiles
     const int mi = lane >> 3, mr = lane & 7;  // ldmatrix: matrix and row this lane addresses
-    float s[2][4];
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) s[j][e] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-        uint32_t kb[4];
-        ldsm_x4(kb, &sm.k[16 * warp + 8 * (mi >> 1) + mr][16 * kk + 8 * (mi & 1)]);
-        mma_bf16_16816(s[0], qa[kk], kb[0], kb[1]);
-        mma_bf16_16816(s[1], qa[kk], kb[2], kb[3]);
-        mma_bf16_16816(s[0], ql[kk], kb[0], kb[1]);
-        mma_bf16_16816(s[1], ql[kk], kb[2], kb[3]);
-    }
-    // mask positions past the context, row maxima (rows g, g+8) over the CTA
-    float mg = -INFINITY, mh = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-            const bool ok = 16 * warp + 8 * j + 2 * c + e < np;
-            s[j][e] = ok ? s[j][e] : -INFINITY;
-            s[j][2 + e] = ok ? s[j][2 + e] : -INFINITY;
-            mg = fmaxf(mg, s[j][e]);
-            mh = fmaxf(mh, s[j][2 + e]);
-        }
-#pragma unroll
-    for (int o = 1; o < 4; o <<= 1) {
-        mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, o));
-        mh = fmaxf(mh, __shfl_xor_sync(0xffffffffu, mh, o));
-    }
-    if (c == 0) {
-        sm.red_m[warp][g] = mg;
-        sm.red_m[warp][g + 8] = mh;
-    }
-    __syncthreads();
-    mg = sm.red_m[0][g];
-    mh = sm.red_m[0][g + 8];
-#pragma unroll
-    for (int w = 1; w < kAttnWarps; ++w) {
-        mg = fmaxf(mg, sm.red_m[w][g]);
-        mh = fmaxf(mh, sm.red_m[w][g + 8]);
-    }
-    // P = exp(S - max) in fp32, fed to the MMA as bf16 pairs hi + lo
-    uint32_t pa[4], pl[4];
-    float lg = 0.f, lh = 0.f;
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const float e0 = __expf(s[j][0] - mg), e1 = __expf(s[j][1] - mg);
-        const float e2 = __expf(s[j][2] - mh), e3 = __expf(s[j][3] - mh);
-        lg += e0 + e1;
-        lh += e2 + e3;
-        split_bf16(e0, e1, pa[2 * j], pl[2 * j]);
-        split_bf16(e2, e3, pa[2 * j + 1], pl[2 * j + 1]);
-    }
-#pragma unroll
-    for (int o = 1; o < 4; o <<= 1) {
-        lg += __shfl_xor_sync(0xffffffffu, lg, o);
-        lh += __shfl_xor_sync(0xffffffffu, lh, o);
-    }
-    if (c == 0) {
-        sm.red_l[warp][g] = lg;
-        sm.red_l[warp][g + 8] = lh;
-    }
-    // O_w = P V over the warp's 16 positions, 16 tiles of 8 head dims
+    float mg = -INFINITY, mh = -INFINITY;      // this warp's running row maxima (rows g, g+8)
+    float lg = 0.f, lh = 0.f;                  // this thread's share of the warp's softmax sums
     float acc[kHeadDim / 8][4];
 #pragma unroll
     for (int n = 0; n < kHeadDim / 8; ++n)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
+
+    for (int i = 0; i < nloc; ++i) {
+        const int buf = i % kAttnBufs;
+        // chunk i has landed: it is in the first fill (one group) or in the group of
+        // iteration i - 2; after that only iteration i - 1's group may be pending
+        if (i < 2) asm volatile("cp.async.wait_group 0;" ::: "memory");
+        else asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();  // ... for every thread; and every warp is done with chunk i - 1
+        if (i >= 1) {
+            if (i + kAttnBufs - 1 < nloc) stage(i + kAttnBufs - 1, (i - 1) % kAttnBufs, false);  // new row included
+            asm volatile("cp.async.commit_group;" ::: "memory");  // one group per iteration, maybe empty
+        }
+        const int np = min(kDecChunk, L - (rank + i * csize) * kDecChunk);
+
+        // S = Q K^T over this warp's two 8-position tiles
+        float s[2][4];
 #pragma unroll
-    for (int q = 0; q < kHeadDim / 16; ++q) {
-        uint32_t vb[4];
-        ldsm_x4_t(vb, &sm.v[16 * warp + 8 * (mi & 1) + mr][16 * q + 8 * (mi >> 1)]);
-        mma_bf16_16816(acc[2 * q], pa, vb[0], vb[1]);
-        mma_bf16_16816(acc[2 * q + 1], pa, vb[2], vb[3]);
-        mma_bf16_16816(acc[2 * q], pl, vb[0], vb[1]);
-        mma_bf16_16816(acc[2 * q + 1], pl, vb[2], vb[3]);
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) s[j][e] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+            uint32_t kb[4];
+            ldsm_x4(kb, &sm.kv[buf][0][16 * warp + 8 * (mi >> 1) + mr][16 * kk + 8 * (mi & 1)]);
+            mma_bf16_16816(s[0], qa[kk], kb[0], kb[1]);
+            mma_bf16_16816(s[1], qa[kk], kb[2], kb[3]);
+            mma_bf16_16816(s[0], ql[kk], kb[0], kb[1]);
+            mma_bf16_16816(s[1], ql[kk], kb[2], kb[3]);
+        }
+        // mask positions past the context; the warp's new row maxima
+        float ng = mg, nh = mh;
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const bool ok = 16 * warp + 8 * j + 2 * c + e < np;
+                s[j][e] = ok ? s[j][e] : -INFINITY;
+                s[j][2 + e] = ok ? s[j][2 + e] : -INFINITY;
+                ng = fmaxf(ng, s[j][e]);
+                nh = fmaxf(nh, s[j][2 + e]);
+            }
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) {
+            ng = fmaxf(ng, __shfl_xor_sync(0xffffffffu, ng, o));
+            nh = fmaxf(nh, __shfl_xor_sync(0xffffffffu, nh, o));
+        }
+        if (ng == -INFINITY && nh == -INFINITY) continue;  // warp-uniform: no position of this warp is valid
+        // rescale the running state to the new maxima (factor 0 on the first valid chunk)
+        const float sg = __expf(mg - ng), sh = __expf(mh - nh);
+        mg = ng;
+        mh = nh;
+        lg *= sg;
+        lh *= sh;
+#pragma unroll
+        for (int n = 0; n < kHeadDim / 8; ++n) {
+            acc[n][0] *= sg;
+            acc[n][1] *= sg;
+            acc[n][2] *= sh;
+            acc[n][3] *= sh;
+        }
+        // P = exp(S - max) in fp32, fed to the MMA as bf16 pairs hi + lo
+        uint32_t pa[4], pl[4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const float e0 = __expf(s[j][0] - mg), e1 = __expf(s[j][1] - mg);
+            const float e2 = __expf(s[j][2] - mh), e3 = __expf(s[j][3] - mh);
+            lg += e0 + e1;
+            lh += e2 + e3;
+            split_bf16(e0, e1, pa[2 * j], pl[2 * j]);
+            split_bf16(e2, e3, pa[2 * j + 1], pl[2 * j + 1]);
+        }
+        // O += P V over the warp's 16 positions, 16 tiles of 8 head dims
+#pragma unroll
+        for (int q = 0; q < kHeadDim / 16; ++q) {
+            uint32_t vb[4];
+            ldsm_x4_t(vb, &sm.kv[buf][1][16 * warp + 8 * (mi & 1) + mr][16 * q + 8 * (mi >> 1)]);
+            mma_bf16_16816(acc[2 * q], pa, vb[0], vb[1]);
+            mma_bf16_16816(acc[2 * q + 1], pa, vb[2], vb[3]);
+            mma_bf16_16816(acc[2 * q], pl, vb[0], vb[1]);
+            mma_bf16_16816(acc[2 * q + 1], pl, vb[2], vb[3]);
+        }
+    }
+
+    // this CTA's partial: the warps' states rescaled to the CTA's row maxima and summed
+    __syncthreads();  // sm.o overlays the K/V ring, which other warps may still be reading
+#pragma unroll
+    for (int o = 1; o < 4; o <<= 1) {
+        lg += __shfl_xor_sync(0xffffffffu, lg, o);
+        lh += __shfl_xor_sync(0xffffffffu, lh, o);
     }
 #pragma unroll
     for (int n = 0; n < kHeadDim / 8; ++n) {
@@ -346,98 +414,75 @@ __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __gri
         if (g + 8 < group)
             *reinterpret_cast<float2*>(&sm.o[warp][g + 8][8 * n + 2 * c]) = make_float2(acc[n][2], acc[n][3]);
     }
+    if (c == 0) {
+        sm.red_m[warp][g] = mg;
+        sm.red_m[warp][g + 8] = mh;
+        sm.red_l[warp][g] = lg;
+        sm.red_l[warp][g + 8] = lh;
+    }
     __syncthreads();
-
-    // chunk partial: O summed over the warps (shared row max), max and sum per head
-    const size_t hc0 = ((size_t) b * x.q_heads + (size_t) kvh * group) * x.max_chunks + chunk;
     for (int hh = 0; hh < group; ++hh) {
-        float v = sm.o[0][hh][tid];
+        float m = sm.red_m[0][hh];
 #pragma unroll
-        for (int w = 1; w < kAttnWarps; ++w) v += sm.o[w][hh][tid];
-        x.attn_o[(hc0 + (size_t) hh * x.max_chunks) * kHeadDim + tid] = v;
-    }
-    if (tid < group) {
-        float l = 0.f, m = sm.red_m[0][tid];
+        for (int w = 1; w < kAttnWarps; ++w) m = fmaxf(m, sm.red_m[w][hh]);
+        float v = 0.f, l = 0.f;
+        if (m != -INFINITY) {
 #pragma unroll
-        for (int w = 0; w < kAttnWarps; ++w) l += sm.red_l[w][tid];
-#pragma unroll
-        for (int w = 1; w < kAttnWarps; ++w) m = fmaxf(m, sm.red_m[w][tid]);
-        x.attn_ml[2 * (hc0 + (size_t) tid * x.max_chunks)] = m;
-        x.attn_ml[2 * (hc0 + (size_t) tid * x.max_chunks) + 1] = l;
-    }
-
-    // arrival ticket: the last chunk CTA of (b, kv head) merges
-    __threadfence();
-    __syncthreads();
-    unsigned int* cnt = x.attn_cnt + (size_t) b * x.kv_heads + kvh;
-    if (tid == 0) sm.ticket = atomicAdd(cnt, 1u);
-    __syncthreads();
-    if (sm.ticket != (unsigned int) (nch - 1)) return;
-    __threadfence();
-    if (tid == 0) *cnt = 0u;  // every chunk CTA of this call has arrived
-
-    // merge with a running max, 8 chunks of loads in flight per step: 16 threads per
-    // head, 8 head dims each; the normalised, fp16-rounded output goes through
-    // shared memory to the warp-per-head rotation of the o projection's input
-    float* merged = &sm.o[0][0][0];  // [kAttnMaxGroup][kOPitch]; the warps' partials are consumed
-    for (int hh = tid >> 4; hh < group; hh += kAttnThreads / 16) {
-        const int d = (tid & 15) * 8;
-        const size_t hb = ((size_t) b * x.q_heads + (size_t) kvh * group + hh) * x.max_chunks;
-        const float* ml = x.attn_ml + 2 * hb;
-        const float* po_c = x.attn_o + hb * kHeadDim + d;
-        float m_run = -INFINITY, l_run = 0.f, o[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = 0.f;
-        for (int c0 = 0; c0 < nch; c0 += 8) {
-            float2 st[8];
-            float4 oa[8], ob[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int cc = c0 + j;
-                if (cc < nch) {
-                    st[j] = __ldcg(reinterpret_cast<const float2*>(ml + 2 * cc));
-                    oa[j] = __ldcg(reinterpret_cast<const float4*>(po_c + (size_t) cc * kHeadDim));
-                    ob[j] = __ldcg(reinterpret_cast<const float4*>(po_c + (size_t) cc * kHeadDim + 4));
-                } else {
-                    st[j] = make_float2(-INFINITY, 0.f);
-                    oa[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    ob[j] = oa[j];
-                }
+            for (int w = 0; w < kAttnWarps; ++w) {
+                const float f = __expf(sm.red_m[w][hh] - m);
+                v += f * sm.o[w][hh][tid];
+                l += f * sm.red_l[w][hh];
             }
-            float mn = m_run;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) mn = fmaxf(mn, st[j].x);
-            const float sc = __expf(m_run - mn);  // 0 on the first step (m_run = -inf)
-            l_run *= sc;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] *= sc;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float f = __expf(st[j].x - mn);
-                l_run += f * st[j].y;
-                o[0] += f * oa[j].x;
-                o[1] += f * oa[j].y;
-                o[2] += f * oa[j].z;
-                o[3] += f * oa[j].w;
-                o[4] += f * ob[j].x;
-                o[5] += f * ob[j].y;
-                o[6] += f * ob[j].z;
-                o[7] += f * ob[j].w;
-            }
-            m_run = mn;
         }
-        const float inv = 1.f / l_run;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) merged[hh * kOPitch + d + i] = __half2float(__float2half_rn(o[i] * inv));
+        sm.part_o[hh][tid] = v;
+        if (tid == 0) {
+            sm.part_m[hh] = m;
+            sm.part_l[hh] = l;
+        }
     }
+    cluster.sync();  // every rank's partial is complete
+
+    // merge: rank r takes heads r, r + csize, ...; thread tid = head dim; ranks
+    // without a chunk contribute max -inf, sum 0
+    for (int hh = rank; hh < group; hh += csize) {
+        float pm[kAttnMaxCluster], pv[kAttnMaxCluster], pl_[kAttnMaxCluster];
+#pragma unroll
+        for (int q = 0; q < kAttnMaxCluster; ++q) {
+            if (q < csize) {
+                const AttnSmem* rs = cluster.map_shared_rank(&sm, q);
+                pm[q] = rs->part_m[hh];
+                pl_[q] = rs->part_l[hh];
+                pv[q] = rs->part_o[hh][tid];
+            } else {
+                pm[q] = -INFINITY;
+                pl_[q] = 0.f;
+                pv[q] = 0.f;
+            }
+        }
+        float m = -INFINITY;
+#pragma unroll
+        for (int q = 0; q < kAttnMaxCluster; ++q) m = fmaxf(m, pm[q]);
+        float l = 0.f, o = 0.f;
+#pragma unroll
+        for (int q = 0; q < kAttnMaxCluster; ++q) {
+            const float f = __expf(pm[q] - m);
+            l += f * pl_[q];
+            o += f * pv[q];
+        }
+        sm.o[0][hh][tid] = __half2float(__float2half_rn(o / l));
+    }
+    // done reading the other ranks' partials: arrive now, wait before exiting
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     __syncthreads();
-    const GvProblem& po = gv_prob(ob, 0);
-    for (int hh = warp; hh < group; hh += kAttnWarps) {
+    for (int j = warp;; j += kAttnWarps) {
+        const int hh = rank + j * csize;
+        if (hh >= group) break;
         float xv[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) xv[i] = merged[hh * kOPitch + lane + 32 * i];
+        for (int i = 0; i < 4; ++i) xv[i] = sm.o[0][hh][lane + 32 * i];
         dec_store_rotated(po, b, kvh * group + hh, lane, xv);
     }
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // partials stay readable until every rank has merged
 }
 
 // h += y and the row's sum of squares (tensor-parallel path, after the all-reduce)
@@ -553,37 +598,73 @@ static int dec_launch(Kern kern, int grid, int block, cudaStream_t stream, Args.
     return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess ? kOk : kErrLaunch;
 }
 
-// The attention kernel's shared memory (K and V chunk, per-warp partials) exceeds
-// the 48 KB default: raise the limit once per device.
-static int dec_attn_smem_setup()
+// The attention kernel: shared memory beyond the 48 KB default and clusters of up
+// to 16 CTAs (beyond the portable 8), set once per device; the cluster size is the
+// largest power of two <= min(16, chunks of the cache) that the device can hold.
+static int dec_attn_setup(int max_chunks, int* csize)
 {
     static int done[64] = {0};
+    static int fits[64][5] = {{0}};  // per device, cluster size 1, 2, 4, 8, 16: 0 unknown, 1 yes, 2 no
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kErrLaunch;
     if (!done[dev]) {
         if (cudaFuncSetAttribute(exl3_dec_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int) sizeof(AttnSmem)) != cudaSuccess)
+                                 (int) sizeof(AttnSmem)) != cudaSuccess ||
+            cudaFuncSetAttribute(exl3_dec_attn_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+                cudaSuccess)
             return kErrLaunch;
         done[dev] = 1;
     }
-    return kOk;
+    int c = 1, li = 0;
+    while (c * 2 <= std::min(kAttnMaxCluster, max_chunks)) {
+        c *= 2;
+        ++li;
+    }
+    for (; c >= 1; c /= 2, --li) {
+        if (!fits[dev][li]) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned) c);
+            cfg.blockDim = dim3((unsigned) kAttnThreads);
+            cfg.dynamicSmemBytes = sizeof(AttnSmem);
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = (unsigned) c;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            fits[dev][li] = (cudaOccupancyMaxActiveClusters(&n, exl3_dec_attn_kernel, &cfg) == cudaSuccess && n > 0)
+                                ? 1 : 2;
+        }
+        if (fits[dev][li] == 1) {
+            *csize = c;
+            return kOk;
+        }
+    }
+    return kErrLaunch;
 }
 
-static int dec_launch_attn(const GvArgs& ob, const DecAux& x, int grid, cudaStream_t stream)
+static int dec_launch_attn(const GvArgs& ob, const DecAux& x, int groups, cudaStream_t stream)
 {
-    const int rc = dec_attn_smem_setup();
+    int csize = 1;
+    const int rc = dec_attn_setup((x.max_ctx + kDecChunk - 1) / kDecChunk, &csize);
     if (rc != kOk) return rc;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned) std::max(grid, 1));
+    cfg.gridDim = dim3((unsigned) (groups * csize));
     cfg.blockDim = dim3((unsigned) kAttnThreads);
     cfg.dynamicSmemBytes = sizeof(AttnSmem);
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned) csize;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, exl3_dec_attn_kernel, ob, x) == cudaSuccess ? kOk : kErrLaunch;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, exl3_dec_attn_kernel, ob, x, csize) == cudaSuccess ? kOk : kErrLaunch;
 }
 
 static int dec_grid(int tasks) { return std::min((tasks + 7) / 8, 8 * gv_sm_count()); }
@@ -620,21 +701,19 @@ static void dec_problem(GvProblem& p, const exl3b200_linear* l, int m, uint32_t*
 
 // Workspace layout of the attention sub-layer.
 struct DecAttnLayout {
-    size_t st_q, st_k, st_v, st_o, st_cnt, state_bytes;
-    size_t xd_q, xd_k, xd_v, sb_q, sb_k, sb_v, qbuf, attn_o, attn_ml, xd_o, sb_o, scratch_bytes;
+    size_t st_q, st_k, st_v, st_o, state_bytes;
+    size_t xd_q, xd_k, xd_v, sb_q, sb_k, sb_v, qbuf, xd_o, sb_o, scratch_bytes;
 };
 
 static DecAttnLayout dec_attn_layout(int batch, int hidden, int q_heads, int kv_heads, int max_ctx)
 {
     DecAttnLayout L = {};
     const int nq = q_heads * kHeadDim, nkv = kv_heads * kHeadDim;
-    const int max_chunks = (max_ctx + kDecChunk - 1) / kDecChunk;
     size_t o = 0;
     L.st_q = o; o += gv_state_bytes_per_problem(nq);
     L.st_k = o; o += gv_state_bytes_per_problem(nkv);
     L.st_v = o; o += gv_state_bytes_per_problem(nkv);
     L.st_o = o; o += gv_state_bytes_per_problem(hidden);
-    L.st_cnt = o; o += al256((size_t) batch * kv_heads * sizeof(unsigned int));
     L.state_bytes = o;
     o = 0;
     L.xd_q = o; o += gv_xd_bytes(batch, hidden);
@@ -644,8 +723,6 @@ static DecAttnLayout dec_attn_layout(int batch, int hidden, int q_heads, int kv_
     L.sb_k = o; o += gv_sblk_bytes(batch, hidden);
     L.sb_v = o; o += gv_sblk_bytes(batch, hidden);
     L.qbuf = o; o += al256((size_t) batch * nq * sizeof(float));
-    L.attn_o = o; o += al256((size_t) batch * q_heads * max_chunks * kHeadDim * sizeof(float));
-    L.attn_ml = o; o += al256((size_t) batch * q_heads * max_chunks * 2 * sizeof(float));
     L.xd_o = o; o += gv_xd_bytes(batch, nq);
     L.sb_o = o; o += gv_sblk_bytes(batch, nq);
     L.scratch_bytes = o;
@@ -854,10 +931,6 @@ extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int
     x.max_ctx = max_ctx;
     x.q_heads = q_heads;
     x.kv_heads = kv_heads;
-    x.max_chunks = (max_ctx + kDecChunk - 1) / kDecChunk;
-    x.attn_o = reinterpret_cast<float*>(W + L.attn_o);
-    x.attn_ml = reinterpret_cast<float*>(W + L.attn_ml);
-    x.attn_cnt = reinterpret_cast<unsigned int*>(S + L.st_cnt);
 
     // 1-3: norm input stage, q/k/v matmul, RoPE + KV append epilogue
     GvArgs a = {};
@@ -876,13 +949,13 @@ extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int
     rc = dec_launch_epilogue<kEpiRopeKV>(a, x, cb, st);
     if (rc != kOk) return rc;
 
-    // 4: attention (chunk partials, merged by the last chunk CTA into the o input)
+    // 4: attention (a cluster per row and kv head; its merge writes the o input)
     GvArgs b = {};
     b.nprob = 1;
     dec_problem(b.inl[0], o, batch, reinterpret_cast<uint32_t*>(W + L.xd_o),
                 mul1 ? reinterpret_cast<float*>(W + L.sb_o) : nullptr, reinterpret_cast<float*>(S + L.st_o));
     gv_prefix_inline(b);
-    rc = dec_launch_attn(b, x, batch * kv_heads * x.max_chunks, st);
+    rc = dec_launch_attn(b, x, batch * kv_heads, st);
     if (rc != kOk) return rc;
 
     // 5-6: o matmul, residual (or fp32 partial for the all-reduce)

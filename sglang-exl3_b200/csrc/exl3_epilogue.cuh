@@ -54,10 +54,7 @@ struct DecAux {
     __nv_bfloat16* k_cache;  // [batch][kv_heads][max_ctx][128]
     __nv_bfloat16* v_cache;
     long long cache_b_stride, cache_h_stride;
-    int max_ctx, q_heads, kv_heads, max_chunks;
-    float* attn_o;           // [batch][q_heads][max_chunks][128] unnormalised partial outputs
-    float* attn_ml;          // [batch][q_heads][max_chunks][2] (chunk max, chunk sum)
-    unsigned int* attn_cnt;  // [batch][kv_heads] chunk arrival tickets (state: zero between calls)
+    int max_ctx, q_heads, kv_heads;
     // residual epilogue
     float* resid;
     long long resid_stride;
@@ -102,6 +99,24 @@ template <int CB>
 __device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, int mode, int pi, const GvProblem& p,
                                               const GvProblem* up, int nb, int r, int lane)
 {
+    // loads and math that do not depend on the partial sums come first
+    float pre[4];
+    long long pos = 0;
+    if (mode == kEpiSwiglu) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pre[e] = __half2float(p.out_suh[nb * 128 + lane + 32 * e]);
+    } else if (mode == kEpiResidual) {
+        const float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) pre[e] = hr[lane + 32 * e];
+    } else if (mode == kEpiRopeKV) {
+        pos = *x.pos;
+        if (pi < 2) {
+            const float fpos = (float) pos;
+            sincosf(fpos * x.inv_freq[lane], &pre[0], &pre[1]);
+            sincosf(fpos * x.inv_freq[lane + 32], &pre[2], &pre[3]);
+        }
+    }
     float v[4];
     gv_finish<CB>(p, nb, r, lane, v);
     if (mode == kEpiStore) {
@@ -131,10 +146,8 @@ __device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, 
             act[e] = __half2float(__float2half_rn(s * uv));
         }
         // rotated input of the down projection for this 128-block of the intermediate
-        const __half* suh_d = p.out_suh + nb * 128;
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
-            act[e] = __half2float(__float2half_rn(__fmul_rn(act[e], __half2float(suh_d[lane + 32 * e]))));
+        for (int e = 0; e < 4; ++e) act[e] = __half2float(__float2half_rn(__fmul_rn(act[e], pre[e])));
         warp_fwht128(act, lane);
         uint32_t* dst = reinterpret_cast<uint32_t*>(p.out) + (size_t) r * p.out_stride + nb * 128;
         float bsum = 0.f;
@@ -151,17 +164,14 @@ __device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, 
             if (lane == 0) p.out_sblk[(size_t) r * (p.n >> 7) + nb] = bsum;
         }
     } else if (mode == kEpiRopeKV) {
-        // problems 0, 1, 2 = q, k, v; block nb = head nb; lane holds dims lane + 32e
-        const long long pos = *x.pos;
+        // problems 0, 1, 2 = q, k, v; block nb = head nb; lane holds dims lane + 32e;
+        // pre = (sin, cos) of the angles of dims lane and lane + 32
         if (pos < 0 || pos >= x.max_ctx) {  // the cache has no row for this position
             if (x.status && lane == 0) atomicCAS(x.status, 0, (int) kErrBadShape);
             return;
         }
         if (pi < 2) {
-            const float fpos = (float) pos;
-            float s0, c0, s1, c1;
-            sincosf(fpos * x.inv_freq[lane], &s0, &c0);
-            sincosf(fpos * x.inv_freq[lane + 32], &s1, &c1);
+            const float s0 = pre[0], c0 = pre[1], s1 = pre[2], c1 = pre[3];
             const float n0 = v[0] * c0 - v[2] * s0, n2 = v[2] * c0 + v[0] * s0;
             const float n1 = v[1] * c1 - v[3] * s1, n3 = v[3] * c1 + v[1] * s1;
             v[0] = n0;
@@ -188,12 +198,12 @@ __device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, 
             for (int e = 0; e < 4; ++e) dst[lane + 32 * e] = v[e];
         }
         __threadfence_system();
-    } else {  // kEpiResidual
+    } else {  // kEpiResidual: pre = h
         float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
         float sq = 0.f;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const float nv = hr[lane + 32 * e] + v[e];
+            const float nv = pre[e] + v[e];
             hr[lane + 32 * e] = nv;
             sq += nv * nv;
         }

@@ -110,7 +110,7 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gv_matmul_kernel(const 
     constexpr int TGRP = 8 / NT;         // warps sharing one slice
     constexpr int SG = kGvWarps / TGRP;  // slice groups
 
-    __shared__ float red[TG * 8][kRedStride];
+    __shared__ float red[SG][TG * 8][kRedStride];  // per slice group: its warps' partial block
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -158,8 +158,6 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gv_matmul_kernel(const 
         const int len = (int) min((long long) (kt_total - kr0), u_end - u);
         const int m = p.m;
         const size_t slice_words = (size_t) n_tiles * TW;  // words per k-slice row of the matrix
-
-        for (int i = threadIdx.x; i < TG * 8 * kRedStride; i += kGvThreads) (&red[0][0])[i] = 0.f;
 
         float acc[NT][TG][4];
 #pragma unroll
@@ -277,9 +275,8 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gv_matmul_kernel(const 
         for (int s = 0; s < P; ++s)
             if (i + s < nr) step(i + s, s);
 
-        __syncthreads();  // red zeroed by all threads before any atomics
-
-        // fragment -> shared block: lane holds (n = 16t + g (+8), rows 8q + 2c (+1))
+        // fragments -> the slice group's partial block (lane holds n = 16t + g (+8),
+        // rows 8q + 2c (+1)); the previous segment's readers passed the barrier below
 #pragma unroll
         for (int q = 0; q < TG; ++q) {
             const int r0 = 8 * q + 2 * c;
@@ -287,23 +284,27 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gv_matmul_kernel(const 
             for (int t = 0; t < NT; ++t) {
                 const int n0 = 16 * (th * NT + t) + g;
                 if (r0 < m) {
-                    atomicAdd(&red[r0][n0], acc[t][q][0]);
-                    atomicAdd(&red[r0][n0 + 8], acc[t][q][2]);
+                    red[sg][r0][n0] = acc[t][q][0];
+                    red[sg][r0][n0 + 8] = acc[t][q][2];
                 }
                 if (r0 + 1 < m) {
-                    atomicAdd(&red[r0 + 1][n0], acc[t][q][1]);
-                    atomicAdd(&red[r0 + 1][n0 + 8], acc[t][q][3]);
+                    red[sg][r0 + 1][n0] = acc[t][q][1];
+                    red[sg][r0 + 1][n0 + 8] = acc[t][q][3];
                 }
             }
         }
         __syncthreads();
 
-        // fire-and-forget: add this CTA's partial block into the zeroed state; the
-        // epilogue kernel (a programmatic dependent of this grid) finishes it
+        // sum over the slice groups, then fire-and-forget: add this CTA's partial block
+        // into the zeroed state; the epilogue kernel (a programmatic dependent of this
+        // grid) finishes it
         float* wsb = p.acc + (size_t) nb * p.acc_nb_stride;
         for (int e = threadIdx.x; e < m * 128; e += kGvThreads) {
             const int r = e >> 7, col = e & 127;
-            atomicAdd(wsb + r * 128 + col, red[r][col]);
+            float s = red[0][r][col];
+#pragma unroll
+            for (int j = 1; j < SG; ++j) s += red[j][r][col];
+            atomicAdd(wsb + r * 128 + col, s);
         }
         __syncthreads();
         u += len;
@@ -321,9 +322,10 @@ template <int CB, int MODE>
 __global__ __launch_bounds__(256) void exl3_gv_epilogue_kernel(const __grid_constant__ GvArgs a)
 {
     griddep_launch();
+    const int lane = threadIdx.x & 31;
+    gv_prefetch_epilogue(a, lane);
     griddep_wait();
     const GvTotals tot = gv_totals(a);
-    const int lane = threadIdx.x & 31;
     const int warps = gridDim.x * (blockDim.x >> 5);
     for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < tot.out_tasks; task += warps) {
         const int pi = gv_find<1>(a, tot.nprob, task);

@@ -59,12 +59,16 @@ __device__ __forceinline__ int gv_find(const GvArgs& a, int nprob, int task)
 template <int CB>
 __device__ __forceinline__ void gv_finish(const GvProblem& p, int nb, int r, int lane, float (&v)[4])
 {
+    // the output scales do not depend on the partial sums: load them first, so the
+    // two memory round trips overlap
+    float sv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sv[e] = __half2float(p.svh[nb * 128 + lane + 32 * e]);
     float* src = p.acc + (size_t) nb * p.acc_nb_stride + (size_t) r * 128;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        v[e] = __ldcg(src + lane + 32 * e);
-        __stcg(src + lane + 32 * e, 0.f);
-    }
+    for (int e = 0; e < 4; ++e) v[e] = __ldcg(src + lane + 32 * e);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) __stcg(src + lane + 32 * e, 0.f);
     if constexpr (CB == 2) {
         const float k_inv = __half2float(__ushort_as_half(kMul1InvBits));
         const float k_bias = __half2float(__ushort_as_half(kMul1BiasBits));
@@ -78,7 +82,25 @@ __device__ __forceinline__ void gv_finish(const GvProblem& p, int nb, int r, int
     }
     warp_fwht128(v, lane);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = v[e] * kHadScale * __half2float(p.svh[nb * 128 + lane + 32 * e]);
+    for (int e = 0; e < 4; ++e) v[e] = v[e] * kHadScale * sv[e];
+}
+
+// Bring 256 bytes of constant data (scales, norm weights) into L2; safe before the
+// previous kernel in the stream has finished.
+__device__ __forceinline__ void prefetch_l2_256(const void* ptr, int lane)
+{
+    if (lane < 2) asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(ptr) + 128 * lane));
+}
+
+// Before griddep_wait: prefetch the output scales of the warp's first epilogue task
+// (host-built tables only: a device table may still be in the making).
+__device__ __forceinline__ void gv_prefetch_epilogue(const GvArgs& a, int lane)
+{
+    if (a.dev || a.dev_totals) return;
+    const int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (task >= a.out_tasks) return;
+    const GvProblem& p = gv_prob(a, gv_find<1>(a, a.nprob, task));
+    prefetch_l2_256(p.svh + (size_t) ((task - p.out_task_begin) % (p.n >> 7)) * 128, lane);
 }
 
 }  // namespace exl3b200
