@@ -684,8 +684,11 @@ def run_decode(args, world, rank, local, device):
     tok_s = batch / (ms * 1e-3)
     step_bytes = exl3_weight_bytes(cfg, world)
 
-    # end to end through the public API: host prompt token in, each step's token out
-    e2e_n = 8
+    # end to end through the public API: each step's tokens in from pinned host memory,
+    # its output tokens back to the host
+    e2e_n = 32
+    model.pos.fill_(args.ctx)
+    model.generate(torch.zeros(batch, dtype=torch.long), 2)  # allocates the pinned buffers
     model.pos.fill_(args.ctx)
     torch.cuda.synchronize()
     barrier(world)
@@ -729,7 +732,7 @@ def run_decode(args, world, rank, local, device):
                      "kernel": f"fused gate+up EXL3 matmul 8192x2x{model.i_loc} 4bpw M={batch} (3 kernels)"},
         "e2e": {"value": batch / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": 8 * batch, "d2h_bytes_per_step": 8 * batch,
-                "path": "DecodeModel.generate: host token in, per-step token out, stream sync each step"},
+                "path": "DecodeModel.generate: per step, tokens H2D from pinned host memory, graph replay, tokens D2H, stream sync"},
         # fused: per layer 6 (attention) + 5 (MLP) launches, + 2 peer-reduce kernels per layer under TP
         "gpu_launches": steps * cfg.layers * ((11 + (2 if world > 1 else 0)) if model.fused else 12),
         "clocks": clk.summary(),

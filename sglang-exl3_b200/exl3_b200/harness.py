@@ -253,21 +253,34 @@ class DecodeModel:
             self.peers.close()
             self.peers = None
 
+    def _pinned(self, n: int):
+        """Pinned host buffers of a generate call (kept across calls: allocating page-locked
+        memory costs far more than a decode step)."""
+        buf = getattr(self, "_host_bufs", None)
+        if buf is None or buf[1].size(1) < n:
+            buf = (torch.empty(self.batch, dtype=torch.long).pin_memory(),
+                   torch.empty((self.batch, n), dtype=torch.long).pin_memory())
+            self._host_bufs = buf
+        return buf
+
     def generate(self, prompt_tokens: torch.Tensor, n: int) -> torch.Tensor:
         """Public API: greedy-decode n tokens after ``prompt_tokens`` (host [B] last
         prompt tokens); returns the host [B, n] tokens.  Each step copies its input
-        token from host memory and its output token back, as a serving loop does."""
+        tokens from pinned host memory (the previous step's output as the host received
+        it) and its output tokens back, then waits for them, as a serving loop does."""
         if self.graph is None:
             raise RuntimeError("call capture() first")
-        host_in = prompt_tokens.to(torch.long).pin_memory()
-        host_out = torch.empty((self.batch, n), dtype=torch.long).pin_memory()
+        host_in, host_out = self._pinned(n)
+        host_in.copy_(prompt_tokens.to(torch.long))
         with torch.cuda.stream(self.stream):
-            self.tokens.copy_(host_in, non_blocking=True)
             for i in range(n):
+                if i > 0:
+                    host_in.copy_(host_out[:, i - 1])
+                self.tokens.copy_(host_in, non_blocking=True)
                 self.graph.replay()
                 host_out[:, i].copy_(self.next_tokens, non_blocking=True)
                 self.stream.synchronize()
-        return host_out
+        return host_out[:, :n].clone()
 
     def decode(self, n: int):
         """Run n captured decode steps (feeding back the greedy tokens)."""
