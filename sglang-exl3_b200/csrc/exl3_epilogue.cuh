@@ -95,13 +95,22 @@ __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v)
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-template <int CB>
-__device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, int mode, int pi, const GvProblem& p,
-                                              const GvProblem* up, int nb, int r, int lane)
-{
-    // loads and math that do not depend on the partial sums come first
+// Loads and math of an epilogue that do not depend on the partial sums (issued
+// first so their round trips overlap the partials' read).
+struct EpiPre {
     float pre[4];
-    long long pos = 0;
+    long long pos;
+};
+
+__device__ __forceinline__ EpiPre epi_preload(const GvProblem& p, const DecAux& x, int mode, int pi, int nb, int r,
+                                              int lane)
+{
+    EpiPre ep;
+    float (&pre)[4] = ep.pre;
+    long long& pos = ep.pos;
+    pos = 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) pre[e] = 0.f;
     if (mode == kEpiSwiglu) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) pre[e] = __half2float(p.out_suh[nb * 128 + lane + 32 * e]);
@@ -117,8 +126,17 @@ __device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, 
             sincosf(fpos * x.inv_freq[lane + 32], &pre[2], &pre[3]);
         }
     }
-    float v[4];
-    gv_finish<CB>(p, nb, r, lane, v);
+    return ep;
+}
+
+// The output side of an epilogue: v = the finished block row of problem p (for
+// SwiGLU the gate), u = the up projection's (SwiGLU only).
+template <int CB>
+__device__ __forceinline__ void epi_apply(const GvArgs& a, const DecAux& x, int mode, int pi, const GvProblem& p, int nb,
+                                          int r, int lane, float (&v)[4], const float (&u)[4], const EpiPre& ep)
+{
+    const float (&pre)[4] = ep.pre;
+    const long long pos = ep.pos;
     if (mode == kEpiStore) {
 #pragma unroll
         for (int e = 0; e < 4; ++e)
@@ -130,8 +148,6 @@ __device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, 
 #pragma unroll
         for (int e = 0; e < 4; ++e) atomicAdd(o + lane + 32 * e, w * v[e]);
     } else if (mode == kEpiSwiglu) {
-        float u[4];
-        gv_finish<CB>(*up, nb, r, lane, u);
         const float lim = a.swiglu_limit;
         const bool clip = lim > 0.f && lim < 3.0e38f;
         float act[4];
@@ -211,6 +227,17 @@ __device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, 
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
         if (lane == 0) atomicAdd(x.ss_acc + r, sq);
     }
+}
+
+template <int CB>
+__device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, int mode, int pi, const GvProblem& p,
+                                              const GvProblem* up, int nb, int r, int lane)
+{
+    const EpiPre ep = epi_preload(p, x, mode, pi, nb, r, lane);
+    float v[4], u[4] = {0.f, 0.f, 0.f, 0.f};
+    gv_finish<CB>(p, nb, r, lane, v);
+    if (mode == kEpiSwiglu) gv_finish<CB>(*up, nb, r, lane, u);
+    epi_apply<CB>(a, x, mode, pi, p, nb, r, lane, v, u, ep);
 }
 
 }  // namespace exl3b200

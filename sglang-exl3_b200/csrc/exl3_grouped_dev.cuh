@@ -56,19 +56,19 @@ __device__ __forceinline__ int gv_find(const GvArgs& a, int nprob, int task)
     return lo;
 }
 
-template <int CB>
-__device__ __forceinline__ void gv_finish(const GvProblem& p, int nb, int r, int lane, float (&v)[4])
+// The block-row's output scales (loaded ahead of the partial sums, so the two
+// memory round trips overlap).
+__device__ __forceinline__ void gv_load_svh(const GvProblem& p, int nb, int lane, float (&sv)[4])
 {
-    // the output scales do not depend on the partial sums: load them first, so the
-    // two memory round trips overlap
-    float sv[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) sv[e] = __half2float(p.svh[nb * 128 + lane + 32 * e]);
-    float* src = p.acc + (size_t) nb * p.acc_nb_stride + (size_t) r * 128;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) v[e] = __ldcg(src + lane + 32 * e);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) __stcg(src + lane + 32 * e, 0.f);
+}
+
+// Summed partials of one (problem, block, row) -> outputs: mul1 correction, H128,
+// * 1/sqrt(128) * svh.  Lane holds columns lane + 32 e.
+template <int CB>
+__device__ __forceinline__ void gv_finish_math(const GvProblem& p, int r, int lane, const float (&sv)[4], float (&v)[4])
+{
     if constexpr (CB == 2) {
         const float k_inv = __half2float(__ushort_as_half(kMul1InvBits));
         const float k_bias = __half2float(__ushort_as_half(kMul1BiasBits));
@@ -83,6 +83,21 @@ __device__ __forceinline__ void gv_finish(const GvProblem& p, int nb, int r, int
     warp_fwht128(v, lane);
 #pragma unroll
     for (int e = 0; e < 4; ++e) v[e] = v[e] * kHadScale * sv[e];
+}
+
+// Read and re-zero the split-K partials of (problem, block nb, row r) in the state,
+// then finish them.
+template <int CB>
+__device__ __forceinline__ void gv_finish(const GvProblem& p, int nb, int r, int lane, float (&v)[4])
+{
+    float sv[4];
+    gv_load_svh(p, nb, lane, sv);
+    float* src = p.acc + (size_t) nb * p.acc_nb_stride + (size_t) r * 128;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = __ldcg(src + lane + 32 * e);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) __stcg(src + lane + 32 * e, 0.f);
+    gv_finish_math<CB>(p, r, lane, sv, v);
 }
 
 // Bring 256 bytes of constant data (scales, norm weights) into L2; safe before the
