@@ -271,9 +271,10 @@ EXL3B200_API int exl3b200_peer_buffer_free(void* ptr);
  * (tensor parallelism) it stores its fp32 partial output in y_out instead; after
  * the all-reduce, exl3b200_residual_add(h, y, ss_out) completes the sub-layer.
  * With peers (non-NULL; y_out ignored) the sub-layer exchanges the partials itself
- * through the peer buffers (stores over NVLink, a flag per rank, a bounded wait of
- * 2 s that records EXL3B200_ETIMEOUT in the device status when it gives up) and adds
- * their sum into h; every rank must make the same sequence of calls.
+ * through the peer buffers (stores over NVLink, an arrival counter per call, a
+ * bounded wait of 2 s that records EXL3B200_ETIMEOUT in the device status when it
+ * gives up; the exchange state is then undefined until the buffers are re-created)
+ * and adds their sum into h; every rank must make the same sequence of calls.
  *
  * Attention: k_cache / v_cache are this layer's bf16 [batch][kv_heads][max_ctx][128];
  * *pos (device) is the new token's position, the cache holds 0..pos-1 and the

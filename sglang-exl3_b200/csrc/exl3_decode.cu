@@ -33,13 +33,14 @@
 // grouped matmul, the SwiGLU epilogue that writes the down projection's rotated
 // input, the down matmul and the residual epilogue.
 //
-// Tensor parallelism without NCCL (peers != NULL): the o / down epilogue writes its
-// fp32 partial straight into a slot of every rank's peer buffer (CUDA IPC mapping,
-// plain stores over NVLink), then a reduce kernel raises this rank's flag in every
-// buffer, waits (bounded, 2 s) until all ranks' flags for this call are up in its
-// own buffer, sums the slots into h and accumulates the sum of squares.  Slots and
-// flags alternate between two parities by call; a rank cannot reach call k+2 before
-// every peer has finished reading call k (it waits for their call k+1 flags first).
+// Tensor parallelism without NCCL (peers != NULL): the o / down matmul's epilogue
+// kernel does the exchange itself - it stores each fp32 partial straight into a
+// slot of every rank's peer buffer (CUDA IPC mapping, plain stores over NVLink),
+// adds one arrival per CTA to a counter in every rank's buffer, waits (bounded, 2 s)
+// until its own counter holds every rank's arrivals, then sums the slots into h
+// and accumulates the sum of squares.  Counters and slots alternate between two
+// parities by call; a rank cannot reach call k+2 before every peer has finished
+// reading call k (its call k+1 waits for their call k+1 arrivals).
 //
 // The reference has no decode-layer fusion (its layers call SGLang's norm,
 // attention and activation kernels around the EXL3 ops); the arithmetic of each
@@ -512,44 +513,69 @@ __global__ __launch_bounds__(256) void exl3_dec_residual_kernel(float* __restric
     }
 }
 
-// Tensor-parallel exchange: signal, bounded wait for every rank's partial of this
-// call, h += sum of the partials, sum of squares.  The last CTA advances the epoch.
-__global__ __launch_bounds__(256) void exl3_dec_peer_reduce_kernel(const __grid_constant__ DecAux x, int batch,
-                                                                   int hidden)
+// Tensor-parallel output epilogue with the exchange folded in (o / down projection,
+// one launch per sub-layer).  Every CTA: finishes its (row, block) tasks and stores
+// each fp32 partial into this rank's slot of every rank's peer buffer (NVLink); a
+// system fence; one arrival on the call's counter in every rank's buffer; a
+// bounded wait (2 s of %globaltimer, then EXL3B200_ETIMEOUT in the device status
+// and no update) until its own counter holds world x grid arrivals; then h += the
+// sum of the slots for the same tasks, and the rows' sums of squares.  The last
+// CTA to finish re-arms the counter and advances the epoch.  The grid is at most
+// one CTA per SM, so every CTA is resident while it waits, and it is the same on
+// every rank (same shapes).  Counters and slots alternate between two parities by
+// call; a rank cannot reach call k+2 before every peer has finished reading call k
+// (its call k+1 needs their call k+1 arrivals).
+template <int CB>
+__global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __grid_constant__ GvArgs a,
+                                                                     const __grid_constant__ DecAux x)
 {
     griddep_launch();
-    griddep_wait();  // this rank's partials (previous kernel) are stored
+    const int lane = threadIdx.x & 31;
+    gv_prefetch_epilogue(a, lane);
+    griddep_wait();
     __shared__ int ok;
     PeerCtl* ctl = reinterpret_cast<PeerCtl*>(x.peer[x.peer_rank]);
     const unsigned int epoch = *reinterpret_cast<volatile unsigned int*>(&ctl->epoch) + 1u;
     const unsigned int parity = epoch & 1u;
-    if (blockIdx.x == 0 && threadIdx.x < x.peer_world) {
-        __threadfence_system();
-        st_release_sys(peer_flag(x, threadIdx.x, parity, x.peer_rank), epoch);
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    const int task0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    for (int task = task0; task < a.out_tasks; task += warps) {
+        const GvProblem& p = gv_prob(a, 0);
+        const int nblocks = p.n >> 7;
+        const int r = task / nblocks, nb = task - r * nblocks;
+        float v[4];
+        gv_finish<CB>(p, nb, r, lane, v);
+        for (int q = 0; q < x.peer_world; ++q) {
+            float* dst = peer_slot(x, q, parity, x.peer_rank, r) + nb * 128;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) dst[lane + 32 * e] = v[e];
+        }
     }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x < x.peer_world)
+        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(peer_flag(x, threadIdx.x, parity, 0)) : "memory");
     if (threadIdx.x == 0) {
+        const unsigned int expect = (unsigned int) x.peer_world * gridDim.x;
+        const unsigned int* cnt = peer_flag(x, x.peer_rank, parity, 0);
         int good = 1;
         const unsigned long long t0 = globaltimer_ns();
-        for (int q = 0; q < x.peer_world && good; ++q) {
-            const unsigned int* f = peer_flag(x, x.peer_rank, parity, q);
-            while (ld_acquire_sys(f) != epoch) {
-                if (globaltimer_ns() - t0 > kPeerTimeoutNs) {
-                    good = 0;
-                    if (x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
-                    break;
-                }
-                __nanosleep(64);
+        while (ld_acquire_sys(cnt) < expect) {
+            if (globaltimer_ns() - t0 > kPeerTimeoutNs) {
+                good = 0;
+                if (x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
+                break;
             }
+            __nanosleep(32);
         }
         ok = good;
     }
     __syncthreads();
     if (ok) {
-        const int lane = threadIdx.x & 31;
-        const int nblk = hidden >> 7;
-        const int warps = gridDim.x * (blockDim.x >> 5);
-        for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < batch * nblk; task += warps) {
-            const int r = task / nblk, b = task - r * nblk;
+        for (int task = task0; task < a.out_tasks; task += warps) {
+            const GvProblem& p = gv_prob(a, 0);
+            const int nblocks = p.n >> 7;
+            const int r = task / nblocks, b = task - r * nblocks;
             float sum[4] = {0.f, 0.f, 0.f, 0.f};
             for (int q = 0; q < x.peer_world; ++q) {
                 const float* src = peer_slot(x, x.peer_rank, parity, q, r) + b * 128;
@@ -574,6 +600,7 @@ __global__ __launch_bounds__(256) void exl3_dec_peer_reduce_kernel(const __grid_
         __threadfence();
         if (atomicAdd(&ctl->done, 1u) == gridDim.x - 1) {
             ctl->done = 0u;
+            *peer_flag(x, x.peer_rank, parity, 0) = 0u;  // every rank's arrivals of this call are in
             __threadfence();
             *reinterpret_cast<volatile unsigned int*>(&ctl->epoch) = epoch;
         }
@@ -768,10 +795,9 @@ static int dec_finish(GvArgs& a, DecAux& x, int cb, float* h, long long h_stride
         x.resid = h;
         x.resid_stride = h_stride;
         x.ss_acc = ss_out;
-        int rc = dec_launch_epilogue<kEpiPeerStore>(a, x, cb, st);
-        if (rc != kOk) return rc;
-        return dec_launch(exl3_dec_peer_reduce_kernel, std::min(dec_grid(batch * (hidden / 128)), 2 * gv_sm_count()),
-                          256, st, x, batch, hidden);
+        const int g = std::min(dec_grid(a.out_tasks), gv_sm_count());  // resident: its CTAs wait on each other
+        return cb == 2 ? dec_launch(exl3_dec_peer_epilogue_kernel<2>, g, 256, st, a, x)
+                       : dec_launch(exl3_dec_peer_epilogue_kernel<0>, g, 256, st, a, x);
     }
     if (y_out) {
         a.inl[0].out = y_out;

@@ -9,8 +9,6 @@
 //   kEpiRopeKV    decode q/k/v: RoPE (rotate-half), q scaled into the attention
 //                 buffer, k and v appended to the bf16 cache
 //   kEpiResidual  decode: h += y and the row's sum of squares
-//   kEpiPeerStore decode, tensor parallel: the fp32 partial into every rank's peer
-//                 buffer over NVLink
 #pragma once
 
 #include <cuda_bf16.h>
@@ -23,10 +21,10 @@ namespace exl3b200 {
 
 constexpr int kHeadDim = 128;
 
-enum DecEpiMode : int { kEpiRopeKV = 10, kEpiResidual = 11, kEpiPeerStore = 12 };
+enum DecEpiMode : int { kEpiRopeKV = 10, kEpiResidual = 11 };
 
-// peer buffer: [control 128 B][flags: 2 parities x 8 ranks x u32, padded to 128 B]
-//              [data: 2 parities x 8 ranks x max_rows x hidden fp32]
+// peer buffer: [control 128 B][arrival counters: 2 parities (u32; room for 2 x 8),
+//              padded to 128 B][data: 2 parities x 8 ranks x max_rows x hidden fp32]
 constexpr int kPeerMaxRanks = 8;
 constexpr size_t kPeerFlags = 128;
 constexpr size_t kPeerData = 256;
@@ -205,15 +203,6 @@ __device__ __forceinline__ void epi_apply(const GvArgs& a, const DecAux& x, int 
 #pragma unroll
             for (int e = 0; e < 4; ++e) c[lane + 32 * e] = __float2bfloat16_rn(v[e]);
         }
-    } else if (mode == kEpiPeerStore) {
-        const PeerCtl* ctl = reinterpret_cast<const PeerCtl*>(x.peer[x.peer_rank]);
-        const unsigned int parity = (*reinterpret_cast<const volatile unsigned int*>(&ctl->epoch) + 1u) & 1u;
-        for (int q = 0; q < x.peer_world; ++q) {
-            float* dst = peer_slot(x, q, parity, x.peer_rank, r) + nb * 128;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) dst[lane + 32 * e] = v[e];
-        }
-        __threadfence_system();
     } else {  // kEpiResidual: pre = h
         float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
         float sq = 0.f;
