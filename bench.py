@@ -54,6 +54,9 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "decode tok/s (70B-shape 4bpw); EXL3 GEMV HBM GB/s vs roofline"
+# DRAM bytes per launch of the fused gate+up matmul kernel (8192 x 2 x 28672, 4 bpw, M = 1),
+# from ncu (profiles/exl3_gv_matmul_gateup_8192x2x28672_4bpw_m1_traffic.md)
+GATEUP_TRAFFIC_BYTES = 237_192_363
 
 # Llama-70B shape (config 4)
 L70 = dict(layers=80, hidden=8192, heads=64, kv_heads=8, head_dim=128, inter=28672, vocab=128256, K=4, cb=0)
@@ -702,6 +705,7 @@ def run_decode(args, world, rank, local, device):
     outs = [torch.empty(batch, model.i_loc, dtype=torch.float16, device=device) for _ in range(2)]
     s = torch.cuda.Stream(device)
     s.wait_stream(torch.cuda.current_stream(device))
+    torch.cuda.nvtx.range_push("roofline")  # ncu --nvtx-include "roofline/" selects these launches
     with torch.cuda.stream(s):
         for pair in gu[:3]:
             ops.matmul_multi(x, pair, cfg.K, cfg.cb, outs=outs)
@@ -711,7 +715,9 @@ def run_decode(args, world, rank, local, device):
                 ops.matmul_multi(x, pair, cfg.K, cfg.cb, outs=outs)
         g.replay()
         kt = time_graph(g, 3, s) / len(gu)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.current_stream(device).wait_stream(s)
+    peer_exchange = model.peers is not None
     kbytes = 2 * (cfg.hidden * model.i_loc * cfg.K // 8) + 2 * batch * (cfg.hidden + 2 * model.i_loc)
     k_gbs = kbytes / (kt * 1e-3) / 1e9
     del g
@@ -728,13 +734,17 @@ def run_decode(args, world, rank, local, device):
                    "exl3_bytes_per_step_per_rank": step_bytes},
         "exl3_gbs_per_rank": step_bytes / (ms * 1e-3) / 1e9,
         "roofline": {"bound": "hbm", "achieved": k_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": k_gbs / hbm_peak,
-                     "traffic": None, "peak_kind": peak_kind,
+                     "traffic": GATEUP_TRAFFIC_BYTES * model.i_loc / 28672, "peak_kind": peak_kind,
+                     "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the matmul kernel, "
+                                       "mean of 3 launches at 8192x2x28672 M=1, scaled by the shard's columns",
                      "kernel": f"fused gate+up EXL3 matmul 8192x2x{model.i_loc} 4bpw M={batch} (3 kernels)"},
         "e2e": {"value": batch / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": 8 * batch, "d2h_bytes_per_step": 8 * batch,
                 "path": "DecodeModel.generate: per step, tokens H2D from pinned host memory, graph replay, tokens D2H, stream sync"},
-        # fused: per layer 6 (attention) + 5 (MLP) launches, + 2 peer-reduce kernels per layer under TP
-        "gpu_launches": steps * cfg.layers * ((11 + (2 if world > 1 else 0)) if model.fused else 12),
+        # fused: per layer 6 (attention) + 5 (MLP) launches (the NVLink exchange runs inside the o/down
+        # epilogues); + 2 residual-add kernels per layer when TP goes through NCCL instead
+        "gpu_launches": steps * cfg.layers * ((11 + (2 if world > 1 and not peer_exchange else 0))
+                                              if model.fused else 12),
         "clocks": clk.summary(),
     }
     return finish(line, args, world)

@@ -43,6 +43,7 @@ extern "C" {
 #define EXL3B200_ENULL 7
 #define EXL3B200_EBADARG 8
 #define EXL3B200_ETIMEOUT 9
+#define EXL3B200_EIO 10
 
 /* output dtypes */
 #define EXL3B200_DTYPE_F16 0
@@ -303,6 +304,27 @@ EXL3B200_API int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, in
                                      size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream);
 EXL3B200_API int exl3b200_residual_add(int batch, int hidden, float* h, long long h_stride, const float* y,
                                        long long y_stride, float* ss_out, void* stream);
+
+/*
+ * Checkpoint reader: copies count byte ranges of the open file fd (offsets[i],
+ * sizes[i] bytes) to dst[i].  Replaces the pread() loop of the reference's
+ * exl3_mmap load format (src/sglang_exl3/loader.py:121-168), which reads every
+ * tensor into a fresh host buffer for SGLang to copy to the GPU afterwards.
+ *
+ * dst_on_device 1: dst are device pointers.  staging is the caller's PINNED host
+ * buffer of staging_bytes, split into `threads` slots (each a multiple of 4 KB,
+ * at least 4 KB, else EXL3B200_EWORKSPACE); `threads` reader threads pread()
+ * chunks into their slots and enqueue the host-to-device copies on `stream`.
+ * dst_on_device 0: dst are host pointers, read into directly by the threads;
+ * no CUDA call is made and staging may be NULL.
+ * drop_cache 1: each range read is dropped from the page cache (posix_fadvise).
+ * threads in 1..64.  Unlike the compute entry points this call blocks: it
+ * returns once every byte is in place (device copies complete).  A file that
+ * ends inside a range returns EXL3B200_EIO.
+ */
+EXL3B200_API int exl3b200_read_ranges(int fd, const long long* offsets, const long long* sizes, void* const* dst,
+                                      int count, int dst_on_device, void* staging, size_t staging_bytes,
+                                      int threads, int drop_cache, void* stream);
 
 #ifdef __cplusplus
 }

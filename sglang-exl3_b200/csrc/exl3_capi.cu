@@ -16,6 +16,7 @@ extern "C" const char* exl3b200_status_string(int status)
         case EXL3B200_ENULL: return "null pointer";
         case EXL3B200_EBADARG: return "bad argument";
         case EXL3B200_ETIMEOUT: return "device wait timed out";
+        case EXL3B200_EIO: return "file read failed (short read)";
         default: return "unknown status";
     }
 }

@@ -24,9 +24,10 @@ STATUS_NAMES = {
     7: "EXL3B200_ENULL",
     8: "EXL3B200_EBADARG",
     9: "EXL3B200_ETIMEOUT",
+    10: "EXL3B200_EIO",
 }
 
-EBADSHAPE, EBADBITS, EBADCODEBOOK, EUNALIGNED, ELAUNCH, EWORKSPACE, ENULL, EBADARG, ETIMEOUT = range(1, 10)
+EBADSHAPE, EBADBITS, EBADCODEBOOK, EUNALIGNED, ELAUNCH, EWORKSPACE, ENULL, EBADARG, ETIMEOUT, EIO = range(1, 11)
 
 DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 FLAG_INPUT_ROTATED = 1
@@ -87,6 +88,7 @@ SIGNATURES = {
     "exl3b200_peer_buffer_close": (_i, [_vp]),
     "exl3b200_peer_buffer_free": (_i, [_vp]),
     "exl3b200_residual_add": (_i, [_i, _i, _vp, _ll, _vp, _ll, _vp, _vp]),
+    "exl3b200_read_ranges": (_i, [_i, _vp, _vp, _vp, _i, _i, _vp, _sz, _i, _i, _vp]),
     "exl3b200_moe_state_size": (_sz, [_i, _i, _i, _i]),
     "exl3b200_moe_scratch_size": (_sz, [_i, _i, _i, _i]),
     "exl3b200_moe": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
