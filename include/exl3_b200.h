@@ -171,7 +171,7 @@ EXL3B200_API int exl3b200_batched_gemv(const void* x, int x_per_expert, long lon
  *   sglang_exl3_c.p2b_fused_moe (reference csrc/p2b_moe.cu:418-468, op
  *   src/sglang_exl3/ops.py:121-184; fixed there to one row, hidden 4096) and the
  *   per-token batched GEMV path (src/sglang_exl3/exl3.py:960-1110).
- *   max_tokens * topk <= 2048, num_experts <= 2048.
+ *   max_tokens * topk <= 8192, num_experts <= 2048.
  */
 EXL3B200_API size_t exl3b200_moe_state_size(int max_tokens, int topk, int hidden, int inter);
 EXL3B200_API size_t exl3b200_moe_scratch_size(int max_tokens, int topk, int hidden, int inter);
@@ -183,6 +183,27 @@ EXL3B200_API int exl3b200_moe(const void* x, long long x_stride, int tokens, int
                               int K_gate, int K_up, int K_down, int cb, float swiglu_limit, float* out,
                               long long out_stride, int accumulate, int max_tokens, void* state, size_t state_bytes,
                               void* scratch, size_t scratch_bytes, void* stream);
+
+/*
+ * The same routed SwiGLU MoE (same arguments and result) on the tensor cores, for
+ * batches whose experts receive many rows each: every expert's codes are decoded
+ * once per 256 of its rows into tcgen05 MMAs (exl3b200_moe streams them once per 16
+ * rows).  Replaces the reference's large-M expert path, the per-expert loop over
+ * sglang_exl3_c.exl3_fat_gemm / exl3_fat_gemm_scatter (src/sglang_exl3/exl3.py:
+ * 1154-1231, csrc/exl3_fat_gemm.cu:65-305), without its host synchronisation.
+ * scratch: exl3b200_moe_tc_scratch_size bytes, 256-byte aligned, no initialisation
+ * (no state buffer).  out must be 16-byte aligned with out_stride a multiple of 4.
+ * max_tokens * topk <= 8192, num_experts <= 2048.
+ */
+EXL3B200_API size_t exl3b200_moe_tc_scratch_size(int max_tokens, int topk, int num_experts, int hidden, int inter);
+EXL3B200_API int exl3b200_moe_tc(const void* x, long long x_stride, int tokens, int hidden, int inter,
+                                 const int* topk_ids, const float* topk_weights, int topk, int num_experts,
+                                 const long long* gate_trellis, const long long* gate_suh, const long long* gate_svh,
+                                 const long long* up_trellis, const long long* up_suh, const long long* up_svh,
+                                 const long long* down_trellis, const long long* down_suh,
+                                 const long long* down_svh, int K_gate, int K_up, int K_down, int cb,
+                                 float swiglu_limit, float* out, long long out_stride, int accumulate,
+                                 int max_tokens, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
  * out[m, k] = H128(x * suh) / sqrt(128) in fp16 over 128-element blocks of each row,

@@ -49,6 +49,7 @@
 
 #include "exl3_common.cuh"
 #include "exl3_capi_internal.h"
+#include "exl3_tc_internal.h"
 
 namespace exl3b200 {
 
@@ -66,20 +67,20 @@ constexpr int kTcStageB = 3;
 constexpr int kTcStageT = 4;
 constexpr int kTcABlock = 128 * 64 * 2;        // one 128-row x 64-k fp16 block (16 KB)
 constexpr int kTcBStage = kTcCols * 64 * 2;    // 32 KB
-constexpr int kTcBars = 2 * kTcStageA + 2 * kTcStageT + 2 * kTcStageB + 2;
 constexpr int kTcSlotFloats = kTcRows * kTcCols;  // one split tile's fp32 partial sums
 constexpr unsigned long long kTcTimeoutNs = 1000000000ull;
 
 __device__ int g_exl3_device_status = 0;  // sticky: first device-side error code
 
-template <int K>
+template <int K, int SA = kTcStageA, int ST = kTcStageT>
 struct TcSmem {
+    static constexpr int kBars = 2 * SA + 2 * ST + 2 * kTcStageB + 2;
     static constexpr uint32_t kTChunk = 4u * 16u * 32u * K;  // codes of one stage at 256 columns
     static constexpr uint32_t kA = 0;
-    static constexpr uint32_t kB = kA + kTcStageA * 2 * kTcABlock;
+    static constexpr uint32_t kB = kA + SA * 2 * kTcABlock;
     static constexpr uint32_t kT = kB + kTcStageB * kTcBStage;
-    static constexpr uint32_t kBar = kT + kTcStageT * kTChunk;
-    static constexpr uint32_t kMisc = kBar + 8 * kTcBars;
+    static constexpr uint32_t kBar = kT + ST * kTChunk;
+    static constexpr uint32_t kMisc = kBar + 8 * kBars;
     static constexpr uint32_t kBytes = kMisc + 16;
     static constexpr uint32_t kLaunchBytes = kBytes + 1024;  // room to align the base to 1024
 };
@@ -96,6 +97,15 @@ struct TcArgs {
     int mtiles, tiles, nkc;
     int out_dtype;            // 0 fp16, 1 bf16, 2 fp32
     int vec_store;            // rows of out are 16-byte aligned
+    // grouped launches (kTcGroupedStore / kTcGroupedCombine): the problem of each
+    // tile and the tile count come from device memory written by an earlier kernel
+    const TcProblem* probs;
+    const int* tile_prob;
+    const int* dev_tiles;
+    const int* dev_tile_base;  // nullable
+    long long xt_rows;         // rows of the k-chunk-major input image
+    const int* slot_token;     // combine: output row of each routed slot
+    const float* slot_weight;  // combine: its routing weight
 };
 
 // ---------------------------------------------------------------------------
@@ -496,6 +506,100 @@ __device__ __forceinline__ void tc_epilogue_block(const TcArgs& a, uint32_t tadd
     }
 }
 
+// Grouped launches: one 128-column block of one 128-row accumulator, this warp's
+// 32 rows, the same transform as tc_epilogue_block; then dst (row < m; null
+// otherwise) receives w * y, stored when PLAIN (a whole tile of a store launch),
+// else added with vector atomics.
+template <bool PLAIN>
+__device__ __forceinline__ void tc_epilogue_block_grouped(uint32_t taddr, const __half* __restrict__ svh,
+                                                          float* __restrict__ dst, float w)
+{
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+        float v[32];
+        tmem_ld32(taddr + 32 * j, v);
+        tmem_ld_wait();
+        fwht32_local(v);
+        tmem_st32(taddr + 32 * j, v);
+    }
+    tmem_st_wait();
+    const uint4* sv4 = reinterpret_cast<const uint4*>(svh);
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+        float u[4][8];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tmem_ld8(taddr + 32 * j + 8 * c, u[j]);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float b0 = __fadd_rn(u[0][i], u[1][i]), b1 = __fsub_rn(u[0][i], u[1][i]);
+            const float b2 = __fadd_rn(u[2][i], u[3][i]), b3 = __fsub_rn(u[2][i], u[3][i]);
+            u[0][i] = __fadd_rn(b0, b2);
+            u[2][i] = __fsub_rn(b0, b2);
+            u[1][i] = __fadd_rn(b1, b3);
+            u[3][i] = __fsub_rn(b1, b3);
+        }
+        if (!dst) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint4 s = __ldg(sv4 + 4 * j + c);
+            const __half* sh = reinterpret_cast<const __half*>(&s);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) u[j][i] = w * (u[j][i] * kHadScale * __half2float(sh[i]));
+            float4* d4 = reinterpret_cast<float4*>(dst + 32 * j + 8 * c);
+            const float4 lo = make_float4(u[j][0], u[j][1], u[j][2], u[j][3]);
+            const float4 hi = make_float4(u[j][4], u[j][5], u[j][6], u[j][7]);
+            if constexpr (PLAIN) {
+                d4[0] = lo;
+                d4[1] = hi;
+            } else {
+                atomicAdd(d4, lo);
+                atomicAdd(d4 + 1, hi);
+            }
+        }
+    }
+}
+
+// What a CTA needs to know about the tile of a segment: the dense launch's single
+// problem, or the grouped launch's problem of that tile.
+struct TcSeg {
+    const uint8_t* xt;  // grouped: the problem's input image
+    const uint8_t* trellis;
+    const __half* svh;
+    float* gout;  // grouped store: fp32 output of the problem's row 0
+    int m, mt, nt, row0, slot0;
+};
+
+template <int MODE>
+__device__ __forceinline__ TcSeg tc_seg(const TcArgs& a, int tile)
+{
+    TcSeg s;
+    if constexpr (MODE == kTcDense) {
+        s.xt = a.xt;
+        s.trellis = a.trellis;
+        s.svh = a.svh;
+        s.gout = nullptr;
+        s.m = a.m;
+        s.mt = tile % a.mtiles;
+        s.nt = tile / a.mtiles;
+        s.row0 = 0;
+        s.slot0 = 0;
+    } else {
+        const TcProblem& p = a.probs[a.tile_prob[tile]];
+        const int local = tile - p.tile_begin;
+        s.xt = p.xt;
+        s.trellis = p.trellis;
+        s.svh = p.svh;
+        s.gout = p.out;
+        s.m = p.m;
+        s.mt = local % p.mtiles;
+        s.nt = local / p.mtiles;
+        s.row0 = p.row0;
+        s.slot0 = p.slot0;
+    }
+    return s;
+}
+
 // first iteration of CTA c, and the CTA that runs iteration it
 __device__ __forceinline__ long long tc_range_start(long long iters, int grid, int c)
 {
@@ -510,18 +614,20 @@ __device__ __forceinline__ int tc_cta_of(long long iters, int grid, long long it
 // ---------------------------------------------------------------------------
 // matmul
 // ---------------------------------------------------------------------------
-template <int K, int CB>
+template <int K, int CB, int MODE>
 __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __grid_constant__ TcArgs a)
 {
-    using L = TcSmem<K>;
+    constexpr int SA = kTcStageA, ST = kTcStageT;
+    using L = TcSmem<K, SA, ST>;
+    static_assert(L::kLaunchBytes <= 232448, "shared memory per CTA");
     extern __shared__ uint8_t tc_smem_raw[];
     const uint32_t raw = smem_u32(tc_smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* gbase = tc_smem_raw + (base - raw);
     const uint32_t sA = base + L::kA, sB = base + L::kB, sT = base + L::kT, sBar = base + L::kBar;
-    const uint32_t full_a = sBar, empty_a = full_a + 8 * kTcStageA;
-    const uint32_t full_t = empty_a + 8 * kTcStageA, empty_t = full_t + 8 * kTcStageT;
-    const uint32_t full_b = empty_t + 8 * kTcStageT, empty_b = full_b + 8 * kTcStageB;
+    const uint32_t full_a = sBar, empty_a = full_a + 8 * SA;
+    const uint32_t full_t = empty_a + 8 * SA, empty_t = full_t + 8 * ST;
+    const uint32_t full_b = empty_t + 8 * ST, empty_b = full_b + 8 * kTcStageB;
     const uint32_t acc_full = empty_b + 8 * kTcStageB, acc_empty = acc_full + 8;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + L::kMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kMisc + 4);
@@ -529,16 +635,14 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     const int grid = gridDim.x;
-    const long long it_begin = tc_range_start(a.iters, grid, blockIdx.x);
-    const long long it_end = tc_range_start(a.iters, grid, blockIdx.x + 1);
     const int nkc = a.nkc;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kTcStageA; ++s) {
+        for (int s = 0; s < SA; ++s) {
             mbar_init(full_a + 8 * s, 1);
             mbar_init(empty_a + 8 * s, 1);
         }
-        for (int s = 0; s < kTcStageT; ++s) {
+        for (int s = 0; s < ST; ++s) {
             mbar_init(full_t + 8 * s, 1);
             mbar_init(empty_t + 8 * s, kTcDecWarps);
         }
@@ -560,6 +664,15 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     tc_griddep_launch();
+    long long iters = a.iters;
+    int tile_base = 0;
+    if constexpr (MODE != kTcDense) {
+        tc_griddep_wait();  // the routing kernel wrote the tile list, the problems and the counts
+        iters = (long long) *reinterpret_cast<const volatile int*>(a.dev_tiles) * nkc;
+        if (a.dev_tile_base) tile_base = *reinterpret_cast<const volatile int*>(a.dev_tile_base);
+    }
+    const long long it_begin = tc_range_start(iters, grid, blockIdx.x);
+    const long long it_end = tc_range_start(iters, grid, blockIdx.x + 1);
 
     if (warp == 0) {
         // activation producer
@@ -570,23 +683,43 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             for (long long it = it_begin; it < it_end && ok;) {
                 const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
                 const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
-                const int mt = tile % a.mtiles;
-                const int nacc = a.m - mt * kTcRows > 128 ? 2 : 1;
-                const uint8_t* src0 = a.xt + (((size_t) (2 * mt) * nkc + kc0) << 14);
-                const size_t acc_step = (size_t) nkc << 14;
-                for (int kc = kc0; kc < kc1; ++kc, src0 += kTcABlock) {
-                    if (!mbar_wait(empty_a + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
-                    mbar_expect_tx(full_a + 8 * s, (uint32_t) (nacc * kTcABlock));
-                    bulk_g2s(sA + (s * 2) * kTcABlock, src0, kTcABlock, full_a + 8 * s);
-                    if (nacc == 2) bulk_g2s(sA + (s * 2 + 1) * kTcABlock, src0 + acc_step, kTcABlock, full_a + 8 * s);
-                    used |= 1u << s;
-                    par = (par & ~(1u << s)) | (ph << s);
-                    if (++s == kTcStageA) { s = 0; ph ^= 1; }
+                const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
+                const int mt = sg.mt;
+                const int rows_t = min(kTcRows, sg.m - mt * kTcRows);
+                const int nacc = rows_t > 128 ? 2 : 1;
+                if constexpr (MODE == kTcDense) {
+                    const uint8_t* src0 = a.xt + (((size_t) (2 * mt) * nkc + kc0) << 14);
+                    const size_t acc_step = (size_t) nkc << 14;
+                    for (int kc = kc0; kc < kc1; ++kc, src0 += kTcABlock) {
+                        if (!mbar_wait(empty_a + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
+                        mbar_expect_tx(full_a + 8 * s, (uint32_t) (nacc * kTcABlock));
+                        bulk_g2s(sA + (s * 2) * kTcABlock, src0, kTcABlock, full_a + 8 * s);
+                        if (nacc == 2) bulk_g2s(sA + (s * 2 + 1) * kTcABlock, src0 + acc_step, kTcABlock, full_a + 8 * s);
+                        used |= 1u << s;
+                        par = (par & ~(1u << s)) | (ph << s);
+                        if (++s == SA) { s = 0; ph ^= 1; }
+                    }
+                } else {
+                    // only the problem's rows (rounded up to 8) of each 128-row block; the
+                    // accumulator rows past them hold garbage that no epilogue stores
+                    const uint32_t b0 = (uint32_t) ((min(128, rows_t) + 7) & ~7) * 128u;
+                    const uint32_t b1 = rows_t > 128 ? (uint32_t) ((rows_t - 128 + 7) & ~7) * 128u : 0u;
+                    const size_t row = (size_t) sg.row0 + (size_t) mt * kTcRows;
+                    for (int kc = kc0; kc < kc1; ++kc) {
+                        if (!mbar_wait(empty_a + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
+                        const uint8_t* src = sg.xt + ((size_t) kc * (size_t) a.xt_rows + row) * 128;
+                        mbar_expect_tx(full_a + 8 * s, b0 + b1);
+                        bulk_g2s(sA + (s * 2) * kTcABlock, src, b0, full_a + 8 * s);
+                        if (b1) bulk_g2s(sA + (s * 2 + 1) * kTcABlock, src + 128 * 128, b1, full_a + 8 * s);
+                        used |= 1u << s;
+                        par = (par & ~(1u << s)) | (ph << s);
+                        if (++s == SA) { s = 0; ph ^= 1; }
+                    }
                 }
                 it += kc1 - kc0;
             }
             // own copies in flight (all consumed already unless the CTA aborted)
-            for (uint32_t j = 0; j < kTcStageA; ++j)
+            for (uint32_t j = 0; j < SA; ++j)
                 if (used >> j & 1) mbar_wait(full_a + 8 * j, par >> j & 1, abort_flag, false);
         }
     } else if (warp == 2) {
@@ -598,10 +731,11 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             for (long long it = it_begin; it < it_end && ok;) {
                 const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
                 const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
-                const int nt = tile / a.mtiles;
+                const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
+                const int nt = sg.nt;
                 const int bn = min(kTcCols, a.n - nt * kTcCols);
                 const uint32_t seg = (uint32_t) (bn >> 4) * 32 * K;
-                const uint8_t* src = a.trellis + (size_t) kc0 * 4 * row_bytes + (size_t) nt * 16 * 32 * K;
+                const uint8_t* src = sg.trellis + (size_t) kc0 * 4 * row_bytes + (size_t) nt * 16 * 32 * K;
                 for (int kc = kc0; kc < kc1; ++kc, src += 4 * row_bytes) {
                     if (!mbar_wait(empty_t + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
                     mbar_expect_tx(full_t + 8 * s, 4 * seg);
@@ -610,11 +744,11 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                     for (int i = 0; i < 4; ++i) bulk_g2s(dst + i * seg, src + i * row_bytes, seg, full_t + 8 * s);
                     used |= 1u << s;
                     par = (par & ~(1u << s)) | (ph << s);
-                    if (++s == kTcStageT) { s = 0; ph ^= 1; }
+                    if (++s == ST) { s = 0; ph ^= 1; }
                 }
                 it += kc1 - kc0;
             }
-            for (uint32_t j = 0; j < kTcStageT; ++j)
+            for (uint32_t j = 0; j < ST; ++j)
                 if (used >> j & 1) mbar_wait(full_t + 8 * j, par >> j & 1, abort_flag, false);
         }
     } else if (warp == 1) {
@@ -627,8 +761,9 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             for (long long it = it_begin; it < it_end && ok; ++seg_i) {
                 const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
                 const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
-                const int mt = tile % a.mtiles, nt = tile / a.mtiles;
-                const int nacc = a.m - mt * kTcRows > 128 ? 2 : 1;
+                const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
+                const int mt = sg.mt, nt = sg.nt;
+                const int nacc = sg.m - mt * kTcRows > 128 ? 2 : 1;
                 const uint32_t idesc = tc_idesc(min(kTcCols, a.n - nt * kTcCols));
                 // the epilogue of the previous segment has read the accumulators
                 if (!mbar_wait(acc_empty, (uint32_t) (seg_i & 1) ^ 1, abort_flag, true)) break;
@@ -651,7 +786,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                     }
                     tc_commit(empty_a + 8 * sa);
                     tc_commit(empty_b + 8 * sb);
-                    if (++sa == kTcStageA) { sa = 0; pa ^= 1; }
+                    if (++sa == SA) { sa = 0; pa ^= 1; }
                     if (++sb == kTcStageB) { sb = 0; pb ^= 1; }
                 }
                 tc_commit(acc_full);
@@ -668,6 +803,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
         const int hq = q == 3 ? warp >> 2 : (warp >> 2) - 1;  // its index among the quarter's warps
         const bool decoder = q != 1;
         const int dw = (warp - 3) - (warp - 2) / 4;           // decoder index 0..15
+
         tc_griddep_wait();
         const LaneWords lw = lane_words<K>(lane);
         uint32_t st = 0, pt = 0, sb = 0, pb = 0;
@@ -676,7 +812,8 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
         for (long long it = it_begin; it < it_end && ok; ++seg_i) {
             const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
             const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
-            const int mt = tile % a.mtiles, nt = tile / a.mtiles;
+            const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
+            const int mt = sg.mt, nt = sg.nt;
             const int bn = min(kTcCols, a.n - nt * kTcCols);
             if (decoder) {
                 for (int kc = kc0; kc < kc1; ++kc) {
@@ -695,7 +832,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                         mbar_arrive(full_b + 8 * sb);
                         mbar_arrive(empty_t + 8 * st);
                     }
-                    if (++st == kTcStageT) { st = 0; pt ^= 1; }
+                    if (++st == ST) { st = 0; pt ^= 1; }
                     if (++sb == kTcStageB) { sb = 0; pb ^= 1; }
                 }
             }
@@ -704,20 +841,36 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                 break;
             }
             tc_fence_after();
-            const int nacc = a.m - mt * kTcRows > 128 ? 2 : 1;
+            const int nacc = sg.m - mt * kTcRows > 128 ? 2 : 1;
             const int nblk = bn >> 7;
             if (hq < nacc * nblk) {
                 const int acc = hq / nblk, cb = hq - acc * nblk;
                 const int row = mt * kTcRows + acc * 128 + q * 32 + lane;
                 const bool whole = kc0 == 0 && kc1 == nkc;
-                float* slot_row = nullptr;
-                if (!whole) {
-                    const int slot = tc_cta_of(a.iters, grid, (long long) tile * nkc);
-                    slot_row = a.slots + (size_t) slot * kTcSlotFloats + (size_t) (acc * 128 + q * 32 + lane) * kTcCols +
-                               cb * 128;
+                const uint32_t taddr = tmem + ((uint32_t) (q * 32) << 16) + acc * 256 + cb * 128;
+                const int col0 = nt * kTcCols + cb * 128;
+                if constexpr (MODE == kTcDense) {
+                    float* slot_row = nullptr;
+                    if (!whole) {
+                        const int slot = tc_cta_of(a.iters, grid, (long long) tile * nkc);
+                        slot_row = a.slots + (size_t) slot * kTcSlotFloats +
+                                   (size_t) (acc * 128 + q * 32 + lane) * kTcCols + cb * 128;
+                    }
+                    tc_epilogue_block(a, taddr, row, col0, whole, slot_row);
+                } else if constexpr (MODE == kTcGroupedStore) {
+                    float* dst = row < sg.m ? sg.gout + (size_t) row * a.out_stride + col0 : nullptr;
+                    if (whole) tc_epilogue_block_grouped<true>(taddr, sg.svh + col0, dst, 1.f);
+                    else tc_epilogue_block_grouped<false>(taddr, sg.svh + col0, dst, 1.f);
+                } else {
+                    float* dst = nullptr;
+                    float w = 0.f;
+                    if (row < sg.m) {
+                        const int sl = sg.slot0 + row;
+                        dst = reinterpret_cast<float*>(a.out) + (size_t) a.slot_token[sl] * a.out_stride + col0;
+                        w = a.slot_weight[sl];
+                    }
+                    tc_epilogue_block_grouped<false>(taddr, sg.svh + col0, dst, w);
                 }
-                tc_epilogue_block(a, tmem + ((uint32_t) (q * 32) << 16) + acc * 256 + cb * 128, row,
-                                  nt * kTcCols + cb * 128, whole, slot_row);
             }
             tc_fence_before();
             __syncwarp();
@@ -793,7 +946,7 @@ static cudaError_t tc_launch(const void* kern, int grid, int block, size_t smem,
     return cudaLaunchKernelExC(&cfg, kern, args);
 }
 
-template <int K, int CB>
+template <int K, int CB, int MODE>
 static int tc_launch_gemm(const TcArgs& a, int grid, cudaStream_t stream)
 {
     using L = TcSmem<K>;
@@ -801,25 +954,64 @@ static int tc_launch_gemm(const TcArgs& a, int grid, cudaStream_t stream)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kErrLaunch;
     if (!configured[dev]) {
-        if (cudaFuncSetAttribute(exl3_tc_gemm_kernel<K, CB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(exl3_tc_gemm_kernel<K, CB, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int) L::kLaunchBytes) != cudaSuccess)
             return kErrLaunch;
         configured[dev] = true;
     }
     TcArgs arg = a;
     void* args[] = {&arg};
-    return tc_launch((const void*) exl3_tc_gemm_kernel<K, CB>, grid, kTcThreads, L::kLaunchBytes, stream, args) ==
-                   cudaSuccess
+    return tc_launch((const void*) exl3_tc_gemm_kernel<K, CB, MODE>, grid, kTcThreads, L::kLaunchBytes, stream,
+                     args) == cudaSuccess
                ? kOk
                : kErrLaunch;
 }
 
-template <int K>
+template <int K, int MODE>
 static int tc_launch_cb(const TcArgs& a, int cb, int grid, cudaStream_t stream)
 {
-    if (cb == 0) return tc_launch_gemm<K, 0>(a, grid, stream);
-    if (cb == 1) return tc_launch_gemm<K, 1>(a, grid, stream);
-    return tc_launch_gemm<K, 2>(a, grid, stream);
+    if (cb == 0) return tc_launch_gemm<K, 0, MODE>(a, grid, stream);
+    if (cb == 1) return tc_launch_gemm<K, 1, MODE>(a, grid, stream);
+    return tc_launch_gemm<K, 2, MODE>(a, grid, stream);
+}
+
+template <int MODE>
+static int tc_launch_k(const TcArgs& a, int K, int cb, int grid, cudaStream_t stream)
+{
+    switch (K) {
+        case 2: return tc_launch_cb<2, MODE>(a, cb, grid, stream);
+        case 3: return tc_launch_cb<3, MODE>(a, cb, grid, stream);
+        default: return tc_launch_cb<4, MODE>(a, cb, grid, stream);
+    }
+}
+
+int tc_device_sms() { return tc_sm_count(); }
+
+int tc_grouped_matmul(const TcGroupedCall& c, int K, int cb, cudaStream_t stream)
+{
+    if (K < 2 || K > 4) return kErrBadBits;
+    if (cb < 0 || cb > 2) return kErrBadCodebook;
+    if (c.k <= 0 || c.n <= 0 || c.k % 128 || c.n % 128 || c.xt_rows % 8 || c.out_stride % 4) return kErrBadShape;
+    if (!c.probs || !c.tile_prob || !c.dev_tiles || !c.out) return kErrNullPointer;
+    if (c.mode == kTcGroupedCombine && (!c.slot_token || !c.slot_weight)) return kErrNullPointer;
+    TcArgs a = {};
+    a.out = c.out;
+    a.out_stride = c.out_stride;
+    a.k = c.k;
+    a.n = c.n;
+    a.nkc = c.k / 64;
+    a.out_dtype = 2;
+    a.probs = c.probs;
+    a.tile_prob = c.tile_prob;
+    a.dev_tiles = c.dev_tiles;
+    a.dev_tile_base = c.dev_tile_base;
+    a.xt_rows = c.xt_rows;
+    a.slot_token = c.slot_token;
+    a.slot_weight = c.slot_weight;
+    const int grid = tc_sm_count();  // the tile count is known on the device only
+    if (c.mode == kTcGroupedStore) return tc_launch_k<kTcGroupedStore>(a, K, cb, grid, stream);
+    if (c.mode == kTcGroupedCombine) return tc_launch_k<kTcGroupedCombine>(a, K, cb, grid, stream);
+    return kErrBadArgument;
 }
 
 static size_t tc_xt_bytes(int m, int k) { return (size_t) ((m + 127) / 128) * 128 * (size_t) k * 2; }
@@ -890,12 +1082,7 @@ extern "C" int exl3b200_gemm(const void* x, long long x_stride, int m, int k, co
     a.out_dtype = out_dtype;
     const int esz = out_dtype == 2 ? 4 : 2;
     a.vec_store = ((uintptr_t) out % 16 == 0) && ((out_stride * esz) % 16 == 0);
-    int rc;
-    switch (K) {
-        case 2: rc = tc_launch_cb<2>(a, cb, grid, st); break;
-        case 3: rc = tc_launch_cb<3>(a, cb, grid, st); break;
-        default: rc = tc_launch_cb<4>(a, cb, grid, st); break;
-    }
+    const int rc = tc_launch_k<kTcDense>(a, K, cb, grid, st);
     if (rc != kOk) return rc;
     if (grid > 1) {
         int g = grid;

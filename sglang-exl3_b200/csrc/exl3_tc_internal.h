@@ -1,0 +1,63 @@
+// Internal interface of the grouped tensor-core matmul (exl3_tc.cu) for the
+// routed-MoE pipeline (exl3_tc_moe.cu): a launch over many problems that share k,
+// n, K and the codebook, each with its own trellis, svh, rows and output, whose
+// tiles and problem table were written on the device by an earlier kernel.
+#pragma once
+
+#include <cstdint>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+namespace exl3b200 {
+
+// One problem of a grouped launch (written by a routing kernel).
+struct TcProblem {
+    const uint8_t* xt;       // input image holding the problem's rows (layout below)
+    const uint8_t* trellis;  // [k/16][n/16][32K bytes]
+    const __half* svh;       // [n]
+    float* out;              // grouped store: fp32 output of the problem's row 0
+    int m;                   // rows
+    int mtiles;              // ceil(m / 256)
+    int tile_begin;          // first tile of the problem in the launch's tile list
+    int row0;                // first row in the input image (multiple of 8)
+    int slot0;               // first routed slot (token / weight lists) of the problem
+    int pad;
+};
+
+enum TcMode : int {
+    kTcDense = 0,         // one problem, host-known sizes (exl3b200_gemm)
+    kTcGroupedStore = 1,  // fp32 out rows of each problem (whole tiles stored, split tiles added)
+    kTcGroupedCombine = 2 // fp32 out[slot_token[s]] += slot_weight[s] * y
+};
+
+// Input image of a grouped launch: k-chunk major, xt_rows rows of 128 bytes per
+// 64-wide k chunk, each 8-row group's 16-byte chunks XOR-swizzled by (row % 8):
+// byte ((kc * xt_rows + row) * 128 + ((((kk & 63) >> 3) ^ (row & 7)) << 4) + (kk & 7) * 2)
+// holds element kk of row row.  A problem's rows start at a multiple of 8.
+__host__ __device__ __forceinline__ size_t tc_image_offset(long long xt_rows, int row, int kk)
+{
+    return ((size_t) (kk >> 6) * (size_t) xt_rows + (size_t) row) * 128 + (size_t) ((((kk & 63) >> 3) ^ (row & 7)) << 4) +
+           (size_t) (kk & 7) * 2;
+}
+
+struct TcGroupedCall {
+    long long xt_rows;        // rows of every problem's input image
+    const TcProblem* probs;
+    const int* tile_prob;     // problem index of every tile of the list
+    const int* dev_tiles;     // device: number of tiles of this launch
+    const int* dev_tile_base; // device: first tile of this launch in the list (nullable: 0)
+    int k, n;
+    float* out;               // combine: fp32 [tokens][n]
+    long long out_stride;     // elements, multiple of 4 (both modes)
+    const int* slot_token;    // combine
+    const float* slot_weight; // combine
+    int mode;                 // kTcGroupedStore or kTcGroupedCombine
+};
+
+// Enqueues one grouped launch (programmatic dependent of the previous kernel).
+int tc_grouped_matmul(const TcGroupedCall& c, int K, int cb, cudaStream_t stream);
+
+// SMs of the current device.
+int tc_device_sms();
+
+}  // namespace exl3b200

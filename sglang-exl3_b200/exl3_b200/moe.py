@@ -10,6 +10,7 @@ functions keep the signatures of ``sglang_exl3_c``
 
 from __future__ import annotations
 
+import os
 from typing import Optional
 
 import torch
@@ -19,6 +20,8 @@ from .ops import (_OUT_DTYPES, _require_cuda, _stream_ptr, codebook_id, legacy_c
 
 MOE_MAX_PAIRS = 8192
 MOE_MAX_EXPERTS = 2048
+# average routed rows per local expert from which the tensor-core pipeline is used
+MOE_TC_MIN_ROWS = 12
 
 
 def _table(t: torch.Tensor, name: str) -> torch.Tensor:
@@ -82,16 +85,27 @@ def workspace_tokens(tokens: int, chunk: int) -> int:
     return min(cap, chunk)
 
 
+def moe_path(tokens: int, topk: int, experts: int) -> str:
+    """``"tc"`` (tensor-core pipeline, codes decoded once per 256 rows of an expert)
+    when the experts get ``MOE_TC_MIN_ROWS`` rows each on average, else ``"small"``
+    (small-M pipeline, once per 16 rows).  ``EXL3_B200_MOE_PATH`` = small / tc
+    forces one.  Decided from host-known sizes only (no synchronisation)."""
+    forced = os.environ.get("EXL3_B200_MOE_PATH", "auto").lower()
+    if forced in ("small", "tc"):
+        return forced
+    return "tc" if tokens * topk >= MOE_TC_MIN_ROWS * experts else "small"
+
+
 def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, tables: dict,
                 K_gate: int, K_up: int, K_down: int, cb: int, intermediate_size: int,
                 swiglu_limit: float = 0.0, out: Optional[torch.Tensor] = None, accumulate: bool = False,
-                max_tokens: Optional[int] = None) -> torch.Tensor:
+                max_tokens: Optional[int] = None, path: Optional[str] = None) -> torch.Tensor:
     """Routed SwiGLU MoE: ``out[t] (+)= sum_j w[t,j] * down_e(silu(gate_e x_t) * up_e x_t)``.
 
     ``tables`` holds the nine int64 device pointer tables of the local experts
     (``gate_trellis`` ... ``down_svh``, as built by ``build_exl3_fused_state``,
     ``src/sglang_exl3/exl3.py:579-607``).  Ids outside ``[0, E)`` are skipped.
-    Returns fp32 ``[T, H]``."""
+    ``path``: ``"small"``, ``"tc"`` or None (``moe_path``).  Returns fp32 ``[T, H]``."""
     if x.dim() != 2 or x.dtype != torch.float16:
         raise RuntimeError("MoE input must be fp16 [tokens, hidden]")
     T, H = x.shape
@@ -120,6 +134,22 @@ def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Ten
     if out.dtype != torch.float32 or out.dim() != 2 or out.stride(-1) != 1 or out.size(0) < T:
         raise RuntimeError("MoE output must be float32 [tokens, hidden]")
     L = _lib.lib()
+    path = path or moe_path(T, topk, E)
+    if path == "tc":
+        if out.data_ptr() % 16 or out.stride(0) % 4:
+            raise RuntimeError("tensor-core MoE output must be 16-byte aligned with a row stride multiple of 4")
+        with torch.cuda.device(dev):
+            nbytes = L.exl3b200_moe_tc_scratch_size(max_tokens, topk, E, H, intermediate_size)
+            scratch = workspace.scratch_buffer(dev, nbytes)
+            st = L.exl3b200_moe_tc(x.data_ptr(), x.stride(0), T, H, intermediate_size, ids.data_ptr(), w.data_ptr(),
+                                   topk, E, *[t.data_ptr() for t in tabs], int(K_gate), int(K_up), int(K_down),
+                                   int(cb), float(swiglu_limit if swiglu_limit is not None else 0.0), out.data_ptr(),
+                                   out.stride(0), int(accumulate), int(max_tokens), scratch.data_ptr(),
+                                   scratch.numel(), _stream_ptr(dev))
+        _lib.check(st, "exl3b200_moe_tc")
+        return out
+    if path != "small":
+        raise RuntimeError(f"unknown MoE path {path!r}")
     with torch.cuda.device(dev):
         state = workspace.state_buffer(dev, L.exl3b200_moe_state_size(max_tokens, topk, H, intermediate_size))
         scratch = workspace.scratch_buffer(dev, L.exl3b200_moe_scratch_size(max_tokens, topk, H, intermediate_size))

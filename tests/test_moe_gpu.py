@@ -83,9 +83,12 @@ def test_p2b_gemv_batched(cuda_device, cb, per_expert):
         assert O.normwise_rel_err(out[j].float().cpu().numpy(), O.gemv_ref(xe, tr, su, sv, K, cb)) < TOL
 
 
+@pytest.mark.parametrize("path", ["small", "tc"])
 @pytest.mark.parametrize("T,topk,E", [(1, 8, 16), (5, 4, 8), (16, 8, 12), (40, 2, 6), (600, 8, 16)])
 @pytest.mark.parametrize("cb", [0, 1])
-def test_moe_forward(cuda_device, T, topk, E, cb):
+def test_moe_forward(cuda_device, T, topk, E, cb, path):
+    """Both pipelines at every size: the tensor-core one from 1 row per expert to
+    300 (two 256-row tiles, one of them with both 128-row accumulators)."""
     rng = np.random.default_rng(1000 * T + 10 * topk + cb)
     H, I, K = 256, 384, 3
     experts = _with_cb(_experts(rng, E, H, I, K), cb)
@@ -95,12 +98,14 @@ def test_moe_forward(cuda_device, T, topk, E, cb):
     ids = np.argsort(-logits, axis=1)[:, :topk].astype(np.int32)
     w = np.take_along_axis(logits, ids, 1)
     w = (np.exp(w) / np.exp(w).sum(1, keepdims=True)).astype(np.float32)
-    y = moe.moe_forward(_t(x, cuda_device), _t(ids, cuda_device), _t(w, cuda_device), tabs, K, K, K, cb, I)
+    y = moe.moe_forward(_t(x, cuda_device), _t(ids, cuda_device), _t(w, cuda_device), tabs, K, K, K, cb, I,
+                        path=path)
     ref = O.moe_ref(x, experts, ids, w)
     assert O.normwise_rel_err(y.cpu().numpy(), ref) < TOL_MOE
 
 
-def test_moe_invalid_ids_and_clip(cuda_device):
+@pytest.mark.parametrize("path", ["small", "tc"])
+def test_moe_invalid_ids_and_clip(cuda_device, path):
     rng = np.random.default_rng(77)
     T, topk, E, H, I, K, cb = 3, 3, 5, 256, 256, 4, 1
     experts = _with_cb(_experts(rng, E, H, I, K), cb)
@@ -109,12 +114,13 @@ def test_moe_invalid_ids_and_clip(cuda_device):
     ids = np.array([[0, 7, 2], [-1, 4, 4], [3, 1, 9]], dtype=np.int32)  # 7, -1, 9 are not local
     w = rng.uniform(0.1, 1.0, size=(T, topk)).astype(np.float32)
     y = moe.moe_forward(_t(x, cuda_device), _t(ids, cuda_device), _t(w, cuda_device), tabs, K, K, K, cb, I,
-                        swiglu_limit=1.5)
+                        swiglu_limit=1.5, path=path)
     ref = O.moe_ref(x, experts, ids, w, limit=1.5)
     assert O.normwise_rel_err(y.cpu().numpy(), ref) < TOL_MOE
 
 
-def test_moe_mixed_bits_and_accumulate(cuda_device):
+@pytest.mark.parametrize("path", ["small", "tc"])
+def test_moe_mixed_bits_and_accumulate(cuda_device, path):
     """gate/up/down with different K (two gate/up launches), then a shared expert
     added with accumulate."""
     rng = np.random.default_rng(78)
@@ -131,10 +137,10 @@ def test_moe_mixed_bits_and_accumulate(cuda_device):
     ids = np.array([[0, 3], [1, 2], [2, 2], [3, 0]], dtype=np.int32)
     w = rng.uniform(0.2, 0.8, size=(T, topk)).astype(np.float32)
     xd = _t(x, cuda_device)
-    y = moe.moe_forward(xd, _t(ids, cuda_device), _t(w, cuda_device), tabs, 2, 3, 4, 0, I)
+    y = moe.moe_forward(xd, _t(ids, cuda_device), _t(w, cuda_device), tabs, 2, 3, 4, 0, I, path=path)
     ones = torch.ones((T, 1), dtype=torch.float32, device=cuda_device)
     zeros = torch.zeros((T, 1), dtype=torch.int32, device=cuda_device)
-    moe.moe_forward(xd, zeros, ones, stabs, 4, 4, 4, 0, I, out=y, accumulate=True)
+    moe.moe_forward(xd, zeros, ones, stabs, 4, 4, 4, 0, I, out=y, accumulate=True, path=path)
     ref = O.moe_ref(x, experts, ids, w) + O.moe_ref(x, shared, np.zeros((T, 1), np.int64), np.ones((T, 1), np.float32))
     assert O.normwise_rel_err(y.cpu().numpy(), ref) < TOL_MOE
 
@@ -178,7 +184,8 @@ def test_fat_gemm_and_scatter(cuda_device, K, cb):
     assert O.normwise_rel_err(acc.cpu().numpy(), exp) < TOL
 
 
-def test_moe_graph_capture_replay(cuda_device):
+@pytest.mark.parametrize("path", ["small", "tc"])
+def test_moe_graph_capture_replay(cuda_device, path):
     rng = np.random.default_rng(81)
     T, topk, E, H, I, K = 2, 4, 8, 256, 256, 3
     experts = _with_cb(_experts(rng, E, H, I, K), 0)
@@ -191,11 +198,11 @@ def test_moe_graph_capture_replay(cuda_device):
     s.wait_stream(torch.cuda.current_stream(cuda_device))
     with torch.cuda.stream(s):
         for _ in range(2):
-            moe.moe_forward(x, ids, w, tabs, K, K, K, 0, I, out=out)
+            moe.moe_forward(x, ids, w, tabs, K, K, K, 0, I, out=out, path=path)
     torch.cuda.current_stream(cuda_device).wait_stream(s)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=s):
-        moe.moe_forward(x, ids, w, tabs, K, K, K, 0, I, out=out)
+        moe.moe_forward(x, ids, w, tabs, K, K, K, 0, I, out=out, path=path)
     for trial in range(2):
         new_ids = rng.integers(0, E, size=(T, topk)).astype(np.int32)
         ids.copy_(_t(new_ids, cuda_device))
@@ -203,3 +210,21 @@ def test_moe_graph_capture_replay(cuda_device):
         torch.cuda.synchronize()
         ref = O.moe_ref(x.cpu().numpy(), experts, new_ids, w.cpu().numpy())
         assert O.normwise_rel_err(out.cpu().numpy(), ref) < TOL_MOE
+
+
+@pytest.mark.parametrize("K,cb", [(3, 0), (4, 1), (2, 2)])
+def test_moe_tc_matches_small_at_config5_width(cuda_device, K, cb):
+    """Config-5 expert shape (hidden 4096, intermediate 1536), 32 experts with ~20
+    rows each: the two pipelines agree (no oracle: its dequant is slow at this size)."""
+    rng = np.random.default_rng(300 + K)
+    T, topk, E, H, I = 80, 8, 32, 4096, 1536
+    experts = _with_cb(_experts(rng, E, H, I, K), cb)
+    tabs, keep = _tables(experts, cuda_device, cb)
+    # inputs scaled so that the fp16 SwiGLU intermediate of random-code experts stays finite
+    x = _t((0.05 * rng.standard_normal((T, H))).astype(np.float16), cuda_device)
+    ids = _t(np.stack([rng.permutation(E)[:topk] for _ in range(T)]).astype(np.int32), cuda_device)
+    w = _t(rng.uniform(0.05, 0.3, size=(T, topk)).astype(np.float32), cuda_device)
+    ys = moe.moe_forward(x, ids, w, tabs, K, K, K, cb, I, path="small")
+    yt = moe.moe_forward(x, ids, w, tabs, K, K, K, cb, I, path="tc")
+    assert torch.isfinite(ys).all() and torch.isfinite(yt).all()
+    assert O.normwise_rel_err(yt.cpu().numpy(), ys.cpu().numpy().astype(np.float64)) < TOL_MOE
