@@ -112,6 +112,22 @@ EXL3B200_API int exl3b200_gemv_combine(const void* x, long long x_stride, int m,
                                        size_t scratch_bytes, void* stream);
 
 /*
+ * The same routed, weighted accumulation for any m on the tensor cores (codes
+ * decoded once per 256 rows): out[out_rows[r], :] += out_scale[r] * (x[r] @ W).
+ * out_rows / out_scale may be NULL (row r, weight 1); repeated rows add up (fp32
+ * vector atomics).  Replaces sglang_exl3_c.exl3_fat_gemm_scatter (reference
+ * csrc/exl3_fat_gemm.cu:286-305, one tile pass per 128 rows there).  out must be
+ * 16-byte aligned with out_stride a multiple of 4; scratch:
+ * exl3b200_gemm_combine_scratch_size(m, k, n) bytes, 256-byte aligned, no
+ * initialisation (no state buffer).
+ */
+EXL3B200_API size_t exl3b200_gemm_combine_scratch_size(int m, int k, int n);
+EXL3B200_API int exl3b200_gemm_combine(const void* x, long long x_stride, int m, int k, const void* trellis, int n,
+                                       int K, int cb, const void* suh, const void* svh, float* out,
+                                       long long out_stride, const int* out_rows, const float* out_scale,
+                                       int flags, void* scratch, size_t scratch_bytes, void* stream);
+
+/*
  * Small-M matmul that allocates nothing and takes no workspace: out = x @ W as
  * exl3b200_gemv, for callers that cannot allocate device memory (an
  * allocator-less runtime that owns all device memory up front, or a thread that

@@ -240,8 +240,10 @@ __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs 
     }
 }
 
-// One warp per (slot, 128-block, gate/up): the rotated input row block into its
-// image; the grid also zeroes the fp32 gate/up rows and (unless accumulating) out.
+// One warp per (slot, 128-block): the row block of x[token] loaded once, rotated
+// with the gate's and with the up projection's suh (rotate_block's roundings) into
+// the two images; the grid also zeroes the fp32 gate/up rows and (unless
+// accumulating) out.
 __global__ __launch_bounds__(256) void exl3_tm_input_kernel(const TmArgs t)
 {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -251,25 +253,34 @@ __global__ __launch_bounds__(256) void exl3_tm_input_kernel(const TmArgs t)
     const int H = t.hidden, I = t.inter;
     const int nblk = H >> 7;
     const int rows = tm_tot(t)[4];
-    const int tasks = rows * nblk * 2;
+    const int tasks = rows * nblk;
     const int* slot_token = reinterpret_cast<const int*>(t.scratch + L.slot_token);
     const int* slot_row = reinterpret_cast<const int*>(t.scratch + L.slot_row);
     const int* slot_exp = reinterpret_cast<const int*>(t.scratch + L.slot_exp);
     const int warps = gridDim.x * (blockDim.x >> 5);
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     for (int task = gw; task < tasks; task += warps) {
-        const int which = task & 1;  // 0 gate, 1 up
-        const int rb = task >> 1;
-        const int s = rb / nblk, b = rb - s * nblk;
+        const int s = task / nblk, b = task - s * nblk;
         const int e = slot_exp[s];
         const int row = slot_row[s];
-        const __half* suh = reinterpret_cast<const __half*>(which ? t.uu[e] : t.gu[e]) + b * 128;
-        __half h[4];
-        rotate_block(t.x + (size_t) slot_token[s] * t.x_stride + b * 128, suh, lane, h);
-        uint8_t* img = reinterpret_cast<uint8_t*>(t.scratch + (which ? L.xt_u : L.xt_g));
+        const __half* src = t.x + (size_t) slot_token[s] * t.x_stride + b * 128;
+        float xv[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-            *reinterpret_cast<__half*>(img + tc_image_offset(L.xt_rows, row, b * 128 + lane + 32 * i)) = h[i];
+        for (int i = 0; i < 4; ++i) xv[i] = __half2float(src[lane + 32 * i]);
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+            const __half* suh = reinterpret_cast<const __half*>(which ? t.uu[e] : t.gu[e]) + b * 128;
+            float v[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                v[i] = __half2float(__float2half_rn(__fmul_rn(xv[i], __half2float(suh[lane + 32 * i]))));
+            warp_fwht128(v, lane);
+            uint8_t* img = reinterpret_cast<uint8_t*>(t.scratch + (which ? L.xt_u : L.xt_g));
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                *reinterpret_cast<__half*>(img + tc_image_offset(L.xt_rows, row, b * 128 + lane + 32 * i)) =
+                    __float2half_rn(__fmul_rn(v[i], kHadScale));
+        }
     }
     // zero the gate/up rows (split tiles add into them) and the output
     const int gthreads = gridDim.x * blockDim.x;
@@ -411,7 +422,7 @@ extern "C" int exl3b200_moe_tc(const void* x, long long x_stride, int tokens, in
     if (rc != kOk) return rc;
     const int sms = tc_device_sms();
     const int pairs = tokens * topk;
-    const int in_grid = std::min((2 * pairs * (hidden / 128) + 7) / 8, 4 * sms);
+    const int in_grid = std::min((pairs * (hidden / 128) + 7) / 8, 4 * sms);
     rc = tm_launch((const void*) exl3_tm_input_kernel, in_grid, 256, true, st, args);
     if (rc != kOk) return rc;
 
@@ -458,4 +469,146 @@ extern "C" int exl3b200_moe_tc(const void* x, long long x_stride, int tokens, in
     d.slot_weight = reinterpret_cast<const float*>(sc + L.slot_weight);
     d.mode = kTcGroupedCombine;
     return tc_grouped_matmul(d, K_down, cb, st);
+}
+
+// ---------------------------------------------------------------------------
+// One routed linear on the tensor cores: out[out_rows[r]] += out_scale[r] * (x[r] @ W)
+// for any m (the large-M form of the reference's exl3_fat_gemm_scatter).  A setup
+// kernel writes the rotated input image, the row and weight lists and a one-problem
+// table; then one grouped launch in combine mode.
+// ---------------------------------------------------------------------------
+namespace exl3b200 {
+
+struct GcLayout {
+    size_t tot, prob, tiles, token, weight, img, bytes;
+    long long xt_rows;
+    int mtiles, ntiles;
+};
+
+static GcLayout gc_layout(int m, int k, int n)
+{
+    GcLayout L;
+    L.xt_rows = ((long long) m + 7) & ~7ll;
+    L.mtiles = (m + 255) / 256;
+    L.ntiles = (n + 255) / 256;
+    size_t o = 0;
+    L.tot = o; o = tm_al(o + 16 * sizeof(int));
+    L.prob = o; o = tm_al(o + sizeof(TcProblem));
+    L.tiles = o; o = tm_al(o + (size_t) L.mtiles * L.ntiles * sizeof(int));
+    L.token = o; o = tm_al(o + (size_t) m * sizeof(int));
+    L.weight = o; o = tm_al(o + (size_t) m * sizeof(float));
+    L.img = o; o = tm_al(o + (size_t) L.xt_rows * k * 2);
+    L.bytes = o;
+    return L;
+}
+
+struct GcArgs {
+    const __half* x;
+    long long x_stride;
+    const __half* suh;  // null: x is already rotated
+    const int* rows;    // null: row r
+    const float* scale; // null: 1
+    const uint8_t* trellis;
+    const __half* svh;
+    char* scratch;
+    GcLayout L;
+    int m, k;
+};
+
+__global__ __launch_bounds__(256) void exl3_gc_setup_kernel(const GcArgs g)
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    const GcLayout& L = g.L;
+    const int tid = blockIdx.x * blockDim.x + threadIdx.x;
+    const int nth = gridDim.x * blockDim.x;
+    if (tid == 0) {
+        TcProblem p = {};
+        p.xt = reinterpret_cast<const uint8_t*>(g.scratch + L.img);
+        p.trellis = g.trellis;
+        p.svh = g.svh;
+        p.m = g.m;
+        p.mtiles = L.mtiles;
+        *reinterpret_cast<TcProblem*>(g.scratch + L.prob) = p;
+        reinterpret_cast<int*>(g.scratch + L.tot)[0] = L.mtiles * L.ntiles;
+    }
+    int* tiles = reinterpret_cast<int*>(g.scratch + L.tiles);
+    for (int i = tid; i < L.mtiles * L.ntiles; i += nth) tiles[i] = 0;
+    int* token = reinterpret_cast<int*>(g.scratch + L.token);
+    float* weight = reinterpret_cast<float*>(g.scratch + L.weight);
+    for (int r = tid; r < g.m; r += nth) {
+        token[r] = g.rows ? g.rows[r] : r;
+        weight[r] = g.scale ? g.scale[r] : 1.f;
+    }
+    const int lane = threadIdx.x & 31;
+    const int nblk = g.k >> 7;
+    uint8_t* img = reinterpret_cast<uint8_t*>(g.scratch + L.img);
+    const int warps = nth >> 5;
+    for (int task = tid >> 5; task < g.m * nblk; task += warps) {
+        const int r = task / nblk, b = task - r * nblk;
+        __half h[4];
+        rotate_block(g.x + (size_t) r * g.x_stride + b * 128, g.suh ? g.suh + b * 128 : nullptr, lane, h);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<__half*>(img + tc_image_offset(L.xt_rows, r, b * 128 + lane + 32 * i)) = h[i];
+    }
+}
+
+}  // namespace exl3b200
+
+extern "C" size_t exl3b200_gemm_combine_scratch_size(int m, int k, int n)
+{
+    if (m < 1 || k <= 0 || n <= 0 || k % 128 || n % 128) return 0;
+    return gc_layout(m, k, n).bytes;
+}
+
+extern "C" int exl3b200_gemm_combine(const void* x, long long x_stride, int m, int k, const void* trellis, int n,
+                                     int K, int cb, const void* suh, const void* svh, float* out,
+                                     long long out_stride, const int* out_rows, const float* out_scale, int flags,
+                                     void* scratch, size_t scratch_bytes, void* stream)
+{
+    if (!x || !trellis || !svh || !out || !scratch) return kErrNullPointer;
+    if (K < 2 || K > 4) return kErrBadBits;
+    if (cb < 0 || cb > 2) return kErrBadCodebook;
+    if (m < 1 || k <= 0 || n <= 0 || k % 128 || n % 128 || x_stride < k || out_stride < n) return kErrBadShape;
+    const bool pre_rotated = (flags & EXL3B200_FLAG_INPUT_ROTATED) != 0;
+    if (!pre_rotated && !suh) return kErrNullPointer;
+    if (((uintptr_t) x & 1) || ((uintptr_t) trellis & 15) || ((uintptr_t) svh & 15) || ((uintptr_t) scratch & 255) ||
+        ((uintptr_t) out & 15) || (out_stride & 3))
+        return kErrUnaligned;
+    const GcLayout L = gc_layout(m, k, n);
+    if (scratch_bytes < L.bytes) return kErrWorkspace;
+    if ((long long) L.mtiles * L.ntiles > 0x7fffffffLL) return kErrBadShape;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    char* sc = reinterpret_cast<char*>(scratch);
+    GcArgs g;
+    g.x = reinterpret_cast<const __half*>(x);
+    g.x_stride = x_stride;
+    g.suh = pre_rotated ? nullptr : reinterpret_cast<const __half*>(suh);
+    g.rows = out_rows;
+    g.scale = out_scale;
+    g.trellis = reinterpret_cast<const uint8_t*>(trellis);
+    g.svh = reinterpret_cast<const __half*>(svh);
+    g.scratch = sc;
+    g.L = L;
+    g.m = m;
+    g.k = k;
+    void* args[] = {&g};
+    const int grid = std::min((m * (k / 128) + 7) / 8, 4 * tc_device_sms());
+    int rc = tm_launch((const void*) exl3_gc_setup_kernel, grid, 256, true, st, args);
+    if (rc != kOk) return rc;
+    TcGroupedCall c = {};
+    c.xt_rows = L.xt_rows;
+    c.probs = reinterpret_cast<const TcProblem*>(sc + L.prob);
+    c.tile_prob = reinterpret_cast<const int*>(sc + L.tiles);
+    c.dev_tiles = reinterpret_cast<const int*>(sc + L.tot);
+    c.dev_tile_base = nullptr;
+    c.k = k;
+    c.n = n;
+    c.out = out;
+    c.out_stride = out_stride;
+    c.slot_token = reinterpret_cast<const int*>(sc + L.token);
+    c.slot_weight = reinterpret_cast<const float*>(sc + L.weight);
+    c.mode = kTcGroupedCombine;
+    return tc_grouped_matmul(c, K, cb, st);
 }

@@ -91,6 +91,9 @@ SIGNATURES = {
     "exl3b200_moe_tc_scratch_size": (_sz, [_i, _i, _i, _i, _i]),
     "exl3b200_moe_tc": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                              _i, _i, _i, ctypes.c_float, _vp, _ll, _i, _i, _vp, _sz, _vp]),
+    "exl3b200_gemm_combine_scratch_size": (_sz, [_i, _i, _i]),
+    "exl3b200_gemm_combine": (_i, [_vp, _ll, _i, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _ll, _vp, _vp, _i, _vp, _sz,
+                                   _vp]),
     "exl3b200_read_ranges": (_i, [_i, _vp, _vp, _vp, _i, _i, _vp, _sz, _i, _i, _vp]),
     "exl3b200_moe_state_size": (_sz, [_i, _i, _i, _i]),
     "exl3b200_moe_scratch_size": (_sz, [_i, _i, _i, _i]),

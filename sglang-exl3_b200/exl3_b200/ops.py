@@ -350,8 +350,11 @@ def matmul_multi(x: torch.Tensor, linears, K: int, cb: int, outs=None,
 def matmul_combine(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], svh: torch.Tensor,
                    K: int, cb: int, out: torch.Tensor, rows: torch.Tensor, scale: Optional[torch.Tensor] = None,
                    input_rotated: bool = False) -> torch.Tensor:
-    """``out[rows[r]] += scale[r] * (x[r] @ W)`` (fp32 out; rows int32, scale fp32;
-    rows of one 16-row chunk must be distinct)."""
+    """``out[rows[r]] += scale[r] * (x[r] @ W)`` (fp32 out; rows int32, scale fp32).
+
+    Up to 16 rows: the small-M kernel (rows must be distinct).  More: one
+    tensor-core launch that decodes the codes once per 256 rows and adds with
+    atomics (repeated rows add up; out 16-byte aligned, row stride a multiple of 4)."""
     x2 = x.reshape(-1, x.shape[-1])
     if x2.stride(-1) != 1 or (x2.stride(0) % 2):
         x2 = x2.contiguous()
@@ -365,6 +368,16 @@ def matmul_combine(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.T
     n = trellis.size(1) * 16
     L = _lib.lib()
     flags = _lib.FLAG_INPUT_ROTATED if input_rotated else 0
+    if m > _lib.GEMV_MAX_M and out.data_ptr() % 16 == 0 and out.stride(0) % 4 == 0:
+        with torch.cuda.device(dev):
+            scratch = workspace.scratch_buffer(dev, L.exl3b200_gemm_combine_scratch_size(m, k, n))
+            st = L.exl3b200_gemm_combine(
+                x2.data_ptr(), x2.stride(0), m, k, trellis.data_ptr(), n, K, cb,
+                suh.data_ptr() if suh is not None else None, svh.data_ptr(), out.data_ptr(), out.stride(0),
+                rows.data_ptr(), scale.data_ptr() if scale is not None else None, flags, scratch.data_ptr(),
+                scratch.numel(), _stream_ptr(dev))
+        _lib.check(st, "exl3b200_gemm_combine")
+        return out
     for r0 in range(0, m, _lib.GEMV_MAX_M):
         r1 = min(m, r0 + _lib.GEMV_MAX_M)
         with torch.cuda.device(dev):

@@ -119,3 +119,19 @@ def test_row_shard_keeps_hadamard_blocks():
     with pytest.raises(ValueError):
         L.shard_exl3_row(tr, "trellis", 0, 2)
     assert L.shard_exl3_row(torch.zeros((32, 8, 32), dtype=torch.int16), "trellis", 1, 2).shape == (16, 8, 32)
+
+
+def test_moe_path_selection(monkeypatch):
+    """Host-side choice between the small-M and the tensor-core MoE pipelines."""
+    from exl3_b200 import moe
+
+    monkeypatch.delenv("EXL3_B200_MOE_PATH", raising=False)
+    assert moe.moe_path(1, 8, 288) == "small"                 # decode: ~0 rows per expert
+    assert moe.moe_path(320, 8, 128) == "tc"                  # config 5 verify, batch 64: 20 rows
+    assert moe.moe_path(80, 8, 128) == "small"                # config 5 verify, batch 16: 5 rows
+    assert moe.moe_path(512, 8, 288) == "tc"                  # config 3, T = 512: 14 rows
+    assert moe.moe_path(12, 1, 1) == "tc" and moe.moe_path(11, 1, 1) == "small"
+    monkeypatch.setenv("EXL3_B200_MOE_PATH", "small")
+    assert moe.moe_path(320, 8, 128) == "small"
+    monkeypatch.setenv("EXL3_B200_MOE_PATH", "tc")
+    assert moe.moe_path(1, 8, 288) == "tc"

@@ -228,3 +228,26 @@ def test_moe_tc_matches_small_at_config5_width(cuda_device, K, cb):
     yt = moe.moe_forward(x, ids, w, tabs, K, K, K, cb, I, path="tc")
     assert torch.isfinite(ys).all() and torch.isfinite(yt).all()
     assert O.normwise_rel_err(yt.cpu().numpy(), ys.cpu().numpy().astype(np.float64)) < TOL_MOE
+
+
+@pytest.mark.parametrize("K,cb,rotated", [(4, 1, True), (3, 0, False), (2, 2, True)])
+def test_matmul_combine_tensor_core(cuda_device, K, cb, rotated):
+    """More than 16 rows: one tensor-core launch (exl3b200_gemm_combine); 300 rows =
+    two 256-row tiles, output rows repeated (they add up), with and without scales."""
+    rng = np.random.default_rng(120 + K)
+    M, k, n, T = 300, 256, 384, 40
+    tr, su, sv = _lin(rng, k, n, K)
+    x = rng.standard_normal((M, k)).astype(np.float16)
+    a = O.input_transform(x, su) if rotated else x
+    ref = O.gemv_ref(x, tr, su, sv, K, cb)
+    tok = rng.integers(0, T, size=M).astype(np.int32)
+    for scaled in (True, False):
+        rw = rng.uniform(0.1, 1.0, size=M).astype(np.float32)
+        acc = torch.zeros((T, n), dtype=torch.float32, device=cuda_device)
+        ops.matmul_combine(_t(a, cuda_device), _t(tr, cuda_device), None if rotated else _t(su, cuda_device),
+                           _t(sv, cuda_device), K, cb, acc, _t(tok, cuda_device),
+                           _t(rw, cuda_device) if scaled else None, input_rotated=rotated)
+        exp = np.zeros((T, n), dtype=np.float64)
+        for i in range(M):
+            exp[tok[i]] += (float(rw[i]) if scaled else 1.0) * ref[i]
+        assert O.normwise_rel_err(acc.cpu().numpy(), exp) < TOL
