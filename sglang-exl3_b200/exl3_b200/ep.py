@@ -4,17 +4,20 @@ MoE pipeline.
 The experts of a layer are split evenly over the ranks of a process group
 (rank r owns global experts ``[r*E/W, (r+1)*E/W)``: the reference's EP layout,
 whose id mapping is ``map_topk_to_local`` / ``_get_expert_map``,
-``src/sglang_exl3/exl3.py:485-509``).  One MoE call:
+``src/sglang_exl3/exl3.py:485-509``).  Two exchange modes:
 
-1. every token goes once to each rank that owns at least one of its top-k experts,
-   with its top-k ids rewritten to that rank's local ids (-1 where another rank
-   owns the expert) and its routing weights;
-2. the per-destination row counts are exchanged (``all_to_all_single`` on the
-   counts; the host reads them to size the variable exchanges), then the token
-   rows (fp16) and the packed ids/weights (int32);
-3. each rank runs its local experts on what it received (``local_fn``: the fused
-   device MoE pipeline, which skips id -1) into fp32 rows;
-4. those rows go back with the reverse exchange and are summed per token.
+* static (default): every token row goes to every rank with its top-k ids
+  rewritten to that rank's local ids (-1 where another rank owns the expert) and
+  its routing weights, so every ``all_to_all_single`` has equal splits of T rows.
+  Nothing is read on the host: a call is stream-ordered end to end (NCCL in the
+  stream), with no host synchronisation.  Each rank runs its local experts
+  on the W*T received rows (``local_fn``: the fused device MoE pipeline, which
+  skips id -1, so rows with no local expert cost routing only), the fp32 results
+  come back with the reverse exchange and the W contributions are summed per
+  token.  The price is bandwidth: W*T rows of H fp16 out and fp32 back per rank.
+* variable (``static=False``): a token goes only to the ranks that own one of its
+  experts; the per-destination counts are exchanged first and read on the host to
+  size the row exchanges (one host synchronisation per call).
 
 Collectives are ``torch.distributed`` calls, so the module runs over NCCL on
 GPUs and over gloo on CPU (the tests use gloo with a host-side expert function).
@@ -33,15 +36,53 @@ LocalFn = Callable[[torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
 class ExpertParallelMoE:
     """Dispatch/combine for ``n_experts`` experts over ``world`` ranks."""
 
-    def __init__(self, n_experts: int, world: int, rank: int, group=None):
+    def __init__(self, n_experts: int, world: int, rank: int, group=None, static: bool = True):
         if world < 1 or n_experts % world:
             raise ValueError(f"{n_experts} experts do not split evenly over {world} ranks")
         self.n_experts = n_experts
         self.world = world
         self.rank = rank
         self.group = group
+        self.static = static
         self.per_rank = n_experts // world
-        self.last_counts: Optional[tuple] = None  # (send, recv) row counts of the last call
+        self.last_counts: Optional[tuple] = None  # variable mode: (send, recv) row counts of the last call
+
+    def local_ids(self, topk_ids: torch.Tensor) -> torch.Tensor:
+        """``[W, T, k]`` int32: each rank's view of the ids (local id, or -1 when the
+        expert is invalid or lives on another rank)."""
+        ids = topk_ids.to(torch.long)
+        valid = (ids >= 0) & (ids < self.n_experts)
+        owner = torch.where(valid, ids // self.per_rank, torch.full_like(ids, -1))
+        ranks = torch.arange(self.world, device=ids.device).view(-1, 1, 1)
+        local = ids.unsqueeze(0) - ranks * self.per_rank
+        return torch.where(owner.unsqueeze(0) == ranks, local, torch.full_like(local, -1)).to(torch.int32)
+
+    def _static(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, local_fn: LocalFn) -> torch.Tensor:
+        T, H = x.shape
+        k = ids.size(1)
+        W = self.world
+        meta = torch.cat([self.local_ids(ids), w.unsqueeze(0).expand(W, T, k).contiguous().view(torch.int32)],
+                         dim=2).contiguous()  # [W, T, 2k]
+        send_x = x.unsqueeze(0).expand(W, T, H).contiguous()
+        recv_x = torch.empty_like(send_x)
+        recv_meta = torch.empty_like(meta)
+        dist.all_to_all_single(recv_x, send_x, group=self.group)
+        dist.all_to_all_single(recv_meta, meta, group=self.group)
+        rows = W * T
+        recv_ids = recv_meta[:, :, :k].reshape(rows, k)
+        recv_w = recv_meta[:, :, k:].reshape(rows, k).contiguous().view(torch.float32)
+        # rows with a local expert first (stable, on the device): when local_fn works in
+        # chunks of rows, the chunks past them route no pair and stream no codes
+        order = torch.argsort((recv_ids < 0).all(1).to(torch.int8), stable=True)
+        y_c = local_fn(recv_x.view(rows, H).index_select(0, order), recv_ids.index_select(0, order).contiguous(),
+                       recv_w.index_select(0, order).contiguous()).to(torch.float32)
+        if y_c.shape != (rows, H):
+            raise RuntimeError("local expert function must return [rows, hidden]")
+        y = torch.empty_like(y_c)
+        y.index_copy_(0, order, y_c)
+        back = torch.empty_like(y)
+        dist.all_to_all_single(back, y, group=self.group)
+        return back.view(W, T, H).sum(0)
 
     def plan(self, topk_ids: torch.Tensor):
         """Destination rows of a call: token index per send row (grouped by
@@ -67,6 +108,10 @@ class ExpertParallelMoE:
         k = topk_ids.shape[-1]
         ids = topk_ids.reshape(T, k).to(torch.long)
         w = topk_weights.reshape(T, k).to(torch.float32)
+        if self.static:
+            if T == 0:
+                return torch.zeros((0, H), dtype=torch.float32, device=x.device)
+            return self._static(x, ids, w, local_fn)
         send_tok, send_rank, dest, counts = self.plan(ids)
 
         # rows to send: the token, its ids local to the destination (-1 elsewhere), weights

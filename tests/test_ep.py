@@ -45,12 +45,12 @@ def _cases():
     return [(x, ids, w), (x[:6], only_low, w[:6]), (x[:0], ids[:0], w[:0])]
 
 
-def _worker(rank, world, port, results):
+def _worker(rank, world, port, results, static):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        ep = ExpertParallelMoE(E, world, rank)
+        ep = ExpertParallelMoE(E, world, rank, static=static)
 
         def local_fn(xr, lids, lw):
             out = torch.zeros(xr.shape, dtype=torch.float32)
@@ -64,7 +64,7 @@ def _worker(rank, world, port, results):
         for ci, (x, ids, w) in enumerate(_cases()):
             got = ep(x, ids, w, local_fn)
             torch.testing.assert_close(got, _reference(x, ids, w), rtol=1e-5, atol=1e-5)
-            if ci == 1 and rank == 1:
+            if ci == 1 and rank == 1 and not static:
                 results.put(("recv_rank1_case1", ep.last_counts[1]))
         results.put(("ok", rank))
     finally:
@@ -77,13 +77,27 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_ep_dispatch_combine_two_ranks():
+@pytest.mark.parametrize("static", [True, False])
+def test_ep_dispatch_combine_two_ranks(static):
+    """Both exchange modes: fixed-size (no host read) and variable-size."""
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
-    mp.start_processes(_worker, args=(2, _free_port(), results), nprocs=2, join=True, start_method="spawn")
-    got = [results.get(timeout=30) for _ in range(3)]
+    mp.start_processes(_worker, args=(2, _free_port(), results, static), nprocs=2, join=True, start_method="spawn")
+    got = [results.get(timeout=30) for _ in range(2 if static else 3)]
     assert sorted(r for k, r in got if k == "ok") == [0, 1]
-    assert [v for k, v in got if k == "recv_rank1_case1"] == [(0, 0)]
+    if not static:
+        assert [v for k, v in got if k == "recv_rank1_case1"] == [(0, 0)]
+
+
+def test_ep_local_ids_per_rank():
+    ep = ExpertParallelMoE(8, 4, 0)
+    ids = torch.tensor([[0, 7, 6], [3, 2, 2], [-1, 8, 5]])
+    lid = ep.local_ids(ids)
+    assert lid.shape == (4, 3, 3)
+    assert lid[0].tolist() == [[0, -1, -1], [-1, -1, -1], [-1, -1, -1]]
+    assert lid[1].tolist() == [[-1, -1, -1], [1, 0, 0], [-1, -1, -1]]
+    assert lid[2].tolist() == [[-1, -1, -1], [-1, -1, -1], [-1, -1, 1]]
+    assert lid[3].tolist() == [[-1, 1, 0], [-1, -1, -1], [-1, -1, -1]]
 
 
 def test_ep_plan_groups_rows_by_destination():

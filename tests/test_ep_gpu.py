@@ -50,11 +50,13 @@ def _worker(rank, world, port):
         w = torch.rand(T, TOPK, device=dev, generator=g)
         ref = M.moe_forward(x, ids.to(torch.int32), w, tables(0, E), K, K, K, 0, I)
         per = E // world
-        ep = ExpertParallelMoE(E, world, rank)
-        got = ep(x, ids, w, exl3_local_experts(tables(rank * per, (rank + 1) * per), K, K, K, 0, I))
-        torch.cuda.synchronize()
-        err = ((got - ref).abs().max() / ref.abs().max()).item()
-        assert err < 2e-3, err
+        local = exl3_local_experts(tables(rank * per, (rank + 1) * per), K, K, K, 0, I)
+        for static in (True, False):
+            ep = ExpertParallelMoE(E, world, rank, static=static)
+            got = ep(x, ids, w, local)
+            torch.cuda.synchronize()
+            err = ((got - ref).abs().max() / ref.abs().max()).item()
+            assert err < 2e-3, (static, err)
     finally:
         dist.destroy_process_group()
 
