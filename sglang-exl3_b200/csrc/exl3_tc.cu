@@ -45,6 +45,16 @@
 // out raises the CTA's abort flag and the library's sticky device status; every
 // role then leaves its loop, waits (bounded) for its own copies and MMAs in
 // flight, and the CTA frees its TMEM and exits.
+//
+// The same kernel runs grouped launches (template MODE 1 and 2, used by the
+// routed-MoE pipeline and the routed combine in exl3_tc_moe.cu): many problems
+// with shared k, n, K and codebook, whose tile list, problem table and tile
+// count an earlier kernel wrote to device memory.  Every role looks up the
+// problem of a segment's tile; activation rows come from the problem's
+// k-chunk-major image, one bulk copy of its (8-rounded) rows per 128-row
+// accumulator and 64-k chunk; the epilogue stores fp32 rows (MODE 1; split tiles
+// add into zeroed rows) or adds weight * y into out[token] (MODE 2).  No slots
+// and no finish kernel.
 #include <algorithm>
 
 #include "exl3_common.cuh"
@@ -72,14 +82,14 @@ constexpr unsigned long long kTcTimeoutNs = 1000000000ull;
 
 __device__ int g_exl3_device_status = 0;  // sticky: first device-side error code
 
-template <int K, int SA = kTcStageA, int ST = kTcStageT>
+template <int K>
 struct TcSmem {
-    static constexpr int kBars = 2 * SA + 2 * ST + 2 * kTcStageB + 2;
+    static constexpr int kBars = 2 * kTcStageA + 2 * kTcStageT + 2 * kTcStageB + 2;
     static constexpr uint32_t kTChunk = 4u * 16u * 32u * K;  // codes of one stage at 256 columns
     static constexpr uint32_t kA = 0;
-    static constexpr uint32_t kB = kA + SA * 2 * kTcABlock;
+    static constexpr uint32_t kB = kA + kTcStageA * 2 * kTcABlock;
     static constexpr uint32_t kT = kB + kTcStageB * kTcBStage;
-    static constexpr uint32_t kBar = kT + ST * kTChunk;
+    static constexpr uint32_t kBar = kT + kTcStageT * kTChunk;
     static constexpr uint32_t kMisc = kBar + 8 * kBars;
     static constexpr uint32_t kBytes = kMisc + 16;
     static constexpr uint32_t kLaunchBytes = kBytes + 1024;  // room to align the base to 1024
@@ -617,8 +627,8 @@ __device__ __forceinline__ int tc_cta_of(long long iters, int grid, long long it
 template <int K, int CB, int MODE>
 __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __grid_constant__ TcArgs a)
 {
-    constexpr int SA = kTcStageA, ST = kTcStageT;
-    using L = TcSmem<K, SA, ST>;
+    constexpr int SA = kTcStageA, ST = kTcStageT;  // activation and code ring depths
+    using L = TcSmem<K>;
     static_assert(L::kLaunchBytes <= 232448, "shared memory per CTA");
     extern __shared__ uint8_t tc_smem_raw[];
     const uint32_t raw = smem_u32(tc_smem_raw);

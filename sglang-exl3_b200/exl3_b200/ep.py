@@ -10,7 +10,7 @@ whose id mapping is ``map_topk_to_local`` / ``_get_expert_map``,
   rewritten to that rank's local ids (-1 where another rank owns the expert) and
   its routing weights, so every ``all_to_all_single`` has equal splits of T rows.
   Nothing is read on the host: a call is stream-ordered end to end (NCCL in the
-  stream), with no host synchronisation.  Each rank runs its local experts
+  stream) and can be captured in a CUDA graph.  Each rank runs its local experts
   on the W*T received rows (``local_fn``: the fused device MoE pipeline, which
   skips id -1, so rows with no local expert cost routing only), the fp32 results
   come back with the reverse exchange and the W contributions are summed per

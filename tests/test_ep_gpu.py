@@ -5,6 +5,7 @@ runs the whole layer alone as the reference; outputs must agree to fp32
 accumulation tolerance.  Skipped unless two GPUs are visible.
 """
 
+import datetime
 import os
 import socket
 
@@ -23,7 +24,8 @@ def _worker(rank, world, port):
     os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
     try:
         from exl3_b200 import moe as M
         from exl3_b200.ep import ExpertParallelMoE, exl3_local_experts
@@ -57,6 +59,31 @@ def _worker(rank, world, port):
             torch.cuda.synchronize()
             err = ((got - ref).abs().max() / ref.abs().max()).item()
             assert err < 2e-3, (static, err)
+
+        # the static exchange has no host read: capture the whole EP layer in a CUDA
+        # graph, replay it with new routing (same on both ranks: same seed)
+        ep = ExpertParallelMoE(E, world, rank, static=True)
+        ids_buf, w_buf = ids.clone(), w.clone()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                ep(x, ids_buf, w_buf, local)  # workspaces of the capture stream
+        torch.cuda.current_stream(dev).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            out_g = ep(x, ids_buf, w_buf, local)
+        try:
+            for trial in range(2):
+                new_ids = torch.randint(0, E, (T, TOPK), device=dev, generator=g)
+                ids_buf.copy_(new_ids)
+                graph.replay()
+                torch.cuda.synchronize()
+                ref2 = M.moe_forward(x, new_ids.to(torch.int32), w, tables(0, E), K, K, K, 0, I)
+                err = ((out_g - ref2).abs().max() / ref2.abs().max()).item()
+                assert err < 2e-3, ("graph", trial, err)
+        finally:
+            del graph  # a graph holding NCCL work goes before the process group
     finally:
         dist.destroy_process_group()
 
