@@ -236,6 +236,9 @@ __global__ __launch_bounds__(kGvThreads, MINB) void exl3_gv_matmul_kernel(const 
                 const uint32_t aB[4] = {pv[2], pv[6], pv[3], pv[7]};  // k = 2c+8, 2c+9
 #pragma unroll
                 for (int q = 0; q < TG; ++q) {
+                    // a row group past the problem's rows would only add zeros (its
+                    // activations are zero): skip its MMAs (warp-uniform per problem)
+                    if (q > 0 && 8 * q >= m) break;
                     mma_16816(aA, xb[q][0].x, xb[q][0].y, acc[t][q]);
                     mma_16816(aB, xb[q][1].x, xb[q][1].y, acc[t][q]);
                 }
