@@ -21,6 +21,7 @@ import json
 import logging
 import os
 import struct
+import threading
 import time
 from dataclasses import dataclass
 from typing import Any, Dict, Iterator, List, Optional, Sequence, Tuple, Union
@@ -202,10 +203,12 @@ def _numel(shape: Sequence[int]) -> int:
 
 
 class _Staging:
-    """Pinned host staging buffer, one slot per reader thread, kept across calls."""
+    """Pinned host staging buffer, one slot per reader thread, kept across calls.
+    ``lock`` serialises the device reads that use it."""
 
     def __init__(self) -> None:
         self.buf: Optional[torch.Tensor] = None
+        self.lock = threading.Lock()
 
     def get(self, threads: int) -> torch.Tensor:
         need = threads * STAGING_SLOT_BYTES
@@ -248,13 +251,15 @@ def _read_into(fd: int, jobs: List[Tuple[torch.Tensor, List[Tuple[int, int]]]], 
     c_size = (ctypes.c_longlong * count)(*sizes)
     c_dst = (ctypes.c_void_p * count)(*dsts)
     threads = max(1, min(64, int(threads)))
-    staging, staging_bytes, stream = None, 0, None
+    L = _lib.lib()
     if on_device:
-        buf = _staging.get(threads)
-        staging, staging_bytes = buf.data_ptr(), buf.numel()
-        stream = torch.cuda.current_stream().cuda_stream
-    rc = _lib.lib().exl3b200_read_ranges(fd, c_off, c_size, c_dst, count, 1 if on_device else 0, staging,
-                                         staging_bytes, threads, 1 if drop_cache else 0, stream)
+        with _staging.lock:
+            buf = _staging.get(threads)
+            rc = L.exl3b200_read_ranges(fd, c_off, c_size, c_dst, count, 1, buf.data_ptr(), buf.numel(), threads,
+                                        1 if drop_cache else 0, torch.cuda.current_stream().cuda_stream)
+    else:
+        rc = L.exl3b200_read_ranges(fd, c_off, c_size, c_dst, count, 0, None, 0, threads, 1 if drop_cache else 0,
+                                    None)
     if rc == _lib.EIO:
         raise IOError(f"[EXL3 loader] short read: the file ends inside a tensor's byte range")
     _lib.check(rc, "exl3b200_read_ranges")

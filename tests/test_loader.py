@@ -122,3 +122,25 @@ def test_narrowed_read_matches_slice(tmp_path, narrow):
         LD.read_safetensors_tensor(path, "m.trellis", narrow=(1, 5, 11))
     with pytest.raises(KeyError):
         LD.read_safetensors_tensor(path, "nope")
+
+
+def test_narrow_ranges_property(tmp_path):
+    """Random shapes, dtypes and slices: the ranges read equal torch.narrow of the tensor."""
+    from hypothesis import given, settings, strategies as st
+
+    path = str(tmp_path / "p.safetensors")
+
+    @settings(max_examples=60, deadline=None)
+    @given(shape=st.lists(st.integers(1, 6), min_size=1, max_size=4),
+           dtype=st.sampled_from([torch.int16, torch.float32, torch.uint8, torch.bfloat16]),
+           data=st.data())
+    def check(shape, dtype, data):
+        t = (torch.arange(int(torch.tensor(shape).prod())) % 251).to(dtype).reshape(shape)
+        save_file({"t": t}, path)
+        dim = data.draw(st.integers(0, len(shape) - 1))
+        start = data.draw(st.integers(0, shape[dim]))
+        stop = data.draw(st.integers(start, shape[dim]))
+        got = LD.read_safetensors_tensor(path, "t", narrow=(dim, start, stop))
+        assert torch.equal(got, t.narrow(dim, start, stop - start))
+
+    check()
