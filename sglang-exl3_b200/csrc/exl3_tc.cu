@@ -346,34 +346,47 @@ __device__ __forceinline__ void tc_decode_lane(uint32_t wa, uint32_t wb, int shi
     }
 }
 
+__device__ __forceinline__ uint32_t lds_u32(uint32_t addr)
+{
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void sts_u32(uint32_t addr, uint32_t v)
+{
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
 // One warp's share of a stage: NB16 = 16 n-tiles (256 columns): n-tile dw, k-tiles
-// 0..3; NB16 = 8 (128 columns): n-tile dw % 8, k-tiles 2 (dw / 8) + {0, 1}.
+// 0..3; NB16 = 8 (128 columns): n-tile dw % 8, k-tiles 2 (dw / 8) + {0, 1}.  tch and
+// bst are shared-memory addresses of the stage's codes and B operand (explicit
+// shared-space loads and stores).
 template <int K, int CB, int NB16>
-__device__ __forceinline__ void tc_decode_stage(const uint8_t* __restrict__ tch, uint8_t* __restrict__ bst, int dw,
-                                                int lane, const LaneWords& lw)
+__device__ __forceinline__ void tc_decode_stage(uint32_t tch, uint32_t bst, int dw, int lane, const LaneWords& lw)
 {
     constexpr int T = NB16 / 4;
     const int ntl = NB16 == 16 ? dw : (dw & 7);
     const int kt0 = NB16 == 16 ? 0 : 2 * (dw >> 3);
-    const uint32_t* tw = reinterpret_cast<const uint32_t*>(tch + (kt0 * NB16 + ntl) * 32 * K);
+    const uint32_t tw = tch + (uint32_t) ((kt0 * NB16 + ntl) * 32 * K);
     uint32_t wa[T], wb[T];
 #pragma unroll
     for (int i = 0; i < T; ++i) {
-        wa[i] = tw[i * NB16 * 8 * K + lw.wa];
-        wb[i] = tw[i * NB16 * 8 * K + lw.wb];
+        wa[i] = lds_u32(tw + 4u * (uint32_t) (i * NB16 * 8 * K + lw.wa));
+        wb[i] = lds_u32(tw + 4u * (uint32_t) (i * NB16 * 8 * K + lw.wb));
     }
     const int sw = lane >> 2;
-    uint8_t* rowp = bst + ntl * 16 * 128 + (lane >> 2) * 128 + 4 * (lane & 3);
+    const uint32_t rowp = bst + (uint32_t) (ntl * 16 * 128 + (lane >> 2) * 128 + 4 * (lane & 3));
 #pragma unroll
     for (int i = 0; i < T; ++i) {
         uint32_t h2[4];
         tc_decode_lane<K, CB>(wa[i], wb[i], lw.shift7, h2);
         const int kt = kt0 + i;
-        const int c_lo = ((2 * kt) ^ sw) << 4, c_hi = ((2 * kt + 1) ^ sw) << 4;
-        *reinterpret_cast<uint32_t*>(rowp + c_lo) = h2[0];
-        *reinterpret_cast<uint32_t*>(rowp + c_hi) = h2[1];
-        *reinterpret_cast<uint32_t*>(rowp + 1024 + c_lo) = h2[2];
-        *reinterpret_cast<uint32_t*>(rowp + 1024 + c_hi) = h2[3];
+        const uint32_t c_lo = (uint32_t) (((2 * kt) ^ sw) << 4), c_hi = (uint32_t) (((2 * kt + 1) ^ sw) << 4);
+        sts_u32(rowp + c_lo, h2[0]);
+        sts_u32(rowp + c_hi, h2[1]);
+        sts_u32(rowp + 1024 + c_lo, h2[2]);
+        sts_u32(rowp + 1024 + c_hi, h2[3]);
     }
 }
 
@@ -832,8 +845,8 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                         ok = false;
                         break;
                     }
-                    const uint8_t* tch = gbase + L::kT + st * L::kTChunk;
-                    uint8_t* bst = gbase + L::kB + sb * kTcBStage;
+                    const uint32_t tch = sT + st * L::kTChunk;
+                    const uint32_t bst = sB + sb * kTcBStage;
                     if (bn == kTcCols) tc_decode_stage<K, CB, 16>(tch, bst, dw, lane, lw);
                     else tc_decode_stage<K, CB, 8>(tch, bst, dw, lane, lw);
                     fence_proxy_async_smem();
