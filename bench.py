@@ -642,7 +642,8 @@ def run_moe(args, world, rank, local, device):
             "config": {"workload": name, "experts": E, "topk": topk, "hidden": H,
                        "intermediate": I, "bpw": K, "codebook": "3INST", "shared_expert": "none" if c5 else "4 bpw",
                        "parallelism": f"ep{world}" if world > 1 else "single GPU",
-                       "experts_touched": touched, "moe_path": M.moe_path(T, topk, el),
+                       "experts_touched": touched, "moe_path": M.moe_path(world * T, topk, el),
+                       "ep_exchange": "static (equal splits, no host read)" if world > 1 else "none",
                        "l2": "expert codes 2.36 MB each; time includes routing (softmax/top-k) and the shared expert"},
             "exl3_gbs_per_rank": gbs,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
@@ -650,9 +651,12 @@ def run_moe(args, world, rank, local, device):
                          "kernel": "whole MoE layer per rank (touched experts' codes / step time)"},
             "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": px.numel() * 2, "d2h_bytes_per_step": py.numel() * 4},
-            # routed layer: 6 launches (small-M pipeline) or 5 (tensor-core pipeline, equal K);
-            # config 3's shared expert: 3 (gate+up) + 3 (down)
-            "gpu_launches": args.steps * ((5 if M.moe_path(T, topk, el) == "tc" else 6) + (0 if c5 else 6)),
+            # routed layer: 6 launches (small-M pipeline) or 5 (tensor-core pipeline, equal K) per
+            # call of at most 8192 (token, slot) pairs; under EP a rank runs world x T rows (static
+            # exchange); config 3's shared expert: 3 (gate+up) + 3 (down)
+            "gpu_launches": args.steps * (-(-(world * T) // (M.MOE_MAX_PAIRS // topk))
+                                          * (5 if M.moe_path(world * T, topk, el) == "tc" else 6)
+                                          + (0 if c5 else 6)),
             "clocks": clk.summary()}
     return finish(line, args, world)
 
