@@ -248,3 +248,30 @@ def test_sidecar_into_real_linear_method():
     assert route_exl3_sidecar(params, "m.up_proj.trellis", u)
     packs = layer._exl3_lin_packs
     assert torch.equal(packs[0]["trellis"].cpu(), g) and torch.equal(packs[1]["trellis"].cpu(), u)
+
+
+def test_non_routed_modules_bf16_and_mtp_source():
+    cfg = EXL3Config.from_config({
+        "quant_method": "exl3", "bits": 2, "scope": "glm53_routed_experts_only",
+        "non_routed_exl3": {"bits": 4, "modules": ["self_attn.o_proj", "mlp.shared_experts.down_proj"],
+                            "layer_bits": {"self_attn.o_proj": 3}, "bf16_modules": ["self_attn.q_proj"]},
+        "mtp_experts": "source", "mtp_experts_start_layer": 40})
+    o = cfg.get_quant_method(RowParallelLinear(), "model.layers.1.self_attn.o_proj")
+    assert isinstance(o, L.EXL3LinearMethod) and o.bits == 3           # per-module bits
+    d = cfg.get_quant_method(RowParallelLinear(), "model.layers.1.mlp.shared_experts.down_proj")
+    assert isinstance(d, L.EXL3LinearMethod) and d.bits == 4           # non-routed default bits
+    assert not isinstance(cfg.get_quant_method(ColumnParallelLinear(), "model.layers.1.self_attn.q_proj"),
+                          L.EXL3LinearMethod)                          # bf16 module
+    assert isinstance(cfg.get_quant_method(FusedMoE(), "model.layers.39.mlp.experts"), L.EXL3MoEMethod)
+    # experts of layers >= mtp_experts_start_layer come from the source checkpoint's delegate
+    assert not isinstance(cfg.get_quant_method(FusedMoE(), "model.layers.40.mlp.experts"), L.EXL3MoEMethod)
+
+
+def test_tensor_parallel_linear_from_layer_class():
+    cfg = EXL3Config.from_config({"quant_method": "exl3", "bits": 4})
+    col = cfg.get_quant_method(ColumnParallelLinear(3, 4), "model.layers.0.self_attn.qkv_proj")
+    row = cfg.get_quant_method(RowParallelLinear(3, 4), "model.layers.0.self_attn.o_proj")
+    single = cfg.get_quant_method(ColumnParallelLinear(0, 1), "model.layers.0.self_attn.qkv_proj")
+    assert (col.parallel, col.tp_rank, col.tp_size) == ("column", 3, 4)
+    assert (row.parallel, row.tp_rank, row.tp_size) == ("row", 3, 4)
+    assert single.parallel == "none"
