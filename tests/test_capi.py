@@ -76,3 +76,51 @@ def test_missing_library_fails_loudly(monkeypatch):
     monkeypatch.setattr(_lib, "LIB_PATH", "/nonexistent/libexl3b200.so")
     with pytest.raises(_lib.Exl3LibraryError):
         _lib.lib()
+
+
+def test_tensor_core_moe_and_combine_validation_without_gpu():
+    """exl3b200_moe_tc / exl3b200_gemm_combine reject bad arguments before any CUDA call."""
+    import ctypes
+
+    L = _lib.lib()
+    f = 256  # never dereferenced
+    assert L.exl3b200_moe_tc_scratch_size(64, 8, 128, 4096, 1536) > 0
+    assert L.exl3b200_moe_tc_scratch_size(2048, 8, 128, 4096, 1536) == 0   # 16384 pairs > 8192
+    assert L.exl3b200_moe_tc_scratch_size(64, 8, 4096, 4096, 1536) == 0    # > 2048 experts
+    assert L.exl3b200_moe_tc_scratch_size(64, 8, 128, 4000, 1536) == 0     # hidden % 128
+    tabs = [f] * 9
+    ok = L.exl3b200_moe_tc_scratch_size(4, 2, 8, 256, 256)
+
+    def moe(**kw):
+        a = dict(x=f, xs=256, T=4, H=256, I=256, ids=f, w=f, topk=2, E=8, Kg=3, Ku=3, Kd=3, cb=0, out=4096,
+                 os=256, mt=4, sc=4096, scb=ok)
+        a.update(kw)
+        return L.exl3b200_moe_tc(a["x"], a["xs"], a["T"], a["H"], a["I"], a["ids"], a["w"], a["topk"], a["E"],
+                                 *tabs, a["Kg"], a["Ku"], a["Kd"], a["cb"], ctypes.c_float(0.0), a["out"], a["os"], 0,
+                                 a["mt"], a["sc"], a["scb"], None)
+
+    assert moe(x=None) == _lib.ENULL
+    assert moe(T=5) == _lib.EBADSHAPE        # tokens > max_tokens
+    assert moe(H=200) == _lib.EBADSHAPE
+    assert moe(Kd=5) == _lib.EBADBITS
+    assert moe(cb=3) == _lib.EBADCODEBOOK
+    assert moe(out=4100) == _lib.EUNALIGNED  # fp32 rows need 16-byte alignment
+    assert moe(os=258) == _lib.EUNALIGNED
+    assert moe(scb=ok - 1) == _lib.EWORKSPACE
+
+    assert L.exl3b200_gemm_combine_scratch_size(300, 256, 384) > 0
+    assert L.exl3b200_gemm_combine_scratch_size(0, 256, 384) == 0
+    g = dict(x=f, xs=256, m=40, k=256, tr=f, n=384, K=4, cb=1, suh=f, svh=f, out=4096, os=384, flags=0, sc=4096,
+             scb=L.exl3b200_gemm_combine_scratch_size(40, 256, 384))
+
+    def comb(**kw):
+        a = dict(g)
+        a.update(kw)
+        return L.exl3b200_gemm_combine(a["x"], a["xs"], a["m"], a["k"], a["tr"], a["n"], a["K"], a["cb"], a["suh"],
+                                       a["svh"], a["out"], a["os"], None, None, a["flags"], a["sc"], a["scb"], None)
+
+    assert comb(suh=None) == _lib.ENULL                     # suh needed unless the input is rotated
+    assert comb(n=300) == _lib.EBADSHAPE
+    assert comb(K=1) == _lib.EBADBITS
+    assert comb(svh=f + 8) == _lib.EUNALIGNED
+    assert comb(scb=0) == _lib.EWORKSPACE
