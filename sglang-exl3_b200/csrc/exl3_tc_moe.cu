@@ -422,7 +422,7 @@ extern "C" int exl3b200_moe_tc(const void* x, long long x_stride, int tokens, in
     if (rc != kOk) return rc;
     const int sms = tc_device_sms();
     const int pairs = tokens * topk;
-    const int in_grid = std::min((pairs * (hidden / 128) + 7) / 8, 4 * sms);
+    const int in_grid = std::min((pairs * (hidden / 128) + 7) / 8, 8 * sms);
     rc = tm_launch((const void*) exl3_tm_input_kernel, in_grid, 256, true, st, args);
     if (rc != kOk) return rc;
 
@@ -451,7 +451,7 @@ extern "C" int exl3b200_moe_tc(const void* x, long long x_stride, int tokens, in
     }
     if (rc != kOk) return rc;
 
-    const int sw_grid = std::min((pairs * (inter / 128) + 7) / 8, 4 * sms);
+    const int sw_grid = std::min((pairs * (inter / 128) + 7) / 8, 8 * sms);
     rc = tm_launch((const void*) exl3_tm_swiglu_kernel, sw_grid, 256, true, st, args);
     if (rc != kOk) return rc;
 
