@@ -308,6 +308,10 @@ def workload_scale(args):
     if args.workload == "mlp":
         H, I = 5120, 25600
         return H * 2 * I + I * H, args.batch, "rows/s"
+    if args.workload == "verify":
+        E, topk, H, I, R = 128, 8, 4096, 1536, 5 * args.batch
+        touched = E * (1.0 - (1.0 - topk / E) ** R)
+        return 48 * (touched * 3 * H * I + 2 * H * H + 2 * H * 512), R, "tok/s"
     if args.workload == "moe":
         if getattr(args, "moe", "c3") == "c5":
             E, topk, H, I, T = 128, 8, 4096, 1536, 5 * args.batch
@@ -394,6 +398,8 @@ def run_ours(args, world, rank, local):
         return run_mlp(args, world, rank, local, device)
     if args.workload == "moe":
         return run_moe(args, world, rank, local, device)
+    if args.workload == "verify":
+        return run_verify(args, world, rank, local, device)
 
     layers, bufs, step_bytes, dims = build_linear_stack(world, rank, device, batch)
     torch.cuda.synchronize()
@@ -661,6 +667,98 @@ def run_moe(args, world, rank, local, device):
     return finish(line, args, world)
 
 
+def run_verify(args, world, rank, local, device):
+    """Config 5: speculative verify of --batch sequences x 5 tokens through the whole
+    48-layer MoE model (experts split over the ranks under torchrun)."""
+    import dataclasses
+
+    from exl3_b200.verify import CONFIG5, VerifyModel
+
+    hbm_peak, tc_peak, peak_kind = peaks()
+    cfg = CONFIG5 if args.layers == 80 else dataclasses.replace(CONFIG5, layers=args.layers)
+    ctx = args.ctx
+    group = torch.distributed.group.WORLD if world > 1 else None
+    model = VerifyModel(cfg, args.batch, ctx + cfg.rows_per_seq, device, world, rank, group)
+    model.fill_random_kv(ctx)
+    model.tokens.random_(0, cfg.vocab, generator=torch.Generator(device=device).manual_seed(9))
+    # one eager step records how many experts the routing touches per layer (HBM roofline)
+    model.record = []
+    with torch.cuda.stream(model.stream):
+        finite = bool(torch.isfinite(model.step()).all())
+    torch.cuda.synchronize()
+    touched = model.record
+    model.record = None
+    model.pos.fill_(ctx)
+    model.capture()
+    for _ in range(args.warmup):
+        model.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    with ClockSampler(local) as clk:
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(model.stream)
+        model.replay(args.steps)
+        e1.record(model.stream)
+        e1.synchronize()
+    ms = max_over_ranks(world, e0.elapsed_time(e1) / args.steps)
+    R = model.rows
+    tok_s = R / (ms * 1e-3)
+    H, hd = cfg.hidden, cfg.head_dim
+    per_expert = 3 * H * cfg.inter * cfg.K_expert // 8
+    attn_codes = cfg.layers * (2 * H * cfg.heads * hd + 2 * H * cfg.kv_heads * hd) * cfg.K_attn // 8
+    kv = cfg.layers * args.batch * (ctx + cfg.rows_per_seq) * cfg.kv_heads * hd * 2 * 2
+    lm = cfg.vocab * H * 2
+    step_bytes = sum(touched) * per_expert / world + attn_codes + kv + lm
+    gbs = step_bytes / (ms * 1e-3) / 1e9
+
+    # end to end: the rows' tokens in from pinned host memory, the argmax of every row out
+    ptok = torch.randint(0, cfg.vocab, (args.batch, cfg.rows_per_seq), dtype=torch.long).pin_memory()
+    pout = torch.empty(R, dtype=torch.long).pin_memory()
+    torch.cuda.synchronize()
+    barrier(world)
+    n_e2e = max(1, min(args.steps, 5))
+    t0 = time.perf_counter()
+    for _ in range(n_e2e):
+        with torch.cuda.stream(model.stream):
+            model.tokens.copy_(ptok, non_blocking=True)
+            model.graph.replay()
+            pout.copy_(model.logits.argmax(-1), non_blocking=True)
+        model.stream.synchronize()
+    e2e_ms = max_over_ranks(world, (time.perf_counter() - t0) / n_e2e * 1e3)
+    model.close()
+    line = {
+        "metric": "C5 speculative verify tok/s (48-layer MoE, 5 tokens per sequence)", "value": tok_s,
+        "unit": "tok/s", "ms_per_step": ms,
+        "config": {"workload": f"config 5 verify: {args.batch} sequences x {cfg.rows_per_seq} tokens, "
+                               f"context {ctx}, one CUDA graph per step",
+                   "layers": cfg.layers, "experts": cfg.experts, "topk": cfg.topk, "hidden": H,
+                   "intermediate": cfg.inter, "expert_bpw": cfg.K_expert, "attention_bpw": cfg.K_attn,
+                   "codebook": "3INST", "global_batch": args.batch, "seq_len": ctx,
+                   "parallelism": f"ep{world}" if world > 1 else "single GPU",
+                   "experts_touched_per_layer": round(sum(touched) / len(touched), 1), "logits_finite": finite,
+                   "moe_path": _moe_path_name(world * R, cfg.topk, cfg.experts // world),
+                   "kv_cache": "bf16, random contents for the context",
+                   "l2": "no flush needed: expert codes per step >> 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
+                     "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "whole verify step per rank (touched expert codes + attention codes + KV + lm_head)"},
+        "e2e": {"value": R / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": ptok.numel() * 8, "d2h_bytes_per_step": pout.numel() * 8,
+                "path": "VerifyModel graph replay: draft tokens H2D from pinned memory, argmax of every row D2H"},
+        # per layer: q/k/v and o EXL3 launches (3 each) + the routed MoE pipeline (5 or 6)
+        "gpu_launches": args.steps * cfg.layers * (6 + (5 if _moe_path_name(world * R, cfg.topk,
+                                                                            cfg.experts // world) == "tc" else 6)),
+        "clocks": clk.summary(),
+    }
+    return finish(line, args, world)
+
+
+def _moe_path_name(rows, topk, experts):
+    from exl3_b200 import moe as M
+    return M.moe_path(rows, topk, experts)
+
+
 def run_decode(args, world, rank, local, device):
     from exl3_b200 import ops
     from exl3_b200.harness import LLAMA_70B, DecodeModel, exl3_weight_bytes
@@ -780,11 +878,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="decode", choices=["decode", "linears", "linear", "mlp", "moe"])
+    ap.add_argument("--workload", default="decode", choices=["decode", "linears", "linear", "mlp", "moe", "verify"])
     ap.add_argument("--k", type=int, default=4096)
     ap.add_argument("--n", type=int, default=4096)
     ap.add_argument("--bits", type=int, default=4)
-    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--ctx", type=int, default=None, help="context length (decode: 2048, verify: 8192)")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=80, help="decode: decoder layers (80 = config 4; fewer for profiling)")
     ap.add_argument("--moe", default="c3", choices=["c3", "c5"],
@@ -792,6 +890,8 @@ def main():
                          "config 5's speculative verify: 128 experts, hidden 4096, 5 rows per sequence")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     args = ap.parse_args()
+    if args.ctx is None:
+        args.ctx = 8192 if args.workload == "verify" else 2048
     world, rank, local = dist_setup(args.gpus)
     try:
         if args.impl == "reference":
