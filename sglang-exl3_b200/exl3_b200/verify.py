@@ -155,9 +155,8 @@ class VerifyModel:
         xf = x.float()
         return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + self.cfg.eps) * w.float()).to(torch.float16)
 
-    def _rope(self, t: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
-        ang = positions.float()[:, None] * self.inv_freq[None, :]  # [R, hd/2]
-        cos, sin = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
+    @staticmethod
+    def _rope(t: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
         t1, t2 = t[..., : t.size(-1) // 2], t[..., t.size(-1) // 2:]
         return torch.cat([t1 * cos - t2 * sin, t2 * cos + t1 * sin], dim=-1)
 
@@ -178,13 +177,15 @@ class VerifyModel:
         cols = torch.arange(kv_len, device=self.device)
         mask = cols[None, :] <= (self.pos + torch.arange(S, device=self.device))[:, None]  # [S, kv_len]
         mask_g = mask.repeat(cfg.heads // cfg.kv_heads, 1)  # [G * S, kv_len], row g * S + j
+        ang = positions.float()[:, None] * self.inv_freq[None, :]  # [R, hd/2], the same for every layer
+        cos, sin = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
         h = self.embed[self.tokens.reshape(-1)].float()  # [R, H]
         for li, L in enumerate(self.layers):
             xn = self._rms(h, L["ln1"])
             outs = [self.qkv[:, :qd], self.qkv[:, qd:qd + kvd], self.qkv[:, qd + kvd:]]
             ops.matmul_multi(xn, L["qkv"], cfg.K_attn, cfg.cb, outs=outs)
-            q = self._rope(self.qkv[:, :qd].float().view(R, nh, hd), positions)
-            k = self._rope(self.qkv[:, qd:qd + kvd].float().view(R, nkv, hd), positions)
+            q = self._rope(self.qkv[:, :qd].float().view(R, nh, hd), cos, sin)
+            k = self._rope(self.qkv[:, qd:qd + kvd].float().view(R, nkv, hd), cos, sin)
             v = self.qkv[:, qd + kvd:].float().view(R, nkv, hd)
             # append the 5 new positions of every sequence
             idx = positions.view(B, S)[0]  # same positions for every sequence
