@@ -23,7 +23,6 @@ prompt of that length would.
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass
 from typing import Optional
 

@@ -60,11 +60,6 @@ class VerifyConfig:
 CONFIG5 = VerifyConfig()
 
 
-def expert_bytes(cfg: VerifyConfig, world: int = 1) -> int:
-    """Code bytes of one rank's experts (each a gate, an up and a down projection)."""
-    return cfg.layers * (cfg.experts // world) * 3 * cfg.hidden * cfg.inter * cfg.K_expert // 8
-
-
 class VerifyModel:
     def __init__(self, cfg: VerifyConfig, batch: int, max_ctx: int, device: torch.device, world: int = 1,
                  rank: int = 0, group=None, seed: int = 4):

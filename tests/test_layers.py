@@ -2,7 +2,6 @@
 TP sharding, codebook markers, expert-id mapping.  Pins follow the reference's
 own CPU tests (tests/test_moe.py, tests/test_dense_marker_codebook.py)."""
 
-import numpy as np
 import pytest
 import torch
 
