@@ -122,3 +122,27 @@ def test_moe_ref_ignores_invalid_ids():
     out = O.moe_ref(x, experts, ids, w)
     ids2 = np.array([[0, 1], [1, -1]])
     np.testing.assert_allclose(out, O.moe_ref(x, experts, ids2, w), rtol=0, atol=0)
+
+
+def test_windows_match_bit_string_definition():
+    """Random tiles, K = 1..8: the vectorised extraction equals a literal reading of the
+    format - little-endian uint32 words, a cyclic MSB-first bit stream, element t the
+    16 bits ending at stream bit (t + 1) * K - 1 (mod 256 K)."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=40, deadline=None)
+    @given(K=st.integers(1, 8), seed=st.integers(0, 2**31 - 1))
+    def check(K, seed):
+        rng = np.random.default_rng(seed)
+        tile = rng.integers(-32768, 32768, size=16 * K).astype(np.int16)
+        u16 = tile.view(np.uint16).astype(np.uint32)
+        words = u16[0::2] | (u16[1::2] << 16)
+        bits = "".join(format(int(w), "032b") for w in words)  # MSB first, word by word
+        n = len(bits)
+        got = O.tile_windows(tile.reshape(1, 1, -1), K)[0, 0]
+        for t in range(256):
+            end = ((t + 1) * K - 1) % n
+            window = "".join(bits[(end - 15 + i) % n] for i in range(16))
+            assert got[t] == int(window, 2), (K, t)
+
+    check()
