@@ -275,3 +275,24 @@ def test_tensor_parallel_linear_from_layer_class():
     assert (col.parallel, col.tp_rank, col.tp_size) == ("column", 3, 4)
     assert (row.parallel, row.tp_rank, row.tp_size) == ("row", 3, 4)
     assert single.parallel == "none"
+
+
+def test_split_fused_group_reassembles():
+    """Random 16-multiple output partitions: the shards concatenate back to the fused
+    trellis (dim 1) and svh, and suh / markers go to every shard unchanged."""
+    from hypothesis import given, settings, strategies as st
+
+    @settings(max_examples=50, deadline=None)
+    @given(sizes=st.lists(st.integers(1, 6).map(lambda v: 16 * v), min_size=1, max_size=4),
+           k_tiles=st.integers(1, 4))
+    def check(sizes, k_tiles):
+        total = sum(sizes)
+        tr = torch.arange(k_tiles * (total // 16) * 32, dtype=torch.int32).reshape(k_tiles, total // 16, 32)
+        sv = torch.arange(total, dtype=torch.float32)
+        su = torch.ones(k_tiles * 16)
+        assert torch.equal(torch.cat(split_fused_group(sizes, "trellis", tr), dim=1), tr)
+        assert torch.equal(torch.cat(split_fused_group(sizes, "svh", sv)), sv)
+        assert all(p is su for p in split_fused_group(sizes, "suh", su))
+        assert [p.shape[1] * 16 for p in split_fused_group(sizes, "trellis", tr)] == sizes
+
+    check()
