@@ -54,8 +54,8 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "decode tok/s (70B-shape 4bpw); EXL3 GEMV HBM GB/s vs roofline"
-# DRAM bytes per launch of the fused gate+up matmul kernel (8192 x 2 x 28672, 4 bpw, M = 1),
-# from ncu (profiles/exl3_gv_matmul_gateup_8192x2x28672_4bpw_m1_traffic.md)
+# DRAM bytes per launch of the fused gate+up matmul kernel (8192 x 2 x 28672, 4 bpw, M = 1):
+# ncu dram__bytes_read.sum + dram__bytes_write.sum, mean of three launches on a B200
 GATEUP_TRAFFIC_BYTES = 237_192_363
 
 # Llama-70B shape (config 4)
