@@ -4,8 +4,8 @@ Run in the build container, where the reference tree is present:
 
     python oracle/build_ref.py                 # compiles the reference into oracle/_ref
     python tests/golden/make_fixtures.py       # CPU fixtures
-    python tests/golden/make_fixtures.py --device-dump gpurun_out/ref_device_decode.bin
-                                               # after running oracle/_ref/ref_codebook_dump on a B200
+    python tests/golden/make_fixtures.py --device-dump <dump file>
+                                               # the file oracle/_ref/ref_codebook_dump wrote on a B200
 
 Fixtures (inputs are seeded; outputs come from the reference's own code):
 
