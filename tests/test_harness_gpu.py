@@ -68,15 +68,33 @@ def test_graph_replay_matches_eager(cuda_device):
     m.release()
 
 
-def test_step_matches_dequantised_torch(cuda_device):
-    m = DecodeModel(TINY, batch=2, max_ctx=32, device=cuda_device)
+def _rel(a, b):
+    return float((a.double() - b.double()).abs().max() / b.double().abs().max())
+
+
+# Normwise tolerances of the fused step against fp32 torch on the dequantised weights.
+# The fused step rounds where the plugin path does (fp16 normed inputs and rotated
+# activations, bf16 KV cache and attention output), so it is held to 1e-2 on the
+# residual stream and on the logits - the bound the fused/unfused comparison uses.
+TOL_RESIDUAL = 1e-2
+TOL_LOGITS = 1e-2
+
+
+@pytest.mark.parametrize("fused", [True, False])
+def test_step_matches_dequantised_torch(cuda_device, fused):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    m = DecodeModel(TINY, batch=2, max_ctx=32, device=cuda_device, fused=fused)
     m.fill_random_kv(10)
     tokens = torch.tensor([5, 9], device=cuda_device)
     m.tokens.copy_(tokens)
     pos = m.pos.clone()
-    _, ref_logits = _torch_step(m, tokens, pos)
+    ref_h, ref_logits = _torch_step(m, tokens, pos)
     m.step()
     torch.cuda.synchronize()
+    err_h, err_l = _rel(m.h, ref_h), _rel(m.last_logits.float(), ref_logits)
+    print(f"residual {err_h:.2e}, logits {err_l:.2e}")
+    assert err_h < TOL_RESIDUAL
+    assert err_l < TOL_LOGITS
     # greedy tokens agree unless the reference's top-2 logits are nearly tied
     top2 = ref_logits.topk(2, dim=-1).values
     margin = (top2[:, 0] - top2[:, 1]).abs()

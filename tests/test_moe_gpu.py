@@ -212,24 +212,6 @@ def test_moe_graph_capture_replay(cuda_device, path):
         assert O.normwise_rel_err(out.cpu().numpy(), ref) < TOL_MOE
 
 
-@pytest.mark.parametrize("K,cb", [(3, 0), (4, 1), (2, 2)])
-def test_moe_tc_matches_small_at_config5_width(cuda_device, K, cb):
-    """Config-5 expert shape (hidden 4096, intermediate 1536), 32 experts with ~20
-    rows each: the two pipelines agree (no oracle: its dequant is slow at this size)."""
-    rng = np.random.default_rng(300 + K)
-    T, topk, E, H, I = 80, 8, 32, 4096, 1536
-    experts = _with_cb(_experts(rng, E, H, I, K), cb)
-    tabs, keep = _tables(experts, cuda_device, cb)
-    # inputs scaled so that the fp16 SwiGLU intermediate of random-code experts stays finite
-    x = _t((0.05 * rng.standard_normal((T, H))).astype(np.float16), cuda_device)
-    ids = _t(np.stack([rng.permutation(E)[:topk] for _ in range(T)]).astype(np.int32), cuda_device)
-    w = _t(rng.uniform(0.05, 0.3, size=(T, topk)).astype(np.float32), cuda_device)
-    ys = moe.moe_forward(x, ids, w, tabs, K, K, K, cb, I, path="small")
-    yt = moe.moe_forward(x, ids, w, tabs, K, K, K, cb, I, path="tc")
-    assert torch.isfinite(ys).all() and torch.isfinite(yt).all()
-    assert O.normwise_rel_err(yt.cpu().numpy(), ys.cpu().numpy().astype(np.float64)) < TOL_MOE
-
-
 @pytest.mark.parametrize("K,cb,rotated", [(4, 1, True), (3, 0, False), (2, 2, True)])
 def test_matmul_combine_tensor_core(cuda_device, K, cb, rotated):
     """More than 16 rows: one tensor-core launch (exl3b200_gemm_combine); 300 rows =

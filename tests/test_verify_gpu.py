@@ -39,3 +39,92 @@ def test_verify_graph_matches_eager(cuda_device, batch):
     print(f"eager vs eager {noise:.2e}, graph vs eager {err:.2e}")
     assert err < max(1e-3, 10 * noise), (err, noise)  # routed-MoE fp32 atomics may add in another order
     m.close()
+
+
+def _torch_verify_step(m):
+    """The same verify step in fp32 torch on the dequantised weights (no EXL3
+    kernels): q/k/v, o and every expert as fp32 matmuls, the MoE as a loop over the
+    routed experts with the SwiGLU activation rounded to fp16 where the kernels keep
+    it.  Returns the logits and, per row, whether any layer's top-k choice was
+    within 1e-3 of a tie (such rows may legitimately route differently)."""
+    import torch.nn.functional as F
+    from exl3_b200 import ops
+
+    cfg = m.cfg
+    B, S, R = m.batch, cfg.rows_per_seq, m.rows
+    hd, nh, nkv = cfg.head_dim, cfg.heads, cfg.kv_heads
+    qd, kvd = nh * hd, nkv * hd
+    dev = m.device
+
+    def W(lin, K):
+        return ops.dequant(*lin, K, cfg.cb, "rn").float()
+
+    positions = (m.pos + torch.arange(S, device=dev)).repeat(B)
+    cols = torch.arange(m.max_ctx, device=dev)
+    mask = cols[None, :] <= (m.pos + torch.arange(S, device=dev))[:, None]
+    ang = positions.float()[:, None] * m.inv_freq[None, :]
+    cos, sin = torch.cos(ang)[:, None, :], torch.sin(ang)[:, None, :]
+    k_cache, v_cache = m.k_cache.clone(), m.v_cache.clone()
+    tie = torch.zeros(R, dtype=torch.bool, device=dev)
+    h = m.embed[m.tokens.reshape(-1)].float()
+    for li, L in enumerate(m.layers):
+        xn = m._rms(h, L["ln1"]).float()
+        q = m._rope((xn @ W(L["qkv"][0], cfg.K_attn)).view(R, nh, hd), cos, sin)
+        k = m._rope((xn @ W(L["qkv"][1], cfg.K_attn)).view(R, nkv, hd), cos, sin)
+        v = (xn @ W(L["qkv"][2], cfg.K_attn)).view(R, nkv, hd)
+        idx = positions.view(B, S)[0]
+        k_cache[li].index_copy_(2, idx, k.view(B, S, nkv, hd).transpose(1, 2).to(torch.bfloat16))
+        v_cache[li].index_copy_(2, idx, v.view(B, S, nkv, hd).transpose(1, 2).to(torch.bfloat16))
+        kk = k_cache[li].float().repeat_interleave(nh // nkv, dim=1)
+        vv = v_cache[li].float().repeat_interleave(nh // nkv, dim=1)
+        qh = q.view(B, S, nh, hd).transpose(1, 2)  # [B, nh, S, hd]
+        att = F.scaled_dot_product_attention(qh, kk, vv, attn_mask=mask[None, None])
+        att = att.transpose(1, 2).reshape(R, qd)
+        h = h + att @ W(L["o"], cfg.K_attn)
+        xn16 = m._rms(h, L["ln2"])
+        logits = xn16.float() @ L["router"].t() + m.route_noise[li]
+        p = torch.softmax(logits, dim=-1)
+        top = torch.topk(p, cfg.topk + 1, dim=-1)
+        tie |= (top.values[:, cfg.topk - 1] - top.values[:, cfg.topk]) < 1e-3
+        w, ids = top.values[:, :cfg.topk], top.indices[:, :cfg.topk]
+        w = w / w.sum(-1, keepdim=True)
+        w13, w2, s13u, s13v, s2u, s2v = L["experts"]
+        y = torch.zeros_like(h)
+        for e in torch.unique(ids).tolist():
+            ts, js = (ids == e).nonzero(as_tuple=True)
+            xt = xn16[ts].float()
+            g = xt @ ops.dequant(w13[e, 0], s13u[e, 0], s13v[e, 0], cfg.K_expert, cfg.cb, "rn").float()
+            u = xt @ ops.dequant(w13[e, 1], s13u[e, 1], s13v[e, 1], cfg.K_expert, cfg.cb, "rn").float()
+            a = (F.silu(g) * u).half().float()
+            d = a @ ops.dequant(w2[e], s2u[e], s2v[e], cfg.K_expert, cfg.cb, "rn").float()
+            y.index_add_(0, ts, w[ts, js, None] * d)
+        h = h + y
+    xf = m._rms(h, m.ln_f).to(torch.bfloat16)
+    return (xf @ m.lm_head.t()).float(), tie
+
+
+# Normwise tolerance of the verify step's logits against fp32 torch on the dequantised
+# weights: the step keeps fp16 normed inputs and projection outputs and a bf16 KV cache
+# and attention, as the plugin path does.
+TOL_LOGITS = 1e-2
+
+
+@pytest.mark.parametrize("batch", [1, 7])
+def test_verify_step_matches_fp32_torch(cuda_device, batch):
+    torch.backends.cuda.matmul.allow_tf32 = False
+    cfg = dataclasses.replace(CONFIG5, layers=2, hidden=1024, heads=8, kv_heads=2, experts=16, inter=512,
+                              vocab=2048)
+    ctx = 64
+    m = VerifyModel(cfg, batch, ctx + cfg.rows_per_seq, cuda_device)
+    m.fill_random_kv(ctx)
+    m.tokens.random_(0, cfg.vocab, generator=torch.Generator(device=cuda_device).manual_seed(2))
+    ref, tie = _torch_verify_step(m)
+    with torch.cuda.stream(m.stream):
+        got = m.step()
+    torch.cuda.synchronize()
+    keep = ~tie
+    assert int(keep.sum()) >= (m.rows + 1) // 2, "too many near-tied routes to compare"
+    err = _rel(got[keep], ref[keep])
+    print(f"verify step vs fp32 torch: {err:.2e} over {int(keep.sum())} of {m.rows} rows")
+    assert err < TOL_LOGITS
+    m.close()
