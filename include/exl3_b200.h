@@ -135,8 +135,11 @@ EXL3B200_API int exl3b200_gemm_combine(const void* x, long long x_stride, int m,
  * the library (about 4 MB, held by every GPU that loads the library until the
  * process exits).  Limits: m <= 16, k <= 32768, n <= 32768; larger sizes return
  * EXL3B200_EBADSHAPE.  All calls share that array: calls that overlap on the GPU
- * race, so serialise them.  The first call on a device looks the array up; make
- * it before capturing a stream.  This entry point has no counterpart in the
+ * race, so serialise them.  The first call on a device looks the array up and,
+ * under CUDA's lazy module loading (the default), is also what loads the
+ * library's device code on that device and so reserves the array: make one
+ * warm-up call on each device before entering code that must not allocate, and
+ * before capturing a stream.  This entry point has no counterpart in the
  * reference.
  */
 EXL3B200_API int exl3b200_gemv_noalloc(const void* x, long long x_stride, int m, int k, const void* trellis, int n,
@@ -266,6 +269,15 @@ EXL3B200_API int exl3b200_gemm(const void* x, long long x_stride, int m, int k, 
 EXL3B200_API int exl3b200_device_status(int* host_status, int reset, void* stream);
 
 /*
+ * Limit, in nanoseconds of the GPU's global timer, of every bounded device-side wait
+ * in kernels launched after this call (the tensor-core pipeline's barrier waits and
+ * the decode peer exchange's arrival wait); 0 restores the defaults (1 s and 2 s).
+ * Process-wide.  A short limit lets a test make a wait run out quickly.  No
+ * counterpart in the reference, whose kernels have no bounded waits.
+ */
+EXL3B200_API int exl3b200_set_wait_limit(unsigned long long ns);
+
+/*
  * One EXL3 linear as the decode-layer entry points take it.
  */
 typedef struct exl3b200_linear {
@@ -294,6 +306,11 @@ EXL3B200_API int exl3b200_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_
 EXL3B200_API int exl3b200_peer_buffer_open(const void* ipc_handle, void** ptr);
 EXL3B200_API int exl3b200_peer_buffer_close(void* ptr);
 EXL3B200_API int exl3b200_peer_buffer_free(void* ptr);
+/*
+ * Enqueue on stream the re-arming of this rank's own peer buffer (call epoch 0, no
+ * arrivals, not poisoned).  Only while no exchange is in flight on any rank.
+ */
+EXL3B200_API int exl3b200_peer_reset(void* own_buffer, void* stream);
 
 /*
  * Fused decode sub-layers of a Llama-style decoder for batch <= 16 sequences,
@@ -310,9 +327,14 @@ EXL3B200_API int exl3b200_peer_buffer_free(void* ptr);
  * the all-reduce, exl3b200_residual_add(h, y, ss_out) completes the sub-layer.
  * With peers (non-NULL; y_out ignored) the sub-layer exchanges the partials itself
  * through the peer buffers (stores over NVLink, an arrival counter per call, a
- * bounded wait of 2 s that records EXL3B200_ETIMEOUT in the device status when it
- * gives up; the exchange state is then undefined until the buffers are re-created)
- * and adds their sum into h; every rank must make the same sequence of calls.
+ * bounded wait - 2 s unless exl3b200_set_wait_limit says otherwise) and adds their
+ * sum into h; every rank must make the same sequence of calls.  A wait that gives
+ * up records EXL3B200_ETIMEOUT in the device status, leaves h, the counters and the
+ * call epoch as they are, and poisons this rank's buffer: every later exchange on
+ * it returns at once (recording EXL3B200_ETIMEOUT again) until
+ * exl3b200_peer_reset.  The caller checks exl3b200_device_status and recovers by
+ * draining every rank's stream, then exl3b200_peer_reset on every rank's own
+ * buffer, with a host barrier before and after the resets.
  *
  * Attention: k_cache / v_cache are this layer's bf16 [batch][kv_heads][max_ctx][128];
  * *pos (device) is the new token's position, the cache holds 0..pos-1 and the

@@ -520,7 +520,11 @@ __global__ __launch_bounds__(256) void exl3_dec_residual_kernel(float* __restric
 // bounded wait (2 s of %globaltimer, then EXL3B200_ETIMEOUT in the device status
 // and no update) until its own counter holds world x grid arrivals; then h += the
 // sum of the slots for the same tasks, and the rows' sums of squares.  The last
-// CTA to finish re-arms the counter and advances the epoch.  The grid is at most
+// CTA to finish re-arms the counter and advances the epoch.  A CTA whose wait gives
+// up poisons the buffer instead: the counter and the epoch stay as they are (a slow
+// peer's late arrivals and stores cannot be mistaken for the next call's), h is not
+// updated, and every later launch on the buffer returns at once with
+// EXL3B200_ETIMEOUT until the host re-arms it (exl3b200_peer_reset).  The grid is at most
 // one CTA per SM, so every CTA is resident while it waits, and it is the same on
 // every rank (same shapes).  Counters and slots alternate between two parities by
 // call; a rank cannot reach call k+2 before every peer has finished reading call k
@@ -535,6 +539,11 @@ __global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __gri
     griddep_wait();
     __shared__ int ok;
     PeerCtl* ctl = reinterpret_cast<PeerCtl*>(x.peer[x.peer_rank]);
+    if (*reinterpret_cast<volatile unsigned int*>(&ctl->poisoned)) {
+        // an earlier exchange gave up: no stores, no arrivals, no update
+        if (threadIdx.x == 0 && x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
+        return;
+    }
     const unsigned int epoch = *reinterpret_cast<volatile unsigned int*>(&ctl->epoch) + 1u;
     const unsigned int parity = epoch & 1u;
     const int warps = gridDim.x * (blockDim.x >> 5);
@@ -561,9 +570,10 @@ __global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __gri
         int good = 1;
         const unsigned long long t0 = globaltimer_ns();
         while (ld_acquire_sys(cnt) < expect) {
-            if (globaltimer_ns() - t0 > kPeerTimeoutNs) {
+            if (globaltimer_ns() - t0 > x.peer_wait_ns) {
                 good = 0;
                 if (x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
+                atomicExch(&ctl->poisoned, 1u);
                 break;
             }
             __nanosleep(32);
@@ -600,9 +610,11 @@ __global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __gri
         __threadfence();
         if (atomicAdd(&ctl->done, 1u) == gridDim.x - 1) {
             ctl->done = 0u;
-            *peer_flag(x, x.peer_rank, parity, 0) = 0u;  // every rank's arrivals of this call are in
-            __threadfence();
-            *reinterpret_cast<volatile unsigned int*>(&ctl->epoch) = epoch;
+            if (!*reinterpret_cast<volatile unsigned int*>(&ctl->poisoned)) {
+                *peer_flag(x, x.peer_rank, parity, 0) = 0u;  // every rank's arrivals of this call are in
+                __threadfence();
+                *reinterpret_cast<volatile unsigned int*>(&ctl->epoch) = epoch;
+            }
         }
     }
 }
@@ -791,6 +803,7 @@ static int dec_finish(GvArgs& a, DecAux& x, int cb, float* h, long long h_stride
         x.peer_rank = peers->rank;
         x.peer_rows = peers->max_rows;
         x.peer_hidden = peers->hidden;
+        x.peer_wait_ns = wait_limit_ns(kPeerTimeoutNs);
         x.status = exl3_status_dev_ptr();
         x.resid = h;
         x.resid_stride = h_stride;
@@ -876,6 +889,16 @@ extern "C" int exl3b200_peer_buffer_close(void* ptr)
 {
     if (!ptr) return kErrNullPointer;
     return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? kOk : kErrLaunch;
+}
+
+extern "C" int exl3b200_peer_reset(void* own_buffer, void* stream)
+{
+    if (!own_buffer) return kErrNullPointer;
+    if ((uintptr_t) own_buffer & 255) return kErrUnaligned;
+    // control word and both parities' arrival counters
+    return cudaMemsetAsync(own_buffer, 0, kPeerData, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
+               ? kOk
+               : kErrLaunch;
 }
 
 extern "C" int exl3b200_peer_buffer_free(void* ptr)

@@ -31,8 +31,9 @@ constexpr size_t kPeerData = 256;
 constexpr unsigned long long kPeerTimeoutNs = 2000000000ull;
 
 struct PeerCtl {
-    unsigned int epoch;  // calls completed
-    unsigned int done;   // CTAs of the running reduce that finished
+    unsigned int epoch;     // calls completed
+    unsigned int done;      // CTAs of the running reduce that finished
+    unsigned int poisoned;  // a wait gave up: exchanges return at once until the host re-arms
 };
 
 struct DecAux {
@@ -60,6 +61,7 @@ struct DecAux {
     // tensor-parallel partial exchange
     char* peer[kPeerMaxRanks];
     int peer_world, peer_rank, peer_rows, peer_hidden;
+    unsigned long long peer_wait_ns;  // limit of the arrival wait
     int* status;
 };
 

@@ -116,6 +116,7 @@ struct TcArgs {
     long long xt_rows;         // rows of the k-chunk-major input image
     const int* slot_token;     // combine: output row of each routed slot
     const float* slot_weight;  // combine: its routing weight
+    unsigned long long wait_ns;  // limit of every bounded barrier wait
 };
 
 // ---------------------------------------------------------------------------
@@ -162,7 +163,8 @@ __device__ __forceinline__ unsigned long long global_ns()
 }
 
 // Slow path of a bounded wait: false once the CTA's abort flag is up
-// (check_abort) or the deadline passes (then raises the flag and the status).
+// (check_abort) or the deadline passes (then raises the flag and the status).  The
+// CTA's wait limit sits in shared memory 4 bytes after its abort flag.
 __device__ __forceinline__ bool mbar_test_sleep(uint32_t bar, uint32_t parity)
 {
     uint32_t ok;
@@ -183,7 +185,8 @@ __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volat
         if (mbar_test_sleep(bar, parity)) return true;
         if ((it & 63u) == 0) {
             if (check_abort && *abort_flag) return false;
-            if (global_ns() - t0 > kTcTimeoutNs) {
+            if (global_ns() - t0 > *reinterpret_cast<volatile unsigned long long*>(
+                                       reinterpret_cast<volatile char*>(abort_flag) + 4)) {
                 *abort_flag = 1;
                 atomicCAS(&g_exl3_device_status, 0, (int) kErrTimeout);
                 return false;
@@ -676,6 +679,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, kTcWarps - 3);  // every decoder and epilogue-only warp
         *abort_flag = 0;
+        *reinterpret_cast<volatile unsigned long long*>(gbase + L::kMisc + 8) = a.wait_ns;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -983,6 +987,7 @@ static int tc_launch_gemm(const TcArgs& a, int grid, cudaStream_t stream)
         configured[dev] = true;
     }
     TcArgs arg = a;
+    arg.wait_ns = wait_limit_ns(kTcTimeoutNs);
     void* args[] = {&arg};
     return tc_launch((const void*) exl3_tc_gemm_kernel<K, CB, MODE>, grid, kTcThreads, L::kLaunchBytes, stream,
                      args) == cudaSuccess

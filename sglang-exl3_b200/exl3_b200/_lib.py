@@ -76,6 +76,7 @@ SIGNATURES = {
     "exl3b200_gemm_scratch_size": (_sz, [_i, _i]),
     "exl3b200_gemm": (_i, [_vp, _ll, _i, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _ll, _i, _i, _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_device_status": (_i, [_vp, _i, _vp]),
+    "exl3b200_set_wait_limit": (_i, [ctypes.c_ulonglong]),
     "exl3b200_decode_attention_workspace": (_i, [_i, _i, _i, _i, _i, _vp, _vp]),
     "exl3b200_decode_mlp_workspace": (_i, [_i, _i, _i, _vp, _vp]),
     "exl3b200_decode_attention": (_i, [_i, _i, _i, _i, _i, _i, _vp, _ll, _vp, _vp, _vp, _f, _vp, _vp, _vp, _vp,
@@ -87,6 +88,7 @@ SIGNATURES = {
     "exl3b200_peer_buffer_open": (_i, [_vp, _vp]),
     "exl3b200_peer_buffer_close": (_i, [_vp]),
     "exl3b200_peer_buffer_free": (_i, [_vp]),
+    "exl3b200_peer_reset": (_i, [_vp, _vp]),
     "exl3b200_residual_add": (_i, [_i, _i, _vp, _ll, _vp, _ll, _vp, _vp]),
     "exl3b200_moe_tc_scratch_size": (_sz, [_i, _i, _i, _i, _i]),
     "exl3b200_moe_tc": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,

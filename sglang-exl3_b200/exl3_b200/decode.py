@@ -156,6 +156,18 @@ class PeerExchange:
                                  max_rows, hidden)
         dist.barrier(group)
 
+    def reset(self) -> None:
+        """Re-arm the exchange after a device wait gave up (every rank, together):
+        drain this rank's work, wait for every rank, re-arm the own buffer, wait again."""
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
+        _lib.check(_lib.lib().exl3b200_peer_reset(self._own, torch.cuda.current_stream().cuda_stream),
+                   "exl3b200_peer_reset")
+        torch.cuda.synchronize()
+        dist.barrier(self.group)
+
     def close(self) -> None:
         import torch.distributed as dist
 

@@ -26,10 +26,12 @@ from __future__ import annotations
 from dataclasses import dataclass
 from typing import Optional
 
+import ctypes
+
 import torch
 import torch.nn.functional as F
 
-from . import ops
+from . import _lib, ops
 
 
 @dataclass
@@ -270,7 +272,9 @@ class DecodeModel:
         if self.graph is None:
             raise RuntimeError("call capture() first")
         host_in, host_out = self._pinned(n)
+        status = self._status_host()
         host_in.copy_(prompt_tokens.to(torch.long))
+        L = _lib.lib()
         with torch.cuda.stream(self.stream):
             for i in range(n):
                 if i > 0:
@@ -278,8 +282,20 @@ class DecodeModel:
                 self.tokens.copy_(host_in, non_blocking=True)
                 self.graph.replay()
                 host_out[:, i].copy_(self.next_tokens, non_blocking=True)
+                # the library's sticky device status rides along with the tokens: a
+                # device wait that gave up (peer exchange, tensor-core pipeline) is an error
+                L.exl3b200_device_status(ctypes.c_void_p(status.data_ptr()), 0, self.stream.cuda_stream)
                 self.stream.synchronize()
+                if int(status[0]) != 0:
+                    raise RuntimeError(f"decode step {i}: device status {_lib.status_string(int(status[0]))}")
         return host_out[:, :n].clone()
+
+    def _status_host(self) -> torch.Tensor:
+        buf = getattr(self, "_status_buf", None)
+        if buf is None:
+            buf = torch.zeros(1, dtype=torch.int32).pin_memory()
+            self._status_buf = buf
+        return buf
 
     def decode(self, n: int):
         """Run n captured decode steps (feeding back the greedy tokens)."""

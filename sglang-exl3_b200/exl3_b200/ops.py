@@ -202,6 +202,14 @@ def device_status(device: Optional[torch.device] = None, reset: bool = True) -> 
     return int(host.item())
 
 
+def set_wait_limit(seconds: Optional[float]) -> None:
+    """Limit of the library's bounded device-side waits for kernels launched from now
+    on (tensor-core pipeline barriers, decode peer exchange); ``None`` restores the
+    defaults.  Process-wide."""
+    ns = 0 if seconds is None else max(1, int(seconds * 1e9))
+    _lib.check(_lib.lib().exl3b200_set_wait_limit(ns), "exl3b200_set_wait_limit")
+
+
 def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], svh: torch.Tensor,
            K: Optional[int] = None, cb: int = 0, out_dtype: torch.dtype = torch.float16,
            out: Optional[torch.Tensor] = None, input_rotated: bool = False,

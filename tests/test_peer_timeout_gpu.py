@@ -1,0 +1,88 @@
+"""A bounded device wait that runs out, on one GPU, without any fault.
+
+The decode peer exchange waits for every rank's arrivals on its own buffer.  Here a
+two-rank exchange is run by one process whose "rank 1" buffer is plain local memory
+that no kernel ever writes arrivals for, so the wait can only run out: with a 10 ms
+limit (``exl3b200_set_wait_limit``) the kernel must return, record
+``EXL3B200_ETIMEOUT`` in the device status, leave the residual stream, the call epoch
+and the arrival counter alone and poison the buffer; a later exchange on the
+poisoned buffer must return at once; and after ``exl3b200_peer_reset`` a normal
+one-rank exchange on the same buffer must equal the path without an exchange.
+"""
+
+import ctypes
+import time
+
+import pytest
+import torch
+
+from exl3_b200 import _lib, ops
+from exl3_b200 import decode as D
+from exl3_b200.harness import _random_linear
+
+pytestmark = pytest.mark.gpu
+
+
+class _PeerArg:
+    def __init__(self, buffers, rank, rows, hidden):
+        ptrs = [b.data_ptr() for b in buffers] + [None] * (8 - len(buffers))
+        self.struct = _lib.Peers((ctypes.c_void_p * 8)(*ptrs), len(buffers), rank, rows, hidden)
+
+
+def _mlp(h, ss, lins, peers=None):
+    ln = torch.ones(h.size(1), dtype=torch.bfloat16, device=h.device)
+    D.decode_mlp(h, ss[0], ss[1], ln, 1e-5, *lins, 4, 0, peers=peers)
+
+
+def test_peer_wait_runs_out_then_recovers(cuda_device):
+    L = _lib.lib()
+    B, H, I = 2, 512, 512
+    g = torch.Generator(device=cuda_device)
+    g.manual_seed(7)
+    lins = [_random_linear(g, H, I, 4, cuda_device), _random_linear(g, H, I, 4, cuda_device),
+            _random_linear(g, I, H, 4, cuda_device)]
+    for lin in lins:
+        lin[2].mul_(float(lin[0].size(0) * 16) ** -0.5)
+    size = L.exl3b200_peer_buffer_size(B, H)
+    bufs = [torch.zeros(size, dtype=torch.uint8, device=cuda_device) for _ in range(2)]
+    h0 = torch.randn(B, H, dtype=torch.float32, device=cuda_device, generator=g)
+
+    def fresh():
+        h = h0.clone()
+        ss = torch.zeros(2, B, dtype=torch.float32, device=cuda_device)
+        ss[0] = (h * h).sum(-1)
+        return h, ss
+
+    ops.device_status(cuda_device)  # clear
+    ops.set_wait_limit(0.01)
+    try:
+        h, ss = fresh()
+        t0 = time.perf_counter()
+        _mlp(h, ss, lins, _PeerArg(bufs, 0, B, H))
+        torch.cuda.synchronize()
+        assert time.perf_counter() - t0 < 1.0  # the 10 ms limit, not the 2 s default
+        assert ops.device_status(cuda_device) == _lib.ETIMEOUT
+        assert torch.equal(h, h0)  # no update after a wait that gave up
+        ctl = bufs[0][:12].view(torch.int32).tolist()  # epoch, done, poisoned
+        assert ctl == [0, 0, 1], ctl
+        # poisoned: the next exchange on this buffer returns at once, again with the status
+        _mlp(h, ss, lins, _PeerArg(bufs, 0, B, H))
+        torch.cuda.synchronize()
+        assert ops.device_status(cuda_device) == _lib.ETIMEOUT
+        assert torch.equal(h, h0)
+    finally:
+        ops.set_wait_limit(None)
+
+    # re-armed, a one-rank exchange on the same buffer equals the residual epilogue
+    _lib.check(L.exl3b200_peer_reset(bufs[0].data_ptr(), torch.cuda.current_stream(cuda_device).cuda_stream),
+               "exl3b200_peer_reset")
+    h_peer, ss_peer = fresh()
+    _mlp(h_peer, ss_peer, lins, _PeerArg(bufs[:1], 0, B, H))
+    h_ref, ss_ref = fresh()
+    _mlp(h_ref, ss_ref, lins)
+    torch.cuda.synchronize()
+    assert ops.device_status(cuda_device) == 0
+    assert not torch.equal(h_peer, h0)
+    torch.testing.assert_close(h_peer, h_ref, rtol=1e-6, atol=1e-5)
+    torch.testing.assert_close(ss_peer[1], ss_ref[1], rtol=1e-5, atol=1e-3)
+    assert bufs[0][:12].view(torch.int32).tolist()[2] == 0
