@@ -38,6 +38,7 @@
 //   down projection (the reference's had_hf_r_128_guad_inner and p2b_moe phase 3,
 //   csrc/quant/hadamard_inner.cuh:283-413, csrc/p2b_moe.cu:300-336).
 #include <algorithm>
+#include <atomic>
 
 #include "exl3_common.cuh"
 #include "exl3_capi_internal.h"
@@ -692,7 +693,10 @@ extern "C" int exl3b200_gemv_combine(const void* x, long long x_stride, int m, i
 // threads) race and corrupt each other's results; serialise them.  Each call
 // clears the partial sums it will use before its kernels run.  The first call on
 // each device looks up the array's device address (cudaGetSymbolAddress, with
-// that device current); make that first call before capturing a stream.
+// that device current).  With CUDA's lazy module loading that lookup is also what
+// loads this library's device code on the device, reserving the array, so the
+// caller makes one warm-up call per device before entering code that must not
+// allocate, and before capturing a stream.
 // ---------------------------------------------------------------------------
 namespace exl3b200 {
 
@@ -707,15 +711,16 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocStateBy
 
 static int noalloc_base(char** base)
 {
-    static void* cache[64] = {nullptr};
+    // one slot per device; threads that race on the first lookup store the same address
+    static std::atomic<void*> cache[64];
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kErrLaunch;
-    if (!cache[dev]) {
-        void* p = nullptr;
+    void* p = cache[dev].load(std::memory_order_relaxed);
+    if (!p) {
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return kErrLaunch;
-        cache[dev] = p;
+        cache[dev].store(p, std::memory_order_relaxed);
     }
-    *base = reinterpret_cast<char*>(cache[dev]);
+    *base = reinterpret_cast<char*>(p);
     return kOk;
 }
 

@@ -19,26 +19,38 @@ pytestmark = pytest.mark.gpu
 TOL = 2e-3  # the matmul tests' tolerance: normwise relative error, fp32 accumulate
 
 
-def _noalloc(L, x, tr, su, sv, K, cb, out):
+_DTYPES = {0: torch.float16, 1: torch.bfloat16, 2: torch.float32}
+TOL_BF16 = 4e-3  # bf16 outputs carry their own 2^-9 rounding
+
+
+def _noalloc(L, x, tr, su, sv, K, cb, out, out_dtype=0):
     stream = torch.cuda.current_stream(x.device).cuda_stream
     return L.exl3b200_gemv_noalloc(x.data_ptr(), x.stride(0), x.size(0), x.size(1), tr.data_ptr(), tr.size(1) * 16,
-                                   K, cb, su.data_ptr(), sv.data_ptr(), out.data_ptr(), out.stride(0), 0, stream)
+                                   K, cb, su.data_ptr(), sv.data_ptr(), out.data_ptr(), out.stride(0), out_dtype,
+                                   stream)
 
 
-@pytest.mark.parametrize("K,cb,m,k,n", [(4, 0, 1, 4096, 4096), (3, 1, 5, 1024, 768), (2, 2, 16, 512, 384)])
-def test_noalloc_matches_workspace_entry_twice(cuda_device, K, cb, m, k, n):
+@pytest.mark.parametrize("K,cb,m,k,n,out_dtype", [(4, 0, 1, 4096, 4096, 0), (3, 1, 5, 1024, 768, 1),
+                                                  (2, 2, 16, 512, 384, 2)])
+def test_noalloc_matches_workspace_entry_twice(cuda_device, K, cb, m, k, n, out_dtype):
+    """Two calls in a row: each agrees with the workspace entry point and with the
+    oracle (fp32 matmul on the dequantised weights)."""
     L = _lib.lib()
     rng = np.random.default_rng(500 + K)
-    tr = torch.from_numpy(O.random_trellis(rng, k, n, K)).to(cuda_device)
-    su = torch.from_numpy(O.random_signs(rng, k)).to(cuda_device)
-    sv = torch.from_numpy(O.random_signs(rng, n)).to(cuda_device)
+    tr_np, su_np, sv_np = O.random_trellis(rng, k, n, K), O.random_signs(rng, k), O.random_signs(rng, n)
+    tr, su, sv = (torch.from_numpy(a).to(cuda_device) for a in (tr_np, su_np, sv_np))
+    dtype = _DTYPES[out_dtype]
+    tol = TOL_BF16 if dtype == torch.bfloat16 else TOL
     for call in range(2):  # the second call reuses the array the first one left behind
-        x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float16)).to(cuda_device)
-        out = torch.empty((m, n), dtype=torch.float16, device=cuda_device)
-        assert _noalloc(L, x, tr, su, sv, K, cb, out) == 0
-        ref = ops.matmul(x, tr, su, sv, K, cb)
+        x_np = rng.standard_normal((m, k)).astype(np.float16)
+        x = torch.from_numpy(x_np).to(cuda_device)
+        out = torch.empty((m, n), dtype=dtype, device=cuda_device)
+        assert _noalloc(L, x, tr, su, sv, K, cb, out, out_dtype) == 0
+        ref = ops.matmul(x, tr, su, sv, K, cb, out_dtype=dtype)
         torch.cuda.synchronize()
-        assert O.normwise_rel_err(out.float().cpu().numpy(), ref.float().cpu().numpy()) < TOL, call
+        got = out.float().cpu().numpy()
+        assert O.normwise_rel_err(got, ref.float().cpu().numpy()) < tol, call
+        assert O.normwise_rel_err(got, O.gemv_ref(x_np, tr_np, su_np, sv_np, K, cb)) < tol, call
 
 
 def test_noalloc_limits(cuda_device):
