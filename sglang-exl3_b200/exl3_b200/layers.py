@@ -22,6 +22,7 @@ reference (``exl3.py:39-67``).
 
 from __future__ import annotations
 
+import itertools
 import logging
 import math
 import os
@@ -69,43 +70,65 @@ def set_weight_attrs(param: Parameter, extra_attrs: dict) -> None:
 
 
 # ---------------------------------------------------------------------------
-# tensor-parallel sharding (exl3.py:347-372; extended to dense layers)
+# tensor-parallel sharding
 # ---------------------------------------------------------------------------
+# The slice a rank takes of each checkpoint tensor, and the block it must keep whole.
+# Column-parallel linears split their output: trellis dim 1 in whole 128-column
+# Hadamard blocks (8 tiles) and svh, so each rank's output transform stays local.
+# Row-parallel linears split their input: trellis dim 0 and suh, in whole 128-row
+# blocks, so each rank's input transform stays local and the partial outputs sum.
+# Every other tensor is replicated.  Routed experts are sharded the same way as the
+# reference's (exl3.py:347-372); its dense layers have no tensor parallelism.
+TP_SPLITS = {
+    "column": {"trellis": (1, 8), "svh": (0, 128)},
+    "row": {"trellis": (0, 8), "suh": (0, 128)},
+}
 
-def _narrow_tp(tensor: torch.Tensor, dim: int, tp_rank: int, tp_size: int, multiple: int = 1) -> torch.Tensor:
-    if tp_size <= 1:
-        return tensor
-    size = int(tensor.shape[dim])
-    if size % tp_size:
-        raise ValueError(f"EXL3 TP shard: dim {dim} size {size} is not divisible by tp={tp_size}")
-    chunk = size // tp_size
-    if chunk % multiple:
-        raise ValueError(f"EXL3 TP shard: chunk {chunk} of dim {dim} is not a multiple of {multiple}")
-    return tensor.narrow(dim, chunk * tp_rank, chunk).contiguous()
+
+def tp_shard(tensor: torch.Tensor, suffix: str, kind: str, tp_rank: int, tp_size: int) -> torch.Tensor:
+    """This rank's slice of one checkpoint tensor under ``kind`` ("column" or "row")
+    parallelism; ValueError unless the extent splits into ``tp_size`` equal slices of
+    whole blocks."""
+    split = TP_SPLITS[kind].get(suffix)
+    if split is None or tp_size <= 1:
+        return tensor.contiguous()
+    dim, block = split
+    extent = int(tensor.shape[dim])
+    per_rank, rem = divmod(extent, tp_size)
+    if rem or per_rank % block:
+        raise ValueError(f"EXL3 TP shard: {suffix} dim {dim} of size {extent} does not split into "
+                         f"{tp_size} slices of whole {block}-blocks")
+    return tensor.narrow(dim, per_rank * tp_rank, per_rank).contiguous()
 
 
 def shard_exl3_col(loaded: torch.Tensor, suffix: str, tp_rank: int, tp_size: int) -> torch.Tensor:
-    """Column-parallel shard: output tiles (trellis dim 1) and svh.  Shards keep whole
-    128-column Hadamard blocks (8 tiles), so each rank's output transform is local."""
-    if suffix == "trellis":
-        return _narrow_tp(loaded, 1, tp_rank, tp_size, 8)
-    if suffix == "svh":
-        return _narrow_tp(loaded, 0, tp_rank, tp_size, 128)
-    return loaded.contiguous()
+    """Column-parallel slice (output tiles of the trellis, svh)."""
+    return tp_shard(loaded, suffix, "column", tp_rank, tp_size)
 
 
 def shard_exl3_row(loaded: torch.Tensor, suffix: str, tp_rank: int, tp_size: int) -> torch.Tensor:
-    """Row-parallel shard: input tiles (trellis dim 0) and suh, whole 128-row blocks,
-    so each rank's input transform is local and partial outputs sum (all-reduce)."""
-    if suffix == "trellis":
-        return _narrow_tp(loaded, 0, tp_rank, tp_size, 8)
-    if suffix == "suh":
-        return _narrow_tp(loaded, 0, tp_rank, tp_size, 128)
-    return loaded.contiguous()
+    """Row-parallel slice (input tiles of the trellis, suh)."""
+    return tp_shard(loaded, suffix, "row", tp_rank, tp_size)
 
 
 def _marker_on(t: Optional[torch.Tensor]) -> bool:
     return t is not None and t.numel() > 0 and int(t.reshape(-1)[0]) != 0
+
+
+_QKV_SHARDS = {"q": 0, "k": 1, "v": 2}
+
+
+def linear_shard_index(shard_id) -> int:
+    """Shard of a dense loader call: None -> 0, "q"/"k"/"v" -> 0/1/2, else an index."""
+    if shard_id is None:
+        return 0
+    key = str(shard_id)
+    if key in _QKV_SHARDS:
+        return _QKV_SHARDS[key]
+    try:
+        return int(key)
+    except ValueError:
+        raise ValueError(f"EXL3 linear shard id {shard_id!r} is neither q/k/v nor an index") from None
 
 
 class EXL3DenseLinear:
@@ -149,62 +172,63 @@ class EXL3LinearMethod(LinearMethodBase):
             raise ValueError("parallel must be none, column or row")
         self.parallel = parallel
 
+    def _output_shards(self, output_partition_sizes) -> list:
+        """Output sizes of the layer's shards: a merged module whose checkpoint keeps
+        separate groups (``split_sizes``, from the quant config) gets one shard each."""
+        sizes = [int(s) for s in output_partition_sizes]
+        split = self.split_sizes
+        if split and len(sizes) == 1 and sum(split) == sizes[0]:
+            sizes = [int(s) for s in split]
+        return sizes
+
     def create_weights(self, layer, input_size_per_partition: int, output_partition_sizes: list, input_size: int,
                        output_size: int, params_dtype: torch.dtype, **extra_weight_attrs) -> None:
-        split = self.split_sizes
-        if split and len(output_partition_sizes) == 1 and sum(split) == output_partition_sizes[0]:
-            output_partition_sizes = [int(x) for x in split]
-        for out_size in output_partition_sizes:
-            if input_size_per_partition % 16 or out_size % 16:
-                raise ValueError(f"EXL3 trellis tiles are 16-wide; in={input_size_per_partition} out={out_size}")
-        extra = {k: v for k, v in extra_weight_attrs.items() if k != "weight_loader"}
+        """Register the ``exl3_{shard}_{suffix}`` parameters (the checkpoint tensors of
+        each output shard land in ``layer._exl3_lin_packs[shard]``) and an empty
+        ``weight`` placeholder, which SGLang's model code expects on every linear."""
+        sizes = self._output_shards(output_partition_sizes)
+        k_in = int(input_size_per_partition)
+        if k_in % 16 or any(n % 16 for n in sizes):
+            raise ValueError(f"EXL3 trellis tiles are 16-wide; in={k_in} out={sizes}")
+        attrs = {k: v for k, v in extra_weight_attrs.items() if k != "weight_loader"}
         layer._exl3_out_dtype = params_dtype or torch.bfloat16
+        layer._exl3_lin_packs = [dict.fromkeys(EXL3_SUFFIXES) for _ in sizes]
+        layer._exl3_lin_n_shards = len(sizes)
+        layer._exl3_lin_input_size_per_partition = k_in
+        layer._exl3_lin_output_partition_sizes = sizes
+        layer._exl3_linears = None
         if not hasattr(layer, "weight"):
             layer.register_parameter("weight", Parameter(torch.empty(0, dtype=torch.int16), requires_grad=False))
-        n = len(output_partition_sizes)
-        layer._exl3_lin_packs = [{s: None for s in EXL3_SUFFIXES} for _ in range(n)]
-        layer._exl3_lin_n_shards = n
-        layer._exl3_lin_input_size_per_partition = int(input_size_per_partition)
-        layer._exl3_lin_output_partition_sizes = [int(s) for s in output_partition_sizes]
-        layer._exl3_linears = None
-        for i in range(n):
-            for suffix in EXL3_SUFFIXES:
-                p = Parameter(torch.empty(0), requires_grad=False)
-                layer.register_parameter(f"exl3_{i}_{suffix}", p)
-                set_weight_attrs(p, extra)
-                p.weight_loader = self._load_linear
-                p._exl3_owner = layer
-                p._exl3_shard = i
-                p._exl3_suffix = suffix
+        for shard, suffix in itertools.product(range(len(sizes)), EXL3_SUFFIXES):
+            p = Parameter(torch.empty(0), requires_grad=False)
+            set_weight_attrs(p, attrs)
+            set_weight_attrs(p, {"weight_loader": self._load_linear, "_exl3_owner": layer, "_exl3_shard": shard,
+                                 "_exl3_suffix": suffix})
+            layer.register_parameter(f"exl3_{shard}_{suffix}", p)
 
     @staticmethod
     def _shard_index(shard_id) -> int:
-        if shard_id is None:
-            return 0
-        if isinstance(shard_id, str):
-            if shard_id in ("q", "k", "v"):
-                return {"q": 0, "k": 1, "v": 2}[shard_id]
-            return int(shard_id)
-        return int(shard_id)
+        """Shard of a loader call: None -> 0, "q"/"k"/"v" -> 0/1/2, else an index."""
+        return linear_shard_index(shard_id)
+
+    def _device_copy(self, src: torch.Tensor, suffix: str) -> torch.Tensor:
+        dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else src.device
+        if suffix in ("mcg", "mul1") and src.numel() == 1:
+            return torch.full((1,), int(src.reshape(())), dtype=torch.int32, device=dev)
+        if self.parallel != "none":
+            src = tp_shard(src, suffix, self.parallel, self.tp_rank, self.tp_size)
+        if suffix in ("suh", "svh"):
+            src = src.to(torch.float16)
+        return src.to(device=dev).contiguous()
 
     def _load_linear(self, param, loaded_weight, shard_id=None):
+        """weight_loader of every ``exl3_*`` parameter: this rank's slice of the tensor,
+        on the current device, into the shard's pack."""
         layer = getattr(param, "_exl3_owner", None)
         suffix = getattr(param, "_exl3_suffix", None)
         if layer is None or suffix is None:
             return
-        pack = layer._exl3_lin_packs[self._shard_index(shard_id)]
-        src = loaded_weight.detach()
-        dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else src.device
-        if src.numel() == 1 and suffix in ("mcg", "mul1"):
-            pack[suffix] = torch.tensor([int(src.reshape(()).item())], dtype=torch.int32, device=dev)
-            return
-        if self.parallel == "column":
-            src = shard_exl3_col(src, suffix, self.tp_rank, self.tp_size)
-        elif self.parallel == "row":
-            src = shard_exl3_row(src, suffix, self.tp_rank, self.tp_size)
-        if suffix in ("suh", "svh"):
-            src = src.to(torch.float16)
-        pack[suffix] = src.to(device=dev).contiguous()
+        layer._exl3_lin_packs[linear_shard_index(shard_id)][suffix] = self._device_copy(loaded_weight.detach(), suffix)
 
     def process_weights_after_loading(self, layer) -> None:
         packs = getattr(layer, "_exl3_lin_packs", None)
@@ -290,31 +314,58 @@ class EXL3LinearMethod(LinearMethodBase):
 # routed experts
 # ---------------------------------------------------------------------------
 
+class ExpertIdMap:
+    """Global -> local expert ids as one device gather.
+
+    The routing contract is the reference's (``exl3.py:485-509``): an id is replaced by
+    its local id when ``expert_map`` (global -> local, -1 elsewhere) gives one in
+    ``[0, n_local)``, and by the sentinel ``n_local`` otherwise (negative, past the
+    map, or another rank's expert), which the MoE kernels skip.  Here the map is
+    folded once into a table of ``n_global + 1`` entries whose last entry is the
+    sentinel, and every id outside ``[0, n_global)`` is pointed at it, so a call is a
+    ``where`` and a gather, with no host synchronisation (graph-capturable)."""
+
+    def __init__(self, n_local: int, expert_map: Optional[torch.Tensor], device: torch.device):
+        if expert_map is None:
+            local = torch.arange(n_local, dtype=torch.long, device=device)
+        else:
+            m = expert_map.to(device=device, dtype=torch.long)
+            local = torch.where((m >= 0) & (m < n_local), m, torch.full_like(m, n_local))
+        self.table = torch.cat([local, torch.full((1,), n_local, dtype=torch.long, device=device)])
+        self.n_global = int(local.numel())
+        self.source = expert_map
+
+    def __call__(self, ids: torch.Tensor) -> torch.Tensor:
+        ids = ids.to(torch.long)
+        inside = (ids >= 0) & (ids < self.n_global)
+        return self.table[torch.where(inside, ids, torch.full_like(ids, self.n_global))]
+
+
 def pin_exl3_expert_map(layer: torch.nn.Module, device: torch.device) -> Optional[torch.Tensor]:
+    """Move the layer's ``expert_map`` to ``device`` as int64 (once) and return it."""
     emap = getattr(layer, "expert_map", None)
-    if emap is None:
-        return None
-    if emap.device != device or emap.dtype != torch.long:
-        layer.expert_map = emap.to(device=device, dtype=torch.long)
-    return layer.expert_map
+    if emap is not None and (emap.device != device or emap.dtype != torch.long):
+        layer.expert_map = emap = emap.to(device=device, dtype=torch.long)
+    return emap
 
 
 def map_topk_to_local(ids: torch.Tensor, n_local: int, expert_map: Optional[torch.Tensor]) -> torch.Tensor:
-    """Global -> local expert ids; invalid ids become the sentinel ``n_local``
-    (``exl3.py:494-509``), which the MoE kernels skip (weight 0)."""
-    shape = ids.shape
-    flat = ids.reshape(-1)
-    if expert_map is None:
-        invalid = (flat < 0) | (flat >= n_local)
-        return torch.where(invalid, flat.new_full(flat.shape, n_local), flat).reshape(shape)
-    if expert_map.device != flat.device or expert_map.dtype != torch.long:
-        raise RuntimeError("EXL3 expert_map is not pinned to the hidden-state device; "
-                           "call pin_exl3_expert_map before fused apply")
-    n_global = int(expert_map.numel())
-    safe = flat.clamp(min=0, max=max(n_global - 1, 0))
-    mapped = expert_map[safe] if n_global else flat.new_full(flat.shape, n_local)
-    invalid = (flat < 0) | (flat >= n_global) | (mapped < 0) | (mapped >= n_local)
-    return torch.where(invalid, flat.new_full(flat.shape, n_local), mapped).reshape(shape)
+    """Global -> local expert ids with the sentinel ``n_local`` for ids that are not
+    local (``ExpertIdMap``); ``expert_map`` must already be int64 on the ids' device."""
+    if expert_map is not None and (expert_map.device != ids.device or expert_map.dtype != torch.long):
+        raise RuntimeError("EXL3 expert_map must be int64 on the hidden-state device: "
+                           "call pin_exl3_expert_map before the fused apply")
+    return ExpertIdMap(n_local, expert_map, ids.device)(ids)
+
+
+def _layer_id_map(layer, n_local: int, device: torch.device) -> ExpertIdMap:
+    """The layer's cached ``ExpertIdMap``, rebuilt when its expert_map changes."""
+    emap = pin_exl3_expert_map(layer, device)
+    cached = getattr(layer, "_exl3_id_map", None)
+    if cached is None or cached.source is not emap or cached.table.device != device:
+        cached = ExpertIdMap(n_local, emap, device)
+        layer._exl3_id_map = cached
+    return cached
 
 
 def _suffix_from_mapped_name(weight_name: str) -> str:
@@ -373,35 +424,34 @@ class EXL3MoEMethod(FusedMoEMethodBase):
         layer._exl3_k_words = k_words
         layer._exl3_bits = self.bits
 
+    # checkpoint shard id -> (index inside the expert's w13 pair, or None for w2; TP kind)
+    EXPERT_SHARDS = {"w1": (0, "column"), "w3": (1, "column"), "w2": (None, "row")}
+
     def _load_exl3(self, param, loaded_weight, weight_name: str, shard_id: str = "w1", expert_id: int = 0,
                    return_success: bool = False):
+        """weight_loader of the stacked expert parameters: this rank's slice of one
+        expert tensor into its slot.  An expert that another rank owns is skipped
+        (False with ``return_success``); a marker scalar fills its one-element slot."""
+        done = True if return_success else None
         owner = getattr(param, "_exl3_owner", None)
-        if owner is not None and hasattr(owner, "_map_global_expert_id_to_local_expert_id"):
-            local_id = owner._map_global_expert_id_to_local_expert_id(expert_id)
-            if local_id == -1:
+        to_local = getattr(owner, "_map_global_expert_id_to_local_expert_id", None)
+        if to_local is not None:
+            expert_id = to_local(expert_id)
+            if expert_id == -1:
                 return False if return_success else None
-            expert_id = local_id
-        suffix = _suffix_from_mapped_name(weight_name)
-        loaded = loaded_weight.detach().contiguous()
-        if shard_id in ("w1", "w3"):
-            sharded = shard_exl3_col(loaded, suffix, self.tp_rank, self.tp_size)
-            dest = param.data[expert_id, 0 if shard_id == "w1" else 1]
-        elif shard_id == "w2":
-            sharded = shard_exl3_row(loaded, suffix, self.tp_rank, self.tp_size)
-            dest = param.data[expert_id]
-        else:
+        if shard_id not in self.EXPERT_SHARDS:
             raise ValueError(f"unknown EXL3 shard_id={shard_id}")
-        if suffix in ("mcg", "mul1") and sharded.numel() == 1 and dest.numel() == 1:
-            dest.view(-1)[0] = sharded.reshape(-1)[0].to(dest.dtype)
-            return True if return_success else None
-        if tuple(dest.shape) != tuple(sharded.shape):
-            if sharded.numel() == dest.numel():
-                dest.copy_(sharded.reshape(dest.shape))
-                return True if return_success else None
+        half, kind = self.EXPERT_SHARDS[shard_id]
+        suffix = _suffix_from_mapped_name(weight_name)
+        src = tp_shard(loaded_weight.detach(), suffix, kind, self.tp_rank, self.tp_size)
+        dest = param.data[expert_id] if half is None else param.data[expert_id, half]
+        if src.numel() != dest.numel():
             raise RuntimeError(f"EXL3 load shape mismatch {weight_name} shard={shard_id} expert={expert_id}: "
-                               f"dest {tuple(dest.shape)} != loaded {tuple(sharded.shape)}")
-        dest.copy_(sharded)
-        return True if return_success else None
+                               f"dest {tuple(dest.shape)} != loaded {tuple(src.shape)}")
+        # same element count: the checkpoint's layout of this slot (a 0-d marker, a
+        # flattened vector) is taken as the slot's
+        dest.copy_(src.reshape(dest.shape))
+        return done
 
     def process_weights_after_loading(self, layer) -> None:
         if not hasattr(layer, "w13_trellis"):
@@ -477,8 +527,7 @@ def apply_exl3_experts(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: to
     x2d = x.reshape(tokens, hidden)
     xh = x2d if (x2d.dtype == torch.float16 and x2d.is_contiguous()) else x2d.to(torch.float16).contiguous()
     n_local = int(layer._exl3_n_local)
-    ids = map_topk_to_local(topk_ids.reshape(tokens, -1).to(torch.long), n_local,
-                            pin_exl3_expert_map(layer, x2d.device)).to(torch.int32)
+    ids = _layer_id_map(layer, n_local, x2d.device)(topk_ids.reshape(tokens, -1)).to(torch.int32)
     w = topk_weights.reshape(tokens, -1).to(torch.float32)
     lim = 0.0 if (limit is None or not math.isfinite(float(limit))) else float(limit)
     topk = ids.shape[1]
