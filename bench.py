@@ -276,27 +276,76 @@ def isolated_kernel_time(tr_list, su_list, sv_list, K, cb, m, reps, device):
     return t / len(tr_list)
 
 
-def cpu_baseline_sample(steps_hint: int = 1):
-    """The reference's CPU path (compiled dequant_trellis + at::mm) on one config-1
-    linear (4096 x 4096, 4 bpw; the binding reaches only MCG/mul1, so MCG) - the
-    bounded sample.  Returns (seconds per linear, weights per linear, threads)."""
+# Reference CPU sample: the reference's dequant_trellis + at::mm on REF_SAMPLE_ROWS x 4096
+# weights (4 bpw MCG: its binding cannot select 3INST) - about a second per step on the
+# single-threaded reference dequant, so a default --steps/--warmup run ends in well under
+# a minute.
+REF_SAMPLE_ROWS, REF_SAMPLE_COLS = 256, 4096
+
+
+def ref_module():
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     from build_ref import load_ref_module
 
-    ref = load_ref_module()
-    if ref is None:
-        return None
+    return load_ref_module()
+
+
+def ref_sample_inputs():
     rng = np.random.default_rng(0)
-    tr = torch.from_numpy(rng.integers(-32768, 32768, size=(256, 256, 64)).astype(np.int16))
-    su = torch.from_numpy((np.where(rng.integers(0, 2, 4096) == 0, -1.0, 1.0) * rng.uniform(0.5, 1.5, 4096)).astype(np.float16))
-    sv = torch.from_numpy((np.where(rng.integers(0, 2, 4096) == 0, -1.0, 1.0) * rng.uniform(0.5, 1.5, 4096)).astype(np.float16))
-    x = torch.from_numpy(rng.standard_normal((1, 4096)).astype(np.float16))
+    k, n = REF_SAMPLE_ROWS, REF_SAMPLE_COLS
+    tr = torch.from_numpy(rng.integers(-32768, 32768, size=(k // 16, n // 16, 64)).astype(np.int16))
+    su = torch.from_numpy((np.where(rng.integers(0, 2, k) == 0, -1.0, 1.0) * rng.uniform(0.5, 1.5, k)).astype(np.float16))
+    sv = torch.from_numpy((np.where(rng.integers(0, 2, n) == 0, -1.0, 1.0) * rng.uniform(0.5, 1.5, n)).astype(np.float16))
+    x = torch.from_numpy(rng.standard_normal((1, k)).astype(np.float16))
+    return x, tr, su, sv
+
+
+def ref_cpu_times(ref, steps: int, warmup: int):
+    """Seconds of each of ``steps`` timed calls of the reference's CPU ``exl3_gemv``
+    (``csrc/bindings.cpp:134-147``: dequant_trellis + at::mm) on the sample, after
+    ``warmup`` untimed ones."""
+    x, tr, su, sv = ref_sample_inputs()
+    for _ in range(warmup):
+        ref.exl3_gemv(x, tr, su, sv, 4, True, 1)
     ts = []
-    for _ in range(max(1, steps_hint)):
+    for _ in range(steps):
         t0 = time.perf_counter()
         ref.exl3_gemv(x, tr, su, sv, 4, True, 1)
         ts.append(time.perf_counter() - t0)
-    return float(np.median(ts)), 4096 * 4096, torch.get_num_threads()
+    return ts
+
+
+def port_sample_shape(args):
+    """(k, n, K, cb, rows, name) of the full projection the CPU port is timed on."""
+    if args.workload == "linear":
+        return args.k, args.n, args.bits, 0, args.batch, f"{args.k}x{args.n} {args.bits}-bpw 3INST linear"
+    if args.workload == "mlp":
+        return 25600, 5120, 4, 1, args.batch, "config-2 down projection 25600x5120 4-bpw MCG"
+    if args.workload in ("moe", "verify"):
+        if args.workload == "verify" or getattr(args, "moe", "c3") == "c5":
+            return 4096, 1536, 3, 0, 5, "config-5 expert gate projection 4096x1536 3-bpw 3INST"
+        return 2048, 1024, 3, 0, 1, "config-3 expert gate projection 2048x1024 3-bpw 3INST"
+    return 8192, 8192, 4, 0, args.batch, "config-4 o projection 8192x8192 4-bpw 3INST"
+
+
+def port_cpu_time(args):
+    """CPU baseline (ii): the pure-torch table decode + torch.mm (oracle/torch_lut.py) on
+    all host cores, one full projection of the workload; returns (seconds, weights, threads, name)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from torch_lut import TorchLutLinear
+
+    k, n, K, cb, rows, name = port_sample_shape(args)
+    g = torch.Generator()
+    g.manual_seed(0)
+    tr = torch.randint(-32768, 32768, (k // 16, n // 16, 16 * K), dtype=torch.int16, generator=g)
+    su = ((torch.randint(0, 2, (k,), generator=g) * 2 - 1) * (torch.rand(k, generator=g) + 0.5)).half()
+    sv = ((torch.randint(0, 2, (n,), generator=g) * 2 - 1) * (torch.rand(n, generator=g) + 0.5)).half()
+    x = torch.randn(rows, k, generator=g).half()
+    lin = TorchLutLinear(tr, su, sv, K, cb)
+    lin(x[:, :])  # warm the allocator and thread pool
+    t0 = time.perf_counter()
+    lin(x)
+    return time.perf_counter() - t0, k * n, torch.get_num_threads(), name
 
 
 def workload_scale(args):
@@ -325,31 +374,78 @@ def workload_scale(args):
     return model_weights, args.batch, "tok/s"
 
 
+def workload_metric(args):
+    if args.workload == "mlp":
+        return "C2 SwiGLU MLP block rows/s"
+    if args.workload == "moe":
+        return ("C5" if args.moe == "c5" else "C3") + " routed MoE layer tokens/s"
+    if args.workload == "verify":
+        return "C5 speculative verify tok/s (48-layer MoE, 5 tokens per sequence)"
+    return METRIC
+
+
+def decode_steps(args):
+    return min(args.steps, 512 - args.warmup - 8)
+
+
+def decode_config(args, world, fused=None):
+    """The ``config`` of the decode workload (both arms print the same one)."""
+    from exl3_b200.harness import LLAMA_70B, exl3_weight_bytes
+
+    import dataclasses
+
+    cfg = LLAMA_70B if args.layers == LLAMA_70B.layers else dataclasses.replace(LLAMA_70B, layers=args.layers)
+    if fused is None:
+        fused = args.batch <= 16
+    return {"workload": "llama70b-shape decode (config 4), greedy, one CUDA graph per step"
+                        + (", fused decode layers" if fused else ", unfused torch glue"),
+            "model": "llama-70b-shape (random init)", "layers": cfg.layers, "global_batch": args.batch,
+            "seq_len": args.ctx, "new_tokens_timed": decode_steps(args), "parallelism": f"tp{world}", "bpw": cfg.K,
+            "codebook": "3INST", "kv_cache": "bf16, random contents for the 2048-token prompt",
+            "l2": "no flush needed: 34.2 GB / tp of codes per step >> 126 MB L2",
+            "exl3_bytes_per_step_per_rank": exl3_weight_bytes(cfg, world)}
+
+
+def workload_config(args, world):
+    if args.workload == "decode":
+        return decode_config(args, world)
+    return {"workload": args.workload, "batch": args.batch,
+            **({"moe": args.moe} if args.workload == "moe" else {}),
+            **({"k": args.k, "n": args.n, "bits": args.bits} if args.workload == "linear" else {}),
+            "parallelism": f"tp{world}" if args.workload in ("mlp", "linears") else
+            (f"ep{world}" if world > 1 else "single GPU")}
+
+
 # ---------------------------------------------------------------------------
 # arms
 # ---------------------------------------------------------------------------
 
 def run_reference(args, world, rank):
+    """The reference's own CPU path on the host cores (rank 0 only): each step is one
+    bounded sample, scaled to the workload's unit by the weights a step decodes."""
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 3))
-    sample = cpu_baseline_sample(steps)
-    if sample is None:
+    ref = ref_module()
+    if ref is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref not built (python oracle/build_ref.py)"}))
         return
-    sec, weights, threads = sample
+    ts = ref_cpu_times(ref, args.steps, args.warmup)
+    sec = float(np.mean(ts))
+    weights = REF_SAMPLE_ROWS * REF_SAMPLE_COLS
     step_weights, units, unit = workload_scale(args)
     step_s = sec * step_weights / weights
     value = units / step_s
-    ms = step_s * 1e3
+    sample = (f"reference dequant_trellis + at::mm (csrc/bindings.cpp:134-147) on a {REF_SAMPLE_ROWS}x{REF_SAMPLE_COLS} "
+              f"4-bpw MCG linear per step (its binding cannot select 3INST), scaled by the {step_weights:.4g} "
+              "weights one workload step decodes")
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": unit, "n_gpus": world, "steps": steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "impl": "reference", "metric": workload_metric(args), "value": value, "unit": unit, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3,
+        "ms_per_step_extrapolated": step_s * 1e3, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "fp32 (reference CPU dequant + at::mm)", "data": "synthetic (seeded)",
-        "config": {"workload": args.workload, "batch": args.batch,
-                   "sample": "one 4096x4096 4-bpw MCG linear per step, scaled by the workload's weight count"},
-        "cpu_baseline": {"value": value, "unit": unit, "cores": threads, "kind": "reference",
-                         "sample": "reference dequant_trellis + at::mm on one 4096x4096 linear (MCG: the binding cannot select 3INST)"},
+        "config": workload_config(args, world),
+        "cpu_baseline": {"value": value, "unit": unit, "cores": torch.get_num_threads(), "kind": "reference",
+                         "sample": sample},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -773,7 +869,7 @@ def run_decode(args, world, rank, local, device):
     model = DecodeModel(cfg, batch, args.ctx + new_tokens, device, world, rank, group)
     model.fill_random_kv(args.ctx)
     model.capture()
-    steps = min(args.steps, new_tokens - args.warmup - 8)
+    steps = decode_steps(args)
     model.pos.fill_(args.ctx)
     model.decode(args.warmup)
     torch.cuda.synchronize()
@@ -829,13 +925,7 @@ def run_decode(args, world, rank, local, device):
 
     line = {
         "metric": METRIC, "value": tok_s, "unit": "tok/s", "ms_per_step": ms,
-        "config": {"workload": "llama70b-shape decode (config 4), greedy, one CUDA graph per step"
-                               + (", fused decode layers" if model.fused else ", unfused torch glue"),
-                   "model": "llama-70b-shape (random init)", "layers": cfg.layers, "global_batch": batch,
-                   "seq_len": args.ctx, "new_tokens_timed": steps, "parallelism": f"tp{world}", "bpw": cfg.K,
-                   "codebook": "3INST", "kv_cache": "bf16, random contents for the 2048-token prompt",
-                   "l2": "no flush needed: 34.2 GB / tp of codes per step >> 126 MB L2",
-                   "exl3_bytes_per_step_per_rank": step_bytes},
+        "config": decode_config(args, world, model.fused),
         "exl3_gbs_per_rank": step_bytes / (ms * 1e-3) / 1e9,
         "roofline": {"bound": "hbm", "achieved": k_gbs, "peak": hbm_peak, "unit": "GB/s", "frac": k_gbs / hbm_peak,
                      "traffic": GATEUP_TRAFFIC_BYTES * model.i_loc / 28672, "peak_kind": peak_kind,
@@ -843,8 +933,9 @@ def run_decode(args, world, rank, local, device):
                                        "mean of 3 launches at 8192x2x28672 M=1, scaled by the shard's columns",
                      "kernel": f"fused gate+up EXL3 matmul 8192x2x{model.i_loc} 4bpw M={batch} (3 kernels)"},
         "e2e": {"value": batch / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
-                "h2d_bytes_per_step": 8 * batch, "d2h_bytes_per_step": 8 * batch,
-                "path": "DecodeModel.generate: per step, tokens H2D from pinned host memory, graph replay, tokens D2H, stream sync"},
+                "h2d_bytes_per_step": 8 * batch, "d2h_bytes_per_step": 8 * batch + 4,
+                "path": "DecodeModel.generate: per step, tokens H2D from pinned host memory, graph replay, tokens "
+                        "and the device status word D2H, stream sync"},
         # fused: per layer 6 (attention) + 5 (MLP) launches (the NVLink exchange runs inside the o/down
         # epilogues); + 2 residual-add kernels per layer when TP goes through NCCL instead
         "gpu_launches": steps * cfg.layers * ((11 + (2 if world > 1 and not peer_exchange else 0))
@@ -860,14 +951,21 @@ def finish(line, args, world):
             "data": "synthetic (seeded random trellis codes, random-init)"}
     base.update(line)
     if int(os.environ.get("RANK", "0")) == 0:
-        if args.cpu_baseline:
-            sample = cpu_baseline_sample(1)
-            if sample is not None:
-                sec, weights, threads = sample
-                step_weights, units, u = workload_scale(args)
-                v = units / (sec * step_weights / weights)
-                base["cpu_baseline"] = {"value": v, "unit": u, "cores": threads, "kind": "reference",
-                                        "sample": "reference dequant_trellis + at::mm, one 4096x4096 4-bpw MCG linear"}
+        if args.cpu_baseline and world == 1:
+            step_weights, units, u = workload_scale(args)
+            sec, weights, threads, name = port_cpu_time(args)
+            base["cpu_baseline"] = {
+                "value": units / (sec * step_weights / weights), "unit": u, "cores": threads, "kind": "port",
+                "sample": f"pure-torch 3INST/MCG table decode + torch.mm (oracle/torch_lut.py) on all host threads, "
+                          f"one full {name} ({sec:.3f} s), scaled by the {step_weights:.4g} weights of a step"}
+            ref = ref_module()
+            if ref is not None:
+                rsec = float(np.median(ref_cpu_times(ref, 2, 1)))
+                base["cpu_baseline_reference"] = {
+                    "value": units / (rsec * step_weights / (REF_SAMPLE_ROWS * REF_SAMPLE_COLS)), "unit": u,
+                    "cores": torch.get_num_threads(), "kind": "reference",
+                    "sample": f"reference dequant_trellis + at::mm on a {REF_SAMPLE_ROWS}x{REF_SAMPLE_COLS} 4-bpw MCG "
+                              f"linear ({rsec:.3f} s; single-threaded dequant), scaled the same way"}
         print(json.dumps(base))
     return base
 

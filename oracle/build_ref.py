@@ -15,9 +15,9 @@ Two artefacts, each compiled from the read-only reference sources where they lie
   extraction for K=1..8); ``tests/golden/make_fixtures.py`` turns the dump into
   a committed fixture.
 
-Usage: ``python oracle/build_ref.py [--reference /path/to/reference]``.  Needs the
-reference tree, so it only runs in the build container; the GPU box uses the
-prebuilt files.
+Usage: ``python oracle/build_ref.py --reference /path/to/reference`` (or with the
+environment variable ``EXL3_REFERENCE_DIR`` set).  Needs the reference tree, so it
+only runs in the build container; the GPU box uses the prebuilt files.
 """
 
 from __future__ import annotations
@@ -30,7 +30,12 @@ import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-DEFAULT_REF = "/root/reference"
+REF_ENV = "EXL3_REFERENCE_DIR"  # where the reference tree lies, when it is present
+
+
+def reference_dir(arg=None):
+    """The reference tree named by the argument or by ``EXL3_REFERENCE_DIR``, else None."""
+    return arg or os.environ.get(REF_ENV) or None
 
 
 def ref_module_path() -> str:
@@ -80,9 +85,10 @@ def build_dump_binary(ref: str) -> str:
     return out
 
 
-def build(ref: str = DEFAULT_REF) -> bool:
+def build(ref=None) -> bool:
     """Build both artefacts; returns False (and builds nothing) without the reference tree."""
-    if not os.path.isdir(os.path.join(ref, "csrc")):
+    ref = reference_dir(ref)
+    if not ref or not os.path.isdir(os.path.join(ref, "csrc")):
         return False
     os.makedirs(OUT, exist_ok=True)
     build_cpu_module(ref)
@@ -107,7 +113,7 @@ def load_ref_module():
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=DEFAULT_REF)
+    ap.add_argument("--reference", default=None, help=f"reference tree (default: ${REF_ENV})")
     args = ap.parse_args()
     if not build(args.reference):
         print(f"reference tree not found at {args.reference}; nothing built", file=sys.stderr)

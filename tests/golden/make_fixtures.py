@@ -2,8 +2,8 @@
 
 Run in the build container, where the reference tree is present:
 
-    python oracle/build_ref.py                 # compiles the reference into oracle/_ref
-    python tests/golden/make_fixtures.py       # CPU fixtures
+    python oracle/build_ref.py --reference R   # compiles the reference into oracle/_ref
+    python tests/golden/make_fixtures.py --reference R   # CPU fixtures
     python tests/golden/make_fixtures.py --device-dump <dump file>
                                                # the file oracle/_ref/ref_codebook_dump wrote on a B200
 
@@ -36,9 +36,7 @@ ROOT = os.path.dirname(os.path.dirname(HERE))
 sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 import exl3_oracle as O  # noqa: E402
-from build_ref import load_ref_module  # noqa: E402
-
-REF = "/root/reference"
+from build_ref import load_ref_module, reference_dir  # noqa: E402
 
 
 def make_dequant(ref) -> None:
@@ -62,8 +60,9 @@ def make_dequant(ref) -> None:
     np.savez_compressed(os.path.join(HERE, "ref_dequant_trunc.npz"), **arrays)
 
 
-def make_mul1_lut() -> None:
-    spec = importlib.util.spec_from_file_location("ref_ple_ngram", os.path.join(REF, "src/sglang_exl3/ple_ngram.py"))
+def make_mul1_lut(ref_dir: str) -> None:
+    spec = importlib.util.spec_from_file_location("ref_ple_ngram",
+                                                  os.path.join(ref_dir, "src/sglang_exl3/ple_ngram.py"))
     mod = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(mod)
     lut = mod.mul1_codebook("cpu").numpy().view(np.uint16)
@@ -114,6 +113,7 @@ def convert_device_dump(path: str) -> None:
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--device-dump", default=None, help="raw output of oracle/_ref/ref_codebook_dump")
+    ap.add_argument("--reference", default=None, help="reference tree (default: $EXL3_REFERENCE_DIR)")
     args = ap.parse_args()
     if args.device_dump:
         convert_device_dump(args.device_dump)
@@ -121,7 +121,10 @@ if __name__ == "__main__":
         ref = load_ref_module()
         if ref is None:
             raise SystemExit("oracle/_ref not built: run python oracle/build_ref.py first")
+        ref_dir = reference_dir(args.reference)
+        if not ref_dir:
+            raise SystemExit("name the reference tree: --reference or EXL3_REFERENCE_DIR")
         make_dequant(ref)
-        make_mul1_lut()
+        make_mul1_lut(ref_dir)
         make_cpu_gemv(ref)
     print("fixtures written to", HERE)
