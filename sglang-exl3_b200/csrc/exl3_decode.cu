@@ -539,11 +539,10 @@ __global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __gri
     griddep_wait();
     __shared__ int ok;
     PeerCtl* ctl = reinterpret_cast<PeerCtl*>(x.peer[x.peer_rank]);
-    if (*reinterpret_cast<volatile unsigned int*>(&ctl->poisoned)) {
-        // an earlier exchange gave up: no stores, no arrivals, no update
-        if (threadIdx.x == 0 && x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
-        return;
-    }
+    // an earlier exchange gave up: the partial sums are still consumed (the matmul
+    // state is left zeroed for the next call), but nothing is stored, no arrival is
+    // made and h is not updated
+    const bool poisoned = *reinterpret_cast<volatile unsigned int*>(&ctl->poisoned) != 0u;
     const unsigned int epoch = *reinterpret_cast<volatile unsigned int*>(&ctl->epoch) + 1u;
     const unsigned int parity = epoch & 1u;
     const int warps = gridDim.x * (blockDim.x >> 5);
@@ -554,11 +553,16 @@ __global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __gri
         const int r = task / nblocks, nb = task - r * nblocks;
         float v[4];
         gv_finish<CB>(p, nb, r, lane, v);
+        if (poisoned) continue;
         for (int q = 0; q < x.peer_world; ++q) {
             float* dst = peer_slot(x, q, parity, x.peer_rank, r) + nb * 128;
 #pragma unroll
             for (int e = 0; e < 4; ++e) dst[lane + 32 * e] = v[e];
         }
+    }
+    if (poisoned) {
+        if (threadIdx.x == 0 && x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
+        return;
     }
     __threadfence_system();
     __syncthreads();

@@ -80,10 +80,19 @@ TOL_RESIDUAL = 1e-2
 TOL_LOGITS = 1e-2
 
 
+def _tame(m):
+    """Output scales 1/sqrt(k): random codes decode to weights of order 1, and without
+    this the unfused step's fp16 projection outputs overflow within two layers."""
+    for L in m.layers:
+        for lin in L["qkv"] + [L["o"]] + L["gu"] + [L["down"]]:
+            lin[2].mul_(float(lin[0].size(0) * 16) ** -0.5)
+    return m
+
+
 @pytest.mark.parametrize("fused", [True, False])
 def test_step_matches_dequantised_torch(cuda_device, fused):
     torch.backends.cuda.matmul.allow_tf32 = False
-    m = DecodeModel(TINY, batch=2, max_ctx=32, device=cuda_device, fused=fused)
+    m = _tame(DecodeModel(TINY, batch=2, max_ctx=32, device=cuda_device, fused=fused))
     m.fill_random_kv(10)
     tokens = torch.tensor([5, 9], device=cuda_device)
     m.tokens.copy_(tokens)
