@@ -66,6 +66,37 @@ EXL3B200_API int exl3b200_abi_version(void);
 EXL3B200_API const char* exl3b200_status_string(int status);
 
 /*
+ * Kernel-shape map: which kernel family serves a problem.  Replaces the
+ * reference's select_gemm_shape / exl3_gemm_num_kernel_shapes /
+ * exl3_gemm_shape_compat (csrc/quant/exl3_kernel_map.cuh:3-5), whose table of
+ * mma.sync tile shapes lives in the unvendored exllamav3.  The B200 table is keyed
+ * by rows (per problem, or per expert for routed MoE) and K, from crossovers
+ * measured on a B200 (the numbers are in the table's comments).
+ */
+#define EXL3B200_SHAPE_GV8 1       /* small-M, one 8-row group, 8 tiles per warp, 2 CTAs per SM */
+#define EXL3B200_SHAPE_GV8_NARROW 2 /* small-M, one 8-row group, 4 tiles per warp, 3 CTAs per SM */
+#define EXL3B200_SHAPE_GV16 3      /* small-M, two 8-row groups (9..16 rows) */
+#define EXL3B200_SHAPE_TC 4        /* tcgen05, 256 x 256 tiles, persistent, whole tiles then stream-K */
+#define EXL3B200_SHAPE_MOE_SMALL 5 /* routed MoE on the grouped small-M pipeline */
+#define EXL3B200_SHAPE_MOE_TC 6    /* routed MoE on grouped tcgen05 GEMMs */
+
+typedef struct exl3b200_shape_desc {
+    const char* name;
+    int max_rows;     /* rows one launch of this shape takes per problem (0 = any) */
+    int tile_rows;    /* rows of one output tile (8, 16 or 256) */
+    int tile_cols;    /* output columns of one tile (128 or 256) */
+    int ctas_per_sm;
+} exl3b200_shape_desc;
+
+EXL3B200_API int exl3b200_num_shapes(void);
+/* experts == 0: a dense matmul of m rows; experts > 0: a routed MoE layer of m tokens
+ * with topk experts each over `experts` local experts.  Returns a shape id. */
+EXL3B200_API int exl3b200_select_shape(int m, int k, int n, int K, int cb, int experts, int topk);
+/* 1 when the shape can run the problem (rows, k/n multiples of 128, K 2..4), else 0 */
+EXL3B200_API int exl3b200_shape_compat(int shape, int m, int k, int n, int K);
+EXL3B200_API int exl3b200_shape_info(int shape, exl3b200_shape_desc* out);
+
+/*
  * Reconstruct the fp16 weight W [k, n] (row-major) from its trellis.
  * Replaces sglang_exl3_c.dequant_trellis (reference csrc/bindings.cpp:117-132,
  * op signature src/sglang_exl3/ops.py:38-54).  k and n must be multiples of 128,

@@ -46,6 +46,16 @@ class Linear(ctypes.Structure):
     _fields_ = [("trellis", _vp), ("suh", _vp), ("svh", _vp), ("k", _i), ("n", _i)]
 
 
+class ShapeDesc(ctypes.Structure):
+    """``exl3b200_shape_desc``: one entry of the kernel-shape map."""
+
+    _fields_ = [("name", ctypes.c_char_p), ("max_rows", ctypes.c_int), ("tile_rows", ctypes.c_int),
+                ("tile_cols", ctypes.c_int), ("ctas_per_sm", ctypes.c_int)]
+
+
+SHAPE_GV8, SHAPE_GV8_NARROW, SHAPE_GV16, SHAPE_TC, SHAPE_MOE_SMALL, SHAPE_MOE_TC = range(1, 7)
+
+
 class Peers(ctypes.Structure):
     """``exl3b200_peers``: every rank's peer buffer as mapped in this process."""
 
@@ -57,6 +67,10 @@ _f = ctypes.c_float
 # name -> (restype, argtypes); one entry per declaration in include/exl3_b200.h
 SIGNATURES = {
     "exl3b200_abi_version": (_i, []),
+    "exl3b200_num_shapes": (_i, []),
+    "exl3b200_select_shape": (_i, [_i, _i, _i, _i, _i, _i, _i]),
+    "exl3b200_shape_compat": (_i, [_i, _i, _i, _i, _i]),
+    "exl3b200_shape_info": (_i, [_i, _vp]),
     "exl3b200_status_string": (ctypes.c_char_p, [_i]),
     "exl3b200_dequant": (_i, [_vp, _i, _i, _i, _i, _vp, _vp, _vp, _i, _vp]),
     "exl3b200_gemv_state_size": (_sz, [_i]),

@@ -21,6 +21,7 @@ from .ops import (_OUT_DTYPES, _require_cuda, _stream_ptr, codebook_id, legacy_c
 MOE_MAX_PAIRS = 8192
 MOE_MAX_EXPERTS = 2048
 # average routed rows per local expert from which the tensor-core pipeline is used
+# (the kernel-shape map's crossover, exl3b200_select_shape)
 MOE_TC_MIN_ROWS = 12
 
 
@@ -87,13 +88,17 @@ def workspace_tokens(tokens: int, chunk: int) -> int:
 
 def moe_path(tokens: int, topk: int, experts: int) -> str:
     """``"tc"`` (tensor-core pipeline, codes decoded once per 256 rows of an expert)
-    when the experts get ``MOE_TC_MIN_ROWS`` rows each on average, else ``"small"``
+    when the kernel-shape map says so (``MOE_TC_MIN_ROWS`` rows per expert on
+    average), else ``"small"``
     (small-M pipeline, once per 16 rows).  ``EXL3_B200_MOE_PATH`` = small / tc
     forces one.  Decided from host-known sizes only (no synchronisation)."""
     forced = os.environ.get("EXL3_B200_MOE_PATH", "auto").lower()
     if forced in ("small", "tc"):
         return forced
-    return "tc" if tokens * topk >= MOE_TC_MIN_ROWS * experts else "small"
+    from .ops import select_shape
+
+    shape = select_shape(max(1, tokens), 128, 128, 3, 0, max(1, experts), max(1, topk))
+    return "tc" if shape == _lib.SHAPE_MOE_TC else "small"
 
 
 def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, tables: dict,

@@ -164,9 +164,24 @@ def _check_linear(x2: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, sv
         raise RuntimeError("suh K dimension does not match trellis")
 
 
-# Row count from which ``matmul`` uses the tensor-core kernel instead of 16-row
-# chunks of the small-M kernel.
-TC_MIN_ROWS = 32
+_SHAPES = {}
+
+
+def select_shape(m: int, k: int, n: int, K: int, cb: int, experts: int = 0, topk: int = 0) -> int:
+    """The library's kernel-shape map (``exl3b200_select_shape``): ``_lib.SHAPE_*``."""
+    key = (m, k, n, K, cb, experts, topk)
+    shape = _SHAPES.get(key)
+    if shape is None:
+        shape = int(_lib.lib().exl3b200_select_shape(m, k, n, K, cb, experts, topk))
+        if shape <= 0:
+            raise RuntimeError(f"no kernel shape for m={m} k={k} n={n} K={K} cb={cb}")
+        if len(_SHAPES) < 65536:
+            _SHAPES[key] = shape
+    return shape
+
+
+def _tc_rows(m: int, k: int, n: int, K: int, cb: int) -> bool:
+    return select_shape(m, k, n, K, cb) == _lib.SHAPE_TC
 
 
 def _gemm_into(x2: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], svh: torch.Tensor,
@@ -216,8 +231,9 @@ def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], 
            variant: Optional[int] = None, path: Optional[str] = None) -> torch.Tensor:
     """``y = x @ W`` for any number of rows: ``x [..., k]`` fp16 -> ``[..., n]``.
 
-    From ``TC_MIN_ROWS`` rows on (or ``path="tc"``), one tensor-core GEMM over all
-    rows; below, the small-M kernel in chunks of at most 16 rows (``path="gemv"``).
+    Where the kernel-shape map says so (17 rows and more; or ``path="tc"``), one
+    tensor-core GEMM over all rows; below, the small-M kernel in chunks of at most 16
+    rows (``path="gemv"``).
     Replaces ``exl3_gemm_cuda`` (``csrc/exl3_gemm.cu:9-31``).  ``out`` may be a
     row-strided 2D view (e.g. a column slice of a fused qkv output)."""
     if K is None:
@@ -243,7 +259,7 @@ def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], 
         flags |= (int(variant) & 3) << 8
     if path not in (None, "tc", "gemv"):
         raise RuntimeError("path must be None, 'tc' or 'gemv'")
-    use_tc = path == "tc" or (path is None and m >= TC_MIN_ROWS and trellis.data_ptr() % 16 == 0)
+    use_tc = path == "tc" or (path is None and trellis.data_ptr() % 16 == 0 and _tc_rows(m, x2.size(1), n, K, cb))
     if use_tc:
         _gemm_into(x2, trellis.contiguous(), suh, svh, K, cb, out2, flags)
     else:
@@ -330,7 +346,7 @@ def matmul_multi(x: torch.Tensor, linears, K: int, cb: int, outs=None,
             raise RuntimeError("matmul_multi outputs must share a dtype")
     L = _lib.lib()
     flags = 0 if variant is None else (int(variant) & 3) << 8
-    if m >= TC_MIN_ROWS and all(lin[0].data_ptr() % 16 == 0 for lin in linears):
+    if _tc_rows(m, k, max(ns), K, cb) and all(lin[0].data_ptr() % 16 == 0 for lin in linears):
         # one tensor-core GEMM per linear: codes streamed once per 256 rows
         for (tr, su, sv), o in zip(linears, outs):
             _gemm_into(x2, tr.contiguous(), su, sv, K, cb, o, 0)
