@@ -626,15 +626,38 @@ __device__ __forceinline__ TcSeg tc_seg(const TcArgs& a, int tile)
     return s;
 }
 
-// first iteration of CTA c, and the CTA that runs iteration it
-__device__ __forceinline__ long long tc_range_start(long long iters, int grid, int c)
+// Work of CTA c: two contiguous ranges of the iteration list (tile-major, k-chunk
+// minor).  First whole tiles, w = tiles / grid per CTA, so the CTAs of this phase
+// all start at k = 0 and walk k together: the activation and code chunks that the
+// concurrent tiles share are read from DRAM about once and then hit in L2 (with
+// every CTA at a different k, as in a plain stream-K split, the working set is the
+// whole input image plus all codes, which does not fit in L2 at large m).  Then the
+// remaining tiles' iterations are split evenly over the grid (stream-K); only
+// these tiles can be split between CTAs.
+struct TcRanges {
+    long long b[2], e[2];
+    long long sk0;  // first iteration of the stream-K phase
+};
+
+__device__ __forceinline__ TcRanges tc_ranges(long long iters, int nkc, int grid, int c)
 {
-    return iters * c / grid;
+    TcRanges r;
+    const long long w = iters / nkc / grid;
+    r.sk0 = w * grid * nkc;
+    r.b[0] = (long long) c * w * nkc;
+    r.e[0] = r.b[0] + w * nkc;
+    const long long rem = iters - r.sk0;
+    r.b[1] = r.sk0 + rem * c / grid;
+    r.e[1] = r.sk0 + rem * (c + 1) / grid;
+    return r;
 }
 
-__device__ __forceinline__ int tc_cta_of(long long iters, int grid, long long it)
+// the CTA whose stream-K range holds iteration it (it >= sk0): its slot collects
+// the partial sums of the tile that starts there
+__device__ __forceinline__ int tc_cta_of(long long iters, int nkc, int grid, long long it)
 {
-    return (int) (((it + 1) * grid - 1) / iters);
+    const long long sk0 = iters / nkc / grid * grid * nkc;
+    return (int) (((it - sk0 + 1) * grid - 1) / (iters - sk0));
 }
 
 // ---------------------------------------------------------------------------
@@ -698,8 +721,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
         iters = (long long) *reinterpret_cast<const volatile int*>(a.dev_tiles) * nkc;
         if (a.dev_tile_base) tile_base = *reinterpret_cast<const volatile int*>(a.dev_tile_base);
     }
-    const long long it_begin = tc_range_start(iters, grid, blockIdx.x);
-    const long long it_end = tc_range_start(iters, grid, blockIdx.x + 1);
+    const TcRanges rg = tc_ranges(iters, nkc, grid, blockIdx.x);
 
     if (warp == 0) {
         // activation producer
@@ -707,7 +729,8 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
         if (lane == 0) {
             uint32_t s = 0, ph = 0, used = 0, par = 0;  // ring slot, phase; per-slot issued / parity bits
             bool ok = true;
-            for (long long it = it_begin; it < it_end && ok;) {
+            for (int r = 0; r < 2; ++r)
+            for (long long it = rg.b[r], it_end = rg.e[r]; it < it_end && ok;) {
                 const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
                 const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
                 const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
@@ -755,7 +778,8 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             const size_t row_bytes = (size_t) (a.n >> 4) * 32 * K;
             uint32_t s = 0, ph = 0, used = 0, par = 0;
             bool ok = true;
-            for (long long it = it_begin; it < it_end && ok;) {
+            for (int r = 0; r < 2; ++r)
+            for (long long it = rg.b[r], it_end = rg.e[r]; it < it_end && ok;) {
                 const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
                 const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
                 const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
@@ -785,7 +809,8 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             int seg_i = 0;
             bool ok = true;
             const uint64_t a_desc0 = sw128_desc(sA), b_desc0 = sw128_desc(sB);
-            for (long long it = it_begin; it < it_end && ok; ++seg_i) {
+            for (int r = 0; r < 2; ++r)
+            for (long long it = rg.b[r], it_end = rg.e[r]; it < it_end && ok; ++seg_i) {
                 const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
                 const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
                 const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
@@ -793,7 +818,10 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                 const int nacc = sg.m - mt * kTcRows > 128 ? 2 : 1;
                 const uint32_t idesc = tc_idesc(min(kTcCols, a.n - nt * kTcCols));
                 // the epilogue of the previous segment has read the accumulators
-                if (!mbar_wait(acc_empty, (uint32_t) (seg_i & 1) ^ 1, abort_flag, true)) break;
+                if (!mbar_wait(acc_empty, (uint32_t) (seg_i & 1) ^ 1, abort_flag, true)) {
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
                 for (int kc = kc0; kc < kc1; ++kc) {
                     if (!mbar_wait(full_a + 8 * sa, pa, abort_flag, true) ||
@@ -836,7 +864,8 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
         uint32_t st = 0, pt = 0, sb = 0, pb = 0;
         int seg_i = 0;
         bool ok = true;
-        for (long long it = it_begin; it < it_end && ok; ++seg_i) {
+        for (int r = 0; r < 2; ++r)
+        for (long long it = rg.b[r], it_end = rg.e[r]; it < it_end && ok; ++seg_i) {
             const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
             const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
             const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
@@ -879,7 +908,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                 if constexpr (MODE == kTcDense) {
                     float* slot_row = nullptr;
                     if (!whole) {
-                        const int slot = tc_cta_of(a.iters, grid, (long long) tile * nkc);
+                        const int slot = tc_cta_of(a.iters, nkc, grid, (long long) tile * nkc);
                         slot_row = a.slots + (size_t) slot * kTcSlotFloats +
                                    (size_t) (acc * 128 + q * 32 + lane) * kTcCols + cb * 128;
                     }
@@ -915,14 +944,15 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
     }
 }
 
-// Split tiles: the slot of CTA c holds the tile that contains c's range end,
-// when that tile starts inside c's range.  One CTA per slot.
+// Split tiles: the slot of CTA c holds the tile that contains the end of c's
+// stream-K range, when that tile starts inside the range.  One CTA per slot.
 __global__ __launch_bounds__(256) void exl3_tc_finish_kernel(const __grid_constant__ TcArgs a, int grid)
 {
     tc_griddep_wait();
     const int c = blockIdx.x;
-    const long long start = tc_range_start(a.iters, grid, c);
-    const long long end = tc_range_start(a.iters, grid, c + 1);
+    const TcRanges rg = tc_ranges(a.iters, a.nkc, grid, c);
+    const long long start = rg.b[1];
+    const long long end = rg.e[1];
     if (end >= a.iters || end % a.nkc == 0) return;
     const int tile = (int) (end / a.nkc);
     if ((long long) tile * a.nkc < start) return;
