@@ -21,8 +21,8 @@ Workloads (synthetic, seeded):
   between calls; value in GB/s of trellis + activations.
 * ``mlp``: config 2, the dense SwiGLU MLP block (hidden 5120, intermediate 25600;
   fused gate+up one 3-bpw 3INST trellis of N = 2 x 25600, SiLU*mul, down 4 bpw MCG;
-  seed 1) at ``--batch`` = M rows; small-M kernels below 32 rows, the tensor-core
-  GEMM from 32.  Under torchrun: tensor parallel (gate/up column shards, down row
+  seed 1) at ``--batch`` = M rows, one ``exl3b200_mlp`` call (SiLU*mul fused into the
+  gate+up epilogue); small-M kernels up to 16 rows, the tensor-core GEMMs from 17.  Under torchrun: tensor parallel (gate/up column shards, down row
   shards, NCCL all-reduce).  Value in tokens (rows)/s; roofline in TFLOP/s.
 * ``moe``: config 3, a routed MoE layer (288 experts top-8, hidden 2048, expert
   intermediate 1024, 3 bpw 3INST; one 4-bpw shared expert; router logits fp32
@@ -576,15 +576,13 @@ def run_mlp(args, world, rank, local, device):
     gu = make_linear(gen, H, 2 * i_loc, 3, device)       # [gate_r | up_r], 3 bpw 3INST
     down = make_linear(gen, i_loc, H, 4, device)         # 4 bpw MCG
     x = torch.randn(m, H, dtype=torch.float16, device=device, generator=gen)
-    gu_out = torch.empty(m, 2 * i_loc, dtype=torch.float16, device=device)
-    act = torch.empty(m, i_loc, dtype=torch.float16, device=device)
     out = torch.empty(m, H, dtype=torch.float16, device=device)
     group = torch.distributed.group.WORLD if world > 1 else None
 
     def step():
-        ops.matmul(x, *gu, 3, 0, out=gu_out)
-        torch.mul(torch.nn.functional.silu(gu_out[:, :i_loc]), gu_out[:, i_loc:], out=act)
-        ops.matmul(act, *down, 4, 1, out=out)
+        # one library call: gate|up matmul with the SwiGLU and the down projection's input
+        # transform in its epilogue, then the down matmul (no torch ops in between)
+        ops.mlp(x, gu, down, 3, 0, 4, 1, out=out)
         if world > 1:
             torch.distributed.all_reduce(out, group=group)
 
@@ -613,7 +611,7 @@ def run_mlp(args, world, rank, local, device):
              "frac": tflops / world / tc_peak} if tensor_bound else
             {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak})
     roof.update({"traffic": None, "peak_kind": peak_kind, "per": "rank",
-                 "kernel": "whole MLP block (gate+up, SiLU*mul, down) per rank"})
+                 "kernel": "whole MLP block per rank (exl3b200_mlp: gate+up with SiLU*mul in its epilogue, down)"})
 
     # end to end: host x in, host y out, eager calls
     px = torch.randn(m, H, dtype=torch.float16).pin_memory()
@@ -633,12 +631,15 @@ def run_mlp(args, world, rank, local, device):
             "config": {"workload": f"config 2 SwiGLU MLP block, M={m}", "hidden": H, "intermediate": I,
                        "gate_up": "3 bpw 3INST fused N=2x25600", "down": "4 bpw MCG", "parallelism": f"tp{world}",
                        "l2": f"{wbytes >> 20} MB of codes per step (> 126 MB L2), no flush",
-                       "path": "tensor-core GEMM" if m >= 32 else "small-M kernels"},
+                       "path": "tensor-core GEMMs" if m >= 17 else "small-M kernels",
+                       "swiglu": "fused into the gate+up epilogue"},
             "tflops": tflops, "exl3_gbs_per_rank": gbs,
             "roofline": roof,
             "e2e": {"value": m / (e2e_ms * 1e-3), "unit": "rows/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": px.numel() * 2, "d2h_bytes_per_step": py.numel() * 2},
-            "gpu_launches": args.steps * (6 if m >= 32 else 2 * 3 * ((m + 15) // 16)),
+            # input stage, gate|up matmul (+ its split-tile finish), down matmul (+ finish) on the
+            # tensor cores; input, matmul, epilogue, matmul, epilogue on the small-M path
+            "gpu_launches": args.steps * 5,
             "clocks": clk.summary()}
     return finish(line, args, world)
 

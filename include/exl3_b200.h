@@ -319,6 +319,40 @@ typedef struct exl3b200_linear {
 } exl3b200_linear;
 
 /*
+ * Dense SwiGLU MLP block: out = down(silu(clip(gate(x))) * clip(up(x))), with the
+ * activation fused into the gate|up matmul's epilogue, which writes the down
+ * projection's rotated input directly; no [m, 2 * inter] intermediate.  gate_up is
+ * one fused EXL3 linear of n = 2 * inter columns (gate, then up), the layout the
+ * reference's fat GEMM takes (packed13, src/sglang_exl3/exl3.py:1199-1218, which
+ * runs the activation in torch between exl3_fat_gemm and had_r_128).  Roundings as
+ * the reference: fp32 gate/up, fp16 activation, then the down projection's input
+ * transform.  swiglu_limit 0 or infinite = no clip (gate clipped above, up to
+ * [-limit, limit], csrc/p2b_moe.cu:304-313).  Up to 16 rows on the small-M kernels,
+ * more on the tensor cores (exl3b200_select_shape); the tensor-core path wants the
+ * trellises and svh 16-byte aligned.  state (zeroed once, left zeroed) and scratch
+ * (no initialisation): exl3b200_mlp_workspace bytes, 256-byte aligned.  No
+ * counterpart op in the reference.
+ */
+typedef struct exl3b200_mlp_args {
+    const void* x;            /* fp16 [m][hidden], row stride x_stride */
+    long long x_stride;
+    int m, hidden, inter;
+    exl3b200_linear gate_up;  /* k = hidden, n = 2 * inter */
+    int K_gate_up, cb_gate_up;
+    exl3b200_linear down;     /* k = inter, n = hidden */
+    int K_down, cb_down;
+    float swiglu_limit;
+    void* out;                /* [m][hidden] in out_dtype, row stride out_stride */
+    long long out_stride;
+    int out_dtype;
+} exl3b200_mlp_args;
+
+EXL3B200_API int exl3b200_mlp_workspace(int m, int hidden, int inter, int K_gate_up, int cb_gate_up,
+                                        size_t* state_bytes, size_t* scratch_bytes);
+EXL3B200_API int exl3b200_mlp(const exl3b200_mlp_args* args, void* state, size_t state_bytes, void* scratch,
+                              size_t scratch_bytes, void* stream);
+
+/*
  * Peer buffers for tensor parallelism without NCCL in the decode sub-layers: one per
  * rank, allocated by its owner (the only allocating calls of the library, made once
  * at setup), mapped into every other rank's process through its 64-byte CUDA IPC

@@ -342,6 +342,18 @@ __global__ __launch_bounds__(256) void exl3_gv_epilogue_kernel(const __grid_cons
             // (gate, up) pair: table entries j and j+1 (stride 2 view)
             const GvProblem& pu = a.dev ? a.dev[pi * a.stride + a.offset + 1] : a.inl[pi * a.stride + a.offset + 1];
             epi_block_row<CB>(a, DecAux{}, MODE, pi, p, &pu, nb, r, lane);
+        } else if constexpr (MODE == kEpiSwigluFused) {
+            // one gate|up problem: gate block nb with up block nb + n / 256; the task
+            // grid counts n / 256 blocks per row
+            const int half = p.n >> 8;
+            const int r2 = local / half, nb2 = local - r2 * half;
+            GvProblem pd = p;
+            pd.n = p.n >> 1;  // the down projection's input width, for the output's indexing
+            const EpiPre ep = epi_preload(p, DecAux{}, kEpiSwiglu, pi, nb2, r2, lane);
+            float v[4], u[4];
+            gv_finish<CB>(p, nb2, r2, lane, v);
+            gv_finish<CB>(p, nb2 + half, r2, lane, u);
+            epi_apply<CB>(a, DecAux{}, kEpiSwiglu, pi, pd, nb2, r2, lane, v, u, ep);
         } else {
             epi_block_row<CB>(a, DecAux{}, MODE, pi, p, nullptr, nb, r, lane);
         }
@@ -483,6 +495,9 @@ int gv_launch_epilogue(const GvArgs& a, int cb, int max_out_tasks, bool pdl, cud
         case kEpiSwiglu:
             return mul1 ? launch_ex(exl3_gv_epilogue_kernel<2, kEpiSwiglu>, grid, pdl, stream, a)
                         : launch_ex(exl3_gv_epilogue_kernel<0, kEpiSwiglu>, grid, pdl, stream, a);
+        case kEpiSwigluFused:
+            return mul1 ? launch_ex(exl3_gv_epilogue_kernel<2, kEpiSwigluFused>, grid, pdl, stream, a)
+                        : launch_ex(exl3_gv_epilogue_kernel<0, kEpiSwigluFused>, grid, pdl, stream, a);
         default: return kErrBadArgument;
     }
 }

@@ -27,6 +27,8 @@ enum GvEpilogue : int {
     kEpiCombine = 1,  // fp32 out[out_rows[r] * out_stride + col] += out_scale[r] * y (atomic)
     kEpiSwiglu = 2,   // problems (2q, 2q+1) = (gate, up); writes the rotated down-projection
                       // input: out (uint32 dup pairs) [r][col], pre-scale out_suh
+    kEpiSwigluFused = 3,  // one fused gate|up problem (n = 2 * inter): block nb pairs with block
+                          // nb + n / 256; output as kEpiSwiglu; out_tasks = m * n / 256
 };
 
 struct GvProblem {

@@ -117,6 +117,13 @@ struct TcArgs {
     const int* slot_token;     // combine: output row of each routed slot
     const float* slot_weight;  // combine: its routing weight
     unsigned long long wait_ns;  // limit of every bounded barrier wait
+    // kTcDenseSwiglu: n = 2 * inter (gate columns, then up columns of the trellis);
+    // tiles pair gate block j with up block j; the epilogue writes the down projection's
+    // input image (the exl3_tc_input_kernel layout, k = inter)
+    uint8_t* img;              // down input image [mpad/128][inter/64][16 KB]
+    const __half* suh2;        // down projection suh [inter]
+    float swiglu_limit;        // 0 or infinite: no clip
+    int inter;
 };
 
 // ---------------------------------------------------------------------------
@@ -291,6 +298,34 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8])
                  : "memory");
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+                 "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+                 "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+                 "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float (&v)[4])
+{
+    uint32_t r[4];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr)
+                 : "memory");
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st4(uint32_t taddr, const float (&v)[4])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1,%2,%3,%4};" ::"r"(taddr),
+                 "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+                 "r"(__float_as_uint(v[3]))
+                 : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -586,6 +621,145 @@ __device__ __forceinline__ void tc_epilogue_block_grouped(uint32_t taddr, const 
     }
 }
 
+// In-place 128-point transform of one TMEM block (this thread's row): 32-point
+// transforms of the four 32-column quarters; the stride-32 and stride-64 butterflies
+// run where the block is read back (tc_block_final).
+__device__ __forceinline__ void tc_block_fwht32(uint32_t taddr)
+{
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+        float v[32];
+        tmem_ld32(taddr + 32 * j, v);
+        tmem_ld_wait();
+        fwht32_local(v);
+        tmem_st32(taddr + 32 * j, v);
+    }
+}
+
+// Columns 32 j + 8 c + i (j < 4, i < 8) of a block after tc_block_fwht32: the last
+// two butterfly stages, unscaled.
+__device__ __forceinline__ void tc_block_final(uint32_t taddr, int c, float (&u)[4][8])
+{
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tmem_ld8(taddr + 32 * j + 8 * c, u[j]);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float b0 = __fadd_rn(u[0][i], u[1][i]), b1 = __fsub_rn(u[0][i], u[1][i]);
+        const float b2 = __fadd_rn(u[2][i], u[3][i]), b3 = __fsub_rn(u[2][i], u[3][i]);
+        u[0][i] = __fadd_rn(b0, b2);
+        u[2][i] = __fsub_rn(b0, b2);
+        u[1][i] = __fadd_rn(b1, b3);
+        u[3][i] = __fsub_rn(b1, b3);
+    }
+}
+
+// The same for the 4 columns 32 j + 4 c + i (c < 8, i < 4).
+__device__ __forceinline__ void tc_block_final4(uint32_t taddr, int c, float (&u)[4][4])
+{
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tmem_ld4(taddr + 32 * j + 4 * c, u[j]);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float b0 = __fadd_rn(u[0][i], u[1][i]), b1 = __fsub_rn(u[0][i], u[1][i]);
+        const float b2 = __fadd_rn(u[2][i], u[3][i]), b3 = __fsub_rn(u[2][i], u[3][i]);
+        u[0][i] = __fadd_rn(b0, b2);
+        u[2][i] = __fsub_rn(b0, b2);
+        u[1][i] = __fadd_rn(b1, b3);
+        u[3][i] = __fsub_rn(b1, b3);
+    }
+}
+
+// Clipped SwiGLU of one element, rounded to fp16 where the reference keeps the
+// activation (csrc/p2b_moe.cu:304-313; src/sglang_exl3/exl3.py:1207-1215), then the
+// down projection's fp16 pre-scale x * suh (its input transform's first rounding).
+__device__ __forceinline__ float swiglu_pre(float g, float u, float lim, float suh)
+{
+    if (lim > 0.f && lim < 3.0e38f) {
+        g = fminf(g, lim);
+        u = fminf(fmaxf(u, -lim), lim);
+    }
+    const float act = __half2float(__float2half_rn(g / (1.0f + expf(-g)) * u));
+    return __half2float(__float2half_rn(__fmul_rn(act, suh)));
+}
+
+// Store 8 consecutive fp16 columns (col multiple of 8) of row `row` into an input
+// image in the exl3_tc_input_kernel layout ([row / 128][k / 64][16 KB], rows of
+// 128 bytes, 16-byte chunks XOR-swizzled by row % 8).
+__device__ __forceinline__ void tc_image_store8(uint8_t* img, int nkc, int row, int col, const float (&v)[8])
+{
+    uint32_t pk[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half2 h = __floats2half2_rn(__fmul_rn(v[2 * i], kHadScale), __fmul_rn(v[2 * i + 1], kHadScale));
+        pk[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    const int rr = row & 127, kc = col >> 6, chunk = (col & 63) >> 3;
+    uint8_t* dst = img + ((((size_t) (row >> 7) * nkc + kc) << 14) + rr * 128 + ((chunk ^ (rr & 7)) << 4));
+    *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+}
+
+// SwiGLU epilogue of one 128-row accumulator of a gate|up tile (kTcDenseSwiglu),
+// this warp's 32 rows: TMEM columns 0..127 hold the gate block j, 128..255 the up
+// block j.  Whole tiles: y = H128(acc) * svh / sqrt(128) for both, the clipped SwiGLU
+// rounded to fp16, x * suh of the down projection rounded to fp16, written back over
+// the gate block, then its 128-point transform, / sqrt(128) and one fp16 rounding into
+// the down projection's input image (the roundings of exl3_tc_input_kernel).  Split
+// tiles add y of both blocks into the slot row; the finish kernel completes them.
+__device__ __forceinline__ void tc_epilogue_swiglu(const TcArgs& a, uint32_t taddr, int row, int nt, bool whole,
+                                                   float* __restrict__ slot_row)
+{
+    tc_block_fwht32(taddr);
+    tc_block_fwht32(taddr + 128);
+    tmem_st_wait();
+    const uint2* svg = reinterpret_cast<const uint2*>(a.svh + nt * 128);
+    const uint2* svu = reinterpret_cast<const uint2*>(a.svh + a.inter + nt * 128);
+    const uint2* su2 = reinterpret_cast<const uint2*>(a.suh2 + nt * 128);
+    // 4-column slices keep the gate and up values of a slice within the register budget
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+        float g[4][4], u[4][4];
+        tc_block_final4(taddr, c, g);
+        tc_block_final4(taddr + 128, c, u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint2 sg4 = __ldg(svg + 8 * j + c), su4 = __ldg(svu + 8 * j + c);
+            const __half* sg = reinterpret_cast<const __half*>(&sg4);
+            const __half* sup = reinterpret_cast<const __half*>(&su4);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                g[j][i] = g[j][i] * kHadScale * __half2float(sg[i]);
+                u[j][i] = u[j][i] * kHadScale * __half2float(sup[i]);
+            }
+            if (whole) {
+                const uint2 s24 = __ldg(su2 + 8 * j + c);
+                const __half* s2 = reinterpret_cast<const __half*>(&s24);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) g[j][i] = swiglu_pre(g[j][i], u[j][i], a.swiglu_limit, __half2float(s2[i]));
+                tmem_st4(taddr + 32 * j + 4 * c, g[j]);
+            } else if (row < a.m) {
+                const int col = 32 * j + 4 * c;
+                atomicAdd(reinterpret_cast<float4*>(slot_row + col), make_float4(g[j][0], g[j][1], g[j][2], g[j][3]));
+                atomicAdd(reinterpret_cast<float4*>(slot_row + 128 + col),
+                          make_float4(u[j][0], u[j][1], u[j][2], u[j][3]));
+            }
+        }
+    }
+    if (!whole) return;
+    tmem_st_wait();
+    tc_block_fwht32(taddr);
+    tmem_st_wait();
+    const int nkc2 = a.inter >> 6;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+        float p[4][8];
+        tc_block_final(taddr, c, p);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) tc_image_store8(a.img, nkc2, row, nt * 128 + 32 * j + 8 * c, p[j]);
+    }
+}
+
 // What a CTA needs to know about the tile of a segment: the dense launch's single
 // problem, or the grouped launch's problem of that tile.
 struct TcSeg {
@@ -600,7 +774,7 @@ template <int MODE>
 __device__ __forceinline__ TcSeg tc_seg(const TcArgs& a, int tile)
 {
     TcSeg s;
-    if constexpr (MODE == kTcDense) {
+    if constexpr (MODE == kTcDense || MODE == kTcDenseSwiglu) {
         s.xt = a.xt;
         s.trellis = a.trellis;
         s.svh = a.svh;
@@ -716,7 +890,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
     tc_griddep_launch();
     long long iters = a.iters;
     int tile_base = 0;
-    if constexpr (MODE != kTcDense) {
+    if constexpr (MODE == kTcGroupedStore || MODE == kTcGroupedCombine) {
         tc_griddep_wait();  // the routing kernel wrote the tile list, the problems and the counts
         iters = (long long) *reinterpret_cast<const volatile int*>(a.dev_tiles) * nkc;
         if (a.dev_tile_base) tile_base = *reinterpret_cast<const volatile int*>(a.dev_tile_base);
@@ -737,7 +911,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                 const int mt = sg.mt;
                 const int rows_t = min(kTcRows, sg.m - mt * kTcRows);
                 const int nacc = rows_t > 128 ? 2 : 1;
-                if constexpr (MODE == kTcDense) {
+                if constexpr (MODE == kTcDense || MODE == kTcDenseSwiglu) {
                     const uint8_t* src0 = a.xt + (((size_t) (2 * mt) * nkc + kc0) << 14);
                     const size_t acc_step = (size_t) nkc << 14;
                     for (int kc = kc0; kc < kc1; ++kc, src0 += kTcABlock) {
@@ -784,15 +958,26 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                 const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
                 const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
                 const int nt = sg.nt;
-                const int bn = min(kTcCols, a.n - nt * kTcCols);
+                const int bn = MODE == kTcDenseSwiglu ? kTcCols : min(kTcCols, a.n - nt * kTcCols);
                 const uint32_t seg = (uint32_t) (bn >> 4) * 32 * K;
-                const uint8_t* src = sg.trellis + (size_t) kc0 * 4 * row_bytes + (size_t) nt * 16 * 32 * K;
+                // swiglu: gate tiles 8 nt .. 8 nt + 7, then the up tiles inter / 16 further on
+                const size_t col_off = MODE == kTcDenseSwiglu ? (size_t) nt * 8 * 32 * K : (size_t) nt * 16 * 32 * K;
+                const size_t up_off = (size_t) (a.inter >> 4) * 32 * K;
+                const uint8_t* src = sg.trellis + (size_t) kc0 * 4 * row_bytes + col_off;
                 for (int kc = kc0; kc < kc1; ++kc, src += 4 * row_bytes) {
                     if (!mbar_wait(empty_t + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
                     mbar_expect_tx(full_t + 8 * s, 4 * seg);
                     const uint32_t dst = sT + s * L::kTChunk;
+                    if constexpr (MODE == kTcDenseSwiglu) {
 #pragma unroll
-                    for (int i = 0; i < 4; ++i) bulk_g2s(dst + i * seg, src + i * row_bytes, seg, full_t + 8 * s);
+                        for (int i = 0; i < 4; ++i) {
+                            bulk_g2s(dst + i * seg, src + i * row_bytes, seg / 2, full_t + 8 * s);
+                            bulk_g2s(dst + i * seg + seg / 2, src + i * row_bytes + up_off, seg / 2, full_t + 8 * s);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) bulk_g2s(dst + i * seg, src + i * row_bytes, seg, full_t + 8 * s);
+                    }
                     used |= 1u << s;
                     par = (par & ~(1u << s)) | (ph << s);
                     if (++s == ST) { s = 0; ph ^= 1; }
@@ -816,7 +1001,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                 const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
                 const int mt = sg.mt, nt = sg.nt;
                 const int nacc = sg.m - mt * kTcRows > 128 ? 2 : 1;
-                const uint32_t idesc = tc_idesc(min(kTcCols, a.n - nt * kTcCols));
+                const uint32_t idesc = tc_idesc(MODE == kTcDenseSwiglu ? kTcCols : min(kTcCols, a.n - nt * kTcCols));
                 // the epilogue of the previous segment has read the accumulators
                 if (!mbar_wait(acc_empty, (uint32_t) (seg_i & 1) ^ 1, abort_flag, true)) {
                     ok = false;
@@ -870,7 +1055,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
             const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
             const int mt = sg.mt, nt = sg.nt;
-            const int bn = min(kTcCols, a.n - nt * kTcCols);
+            const int bn = MODE == kTcDenseSwiglu ? kTcCols : min(kTcCols, a.n - nt * kTcCols);
             if (decoder) {
                 for (int kc = kc0; kc < kc1; ++kc) {
                     if (!mbar_wait(full_t + 8 * st, pt, abort_flag, true) ||
@@ -898,14 +1083,21 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             }
             tc_fence_after();
             const int nacc = sg.m - mt * kTcRows > 128 ? 2 : 1;
-            const int nblk = bn >> 7;
+            const int nblk = MODE == kTcDenseSwiglu ? 1 : bn >> 7;  // swiglu: one task per accumulator
             if (hq < nacc * nblk) {
                 const int acc = hq / nblk, cb = hq - acc * nblk;
                 const int row = mt * kTcRows + acc * 128 + q * 32 + lane;
                 const bool whole = kc0 == 0 && kc1 == nkc;
                 const uint32_t taddr = tmem + ((uint32_t) (q * 32) << 16) + acc * 256 + cb * 128;
                 const int col0 = nt * kTcCols + cb * 128;
-                if constexpr (MODE == kTcDense) {
+                if constexpr (MODE == kTcDenseSwiglu) {
+                    float* slot_row = nullptr;
+                    if (!whole) {
+                        const int slot = tc_cta_of(a.iters, nkc, grid, (long long) tile * nkc);
+                        slot_row = a.slots + (size_t) slot * kTcSlotFloats + (size_t) (acc * 128 + q * 32 + lane) * kTcCols;
+                    }
+                    tc_epilogue_swiglu(a, taddr, row, nt, whole, slot_row);
+                } else if constexpr (MODE == kTcDense) {
                     float* slot_row = nullptr;
                     if (!whole) {
                         const int slot = tc_cta_of(a.iters, nkc, grid, (long long) tile * nkc);
@@ -969,6 +1161,47 @@ __global__ __launch_bounds__(256) void exl3_tc_finish_kernel(const __grid_consta
         __stcg(src + 1, make_float4(0.f, 0.f, 0.f, 0.f));
         const float v[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
         store8(a, mt * kTcRows + r, nt * kTcCols + c8, v);
+    }
+}
+
+// Split tiles of a SwiGLU launch: the slot row holds y of the gate block (columns
+// 0..127) and of the up block (128..255); one warp per row completes the epilogue
+// of tc_epilogue_swiglu (lane holds columns lane + 32 i) and re-zeroes the slot.
+__global__ __launch_bounds__(256) void exl3_tc_finish_swiglu_kernel(const __grid_constant__ TcArgs a, int grid)
+{
+    tc_griddep_wait();
+    const int c = blockIdx.x;
+    const TcRanges rg = tc_ranges(a.iters, a.nkc, grid, c);
+    const long long start = rg.b[1];
+    const long long end = rg.e[1];
+    if (end >= a.iters || end % a.nkc == 0) return;
+    const int tile = (int) (end / a.nkc);
+    if ((long long) tile * a.nkc < start) return;
+    const int mt = tile % a.mtiles, nt = tile / a.mtiles;
+    const int rows = min(kTcRows, a.m - mt * kTcRows);
+    const int lane = threadIdx.x & 31;
+    const int nkc2 = a.inter >> 6;
+    float* slot = a.slots + (size_t) c * kTcSlotFloats;
+    for (int r = threadIdx.x >> 5; r < rows; r += blockDim.x >> 5) {
+        float* sr = slot + (size_t) r * kTcCols;
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int col = lane + 32 * i;
+            const float g = __ldcg(sr + col), u = __ldcg(sr + 128 + col);
+            __stcg(sr + col, 0.f);
+            __stcg(sr + 128 + col, 0.f);
+            v[i] = swiglu_pre(g, u, a.swiglu_limit, __half2float(a.suh2[nt * 128 + col]));
+        }
+        warp_fwht128(v, lane);
+        const int row = mt * kTcRows + r, rr = row & 127;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const int col = nt * 128 + lane + 32 * i;
+            uint8_t* dst = a.img + ((((size_t) (row >> 7) * nkc2 + (col >> 6)) << 14) + rr * 128 +
+                                    ((((col & 63) >> 3) ^ (rr & 7)) << 4) + (col & 7) * 2);
+            *reinterpret_cast<__half*>(dst) = __float2half_rn(__fmul_rn(v[i], kHadScale));
+        }
     }
 }
 
@@ -1072,9 +1305,64 @@ int tc_grouped_matmul(const TcGroupedCall& c, int K, int cb, cudaStream_t stream
     return kErrBadArgument;
 }
 
-static size_t tc_xt_bytes(int m, int k) { return (size_t) ((m + 127) / 128) * 128 * (size_t) k * 2; }
+size_t tc_xt_bytes(int m, int k) { return (size_t) ((m + 127) / 128) * 128 * (size_t) k * 2; }
 
-static size_t tc_state_bytes() { return (size_t) tc_sm_count() * kTcSlotFloats * sizeof(float); }
+size_t tc_state_bytes() { return (size_t) tc_sm_count() * kTcSlotFloats * sizeof(float); }
+
+// One dense tensor-core matmul: the input stage (x -> image, unless the image was
+// written by an earlier kernel), the GEMM (plain epilogue, or the SwiGLU epilogue that
+// writes the down projection's image), and the kernel finishing split tiles.
+int tc_dense_run(const TcDenseRun& r, cudaStream_t st)
+{
+    const bool swiglu = r.img != nullptr;
+    const int mtiles = (r.m + kTcRows - 1) / kTcRows;
+    const int ntiles = swiglu ? r.n / 256 : (r.n + kTcCols - 1) / kTcCols;
+    const long long tiles = (long long) mtiles * ntiles;
+    if (tiles > 0x7fffffffLL) return kErrBadShape;
+    const int nkc = r.k / 64;
+    const long long iters = tiles * nkc;
+    const int grid = (int) std::min<long long>(tc_sm_count(), iters);
+
+    if (r.run_input) {
+        const int mpad = (r.m + 127) / 128 * 128;
+        const int in_tasks = mpad * (r.k / 128);
+        const int in_grid = std::min((in_tasks + 7) / 8, 8 * tc_sm_count());
+        exl3_tc_input_kernel<<<in_grid, 256, 0, st>>>(reinterpret_cast<const __half*>(r.x), r.x_stride, r.suh, r.m,
+                                                       mpad, r.k, r.xt);
+        if (cudaPeekAtLastError() != cudaSuccess) return kErrLaunch;
+    }
+
+    TcArgs a = {};
+    a.xt = r.xt;
+    a.trellis = reinterpret_cast<const uint8_t*>(r.trellis);
+    a.svh = r.svh;
+    a.out = r.out;
+    a.slots = r.slots;
+    a.out_stride = r.out_stride;
+    a.iters = iters;
+    a.m = r.m;
+    a.k = r.k;
+    a.n = r.n;
+    a.mtiles = mtiles;
+    a.tiles = (int) tiles;
+    a.nkc = nkc;
+    a.out_dtype = r.out_dtype;
+    const int esz = r.out_dtype == 2 ? 4 : 2;
+    a.vec_store = r.out && ((uintptr_t) r.out % 16 == 0) && ((r.out_stride * esz) % 16 == 0);
+    a.img = r.img;
+    a.suh2 = r.suh2;
+    a.swiglu_limit = r.swiglu_limit;
+    a.inter = r.n / 2;
+    const int rc = swiglu ? tc_launch_k<kTcDenseSwiglu>(a, r.K, r.cb, grid, st) : tc_launch_k<kTcDense>(a, r.K, r.cb, grid, st);
+    if (rc != kOk) return rc;
+    if (grid > 1) {
+        int g = grid;
+        void* args[] = {&a, &g};
+        const void* fin = swiglu ? (const void*) exl3_tc_finish_swiglu_kernel : (const void*) exl3_tc_finish_kernel;
+        if (tc_launch(fin, grid, 256, 0, st, args) != cudaSuccess) return kErrLaunch;
+    }
+    return kOk;
+}
 
 }  // namespace exl3b200
 
@@ -1105,49 +1393,24 @@ extern "C" int exl3b200_gemm(const void* x, long long x_stride, int m, int k, co
     if (((uintptr_t) trellis & 15) || ((uintptr_t) scratch & 15) || ((uintptr_t) svh & 15)) return kErrUnaligned;
     if ((uintptr_t) state & 15) return kErrUnaligned;
     if (scratch_bytes < tc_xt_bytes(m, k) || state_bytes < tc_state_bytes()) return kErrWorkspace;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-
-    const int mtiles = (m + kTcRows - 1) / kTcRows;
-    const int ntiles = (n + kTcCols - 1) / kTcCols;
-    const long long tiles = (long long) mtiles * ntiles;
-    if (tiles > 0x7fffffffLL) return kErrBadShape;
-    const int nkc = k / 64;
-    const long long iters = tiles * nkc;
-    const int grid = (int) std::min<long long>(tc_sm_count(), iters);
-
-    const int mpad = (m + 127) / 128 * 128;
-    const int in_tasks = mpad * (k / 128);
-    const int in_grid = std::min((in_tasks + 7) / 8, 8 * tc_sm_count());
-    exl3_tc_input_kernel<<<in_grid, 256, 0, st>>>(reinterpret_cast<const __half*>(x), x_stride,
-                                                   pre_rotated ? nullptr : reinterpret_cast<const __half*>(suh), m,
-                                                   mpad, k, reinterpret_cast<uint8_t*>(scratch));
-    if (cudaPeekAtLastError() != cudaSuccess) return kErrLaunch;
-
-    TcArgs a = {};
-    a.xt = reinterpret_cast<const uint8_t*>(scratch);
-    a.trellis = reinterpret_cast<const uint8_t*>(trellis);
-    a.svh = reinterpret_cast<const __half*>(svh);
-    a.out = out;
-    a.slots = reinterpret_cast<float*>(state);
-    a.out_stride = out_stride;
-    a.iters = iters;
-    a.m = m;
-    a.k = k;
-    a.n = n;
-    a.mtiles = mtiles;
-    a.tiles = (int) tiles;
-    a.nkc = nkc;
-    a.out_dtype = out_dtype;
-    const int esz = out_dtype == 2 ? 4 : 2;
-    a.vec_store = ((uintptr_t) out % 16 == 0) && ((out_stride * esz) % 16 == 0);
-    const int rc = tc_launch_k<kTcDense>(a, K, cb, grid, st);
-    if (rc != kOk) return rc;
-    if (grid > 1) {
-        int g = grid;
-        void* args[] = {&a, &g};
-        if (tc_launch((const void*) exl3_tc_finish_kernel, grid, 256, 0, st, args) != cudaSuccess) return kErrLaunch;
-    }
-    return kOk;
+    TcDenseRun r = {};
+    r.x = x;
+    r.x_stride = x_stride;
+    r.suh = pre_rotated ? nullptr : reinterpret_cast<const __half*>(suh);
+    r.run_input = true;
+    r.xt = reinterpret_cast<uint8_t*>(scratch);
+    r.trellis = trellis;
+    r.svh = reinterpret_cast<const __half*>(svh);
+    r.m = m;
+    r.k = k;
+    r.n = n;
+    r.K = K;
+    r.cb = cb;
+    r.out = out;
+    r.out_stride = out_stride;
+    r.out_dtype = out_dtype;
+    r.slots = reinterpret_cast<float*>(state);
+    return tc_dense_run(r, reinterpret_cast<cudaStream_t>(stream));
 }
 
 namespace exl3b200 {

@@ -27,7 +27,9 @@ struct TcProblem {
 enum TcMode : int {
     kTcDense = 0,         // one problem, host-known sizes (exl3b200_gemm)
     kTcGroupedStore = 1,  // fp32 out rows of each problem (whole tiles stored, split tiles added)
-    kTcGroupedCombine = 2 // fp32 out[slot_token[s]] += slot_weight[s] * y
+    kTcGroupedCombine = 2, // fp32 out[slot_token[s]] += slot_weight[s] * y
+    kTcDenseSwiglu = 3     // one fused gate|up problem; a tile is 128 gate + the matching 128 up
+                           // columns, its epilogue writes the down projection's rotated input image
 };
 
 // Input image of a grouped launch: k-chunk major, xt_rows rows of 128 bytes per
@@ -59,5 +61,29 @@ int tc_grouped_matmul(const TcGroupedCall& c, int K, int cb, cudaStream_t stream
 
 // SMs of the current device.
 int tc_device_sms();
+
+// One dense tensor-core matmul launch sequence (exl3_tc.cu).  img == null: plain
+// epilogue into out; img != null: n = 2 * inter fused gate|up columns, the SwiGLU
+// epilogue writes the down projection's input image (k = inter) into img.
+struct TcDenseRun {
+    const void* x;          // input rows (run_input)
+    long long x_stride;
+    const __half* suh;      // null: x already rotated
+    bool run_input;         // false: xt was written by an earlier kernel
+    uint8_t* xt;            // input image, tc_xt_bytes(m, k)
+    const void* trellis;
+    const __half* svh;
+    int m, k, n, K, cb;
+    void* out;
+    long long out_stride;
+    int out_dtype;
+    uint8_t* img;           // swiglu: output image, tc_xt_bytes(m, n / 2)
+    const __half* suh2;     // swiglu: down projection suh [n / 2]
+    float swiglu_limit;
+    float* slots;           // tc_state_bytes(), zeroed, left zeroed
+};
+int tc_dense_run(const TcDenseRun& r, cudaStream_t stream);
+size_t tc_xt_bytes(int m, int k);
+size_t tc_state_bytes();
 
 }  // namespace exl3b200

@@ -56,6 +56,14 @@ class ShapeDesc(ctypes.Structure):
 SHAPE_GV8, SHAPE_GV8_NARROW, SHAPE_GV16, SHAPE_TC, SHAPE_MOE_SMALL, SHAPE_MOE_TC = range(1, 7)
 
 
+class MlpArgs(ctypes.Structure):
+    """``exl3b200_mlp_args``: one fused SwiGLU MLP block."""
+
+    _fields_ = [("x", _vp), ("x_stride", _ll), ("m", _i), ("hidden", _i), ("inter", _i), ("gate_up", Linear),
+                ("K_gate_up", _i), ("cb_gate_up", _i), ("down", Linear), ("K_down", _i), ("cb_down", _i),
+                ("swiglu_limit", ctypes.c_float), ("out", _vp), ("out_stride", _ll), ("out_dtype", _i)]
+
+
 class Peers(ctypes.Structure):
     """``exl3b200_peers``: every rank's peer buffer as mapped in this process."""
 
@@ -104,6 +112,8 @@ SIGNATURES = {
     "exl3b200_peer_buffer_free": (_i, [_vp]),
     "exl3b200_peer_reset": (_i, [_vp, _vp]),
     "exl3b200_residual_add": (_i, [_i, _i, _vp, _ll, _vp, _ll, _vp, _vp]),
+    "exl3b200_mlp_workspace": (_i, [_i, _i, _i, _i, _i, _vp, _vp]),
+    "exl3b200_mlp": (_i, [_vp, _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_moe_tc_scratch_size": (_sz, [_i, _i, _i, _i, _i]),
     "exl3b200_moe_tc": (_i, [_vp, _ll, _i, _i, _i, _vp, _vp, _i, _i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i,
                              _i, _i, _i, ctypes.c_float, _vp, _ll, _i, _i, _vp, _sz, _vp]),

@@ -308,6 +308,59 @@ def exl3_gemm(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: to
     return matmul(x2, trellis, suh, svh, int(K), legacy_codebook(mcg, cb))
 
 
+def mlp(x: torch.Tensor, gate_up, down, K_gate_up: int, cb_gate_up: int, K_down: int, cb_down: int,
+        swiglu_limit: float = 0.0, out_dtype: torch.dtype = torch.float16,
+        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Dense SwiGLU MLP block ``down(silu(gate(x)) * up(x))`` in one library call, the
+    activation fused into the gate|up matmul's epilogue (``exl3b200_mlp``).
+    ``gate_up`` = (trellis, suh, svh) of the fused gate|up linear (n = 2 * inter, gate
+    columns first: the reference's packed13 layout, ``exl3.py:1199-1218``), ``down`` =
+    (trellis, suh, svh).  Small-M kernels up to 16 rows, tensor cores from 17."""
+    import ctypes
+
+    from .decode import linear_desc
+
+    lead = x.shape[:-1]
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.dtype != torch.float16:
+        raise RuntimeError("mlp requires fp16 input")
+    if x2.stride(-1) != 1 or (x2.stride(0) % 2):
+        x2 = x2.contiguous()
+    gtr, gsu, gsv = gate_up
+    dtr, dsu, dsv = down
+    _check_linear(x2, gtr, gsu, gsv, K_gate_up)
+    inter = gtr.size(1) * 8
+    if dtr.size(0) * 16 != inter or dtr.size(1) * 16 != x2.size(1):
+        raise RuntimeError("down projection does not match the gate|up linear")
+    _check_linear(torch.empty((0, inter), dtype=torch.float16, device=x2.device), dtr, dsu, dsv, K_down)
+    dev = _require_cuda(x2, gtr, gsv, dtr, dsv)
+    m, hidden = x2.shape
+    if out is None:
+        out2 = torch.empty((m, hidden), dtype=out_dtype, device=dev)
+    else:
+        out2 = out.reshape(m, hidden) if out.dim() != 2 else out
+        if out2.stride(-1) != 1 or out2.dtype not in _OUT_DTYPES:
+            raise RuntimeError("out must be fp16 / bf16 / fp32 with unit column stride")
+    L = _lib.lib()
+    aligned = [t if t.data_ptr() % 16 == 0 else t.clone() for t in (gsv, dsu, dsv)]
+    gsv, dsu, dsv = aligned
+    st_n, sc_n = ctypes.c_size_t(), ctypes.c_size_t()
+    _lib.check(L.exl3b200_mlp_workspace(m, hidden, inter, K_gate_up, cb_gate_up, ctypes.byref(st_n),
+                                        ctypes.byref(sc_n)), "exl3b200_mlp_workspace")
+    args = _lib.MlpArgs(x2.data_ptr(), x2.stride(0), m, hidden, inter, linear_desc(gtr.contiguous(), gsu, gsv),
+                        K_gate_up, cb_gate_up, linear_desc(dtr.contiguous(), dsu, dsv), K_down, cb_down,
+                        float(swiglu_limit), out2.data_ptr(), out2.stride(0), _OUT_DTYPES[out2.dtype])
+    with torch.cuda.device(dev):
+        state = workspace.state_buffer(dev, st_n.value)
+        scratch = workspace.scratch_buffer(dev, sc_n.value)
+        st = L.exl3b200_mlp(ctypes.byref(args), state.data_ptr(), state.numel(), scratch.data_ptr(), scratch.numel(),
+                            _stream_ptr(dev))
+    _lib.check(st, "exl3b200_mlp")
+    if out is not None:
+        return out
+    return out2.view(*lead, hidden)
+
+
 def _ptr_array(vals) -> "ctypes.Array":
     import ctypes
 

@@ -13,7 +13,8 @@ Tolerances (normwise: max|y - y_ref| / max|y_ref|):
 * a block with an fp16 intermediate (SwiGLU activation, routed MoE): 4e-3.
 
 Shapes: config 2's fused gate+up (5120 -> 2 x 25600, 3 bpw 3INST) and down
-(25600 -> 5120, 4 bpw MCG) at M in {1, 4, 16, 64, 256, 2048}; config 4's q/k/v
+(25600 -> 5120, 4 bpw MCG) at M in {1, 4, 16, 64, 256, 2048}, and the whole block
+through the fused MLP entry point; config 4's q/k/v
 group, o, gate+up and down at TP 1 and at the TP-8 shard widths, M in {1, 8, 64};
 config 3's 288-expert layer (hidden 2048, intermediate 1024, 3 bpw) plus its 4-bpw
 shared expert at T in {1, 8, 64, 512}; config 5's MoE layer (128 experts, hidden
@@ -118,6 +119,18 @@ def test_c2_mlp_block(cuda_device, c2, m):
     # the whole block against fp32 throughout (fp16 intermediate on the product side only)
     ref_act = F.silu(ref_gu[:, :I]) * ref_gu[:, I:]
     assert _rel(y, ref_act @ c2["w_d"]) < TOL_BLOCK
+
+
+@pytest.mark.parametrize("m", [1, 16, 17, 64, 2048])
+def test_c2_fused_mlp(cuda_device, c2, m):
+    """The whole block in one call (exl3b200_mlp), SwiGLU in the gate|up epilogue."""
+    H, I = c2["H"], c2["I"]
+    x = torch.randn(m, H, dtype=torch.float16, device=cuda_device, generator=_gen(150 + m, cuda_device))
+    y = ops.mlp(x, c2["gu"], c2["down"], 3, 0, 4, 1)
+    g = x.float() @ c2["w_gu"]
+    act = (F.silu(g[:, :I]) * g[:, I:]).half().float()
+    assert torch.isfinite(y).all()
+    assert _rel(y, act @ c2["w_d"]) < TOL_BLOCK
 
 
 # ---------------------------------------------------------------------------
