@@ -700,25 +700,51 @@ __device__ __forceinline__ void tc_image_store8(uint8_t* img, int nkc, int row, 
     *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
 }
 
-// SwiGLU epilogue of one 128-row accumulator of a gate|up tile (kTcDenseSwiglu),
-// this warp's 32 rows: TMEM columns 0..127 hold the gate block j, 128..255 the up
-// block j.  Whole tiles: y = H128(acc) * svh / sqrt(128) for both, the clipped SwiGLU
-// rounded to fp16, x * suh of the down projection rounded to fp16, written back over
-// the gate block, then its 128-point transform, / sqrt(128) and one fp16 rounding into
-// the down projection's input image (the roundings of exl3_tc_input_kernel).  Split
-// tiles add y of both blocks into the slot row; the finish kernel completes them.
-__device__ __forceinline__ void tc_epilogue_swiglu(const TcArgs& a, uint32_t taddr, int row, int nt, bool whole,
-                                                   float* __restrict__ slot_row)
+// Named barrier of the two epilogue warps of one accumulator in one TMEM lane quarter
+// (ids 1..8; id 0 is __syncthreads), with the tcgen05 fences that order their TMEM
+// accesses around it.
+__device__ __forceinline__ void tc_pair_sync(int id)
 {
-    tc_block_fwht32(taddr);
-    tc_block_fwht32(taddr + 128);
+    tc_fence_before();
+    asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+    tc_fence_after();
+}
+
+// 32-point transforms of quarters j0, j0 + 1 of one TMEM block (this thread's row).
+__device__ __forceinline__ void tc_block_fwht32_half(uint32_t taddr, int j0)
+{
+#pragma unroll 1
+    for (int j = j0; j < j0 + 2; ++j) {
+        float v[32];
+        tmem_ld32(taddr + 32 * j, v);
+        tmem_ld_wait();
+        fwht32_local(v);
+        tmem_st32(taddr + 32 * j, v);
+    }
+}
+
+// SwiGLU epilogue of one 128-row accumulator of a gate|up tile (kTcDenseSwiglu),
+// shared by two warps of the same TMEM lane quarter (role 0 and 1; 32 rows): TMEM
+// columns 0..127 hold the gate block j, 128..255 the up block j.  Whole tiles:
+// y = H128(acc) * svh / sqrt(128) for both blocks, the clipped SwiGLU rounded to
+// fp16, x * suh of the down projection rounded to fp16, written back over the gate
+// block, then its 128-point transform, / sqrt(128) and one fp16 rounding into the
+// down projection's input image (the roundings of exl3_tc_input_kernel).  Split tiles
+// add y of both blocks into the slot row; the finish kernel completes them.  Each
+// phase is halved between the two warps (role 0 transforms the gate block, role 1 the
+// up block, then each takes half of the column slices).
+__device__ __forceinline__ void tc_epilogue_swiglu(const TcArgs& a, uint32_t taddr, int row, int nt, bool whole,
+                                                   float* __restrict__ slot_row, int role, int bar_id)
+{
+    tc_block_fwht32(taddr + 128 * role);
     tmem_st_wait();
+    tc_pair_sync(bar_id);
     const uint2* svg = reinterpret_cast<const uint2*>(a.svh + nt * 128);
     const uint2* svu = reinterpret_cast<const uint2*>(a.svh + a.inter + nt * 128);
     const uint2* su2 = reinterpret_cast<const uint2*>(a.suh2 + nt * 128);
     // 4-column slices keep the gate and up values of a slice within the register budget
 #pragma unroll 1
-    for (int c = 0; c < 8; ++c) {
+    for (int c = 4 * role; c < 4 * role + 4; ++c) {
         float g[4][4], u[4][4];
         tc_block_final4(taddr, c, g);
         tc_block_final4(taddr + 128, c, u);
@@ -746,13 +772,15 @@ __device__ __forceinline__ void tc_epilogue_swiglu(const TcArgs& a, uint32_t tad
             }
         }
     }
-    if (!whole) return;
+    if (!whole) return;  // uniform over the pair (same segment)
     tmem_st_wait();
-    tc_block_fwht32(taddr);
+    tc_pair_sync(bar_id);
+    tc_block_fwht32_half(taddr, 2 * role);
     tmem_st_wait();
+    tc_pair_sync(bar_id);
     const int nkc2 = a.inter >> 6;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 2 * role; c < 2 * role + 2; ++c) {
         float p[4][8];
         tc_block_final(taddr, c, p);
 #pragma unroll
@@ -1083,7 +1111,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             }
             tc_fence_after();
             const int nacc = sg.m - mt * kTcRows > 128 ? 2 : 1;
-            const int nblk = MODE == kTcDenseSwiglu ? 1 : bn >> 7;  // swiglu: one task per accumulator
+            const int nblk = bn >> 7;  // swiglu: tasks (accumulator, role) instead of (accumulator, block)
             if (hq < nacc * nblk) {
                 const int acc = hq / nblk, cb = hq - acc * nblk;
                 const int row = mt * kTcRows + acc * 128 + q * 32 + lane;
@@ -1096,7 +1124,8 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                         const int slot = tc_cta_of(a.iters, nkc, grid, (long long) tile * nkc);
                         slot_row = a.slots + (size_t) slot * kTcSlotFloats + (size_t) (acc * 128 + q * 32 + lane) * kTcCols;
                     }
-                    tc_epilogue_swiglu(a, taddr, row, nt, whole, slot_row);
+                    // the two warps (cb = role 0, 1) of this quarter share accumulator acc
+                    tc_epilogue_swiglu(a, taddr - cb * 128, row, nt, whole, slot_row, cb, 1 + 2 * q + acc);
                 } else if constexpr (MODE == kTcDense) {
                     float* slot_row = nullptr;
                     if (!whole) {
