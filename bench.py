@@ -648,7 +648,7 @@ def run_moe(args, world, rank, local, device):
     """Config 3: routed MoE layer (288 experts top-8) + shared expert at T = --batch tokens."""
     from exl3_b200 import moe as M
     from exl3_b200 import ops
-    from exl3_b200.ep import ExpertParallelMoE, exl3_local_experts
+    from exl3_b200.ep import PeerExpertParallelMoE, exl3_local_experts
 
     hbm_peak, tc_peak, peak_kind = peaks()
     c5 = args.moe == "c5"
@@ -681,11 +681,12 @@ def run_moe(args, world, rank, local, device):
     sh_up = make_linear(shared_gen, H, I, 4, device)
     sh_down = make_linear(shared_gen, I, H, 4, device)
     rgen = torch.Generator(device=device)
-    rgen.manual_seed(seed)
+    rgen.manual_seed(seed + 1000 * rank)  # every rank holds its own T tokens
     x = torch.randn(T, H, dtype=torch.float16, device=device, generator=rgen)
     logits = torch.randn(T, E, dtype=torch.float32, device=device, generator=rgen)
     local_fn = exl3_local_experts(tables, K, K, K, 0, I)
-    ep = ExpertParallelMoE(E, world, rank, torch.distributed.group.WORLD) if world > 1 else None
+    # expert parallelism: dispatch and combine over NVLink peer memory by the library
+    ep = PeerExpertParallelMoE(E, T, topk, H, group=torch.distributed.group.WORLD) if world > 1 else None
     sh_gu = [torch.empty(T, I, dtype=torch.float16, device=device) for _ in range(2)]
     sh_act = torch.empty(T, I, dtype=torch.float16, device=device)
     sh_out = torch.empty(T, H, dtype=torch.float16, device=device)
@@ -697,7 +698,7 @@ def run_moe(args, world, rank, local, device):
         if ep is None:
             out = local_fn(x, ids.to(torch.int32), w)
         else:
-            out = ep(x, ids, w, local_fn)
+            out = ep(x, ids, w, tables, K, K, K, 0, I)
         if not c5:  # config 3's shared expert (config 5 has none)
             ops.matmul_multi(x, [sh_gate, sh_up], 4, 0, outs=sh_gu)
             torch.mul(torch.nn.functional.silu(sh_gu[0]), sh_gu[1], out=sh_act)
@@ -718,9 +719,14 @@ def run_moe(args, world, rank, local, device):
         e1.record()
         e1.synchronize()
     ms = max_over_ranks(world, e0.elapsed_time(e1) / args.steps)
-    # distinct experts touched and their code bytes (the HBM roofline of the step)
+    # distinct experts touched by the job's tokens (every rank's) and their code bytes:
+    # the HBM roofline of the step; a rank streams its own share of them
     with torch.no_grad():
-        ids_all = torch.topk(torch.softmax(logits, -1), topk, dim=-1)[1]
+        ids_all = torch.topk(torch.softmax(logits, -1), topk, dim=-1)[1].to(torch.int32)
+        if world > 1:
+            parts = [torch.empty_like(ids_all) for _ in range(world)]
+            torch.distributed.all_gather(parts, ids_all)
+            ids_all = torch.cat(parts)
         touched = int(torch.unique(ids_all).numel())
     expert_bytes = (2 * H * I + I * H) * K // 8
     step_bytes = touched * expert_bytes / world + (0 if c5 else 3 * H * I * 4 // 8)
@@ -740,25 +746,28 @@ def run_moe(args, world, rank, local, device):
     e2e_ms = max_over_ranks(world, (time.perf_counter() - t0) / n_e2e * 1e3)
     name = (f"config 5 MoE layer, speculative verify of {args.batch} sequences x 5 tokens (T={T})" if c5
             else f"config 3 MoE layer, T={T}")
-    line = {"metric": ("C5" if c5 else "C3") + " routed MoE layer tokens/s", "value": T / (ms * 1e-3), "unit": "tok/s",
-            "ms_per_step": ms,
+    if ep is not None:
+        ep.close()
+    # every rank holds its own T tokens: the job processes world x T tokens per step
+    line = {"metric": ("C5" if c5 else "C3") + " routed MoE layer tokens/s", "value": world * T / (ms * 1e-3),
+            "unit": "tok/s", "ms_per_step": ms, "scaling": "weak",
             "config": {"workload": name, "experts": E, "topk": topk, "hidden": H,
                        "intermediate": I, "bpw": K, "codebook": "3INST", "shared_expert": "none" if c5 else "4 bpw",
                        "parallelism": f"ep{world}" if world > 1 else "single GPU",
-                       "experts_touched": touched, "moe_path": M.moe_path(world * T, topk, el),
-                       "ep_exchange": "static (equal splits, no host read)" if world > 1 else "none",
+                       "tokens_per_rank": T, "experts_touched": touched, "moe_path": M.moe_path(T, topk, el),
+                       "ep_exchange": ("NVLink peer stores: each token row once to every rank owning one of its "
+                                       "experts, weighted results back (exl3b200_ep_moe)") if world > 1 else "none",
                        "l2": "expert codes 2.36 MB each; time includes routing (softmax/top-k) and the shared expert"},
             "exl3_gbs_per_rank": gbs,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                          "traffic": None, "peak_kind": peak_kind,
                          "kernel": "whole MoE layer per rank (touched experts' codes / step time)"},
-            "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
+            "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": px.numel() * 2, "d2h_bytes_per_step": py.numel() * 4},
-            # routed layer: 6 launches (small-M pipeline) or 5 (tensor-core pipeline, equal K) per
-            # call of at most 8192 (token, slot) pairs; under EP a rank runs world x T rows (static
-            # exchange); config 3's shared expert: 3 (gate+up) + 3 (down)
-            "gpu_launches": args.steps * (-(-(world * T) // (M.MOE_MAX_PAIRS // topk))
-                                          * (5 if M.moe_path(world * T, topk, el) == "tc" else 6)
+            # routed layer: 6 launches (small-M pipeline) or 5 (tensor-core pipeline, equal K);
+            # under EP + plan, dispatch, receive, return, combine; config 3's shared expert:
+            # 3 (gate+up) + 3 (down)
+            "gpu_launches": args.steps * ((5 if M.moe_path(T, topk, el) == "tc" else 6) + (5 if world > 1 else 0)
                                           + (0 if c5 else 6)),
             "clocks": clk.summary()}
     return finish(line, args, world)

@@ -221,7 +221,7 @@ EXL3B200_API int exl3b200_batched_gemv(const void* x, int x_per_expert, long lon
  *   sglang_exl3_c.p2b_fused_moe (reference csrc/p2b_moe.cu:418-468, op
  *   src/sglang_exl3/ops.py:121-184; fixed there to one row, hidden 4096) and the
  *   per-token batched GEMV path (src/sglang_exl3/exl3.py:960-1110).
- *   max_tokens * topk <= 8192, num_experts <= 2048.
+ *   max_tokens * topk <= 65536, num_experts <= 2048.
  */
 EXL3B200_API size_t exl3b200_moe_state_size(int max_tokens, int topk, int hidden, int inter);
 EXL3B200_API size_t exl3b200_moe_scratch_size(int max_tokens, int topk, int hidden, int inter);
@@ -243,7 +243,7 @@ EXL3B200_API int exl3b200_moe(const void* x, long long x_stride, int tokens, int
  * 1154-1231, csrc/exl3_fat_gemm.cu:65-305), without its host synchronisation.
  * scratch: exl3b200_moe_tc_scratch_size bytes, 256-byte aligned, no initialisation
  * (no state buffer).  out must be 16-byte aligned with out_stride a multiple of 4.
- * max_tokens * topk <= 8192, num_experts <= 2048.
+ * max_tokens * topk <= 65536, num_experts <= 2048.
  */
 EXL3B200_API size_t exl3b200_moe_tc_scratch_size(int max_tokens, int topk, int num_experts, int hidden, int inter);
 EXL3B200_API int exl3b200_moe_tc(const void* x, long long x_stride, int tokens, int hidden, int inter,
@@ -376,6 +376,50 @@ EXL3B200_API int exl3b200_peer_buffer_free(void* ptr);
  * arrivals, not poisoned).  Only while no exchange is in flight on any rank.
  */
 EXL3B200_API int exl3b200_peer_reset(void* own_buffer, void* stream);
+
+/*
+ * Expert-parallel routed MoE with the dispatch and the combine done over NVLink peer
+ * memory by this library's kernels (no NCCL, no host synchronisation; CUDA-graph
+ * capturable).  W = peers->world ranks each own experts / W experts (rank r: global
+ * experts [r E/W, (r+1) E/W)) and each holds its own tokens; topk_ids are GLOBAL ids
+ * (ids outside [0, experts) are skipped).  A token row goes once to every rank that
+ * owns one of its experts (with its ids rewritten to that rank's local ids), each
+ * rank runs its local experts with the routed SwiGLU pipeline (path 0: small-M, 1:
+ * tensor cores, -1: by exl3b200_select_shape), the weighted results go back to the
+ * token's rank and out[t] (fp32) is their sum.  Replaces SGLang's standard
+ * dispatcher around the reference's MoE method (src/sglang_exl3/exl3.py:2254-2313;
+ * expert ownership as exl3.py:485-509, 2089-2110).  tables: host array of the 9
+ * DEVICE int64 pointer tables of this rank's experts (gate_trellis, gate_suh,
+ * gate_svh, up_*, down_*; as exl3b200_moe).  Peer buffers: exl3b200_peer_buffer_alloc /
+ * _open with exl3b200_ep_buffer_size(world, max_tokens, topk, hidden) bytes;
+ * peers->max_rows = max_tokens, peers->hidden = hidden.  x and out 16-byte aligned
+ * (x_stride a multiple of 8, out_stride of 4).  Every rank makes the same sequence
+ * of calls.  Waits are bounded (exl3b200_set_wait_limit, default 2 s); a wait that
+ * runs out records EXL3B200_ETIMEOUT, poisons the rank's buffer (later calls return
+ * zeros) until exl3b200_peer_reset on every rank (see the decode sub-layers).
+ * state / scratch: exl3b200_ep_workspace bytes, 256-byte aligned; state zeroed once.
+ */
+typedef struct exl3b200_ep_args {
+    const void* x;              /* fp16 [tokens][hidden] */
+    long long x_stride;
+    int tokens, max_tokens;     /* this rank's tokens, and the capacity the buffers were sized for */
+    int hidden, inter;
+    const int* topk_ids;        /* int32 [tokens][topk] global ids */
+    const float* topk_weights;  /* fp32 [tokens][topk] */
+    int topk, experts;          /* experts: global count, a multiple of world */
+    const void* const* tables;  /* 9 device pointer tables of this rank's experts */
+    int K_gate, K_up, K_down, cb;
+    float swiglu_limit;
+    float* out;                 /* fp32 [tokens][hidden] */
+    long long out_stride;
+    int path;
+} exl3b200_ep_args;
+
+EXL3B200_API size_t exl3b200_ep_buffer_size(int world, int max_tokens, int topk, int hidden);
+EXL3B200_API int exl3b200_ep_workspace(const exl3b200_ep_args* args, const exl3b200_peers* peers,
+                                       size_t* state_bytes, size_t* scratch_bytes);
+EXL3B200_API int exl3b200_ep_moe(const exl3b200_ep_args* args, const exl3b200_peers* peers, void* state,
+                                 size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream);
 
 /*
  * Fused decode sub-layers of a Llama-style decoder for batch <= 16 sequences,

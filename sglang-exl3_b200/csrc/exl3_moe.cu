@@ -30,7 +30,7 @@ namespace exl3b200 {
 
 constexpr int kRouteThreads = 1024;
 constexpr int kMaxLocalExperts = 2048;
-constexpr int kMaxPairs = 8192;
+constexpr int kMaxPairs = 65536;  // (token, slot) pairs of one launch (workspace sizing)
 constexpr int kExpertsPerThread = kMaxLocalExperts / kRouteThreads;
 
 static inline size_t al256(size_t v) { return (v + 255) & ~(size_t) 255; }
@@ -84,7 +84,7 @@ __global__ __launch_bounds__(kRouteThreads) void exl3_moe_route_kernel(const Moe
     __shared__ int s_count[kMaxLocalExperts];
     __shared__ int s_slot[kMaxLocalExperts];   // exclusive prefix of rows
     __shared__ int s_prob[kMaxLocalExperts];   // exclusive prefix of problems
-    __shared__ unsigned short s_pair_rank[kMaxPairs];  // rank of a pair within its expert (< kMaxPairs)
+    __shared__ int s_fill[kMaxLocalExperts];   // rows placed so far (second pass)
     __shared__ int s_warp[32][2];
 
     const int tid = threadIdx.x;
@@ -93,8 +93,7 @@ __global__ __launch_bounds__(kRouteThreads) void exl3_moe_route_kernel(const Moe
     __syncthreads();
     for (int p = tid; p < P; p += kRouteThreads) {
         const int e = t.ids[p];
-        const bool ok = e >= 0 && e < t.experts;
-        s_pair_rank[p] = ok ? (unsigned short) atomicAdd(&s_count[e], 1) : 0;
+        if (e >= 0 && e < t.experts) atomicAdd(&s_count[e], 1);
     }
     __syncthreads();
 
@@ -157,12 +156,17 @@ __global__ __launch_bounds__(kRouteThreads) void exl3_moe_route_kernel(const Moe
     const int total_rows = s_warp[31][0];
     const int total_probs = s_warp[31][1];
 
+    // second pass: a pair's place among its expert's rows from a second count (the
+    // order within an expert is arbitrary; rows are independent), so no per-pair state
+    // limits the pairs of a launch
+    for (int e = tid; e < t.experts; e += kRouteThreads) s_fill[e] = 0;
+    __syncthreads();
     int* token = reinterpret_cast<int*>(t.scratch + L.token);
     float* weight = reinterpret_cast<float*>(t.scratch + L.weight);
     for (int p = tid; p < P; p += kRouteThreads) {
         const int e = t.ids[p];
         if (e < 0 || e >= t.experts) continue;
-        const int slot = s_slot[e] + s_pair_rank[p];
+        const int slot = s_slot[e] + atomicAdd(&s_fill[e], 1);
         token[slot] = p / t.topk;
         weight[slot] = t.weights[p];
     }

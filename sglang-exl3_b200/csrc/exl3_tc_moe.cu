@@ -32,7 +32,7 @@ namespace exl3b200 {
 
 constexpr int kTmThreads = 1024;
 constexpr int kTmMaxExperts = 2048;
-constexpr int kTmMaxPairs = 8192;
+constexpr int kTmMaxPairs = 65536;  // (token, slot) pairs of one launch (workspace sizing)
 constexpr int kTmEpt = kTmMaxExperts / kTmThreads;  // experts per routing thread
 
 static inline size_t tm_al(size_t v) { return (v + 255) & ~(size_t) 255; }
@@ -130,7 +130,7 @@ __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs 
     __shared__ int s_count[kTmMaxExperts];
     __shared__ int s_slot[kTmMaxExperts];  // first slot of each expert
     __shared__ int s_row[kTmMaxExperts];   // first image row of each expert
-    __shared__ unsigned short s_rank[kTmMaxPairs];
+    __shared__ int s_fill[kTmMaxExperts];  // rows placed so far (second pass)
     __shared__ int s_warp[32][4];
 
     const int tid = threadIdx.x;
@@ -140,8 +140,9 @@ __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs 
     __syncthreads();
     for (int p = tid; p < P; p += kTmThreads) {
         const int e = t.ids[p];
-        s_rank[p] = (e >= 0 && e < t.experts) ? (unsigned short) atomicAdd(&s_count[e], 1) : 0;
+        if (e >= 0 && e < t.experts) atomicAdd(&s_count[e], 1);
     }
+    for (int e = tid; e < kTmMaxExperts; e += kTmThreads) s_fill[e] = 0;
     __syncthreads();
 
     // per expert: rows, rows rounded up to 8, active (0/1), 256-row tiles
@@ -172,13 +173,16 @@ __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs 
     float* slot_weight = reinterpret_cast<float*>(t.scratch + L.slot_weight);
     int* slot_row = reinterpret_cast<int*>(t.scratch + L.slot_row);
     int* slot_exp = reinterpret_cast<int*>(t.scratch + L.slot_exp);
+    // a pair's place among its expert's rows from a second count (the order within an
+    // expert is arbitrary; rows are independent): no per-pair state limits the pairs
     for (int p = tid; p < P; p += kTmThreads) {
         const int e = t.ids[p];
         if (e < 0 || e >= t.experts) continue;
-        const int s = s_slot[e] + s_rank[p];
+        const int rank = atomicAdd(&s_fill[e], 1);
+        const int s = s_slot[e] + rank;
         slot_token[s] = p / t.topk;
         slot_weight[s] = t.weights[p];
-        slot_row[s] = s_row[e] + s_rank[p];
+        slot_row[s] = s_row[e] + rank;
         slot_exp[s] = e;
     }
 

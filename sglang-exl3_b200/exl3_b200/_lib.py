@@ -64,6 +64,15 @@ class MlpArgs(ctypes.Structure):
                 ("swiglu_limit", ctypes.c_float), ("out", _vp), ("out_stride", _ll), ("out_dtype", _i)]
 
 
+class EpArgs(ctypes.Structure):
+    """``exl3b200_ep_args``: one expert-parallel MoE call."""
+
+    _fields_ = [("x", _vp), ("x_stride", _ll), ("tokens", _i), ("max_tokens", _i), ("hidden", _i), ("inter", _i),
+                ("topk_ids", _vp), ("topk_weights", _vp), ("topk", _i), ("experts", _i), ("tables", _vp),
+                ("K_gate", _i), ("K_up", _i), ("K_down", _i), ("cb", _i), ("swiglu_limit", ctypes.c_float),
+                ("out", _vp), ("out_stride", _ll), ("path", _i)]
+
+
 class Peers(ctypes.Structure):
     """``exl3b200_peers``: every rank's peer buffer as mapped in this process."""
 
@@ -111,6 +120,9 @@ SIGNATURES = {
     "exl3b200_peer_buffer_close": (_i, [_vp]),
     "exl3b200_peer_buffer_free": (_i, [_vp]),
     "exl3b200_peer_reset": (_i, [_vp, _vp]),
+    "exl3b200_ep_buffer_size": (_sz, [_i, _i, _i, _i]),
+    "exl3b200_ep_workspace": (_i, [_vp, _vp, _vp, _vp]),
+    "exl3b200_ep_moe": (_i, [_vp, _vp, _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_residual_add": (_i, [_i, _i, _vp, _ll, _vp, _ll, _vp, _vp]),
     "exl3b200_mlp_workspace": (_i, [_i, _i, _i, _i, _i, _vp, _vp]),
     "exl3b200_mlp": (_i, [_vp, _vp, _sz, _vp, _sz, _vp]),

@@ -148,6 +148,132 @@ class ExpertParallelMoE:
         return out
 
 
+_TABLE_NAMES = ("gate_trellis", "gate_suh", "gate_svh", "up_trellis", "up_suh", "up_svh",
+                "down_trellis", "down_suh", "down_svh")
+
+
+class PeerExpertParallelMoE:
+    """Expert parallelism with the dispatch and the combine over NVLink peer memory
+    (``exl3b200_ep_moe``): a token row goes once to every rank that owns one of its
+    experts, each rank runs its local experts on what it received, and the weighted
+    results come back to the token's rank, all on the device (no NCCL, no host
+    synchronisation, graph-capturable).  Each rank holds its own tokens (at most
+    ``max_tokens``).  The peer buffers are allocated once and mapped into every rank
+    through CUDA IPC handles exchanged with ``all_gather_object``; ``close`` (every
+    rank, before the process group goes away) unmaps and frees them.  Without a
+    process group (``world == 1``) the exchange runs with the rank itself."""
+
+    def __init__(self, n_experts: int, max_tokens: int, topk: int, hidden: int, group=None):
+        import ctypes
+
+        from . import _lib
+
+        self.world = dist.get_world_size(group) if group is not None else 1
+        self.rank = dist.get_rank(group) if group is not None else 0
+        if self.world > 8 or n_experts % self.world:
+            raise RuntimeError(f"{n_experts} experts over {self.world} ranks (at most 8, evenly) are not supported")
+        self.group = group
+        self.n_experts, self.max_tokens, self.topk, self.hidden = n_experts, max_tokens, topk, hidden
+        L = _lib.lib()
+        size = L.exl3b200_ep_buffer_size(self.world, max_tokens, topk, hidden)
+        if size == 0:
+            raise RuntimeError("bad expert-parallel buffer shape")
+        handle = (ctypes.c_char * 64)()
+        own = ctypes.c_void_p()
+        _lib.check(L.exl3b200_peer_buffer_alloc(size, ctypes.byref(own), handle), "exl3b200_peer_buffer_alloc")
+        self._own = own.value
+        self._opened = []
+        ptrs = [self._own]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            ptrs = []
+            for q in range(self.world):
+                if q == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                buf = (ctypes.c_char * 64).from_buffer_copy(handles[q])
+                _lib.check(L.exl3b200_peer_buffer_open(buf, ctypes.byref(p)), "exl3b200_peer_buffer_open")
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+            dist.barrier(group)
+        self.struct = _lib.Peers((ctypes.c_void_p * 8)(*(ptrs + [None] * (8 - len(ptrs)))), self.world, self.rank,
+                                 max_tokens, hidden)
+
+    def __call__(self, x: torch.Tensor, topk_ids: torch.Tensor, topk_weights: torch.Tensor, tables: dict,
+                 K_gate: int, K_up: int, K_down: int, cb: int, intermediate_size: int, swiglu_limit: float = 0.0,
+                 path: int = -1, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """``out [T, H]`` fp32: every token's routed SwiGLU experts, wherever they live.
+        ``tables``: the nine int64 device pointer tables of this rank's experts."""
+        import ctypes
+
+        from . import _lib, workspace
+
+        T, H = x.shape
+        if H != self.hidden or T > self.max_tokens:
+            raise RuntimeError("expert-parallel input does not fit the buffers")
+        if x.dtype != torch.float16:
+            raise RuntimeError("expert-parallel input must be fp16")
+        if x.stride(-1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
+            x = x.contiguous()
+        ids = topk_ids.reshape(T, -1).to(torch.int32).contiguous()
+        w = topk_weights.reshape(T, -1).to(torch.float32).contiguous()
+        if ids.size(1) != self.topk:
+            raise RuntimeError("top-k does not match the buffers")
+        if out is None:
+            out = torch.empty((T, H), dtype=torch.float32, device=x.device)
+        tabs = [tables[nm].contiguous() for nm in _TABLE_NAMES]
+        tab_ptrs = (ctypes.c_void_p * 9)(*[t.data_ptr() for t in tabs])
+        args = _lib.EpArgs(x.data_ptr(), x.stride(0), T, self.max_tokens, H, int(intermediate_size), ids.data_ptr(),
+                           w.data_ptr(), self.topk, self.n_experts, ctypes.cast(tab_ptrs, ctypes.c_void_p), int(K_gate),
+                           int(K_up), int(K_down), int(cb), float(swiglu_limit or 0.0), out.data_ptr(), out.stride(0),
+                           int(path))
+        L = _lib.lib()
+        st_n, sc_n = ctypes.c_size_t(), ctypes.c_size_t()
+        _lib.check(L.exl3b200_ep_workspace(ctypes.byref(args), ctypes.byref(self.struct), ctypes.byref(st_n),
+                                           ctypes.byref(sc_n)), "exl3b200_ep_workspace")
+        dev = x.device
+        with torch.cuda.device(dev):
+            state = workspace.state_buffer(dev, max(256, st_n.value))
+            scratch = workspace.scratch_buffer(dev, sc_n.value)
+            rc = L.exl3b200_ep_moe(ctypes.byref(args), ctypes.byref(self.struct), state.data_ptr(), state.numel(),
+                                   scratch.data_ptr(), scratch.numel(), torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(rc, "exl3b200_ep_moe")
+        self._keep = (ids, w, tabs, tab_ptrs)  # alive until the enqueued call ran (and for graph replays)
+        return out
+
+    def reset(self) -> None:
+        """Re-arm after a wait gave up (every rank together)."""
+        from . import _lib
+
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(self.group)
+        _lib.check(_lib.lib().exl3b200_peer_reset(self._own, torch.cuda.current_stream().cuda_stream),
+                   "exl3b200_peer_reset")
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(self.group)
+
+    def close(self) -> None:
+        from . import _lib
+
+        if self._own is None:
+            return
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(self.group)
+        L = _lib.lib()
+        for p in self._opened:
+            L.exl3b200_peer_buffer_close(p)
+        self._opened = []
+        if self.world > 1:
+            dist.barrier(self.group)
+        L.exl3b200_peer_buffer_free(self._own)
+        self._own = None
+
+
 def exl3_local_experts(tables: dict, K_gate: int, K_up: int, K_down: int, cb: int, intermediate_size: int,
                        swiglu_limit: float = 0.0) -> LocalFn:
     """``local_fn`` running this rank's experts with the fused device MoE pipeline

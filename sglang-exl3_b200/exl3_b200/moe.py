@@ -18,7 +18,7 @@ import torch
 from . import _lib, workspace
 from .ops import (_OUT_DTYPES, _require_cuda, _stream_ptr, codebook_id, legacy_codebook, matmul, matmul_combine)
 
-MOE_MAX_PAIRS = 8192
+MOE_MAX_PAIRS = 65536
 MOE_MAX_EXPERTS = 2048
 # average routed rows per local expert from which the tensor-core pipeline is used
 # (the kernel-shape map's crossover, exl3b200_select_shape)

@@ -85,7 +85,7 @@ def test_tensor_core_moe_and_combine_validation_without_gpu():
     L = _lib.lib()
     f = 256  # never dereferenced
     assert L.exl3b200_moe_tc_scratch_size(64, 8, 128, 4096, 1536) > 0
-    assert L.exl3b200_moe_tc_scratch_size(2048, 8, 128, 4096, 1536) == 0   # 16384 pairs > 8192
+    assert L.exl3b200_moe_tc_scratch_size(16384, 8, 128, 4096, 1536) == 0  # 131072 pairs > 65536
     assert L.exl3b200_moe_tc_scratch_size(64, 8, 4096, 4096, 1536) == 0    # > 2048 experts
     assert L.exl3b200_moe_tc_scratch_size(64, 8, 128, 4000, 1536) == 0     # hidden % 128
     tabs = [f] * 9
