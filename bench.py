@@ -757,7 +757,9 @@ def run_moe(args, world, rank, local, device):
                        "tokens_per_rank": T, "experts_touched": touched, "moe_path": M.moe_path(T, topk, el),
                        "ep_exchange": ("NVLink peer stores: each token row once to every rank owning one of its "
                                        "experts, weighted results back (exl3b200_ep_moe)") if world > 1 else "none",
-                       "l2": "expert codes 2.36 MB each; time includes routing (softmax/top-k) and the shared expert"},
+                       "l2": (f"expert codes {expert_bytes / 1e6:.2f} MB each, {touched * expert_bytes / 1e6:.0f} MB "
+                              "touched per step (> 126 MB L2), no flush; time includes routing (softmax/top-k)"
+                              + ("" if c5 else " and the shared expert"))},
             "exl3_gbs_per_rank": gbs,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                          "traffic": None, "peak_kind": peak_kind,
