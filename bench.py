@@ -978,8 +978,50 @@ def finish(line, args, world):
                     "cores": torch.get_num_threads(), "kind": "reference",
                     "sample": f"reference dequant_trellis + at::mm on a {REF_SAMPLE_ROWS}x{REF_SAMPLE_COLS} 4-bpw MCG "
                               f"linear ({rsec:.3f} s; single-threaded dequant), scaled the same way"}
-        print(json.dumps(base))
+        if not getattr(args, "quiet", False):
+            print(json.dumps(base))
     return base
+
+
+# The other benchmark configurations, measured after the default decode line in the same
+# process and reported in its "workloads" object (one summary each), so that one run
+# records every config: (name, argument overrides, runs under torchrun too).
+EXTRA_WORKLOADS = [
+    ("config 1 linear 4096x4096 4bpw M=1", dict(workload="linear", k=4096, n=4096, bits=4, batch=1), False),
+    ("config 2 MLP block M=1", dict(workload="mlp", batch=1), False),
+    ("config 2 MLP block M=2048", dict(workload="mlp", batch=2048), False),
+    ("config 3 MoE layer T=64", dict(workload="moe", moe="c3", batch=64), False),
+    ("config 3 MoE layer T=512", dict(workload="moe", moe="c3", batch=512), False),
+    ("config 5 MoE layer, verify batch 64", dict(workload="moe", moe="c5", batch=64), False),
+]
+
+
+def run_extras(args, world, rank, local):
+    """Each extra workload with 10 timed steps; a summary of its line, or the error."""
+    import copy
+
+    out = {}
+    for name, over, multi in EXTRA_WORKLOADS:
+        if world > 1 and not multi:
+            continue
+        sub = copy.copy(args)
+        for k, v in over.items():
+            setattr(sub, k, v)
+        sub.steps, sub.warmup, sub.cpu_baseline, sub.quiet = min(args.steps, 10), 3, False, True
+        try:
+            ln = run_ours(sub, world, rank, local)
+            roof = ln.get("roofline", {})
+            out[name] = {"value": ln["value"], "unit": ln["unit"], "ms_per_step": ln["ms_per_step"],
+                         "steps": sub.steps, "workload": ln["config"].get("workload"),
+                         "path": ln["config"].get("path") or ln["config"].get("moe_path"),
+                         "parallelism": ln["config"].get("parallelism"),
+                         "roofline": {k: roof.get(k) for k in ("bound", "achieved", "unit", "peak", "frac")},
+                         "e2e": (ln.get("e2e") or {}).get("value"),
+                         "gpu_launches": ln.get("gpu_launches"), "clocks": ln.get("clocks")}
+        except Exception as e:  # reported, not fatal: the default line stands on its own
+            out[name] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        torch.cuda.empty_cache()
+    return out
 
 
 def main():
@@ -999,6 +1041,8 @@ def main():
                     help="moe workload: c3 = 288 experts, hidden 2048 (+ shared expert); c5 = the MoE layer of "
                          "config 5's speculative verify: 128 experts, hidden 4096, 5 rows per sequence")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-extra", dest="extra", action="store_false",
+                    help="default decode run: skip the other configs' summaries")
     args = ap.parse_args()
     if args.ctx is None:
         args.ctx = 8192 if args.workload == "verify" else 2048
@@ -1006,6 +1050,12 @@ def main():
     try:
         if args.impl == "reference":
             run_reference(args, world, rank)
+        elif args.workload == "decode" and args.extra:
+            args.quiet = True
+            line = run_ours(args, world, rank, local)
+            line["workloads"] = run_extras(args, world, rank, local)
+            if rank == 0:
+                print(json.dumps(line))
         else:
             run_ours(args, world, rank, local)
     finally:

@@ -84,7 +84,7 @@ __device__ int g_exl3_device_status = 0;  // sticky: first device-side error cod
 
 template <int K>
 struct TcSmem {
-    static constexpr int kBars = 2 * kTcStageA + 2 * kTcStageT + 2 * kTcStageB + 2;
+    static constexpr int kBars = 2 * kTcStageA + 2 * kTcStageT + 2 * kTcStageB + 4;
     static constexpr uint32_t kTChunk = 4u * 16u * 32u * K;  // codes of one stage at 256 columns
     static constexpr uint32_t kA = 0;
     static constexpr uint32_t kB = kA + kTcStageA * 2 * kTcABlock;
@@ -147,6 +147,11 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes)
 __device__ __forceinline__ void mbar_arrive(uint32_t bar)
 {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_n(uint32_t bar, uint32_t count)
+{
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
 
 __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity)
@@ -684,10 +689,10 @@ __device__ __forceinline__ float swiglu_pre(float g, float u, float lim, float s
     return __half2float(__float2half_rn(__fmul_rn(act, suh)));
 }
 
-// Store 8 consecutive fp16 columns (col multiple of 8) of row `row` into an input
-// image in the exl3_tc_input_kernel layout ([row / 128][k / 64][16 KB], rows of
-// 128 bytes, 16-byte chunks XOR-swizzled by row % 8).
-__device__ __forceinline__ void tc_image_store8(uint8_t* img, int nkc, int row, int col, const float (&v)[8])
+// 8 consecutive columns of the down projection's input, / sqrt(128) and rounded to
+// fp16 (the last rounding of exl3_tc_input_kernel), packed as one 16-byte chunk of an
+// input image row.
+__device__ __forceinline__ uint4 tc_pack8(const float (&v)[8])
 {
     uint32_t pk[4];
 #pragma unroll
@@ -695,9 +700,7 @@ __device__ __forceinline__ void tc_image_store8(uint8_t* img, int nkc, int row, 
         const __half2 h = __floats2half2_rn(__fmul_rn(v[2 * i], kHadScale), __fmul_rn(v[2 * i + 1], kHadScale));
         pk[i] = *reinterpret_cast<const uint32_t*>(&h);
     }
-    const int rr = row & 127, kc = col >> 6, chunk = (col & 63) >> 3;
-    uint8_t* dst = img + ((((size_t) (row >> 7) * nkc + kc) << 14) + rr * 128 + ((chunk ^ (rr & 7)) << 4));
-    *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    return make_uint4(pk[0], pk[1], pk[2], pk[3]);
 }
 
 // Named barrier of the two epilogue warps of one accumulator in one TMEM lane quarter
@@ -723,25 +726,29 @@ __device__ __forceinline__ void tc_block_fwht32_half(uint32_t taddr, int j0)
     }
 }
 
-// SwiGLU epilogue of one 128-row accumulator of a gate|up tile (kTcDenseSwiglu),
-// shared by two warps of the same TMEM lane quarter (role 0 and 1; 32 rows): TMEM
-// columns 0..127 hold the gate block j, 128..255 the up block j.  Whole tiles:
-// y = H128(acc) * svh / sqrt(128) for both blocks, the clipped SwiGLU rounded to
-// fp16, x * suh of the down projection rounded to fp16, written back over the gate
-// block, then its 128-point transform, / sqrt(128) and one fp16 rounding into the
-// down projection's input image (the roundings of exl3_tc_input_kernel).  Split tiles
-// add y of both blocks into the slot row; the finish kernel completes them.  Each
-// phase is halved between the two warps (role 0 transforms the gate block, role 1 the
-// up block, then each takes half of the column slices).
-__device__ __forceinline__ void tc_epilogue_swiglu(const TcArgs& a, uint32_t taddr, int row, int nt, bool whole,
-                                                   float* __restrict__ slot_row, int role, int bar_id)
+// SwiGLU epilogue of one 128-row accumulator of a gate|up tile (kTcDenseSwiglu,
+// kTcGroupedSwiglu), shared by two warps of the same TMEM lane quarter (role 0 and 1;
+// 32 rows): TMEM columns 0..127 hold the gate block j, 128..255 the up block j.
+// Whole tiles: y = H128(acc) * svh / sqrt(128) for both blocks, the clipped SwiGLU
+// rounded to fp16, x * suh of the down projection rounded to fp16, written back over
+// the gate block, then its 128-point transform, / sqrt(128) and one fp16 rounding; the
+// caller's store(col, chunk) puts each 8-column chunk into the down projection's input
+// image (the roundings of exl3_tc_input_kernel).  Split tiles add y of both blocks
+// into the slot row; the finish kernel completes them.  Each phase is halved between
+// the two warps (role 0 transforms the gate block, role 1 the up block, then each
+// takes half of the column slices).
+template <class Store>
+__device__ __forceinline__ void tc_epilogue_swiglu(uint32_t taddr, int role, int bar_id, const __half* svh_gate,
+                                                   const __half* svh_up, const __half* suh_down, float lim,
+                                                   bool whole, float* __restrict__ slot_row, bool row_ok,
+                                                   Store store)
 {
     tc_block_fwht32(taddr + 128 * role);
     tmem_st_wait();
     tc_pair_sync(bar_id);
-    const uint2* svg = reinterpret_cast<const uint2*>(a.svh + nt * 128);
-    const uint2* svu = reinterpret_cast<const uint2*>(a.svh + a.inter + nt * 128);
-    const uint2* su2 = reinterpret_cast<const uint2*>(a.suh2 + nt * 128);
+    const uint2* svg = reinterpret_cast<const uint2*>(svh_gate);
+    const uint2* svu = reinterpret_cast<const uint2*>(svh_up);
+    const uint2* su2 = reinterpret_cast<const uint2*>(suh_down);
     // 4-column slices keep the gate and up values of a slice within the register budget
 #pragma unroll 1
     for (int c = 4 * role; c < 4 * role + 4; ++c) {
@@ -762,9 +769,9 @@ __device__ __forceinline__ void tc_epilogue_swiglu(const TcArgs& a, uint32_t tad
                 const uint2 s24 = __ldg(su2 + 8 * j + c);
                 const __half* s2 = reinterpret_cast<const __half*>(&s24);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) g[j][i] = swiglu_pre(g[j][i], u[j][i], a.swiglu_limit, __half2float(s2[i]));
+                for (int i = 0; i < 4; ++i) g[j][i] = swiglu_pre(g[j][i], u[j][i], lim, __half2float(s2[i]));
                 tmem_st4(taddr + 32 * j + 4 * c, g[j]);
-            } else if (row < a.m) {
+            } else if (row_ok) {
                 const int col = 32 * j + 4 * c;
                 atomicAdd(reinterpret_cast<float4*>(slot_row + col), make_float4(g[j][0], g[j][1], g[j][2], g[j][3]));
                 atomicAdd(reinterpret_cast<float4*>(slot_row + 128 + col),
@@ -778,13 +785,12 @@ __device__ __forceinline__ void tc_epilogue_swiglu(const TcArgs& a, uint32_t tad
     tc_block_fwht32_half(taddr, 2 * role);
     tmem_st_wait();
     tc_pair_sync(bar_id);
-    const int nkc2 = a.inter >> 6;
 #pragma unroll 1
     for (int c = 2 * role; c < 2 * role + 2; ++c) {
         float p[4][8];
         tc_block_final(taddr, c, p);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) tc_image_store8(a.img, nkc2, row, nt * 128 + 32 * j + 8 * c, p[j]);
+        for (int j = 0; j < 4; ++j) store(32 * j + 8 * c, tc_pack8(p[j]));
     }
 }
 
@@ -796,6 +802,11 @@ struct TcSeg {
     const __half* svh;
     float* gout;  // grouped store: fp32 output of the problem's row 0
     int m, mt, nt, row0, slot0;
+    // kTcGroupedSwiglu: the up projection's image, codes and svh; the down projection's suh
+    const uint8_t* xt2;
+    const uint8_t* trellis2;
+    const __half* svh2;
+    const __half* suh2;
 };
 
 template <int MODE>
@@ -824,6 +835,13 @@ __device__ __forceinline__ TcSeg tc_seg(const TcArgs& a, int tile)
         s.nt = local / p.mtiles;
         s.row0 = p.row0;
         s.slot0 = p.slot0;
+        if constexpr (MODE == kTcGroupedSwiglu) {
+            const TcProblem& u = a.probs[a.tile_prob[tile] + 1];
+            s.xt2 = u.xt;
+            s.trellis2 = u.trellis;
+            s.svh2 = u.svh;
+            s.suh2 = p.suh2;
+        }
     }
     return s;
 }
@@ -840,6 +858,18 @@ struct TcRanges {
     long long b[2], e[2];
     long long sk0;  // first iteration of the stream-K phase
 };
+
+// Whole tiles only (an epilogue that cannot be split): contiguous runs of tiles,
+// balanced to within one tile.
+__device__ __forceinline__ TcRanges tc_ranges_whole(long long iters, int nkc, int grid, int c)
+{
+    TcRanges r;
+    const long long tiles = iters / nkc;
+    r.b[0] = tiles * c / grid * nkc;
+    r.e[0] = tiles * (c + 1) / grid * nkc;
+    r.b[1] = r.e[1] = r.sk0 = iters;
+    return r;
+}
 
 __device__ __forceinline__ TcRanges tc_ranges(long long iters, int nkc, int grid, int c)
 {
@@ -879,7 +909,11 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
     const uint32_t full_a = sBar, empty_a = full_a + 8 * SA;
     const uint32_t full_t = empty_a + 8 * SA, empty_t = full_t + 8 * ST;
     const uint32_t full_b = empty_t + 8 * ST, empty_b = full_b + 8 * kTcStageB;
+    // accumulator barriers: full / empty of TMEM buffer 0 (columns 0..255, or all 512 for
+    // two 128-row accumulators), then of buffer 1 (columns 256..511; kTcGroupedSwiglu
+    // alternates the buffers by segment, so a tile's epilogue overlaps the next tile's MMAs)
     const uint32_t acc_full = empty_b + 8 * kTcStageB, acc_empty = acc_full + 8;
+    constexpr bool kDblAcc = MODE == kTcGroupedSwiglu;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + L::kMisc);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kMisc + 4);
 
@@ -901,8 +935,11 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             mbar_init(full_b + 8 * s, kTcDecWarps);
             mbar_init(empty_b + 8 * s, 1);
         }
-        mbar_init(acc_full, 1);
-        mbar_init(acc_empty, kTcWarps - 3);  // every decoder and epilogue-only warp
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full + 16 * b, 1);
+            // every decoder and epilogue-only warp; kTcGroupedSwiglu: 6 (see the arrival)
+            mbar_init(acc_empty + 16 * b, kDblAcc ? 6 : kTcWarps - 3);
+        }
         *abort_flag = 0;
         *reinterpret_cast<volatile unsigned long long*>(gbase + L::kMisc + 8) = a.wait_ns;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -918,12 +955,15 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
     tc_griddep_launch();
     long long iters = a.iters;
     int tile_base = 0;
-    if constexpr (MODE == kTcGroupedStore || MODE == kTcGroupedCombine) {
+    constexpr bool kGrouped = MODE == kTcGroupedStore || MODE == kTcGroupedCombine || MODE == kTcGroupedSwiglu;
+    constexpr bool kSwiglu = MODE == kTcDenseSwiglu || MODE == kTcGroupedSwiglu;
+    if constexpr (kGrouped) {
         tc_griddep_wait();  // the routing kernel wrote the tile list, the problems and the counts
         iters = (long long) *reinterpret_cast<const volatile int*>(a.dev_tiles) * nkc;
         if (a.dev_tile_base) tile_base = *reinterpret_cast<const volatile int*>(a.dev_tile_base);
     }
-    const TcRanges rg = tc_ranges(iters, nkc, grid, blockIdx.x);
+    const TcRanges rg = MODE == kTcGroupedSwiglu ? tc_ranges_whole(iters, nkc, grid, blockIdx.x)
+                                                 : tc_ranges(iters, nkc, grid, blockIdx.x);
 
     if (warp == 0) {
         // activation producer
@@ -939,7 +979,24 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                 const int mt = sg.mt;
                 const int rows_t = min(kTcRows, sg.m - mt * kTcRows);
                 const int nacc = rows_t > 128 ? 2 : 1;
-                if constexpr (MODE == kTcDense || MODE == kTcDenseSwiglu) {
+                if constexpr (MODE == kTcGroupedSwiglu) {
+                    // 96-row tiles into rows 32..127 of the A blocks (TMEM lanes 32..127): the gate
+                    // image's rows into block 0, the up image's into block 1.  Rows 0..31 keep stale
+                    // data; their accumulator rows are never read.
+                    const int rows_g = min(kTcSwRows, sg.m - mt * kTcSwRows);
+                    const uint32_t b0 = (uint32_t) ((rows_g + 7) & ~7) * 128u;
+                    const size_t row = (size_t) sg.row0 + (size_t) mt * kTcSwRows;
+                    for (int kc = kc0; kc < kc1; ++kc) {
+                        if (!mbar_wait(empty_a + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
+                        const size_t off = ((size_t) kc * (size_t) a.xt_rows + row) * 128;
+                        mbar_expect_tx(full_a + 8 * s, 2 * b0);
+                        bulk_g2s(sA + (s * 2) * kTcABlock + 32 * 128, sg.xt + off, b0, full_a + 8 * s);
+                        bulk_g2s(sA + (s * 2 + 1) * kTcABlock + 32 * 128, sg.xt2 + off, b0, full_a + 8 * s);
+                        used |= 1u << s;
+                        par = (par & ~(1u << s)) | (ph << s);
+                        if (++s == SA) { s = 0; ph ^= 1; }
+                    }
+                } else if constexpr (MODE == kTcDense || MODE == kTcDenseSwiglu) {
                     const uint8_t* src0 = a.xt + (((size_t) (2 * mt) * nkc + kc0) << 14);
                     const size_t acc_step = (size_t) nkc << 14;
                     for (int kc = kc0; kc < kc1; ++kc, src0 += kTcABlock) {
@@ -986,21 +1043,24 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                 const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
                 const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
                 const int nt = sg.nt;
-                const int bn = MODE == kTcDenseSwiglu ? kTcCols : min(kTcCols, a.n - nt * kTcCols);
+                const int bn = kSwiglu ? kTcCols : min(kTcCols, a.n - nt * kTcCols);
                 const uint32_t seg = (uint32_t) (bn >> 4) * 32 * K;
-                // swiglu: gate tiles 8 nt .. 8 nt + 7, then the up tiles inter / 16 further on
-                const size_t col_off = MODE == kTcDenseSwiglu ? (size_t) nt * 8 * 32 * K : (size_t) nt * 16 * 32 * K;
-                const size_t up_off = (size_t) (a.inter >> 4) * 32 * K;
+                // swiglu: gate tiles 8 nt .. 8 nt + 7, then the same up tiles (dense: inter / 16
+                // tiles further on in the fused trellis; grouped: in the up problem's trellis)
+                const size_t col_off = kSwiglu ? (size_t) nt * 8 * 32 * K : (size_t) nt * 16 * 32 * K;
                 const uint8_t* src = sg.trellis + (size_t) kc0 * 4 * row_bytes + col_off;
-                for (int kc = kc0; kc < kc1; ++kc, src += 4 * row_bytes) {
+                const uint8_t* src_up = MODE == kTcGroupedSwiglu
+                                            ? sg.trellis2 + (size_t) kc0 * 4 * row_bytes + col_off
+                                            : src + (size_t) (a.inter >> 4) * 32 * K;
+                for (int kc = kc0; kc < kc1; ++kc, src += 4 * row_bytes, src_up += 4 * row_bytes) {
                     if (!mbar_wait(empty_t + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
                     mbar_expect_tx(full_t + 8 * s, 4 * seg);
                     const uint32_t dst = sT + s * L::kTChunk;
-                    if constexpr (MODE == kTcDenseSwiglu) {
+                    if constexpr (kSwiglu) {
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             bulk_g2s(dst + i * seg, src + i * row_bytes, seg / 2, full_t + 8 * s);
-                            bulk_g2s(dst + i * seg + seg / 2, src + i * row_bytes + up_off, seg / 2, full_t + 8 * s);
+                            bulk_g2s(dst + i * seg + seg / 2, src_up + i * row_bytes, seg / 2, full_t + 8 * s);
                         }
                     } else {
 #pragma unroll
@@ -1028,10 +1088,15 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                 const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
                 const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
                 const int mt = sg.mt, nt = sg.nt;
-                const int nacc = sg.m - mt * kTcRows > 128 ? 2 : 1;
-                const uint32_t idesc = tc_idesc(MODE == kTcDenseSwiglu ? kTcCols : min(kTcCols, a.n - nt * kTcCols));
+                const int nacc = MODE == kTcGroupedSwiglu ? 1 : (sg.m - mt * kTcRows > 128 ? 2 : 1);
+                const uint32_t idesc = tc_idesc(MODE == kTcGroupedSwiglu ? 128
+                                                : MODE == kTcDenseSwiglu ? kTcCols
+                                                                         : min(kTcCols, a.n - nt * kTcCols));
                 // the epilogue of the previous segment has read the accumulators
-                if (!mbar_wait(acc_empty, (uint32_t) (seg_i & 1) ^ 1, abort_flag, true)) {
+                const int buf = kDblAcc ? (seg_i & 1) : 0;
+                const uint32_t use = (uint32_t) (kDblAcc ? seg_i >> 1 : seg_i);
+                const uint32_t tacc = tmem + (uint32_t) (256 * buf);
+                if (!mbar_wait(acc_empty + 16 * buf, (use & 1) ^ 1, abort_flag, true)) {
                     ok = false;
                     break;
                 }
@@ -1049,20 +1114,34 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
 #pragma unroll
                     for (int ks = 0; ks < 4; ++ks) {
                         const uint32_t acc_flag = (kc != kc0 || ks != 0) ? 1u : 0u;
-                        tc_mma(tmem, ad + 2 * ks, bd + 2 * ks, idesc, acc_flag);
-                        if (nacc == 2) tc_mma(tmem + 256, ad + (kTcABlock >> 4) + 2 * ks, bd + 2 * ks, idesc, acc_flag);
+                        if constexpr (MODE == kTcGroupedSwiglu) {
+                            // gate columns 0..127 from A block 0, up columns 128..255 (B rows
+                            // 128.., 16 KB on) from A block 1
+                            tc_mma(tacc, ad + 2 * ks, bd + 2 * ks, idesc, acc_flag);
+                            tc_mma(tacc + 128, ad + (kTcABlock >> 4) + 2 * ks, bd + (16384 >> 4) + 2 * ks, idesc,
+                                   acc_flag);
+                        } else {
+                            tc_mma(tmem, ad + 2 * ks, bd + 2 * ks, idesc, acc_flag);
+                            if (nacc == 2)
+                                tc_mma(tmem + 256, ad + (kTcABlock >> 4) + 2 * ks, bd + 2 * ks, idesc, acc_flag);
+                        }
                     }
                     tc_commit(empty_a + 8 * sa);
                     tc_commit(empty_b + 8 * sb);
                     if (++sa == SA) { sa = 0; pa ^= 1; }
                     if (++sb == kTcStageB) { sb = 0; pb ^= 1; }
                 }
-                tc_commit(acc_full);
+                tc_commit(acc_full + 16 * buf);
                 it += kc1 - kc0;
             }
             // every MMA issued by this thread has completed before the CTA frees TMEM
             // (a commit tracks all of the thread's earlier tcgen05 operations)
-            if (seg_i > 0) mbar_wait(acc_full, (uint32_t) ((seg_i - 1) & 1), abort_flag, false);
+            if (seg_i > 0) {
+                const int last = seg_i - 1;
+                const int buf = kDblAcc ? (last & 1) : 0;
+                const uint32_t use = (uint32_t) (kDblAcc ? last >> 1 : last);
+                mbar_wait(acc_full + 16 * buf, use & 1, abort_flag, false);
+            }
         }
     } else {
         // decoders (and the epilogue of their TMEM lane quarter) or epilogue-only
@@ -1083,7 +1162,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
             const TcSeg sg = tc_seg<MODE>(a, tile + tile_base);
             const int mt = sg.mt, nt = sg.nt;
-            const int bn = MODE == kTcDenseSwiglu ? kTcCols : min(kTcCols, a.n - nt * kTcCols);
+            const int bn = kSwiglu ? kTcCols : min(kTcCols, a.n - nt * kTcCols);
             if (decoder) {
                 for (int kc = kc0; kc < kc1; ++kc) {
                     if (!mbar_wait(full_t + 8 * st, pt, abort_flag, true) ||
@@ -1105,27 +1184,62 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
                     if (++sb == kTcStageB) { sb = 0; pb ^= 1; }
                 }
             }
-            if (!ok || !mbar_wait(acc_full, (uint32_t) (seg_i & 1), abort_flag, true)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const int nacc = sg.m - mt * kTcRows > 128 ? 2 : 1;
+            const int buf = kDblAcc ? (seg_i & 1) : 0;
+            const uint32_t use = (uint32_t) (kDblAcc ? seg_i >> 1 : seg_i);
+            const int nacc = MODE == kTcGroupedSwiglu ? 1 : (sg.m - mt * kTcRows > 128 ? 2 : 1);
             const int nblk = bn >> 7;  // swiglu: tasks (accumulator, role) instead of (accumulator, block)
-            if (hq < nacc * nblk) {
+            // kTcGroupedSwiglu: a tile's rows sit in TMEM lanes 32..127 (quarters 1..3); only the
+            // two warps of a quarter holding rows wait for the accumulator, the others go on
+            // decoding the next tile (the accumulators are double-buffered)
+            const bool duty = MODE == kTcGroupedSwiglu
+                                  ? (q > 0 && hq < 2 && (q - 1) * 32 < sg.m - mt * kTcSwRows)
+                                  : hq < nacc * nblk;
+            if (MODE != kTcGroupedSwiglu || duty) {
+                if (!ok || !mbar_wait(acc_full + 16 * buf, use & 1, abort_flag, true)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+            }
+            if (duty) {
                 const int acc = hq / nblk, cb = hq - acc * nblk;
-                const int row = mt * kTcRows + acc * 128 + q * 32 + lane;
+                const int row = MODE == kTcGroupedSwiglu ? mt * kTcSwRows + (q - 1) * 32 + lane
+                                                         : mt * kTcRows + acc * 128 + q * 32 + lane;
                 const bool whole = kc0 == 0 && kc1 == nkc;
-                const uint32_t taddr = tmem + ((uint32_t) (q * 32) << 16) + acc * 256 + cb * 128;
+                const uint32_t taddr = tmem + ((uint32_t) (q * 32) << 16) + (acc + buf) * 256 + cb * 128;
                 const int col0 = nt * kTcCols + cb * 128;
-                if constexpr (MODE == kTcDenseSwiglu) {
+                if constexpr (MODE == kTcGroupedSwiglu) {
+                    // whole tiles only; rows past the expert's are not stored.  Image row
+                    // irow: k chunk kc at kc * xt_rows * 128 bytes, 16-byte chunks swizzled
+                    const int irow = sg.row0 + row;
+                    uint8_t* rowp = row < sg.m ? a.img + ((size_t) irow * 128 + (size_t) (nt * 2) * a.xt_rows * 128)
+                                               : nullptr;
+                    const size_t kstride = (size_t) a.xt_rows * 128;
+                    const int sw = irow & 7;
+                    tc_epilogue_swiglu(taddr - cb * 128, cb, 1 + 2 * q, sg.svh + nt * 128, sg.svh2 + nt * 128,
+                                       sg.suh2 + nt * 128, a.swiglu_limit, true, nullptr, false,
+                                       [&](int col, uint4 v) {
+                                           if (rowp)
+                                               *reinterpret_cast<uint4*>(rowp + (col >> 6) * kstride +
+                                                                         ((((col & 63) >> 3) ^ sw) << 4)) = v;
+                                       });
+                } else if constexpr (MODE == kTcDenseSwiglu) {
                     float* slot_row = nullptr;
                     if (!whole) {
                         const int slot = tc_cta_of(a.iters, nkc, grid, (long long) tile * nkc);
                         slot_row = a.slots + (size_t) slot * kTcSlotFloats + (size_t) (acc * 128 + q * 32 + lane) * kTcCols;
                     }
                     // the two warps (cb = role 0, 1) of this quarter share accumulator acc
-                    tc_epilogue_swiglu(a, taddr - cb * 128, row, nt, whole, slot_row, cb, 1 + 2 * q + acc);
+                    uint8_t* img = a.img;
+                    const int nkc2 = a.inter >> 6;
+                    tc_epilogue_swiglu(taddr - cb * 128, cb, 1 + 2 * q + acc, a.svh + nt * 128,
+                                       a.svh + a.inter + nt * 128, a.suh2 + nt * 128, a.swiglu_limit, whole,
+                                       slot_row, row < a.m, [&](int col, uint4 v) {
+                                           const int c = nt * 128 + col, rr = row & 127;
+                                           *reinterpret_cast<uint4*>(
+                                               img + ((((size_t) (row >> 7) * nkc2 + (c >> 6)) << 14) + rr * 128 +
+                                                      ((((c & 63) >> 3) ^ (rr & 7)) << 4))) = v;
+                                       });
                 } else if constexpr (MODE == kTcDense) {
                     float* slot_row = nullptr;
                     if (!whole) {
@@ -1151,7 +1265,17 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty);
+            if constexpr (MODE == kTcGroupedSwiglu) {
+                // 6 arrivals per phase: one per duty warp, the rest given by quarter 1's role-0
+                // warp (always on duty); warps without duty never touch the barrier, so none can
+                // arrive for a later use of the buffer before this phase completes
+                if (duty && lane == 0) {
+                    const int nq = min(3, (sg.m - mt * kTcSwRows + 31) >> 5);
+                    mbar_arrive_n(acc_empty + 16 * buf, (q == 1 && hq == 0) ? 1u + (uint32_t) (6 - 2 * nq) : 1u);
+                }
+            } else {
+                if (lane == 0) mbar_arrive(acc_empty + 16 * buf);
+            }
             it += kc1 - kc0;
         }
     }
@@ -1312,7 +1436,8 @@ int tc_grouped_matmul(const TcGroupedCall& c, int K, int cb, cudaStream_t stream
     if (K < 2 || K > 4) return kErrBadBits;
     if (cb < 0 || cb > 2) return kErrBadCodebook;
     if (c.k <= 0 || c.n <= 0 || c.k % 128 || c.n % 128 || c.xt_rows % 8 || c.out_stride % 4) return kErrBadShape;
-    if (!c.probs || !c.tile_prob || !c.dev_tiles || !c.out) return kErrNullPointer;
+    if (!c.probs || !c.tile_prob || !c.dev_tiles) return kErrNullPointer;
+    if (c.mode == kTcGroupedSwiglu ? !c.img : !c.out) return kErrNullPointer;
     if (c.mode == kTcGroupedCombine && (!c.slot_token || !c.slot_weight)) return kErrNullPointer;
     TcArgs a = {};
     a.out = c.out;
@@ -1328,7 +1453,11 @@ int tc_grouped_matmul(const TcGroupedCall& c, int K, int cb, cudaStream_t stream
     a.xt_rows = c.xt_rows;
     a.slot_token = c.slot_token;
     a.slot_weight = c.slot_weight;
+    a.img = c.img;
+    a.swiglu_limit = c.swiglu_limit;
+    a.inter = c.n;
     const int grid = tc_sm_count();  // the tile count is known on the device only
+    if (c.mode == kTcGroupedSwiglu) return tc_launch_k<kTcGroupedSwiglu>(a, K, cb, grid, stream);
     if (c.mode == kTcGroupedStore) return tc_launch_k<kTcGroupedStore>(a, K, cb, grid, stream);
     if (c.mode == kTcGroupedCombine) return tc_launch_k<kTcGroupedCombine>(a, K, cb, grid, stream);
     return kErrBadArgument;

@@ -22,15 +22,24 @@ struct TcProblem {
     int row0;                // first row in the input image (multiple of 8)
     int slot0;               // first routed slot (token / weight lists) of the problem
     int pad;
+    const __half* suh2;      // fused gate|up (kTcGroupedSwiglu, gate problem): down projection suh
 };
 
 enum TcMode : int {
     kTcDense = 0,         // one problem, host-known sizes (exl3b200_gemm)
     kTcGroupedStore = 1,  // fp32 out rows of each problem (whole tiles stored, split tiles added)
     kTcGroupedCombine = 2, // fp32 out[slot_token[s]] += slot_weight[s] * y
-    kTcDenseSwiglu = 3     // one fused gate|up problem; a tile is 128 gate + the matching 128 up
+    kTcDenseSwiglu = 3,    // one fused gate|up problem; a tile is 128 gate + the matching 128 up
                            // columns, its epilogue writes the down projection's rotated input image
+    kTcGroupedSwiglu = 4   // routed experts: problem p (gate) and p + 1 (up) of the table form one
+                           // problem; a tile is 128 rows x (gate block j | up block j), each half
+                           // with its own input image, whole tiles only; the epilogue writes the
+                           // down projection's input image at the expert's rows
 };
+
+// Rows per kTcGroupedSwiglu tile: A rows 32..127, i.e. TMEM lanes 32..127 (quarters 1..3),
+// so that a tile of at most 32 rows is finished by the warps of lane quarter 1 alone.
+constexpr int kTcSwRows = 96;
 
 // Input image of a grouped launch: k-chunk major, xt_rows rows of 128 bytes per
 // 64-wide k chunk, each 8-row group's 16-byte chunks XOR-swizzled by (row % 8):
@@ -53,7 +62,9 @@ struct TcGroupedCall {
     long long out_stride;     // elements, multiple of 4 (both modes)
     const int* slot_token;    // combine
     const float* slot_weight; // combine
-    int mode;                 // kTcGroupedStore or kTcGroupedCombine
+    int mode;                 // kTcGroupedStore, kTcGroupedCombine or kTcGroupedSwiglu
+    uint8_t* img;             // swiglu: the down projection's input image (xt_rows rows, k = n)
+    float swiglu_limit;       // swiglu: 0 or infinite = no clip
 };
 
 // Enqueues one grouped launch (programmatic dependent of the previous kernel).

@@ -18,9 +18,12 @@
 //     up, written into k-chunk-major swizzled images (the MMA's shared-memory
 //     layout, so the GEMM copies each expert's rows with one bulk copy per k
 //     chunk); zeroes the fp32 gate/up outputs and, unless accumulating, out.
-//   grouped GEMM: gate and up (one launch when both have the same K), fp32 rows.
-//   SwiGLU stage: clipped silu(g) * u rounded to fp16, then the down projection's
-//     rotated input into its image (the arithmetic of the small-M SwiGLU epilogue).
+//   grouped GEMM over gate and up.  When both have the same K (every checkpoint
+//     seen), one launch whose 128-row tiles hold gate block j and up block j of an
+//     expert side by side, with the clipped SwiGLU, its fp16 rounding, the down
+//     projection's x * suh and H128 in the epilogue, written straight into the down
+//     projection's image.  Otherwise two launches into fp32 rows and a SwiGLU stage
+//     doing the same arithmetic (that of the small-M SwiGLU epilogue).
 //   grouped GEMM: down, combined as out[token] += weight * y (fp32 vector atomics).
 #include <algorithm>
 
@@ -37,8 +40,8 @@ constexpr int kTmEpt = kTmMaxExperts / kTmThreads;  // experts per routing threa
 
 static inline size_t tm_al(size_t v) { return (v + 255) & ~(size_t) 255; }
 
-// tot[]: 0 gate+up tiles, 1 gate tiles (= up tiles), 2 first up tile, 3 down tiles,
-//        4 routed slots, 5 zero
+// tot[]: 0 gate+up tiles (fused: gate|up tiles), 1 gate tiles (= up tiles), 2 first up
+//        tile, 3 down tiles, 4 routed slots, 5 zero
 struct TmLayout {
     size_t tot, slot_token, slot_weight, slot_row, slot_exp, probs_gu, probs_d, tiles_gu, tiles_d;
     size_t xt_g, xt_u, xt_d, gu_out, bytes;
@@ -54,6 +57,8 @@ static TmLayout tm_layout(int pmax, int experts, int hidden, int inter)
     L.xt_rows = ((long long) pmax + 7ll * L.act_max + 7) & ~7ll;
     L.mt_max = pmax / 256 + L.act_max;                  // sum over experts of ceil(rows / 256)
     const long long ntg = (inter + 255) / 256, ntd = (hidden + 255) / 256;
+    // fused gate|up tiles: inter / 128 blocks x sum over experts of ceil(rows / 96)
+    const long long fused_tiles = (long long) (inter / 128) * (pmax / kTcSwRows + L.act_max);
     size_t o = 0;
     L.tot = o; o = tm_al(o + 16 * sizeof(int));
     L.slot_token = o; o = tm_al(o + (size_t) pmax * sizeof(int));
@@ -62,7 +67,7 @@ static TmLayout tm_layout(int pmax, int experts, int hidden, int inter)
     L.slot_exp = o; o = tm_al(o + (size_t) pmax * sizeof(int));
     L.probs_gu = o; o = tm_al(o + (size_t) 2 * L.act_max * sizeof(TcProblem));
     L.probs_d = o; o = tm_al(o + (size_t) L.act_max * sizeof(TcProblem));
-    L.tiles_gu = o; o = tm_al(o + (size_t) 2 * ntg * L.mt_max * sizeof(int));
+    L.tiles_gu = o; o = tm_al(o + (size_t) std::max(2 * ntg * L.mt_max, fused_tiles) * sizeof(int));
     L.tiles_d = o; o = tm_al(o + (size_t) ntd * L.mt_max * sizeof(int));
     L.xt_g = o; o = tm_al(o + (size_t) L.xt_rows * hidden * 2);
     L.xt_u = o; o = tm_al(o + (size_t) L.xt_rows * hidden * 2);
@@ -83,46 +88,48 @@ struct TmArgs {
     char* scratch;
     TmLayout L;
     int tokens, topk, experts, hidden, inter, accumulate;
+    int fused;  // gate and up in one launch with the SwiGLU epilogue (same K)
     float swiglu_limit;
 };
 
 __device__ __forceinline__ int* tm_tot(const TmArgs& t) { return reinterpret_cast<int*>(t.scratch + t.L.tot); }
 
-// Inclusive block-wide scan of 4 values per thread over kTmThreads threads.
-__device__ __forceinline__ void tm_block_scan4(int (&v)[4], int (*s_warp)[4])
+// Inclusive block-wide scan of NV values per thread over kTmThreads threads.
+template <int NV>
+__device__ __forceinline__ void tm_block_scan(int (&v)[NV], int (*s_warp)[NV])
 {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < NV; ++j) {
             const int n = __shfl_up_sync(0xffffffffu, v[j], o);
             if (lane >= o) v[j] += n;
         }
     }
     if (lane == 31)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) s_warp[warp][j] = v[j];
+        for (int j = 0; j < NV; ++j) s_warp[warp][j] = v[j];
     __syncthreads();
     if (warp == 0) {
-        int w[4];
+        int w[NV];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) w[j] = s_warp[lane][j];
+        for (int j = 0; j < NV; ++j) w[j] = s_warp[lane][j];
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < NV; ++j) {
                 const int n = __shfl_up_sync(0xffffffffu, w[j], o);
                 if (lane >= o) w[j] += n;
             }
         }
 #pragma unroll
-        for (int j = 0; j < 4; ++j) s_warp[lane][j] = w[j];  // inclusive over warps
+        for (int j = 0; j < NV; ++j) s_warp[lane][j] = w[j];  // inclusive over warps
     }
     __syncthreads();
     if (warp > 0)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) v[j] += s_warp[warp - 1][j];
+        for (int j = 0; j < NV; ++j) v[j] += s_warp[warp - 1][j];
 }
 
 __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs t)
@@ -131,7 +138,7 @@ __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs 
     __shared__ int s_slot[kTmMaxExperts];  // first slot of each expert
     __shared__ int s_row[kTmMaxExperts];   // first image row of each expert
     __shared__ int s_fill[kTmMaxExperts];  // rows placed so far (second pass)
-    __shared__ int s_warp[32][4];
+    __shared__ int s_warp[32][5];
 
     const int tid = threadIdx.x;
     const TmLayout& L = t.L;
@@ -145,21 +152,24 @@ __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs 
     for (int e = tid; e < kTmMaxExperts; e += kTmThreads) s_fill[e] = 0;
     __syncthreads();
 
-    // per expert: rows, rows rounded up to 8, active (0/1), 256-row tiles
-    int c[kTmEpt], ex[kTmEpt][4], sum[4] = {0, 0, 0, 0};
+    // per expert: rows, rows rounded up to 8, active (0/1), 256-row tiles, fused-tile rows
+    int c[kTmEpt], ex[kTmEpt][5], sum[5] = {0, 0, 0, 0, 0};
 #pragma unroll
     for (int j = 0; j < kTmEpt; ++j) {
         c[j] = s_count[tid * kTmEpt + j];
-        const int v[4] = {c[j], (c[j] + 7) & ~7, c[j] > 0 ? 1 : 0, (c[j] + 255) / 256};
+        const int v[5] = {c[j], (c[j] + 7) & ~7, c[j] > 0 ? 1 : 0, (c[j] + 255) / 256,
+                          (c[j] + kTcSwRows - 1) / kTcSwRows};
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 5; ++q) {
             ex[j][q] = sum[q];
             sum[q] += v[q];
         }
     }
-    int inc[4] = {sum[0], sum[1], sum[2], sum[3]};
-    tm_block_scan4(inc, s_warp);
-    const int base[4] = {inc[0] - sum[0], inc[1] - sum[1], inc[2] - sum[2], inc[3] - sum[3]};
+    int inc[5] = {sum[0], sum[1], sum[2], sum[3], sum[4]};
+    tm_block_scan<5>(inc, s_warp);
+    int base[5];
+#pragma unroll
+    for (int q = 0; q < 5; ++q) base[q] = inc[q] - sum[q];
 #pragma unroll
     for (int j = 0; j < kTmEpt; ++j) {
         s_slot[tid * kTmEpt + j] = base[0] + ex[j][0];
@@ -168,6 +178,7 @@ __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs 
     __syncthreads();
     const int total_rows = s_warp[31][0];
     const int total_mt = s_warp[31][3];
+    const int total_mtf = s_warp[31][4];
 
     int* slot_token = reinterpret_cast<int*>(t.scratch + L.slot_token);
     float* slot_weight = reinterpret_cast<float*>(t.scratch + L.slot_weight);
@@ -189,7 +200,7 @@ __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs 
     // problems and tile lists: gate tiles of every expert, then up tiles, then (own
     // list) down tiles; within a problem the 256-row tiles run fastest
     const int H = t.hidden, I = t.inter;
-    const int ntg = (I + 255) / 256, ntd = (H + 255) / 256;
+    const int ntg = (I + 255) / 256, ntd = (H + 255) / 256, ntf = I / 128;
     const int G = ntg * total_mt;
     TcProblem* pg = reinterpret_cast<TcProblem*>(t.scratch + L.probs_gu);
     TcProblem* pd = reinterpret_cast<TcProblem*>(t.scratch + L.probs_d);
@@ -203,6 +214,8 @@ __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs 
         const int a = base[2] + ex[j][2];    // active-expert index
         const int mtp = base[3] + ex[j][3];  // 256-row tiles before this expert
         const int mt = (c[j] + 255) / 256;
+        const int mtpf = base[4] + ex[j][4];  // fused tiles' row groups before this expert
+        const int mtf = (c[j] + kTcSwRows - 1) / kTcSwRows;
         TcProblem g = {};
         g.m = c[j];
         g.mtiles = mt;
@@ -224,18 +237,28 @@ __global__ __launch_bounds__(kTmThreads) void exl3_tm_route_kernel(const TmArgs 
         d.svh = reinterpret_cast<const __half*>(t.dv[e]);
         d.out = nullptr;
         d.tile_begin = ntd * mtp;
+        if (t.fused) {
+            // one problem (gate, up = the next entry) in 96-row tiles, no fp32 rows
+            g.mtiles = mtf;
+            g.tile_begin = ntf * mtpf;
+            g.out = nullptr;
+            g.suh2 = reinterpret_cast<const __half*>(t.du[e]);
+            u.out = nullptr;
+            for (int i = 0; i < ntf * mtf; ++i) tg[g.tile_begin + i] = 2 * a;
+        } else {
+            for (int i = 0; i < ntg * mt; ++i) {
+                tg[g.tile_begin + i] = 2 * a;
+                tg[u.tile_begin + i] = 2 * a + 1;
+            }
+        }
         pg[2 * a] = g;
         pg[2 * a + 1] = u;
         pd[a] = d;
-        for (int i = 0; i < ntg * mt; ++i) {
-            tg[g.tile_begin + i] = 2 * a;
-            tg[u.tile_begin + i] = 2 * a + 1;
-        }
         for (int i = 0; i < ntd * mt; ++i) td[d.tile_begin + i] = a;
     }
     if (tid == 0) {
         int* tot = tm_tot(t);
-        tot[0] = 2 * G;
+        tot[0] = t.fused ? ntf * total_mtf : 2 * G;
         tot[1] = G;
         tot[2] = G;
         tot[3] = ntd * total_mt;
@@ -286,11 +309,11 @@ __global__ __launch_bounds__(256) void exl3_tm_input_kernel(const TmArgs t)
                     __float2half_rn(__fmul_rn(v[i], kHadScale));
         }
     }
-    // zero the gate/up rows (split tiles add into them) and the output
+    // zero the gate/up rows (split tiles add into them; not used when fused) and the output
     const int gthreads = gridDim.x * blockDim.x;
     const int gt = blockIdx.x * blockDim.x + threadIdx.x;
     float4* gu4 = reinterpret_cast<float4*>(t.scratch + L.gu_out);
-    const long long n_gu4 = (long long) rows * 2 * I / 4;
+    const long long n_gu4 = t.fused ? 0 : (long long) rows * 2 * I / 4;
     for (long long i = gt; i < n_gu4; i += gthreads) gu4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (!t.accumulate) {
         const long long n_out = (long long) t.tokens * H;
@@ -419,6 +442,7 @@ extern "C" int exl3b200_moe_tc(const void* x, long long x_stride, int tokens, in
     t.hidden = hidden;
     t.inter = inter;
     t.accumulate = accumulate;
+    t.fused = K_gate == K_up ? 1 : 0;
     t.swiglu_limit = swiglu_limit;
     void* args[] = {&t};
 
@@ -440,8 +464,13 @@ extern "C" int exl3b200_moe_tc(const void* x, long long x_stride, int tokens, in
     g.out = reinterpret_cast<float*>(sc + L.gu_out);  // rows come from the problems
     g.out_stride = 2 * inter;
     g.mode = kTcGroupedStore;
-    if (K_gate == K_up) {
-        // one launch over the gate tiles and the up tiles
+    if (t.fused) {
+        // one launch over the gate|up tiles; its epilogue writes the down image
+        g.mode = kTcGroupedSwiglu;
+        g.out = nullptr;
+        g.out_stride = 0;
+        g.img = reinterpret_cast<uint8_t*>(sc + L.xt_d);
+        g.swiglu_limit = swiglu_limit;
         g.dev_tiles = tot + 0;
         g.dev_tile_base = tot + 5;
         rc = tc_grouped_matmul(g, K_gate, cb, st);
@@ -455,9 +484,11 @@ extern "C" int exl3b200_moe_tc(const void* x, long long x_stride, int tokens, in
     }
     if (rc != kOk) return rc;
 
-    const int sw_grid = std::min((pairs * (inter / 128) + 7) / 8, 8 * sms);
-    rc = tm_launch((const void*) exl3_tm_swiglu_kernel, sw_grid, 256, true, st, args);
-    if (rc != kOk) return rc;
+    if (!t.fused) {
+        const int sw_grid = std::min((pairs * (inter / 128) + 7) / 8, 8 * sms);
+        rc = tm_launch((const void*) exl3_tm_swiglu_kernel, sw_grid, 256, true, st, args);
+        if (rc != kOk) return rc;
+    }
 
     TcGroupedCall d = {};
     d.xt_rows = L.xt_rows;
