@@ -985,14 +985,15 @@ def finish(line, args, world):
 
 # The other benchmark configurations, measured after the default decode line in the same
 # process and reported in its "workloads" object (one summary each), so that one run
-# records every config: (name, argument overrides, runs under torchrun too).
+# records every config: (name, argument overrides, runs under torchrun too - the MoE
+# layers then run expert-parallel over the ranks, every rank with its own tokens).
 EXTRA_WORKLOADS = [
     ("config 1 linear 4096x4096 4bpw M=1", dict(workload="linear", k=4096, n=4096, bits=4, batch=1), False),
     ("config 2 MLP block M=1", dict(workload="mlp", batch=1), False),
     ("config 2 MLP block M=2048", dict(workload="mlp", batch=2048), False),
     ("config 3 MoE layer T=64", dict(workload="moe", moe="c3", batch=64), False),
-    ("config 3 MoE layer T=512", dict(workload="moe", moe="c3", batch=512), False),
-    ("config 5 MoE layer, verify batch 64", dict(workload="moe", moe="c5", batch=64), False),
+    ("config 3 MoE layer T=512", dict(workload="moe", moe="c3", batch=512), True),
+    ("config 5 MoE layer, verify batch 64", dict(workload="moe", moe="c5", batch=64), True),
 ]
 
 

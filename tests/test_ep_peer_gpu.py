@@ -6,9 +6,9 @@ on the same experts (same rows, same weights; only the order of the fp32 atomics
 differs) and the oracle; several calls in a row alternate the buffer's parity; a
 CUDA graph of one call replays correctly.  A two-rank exchange whose second rank
 never answers (its buffer is local memory nobody writes) must give up within the
-wait limit, record EXL3B200_ETIMEOUT and recover after exl3b200_peer_reset.  Two
-GPUs (skipped with fewer): every rank owns half of the experts and its own tokens;
-each rank's output equals the single-GPU MoE over all experts for its tokens.
+wait limit, record EXL3B200_ETIMEOUT and recover after exl3b200_peer_reset.  On 2, 4
+and 8 GPUs (skipped with fewer): every rank owns 1/world of the experts and its own
+tokens; each rank's output equals the single-GPU MoE over all experts for its tokens.
 """
 
 import os
@@ -182,7 +182,7 @@ def test_ep_peer_wait_runs_out(cuda_device):
     assert _rel(y, ref) < TOL_SAME
 
 
-def _two_rank_worker(rank, world, port):
+def _rank_worker(rank, world, port):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -216,10 +216,11 @@ def _two_rank_worker(rank, world, port):
         dist.destroy_process_group()
 
 
-def test_ep_peer_two_gpus():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_peer_multi_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
-    mp.start_processes(_two_rank_worker, args=(2, port), nprocs=2, join=True, start_method="spawn")
+    mp.start_processes(_rank_worker, args=(world, port), nprocs=world, join=True, start_method="spawn")
