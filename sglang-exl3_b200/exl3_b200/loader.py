@@ -39,21 +39,15 @@ class LoadFormatEXL3:
     EXL3_MMAP = LOAD_FORMAT_EXL3_MMAP
 
 
+# safetensors header dtype names (the format's own names) -> torch dtypes; the fp8
+# kinds only where this torch has them
 SAFETENSORS_DTYPES: Dict[str, torch.dtype] = {
-    "BF16": torch.bfloat16,
-    "F16": torch.float16,
-    "F32": torch.float32,
-    "F64": torch.float64,
-    "I8": torch.int8,
-    "U8": torch.uint8,
-    "I16": torch.int16,
-    "I32": torch.int32,
-    "I64": torch.int64,
-    "BOOL": torch.bool,
+    st_name: getattr(torch, attr)
+    for st_name, attr in (("BOOL", "bool"), ("U8", "uint8"), ("I8", "int8"), ("I16", "int16"), ("I32", "int32"),
+                          ("I64", "int64"), ("F16", "float16"), ("BF16", "bfloat16"), ("F32", "float32"),
+                          ("F64", "float64"), ("F8_E4M3", "float8_e4m3fn"), ("F8_E5M2", "float8_e5m2"))
+    if hasattr(torch, attr)
 }
-for _name, _attr in (("F8_E4M3", "float8_e4m3fn"), ("F8_E5M2", "float8_e5m2")):
-    if hasattr(torch, _attr):
-        SAFETENSORS_DTYPES[_name] = getattr(torch, _attr)
 
 STAGING_SLOT_BYTES = 8 << 20  # per reader thread
 BATCH_BYTES = 1 << 30  # device bytes read per native call by the weights iterator
@@ -79,44 +73,43 @@ def is_unified_memory_platform() -> bool:
 
 
 def madvise_file_preload(file_path: str) -> bool:
-    """Ask the kernel to read a file ahead (POSIX_FADV_WILLNEED); False if unsupported."""
-    if not hasattr(os, "posix_fadvise"):
+    """Map the file read-only and madvise(MADV_WILLNEED) the mapping, so the kernel
+    starts reading it ahead; the mapping is dropped again at once (the advice applies
+    to the file's page cache).  False where mmap or the advice is unavailable."""
+    import mmap
+
+    advice = getattr(mmap, "MADV_WILLNEED", None)
+    if advice is None:
         return False
     try:
-        fd = os.open(file_path, os.O_RDONLY)
-    except OSError:
-        return False
-    try:
-        os.posix_fadvise(fd, 0, os.fstat(fd).st_size, getattr(os, "POSIX_FADV_WILLNEED", 3))
+        with open(file_path, "rb") as fh:
+            if os.fstat(fh.fileno()).st_size == 0:
+                return False
+            with mmap.mmap(fh.fileno(), 0, access=mmap.ACCESS_READ) as mm:
+                mm.madvise(advice)
         return True
-    except OSError:
+    except (OSError, ValueError):
         return False
-    finally:
-        os.close(fd)
 
 
 def host_memory_summary(device: Union[str, torch.device, None] = None) -> str:
-    """One line of host and device memory figures for load-time logs."""
-    avail = swap = float("nan")
+    """Free host memory (free physical pages) and the CUDA device's free / total
+    memory as the driver reports it, for the load-time log line."""
+    host_free = float("nan")
     try:
-        info: Dict[str, int] = {}
-        with open("/proc/meminfo") as fh:
-            for line in fh:
-                key, _, rest = line.partition(":")
-                info[key] = int(rest.split()[0])
-        avail = info["MemAvailable"] / (1 << 20)
-        swap = (info["SwapTotal"] - info["SwapFree"]) / 1024
-    except (OSError, KeyError, ValueError, IndexError):
+        host_free = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE") / 2**30
+    except (AttributeError, OSError, ValueError):
         pass
-    dev_gib = float("nan")
+    dev_free = dev_total = float("nan")
     if torch.cuda.is_available():
         try:
-            dev = torch.device(device) if device is not None else None
-            if dev is None or dev.type == "cuda":
-                dev_gib = torch.cuda.memory_allocated(dev) / (1 << 30)
-        except Exception:
+            dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+            if dev.type == "cuda":
+                free_b, total_b = torch.cuda.mem_get_info(dev)
+                dev_free, dev_total = free_b / 2**30, total_b / 2**30
+        except Exception:  # a log line must not fail the load
             pass
-    return f"MemAvailable={avail:.2f}GiB swap_used={swap:.0f}MiB cuda_allocated={dev_gib:.2f}GiB"
+    return f"host_free={host_free:.1f}GiB device_free={dev_free:.1f}/{dev_total:.1f}GiB"
 
 
 @dataclass(frozen=True)

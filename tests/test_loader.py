@@ -18,7 +18,8 @@ from exl3_b200 import loader as LD
 def test_constants_and_platform():
     assert LD.LoadFormatEXL3.EXL3_MMAP == "exl3_mmap" == LD.LOAD_FORMAT_EXL3_MMAP
     assert isinstance(LD.is_unified_memory_platform(), bool)
-    assert "MemAvailable" in LD.host_memory_summary()
+    line = LD.host_memory_summary()
+    assert line.startswith("host_free=") and "device_free=" in line
     assert LD.EXL3MMapModelLoader(load_config=None).load_format == "exl3_mmap"
 
 
