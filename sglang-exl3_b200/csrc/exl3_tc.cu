@@ -107,6 +107,7 @@ struct TcArgs {
     int mtiles, tiles, nkc;
     int out_dtype;            // 0 fp16, 1 bf16, 2 fp32
     int vec_store;            // rows of out are 16-byte aligned
+    int pair;                 // exl3_tc_pair_kernel launch: 512-row tiles, slots per CTA of each pair
     // grouped launches (kTcGroupedStore / kTcGroupedCombine): the problem of each
     // tile and the tile count come from device memory written by an earlier kernel
     const TcProblem* probs;
@@ -241,6 +242,116 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
+// --- CTA pairs (cta_group::2): one MMA spans the TMEM and shared memory of both CTAs of
+// a 2-CTA cluster.  A rows are split between the CTAs (M / 2 each, same shared memory
+// offset), B columns likewise (N / 2 each); the leader (cluster rank 0) issues.
+__device__ __forceinline__ uint32_t cluster_ctarank()
+{
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Address in the shared::cluster window of the variable at `addr` in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank)
+{
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+// Arrive on an mbarrier of another CTA of the cluster (release at cluster scope).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
+{
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// try_wait with acquire at cluster scope (for barriers that another CTA arrives on).
+__device__ __forceinline__ bool mbar_test_cl(uint32_t bar, uint32_t parity, uint32_t hint_ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __noinline__ bool mbar_wait_cl_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag)
+{
+    const unsigned long long t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_test_cl(bar, parity, 200000u)) return true;
+        if ((it & 63u) == 0) {
+            if (*abort_flag) return false;
+            if (global_ns() - t0 > *reinterpret_cast<volatile unsigned long long*>(
+                                       reinterpret_cast<volatile char*>(abort_flag) + 4)) {
+                *abort_flag = 1;
+                atomicCAS(&g_exl3_device_status, 0, (int) kErrTimeout);
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ bool mbar_wait_cl(uint32_t bar, uint32_t parity, volatile int* abort_flag)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    return mbar_wait_cl_slow(bar, parity, abort_flag);
+}
+
+__device__ __forceinline__ void cluster_sync_all()
+{
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t slot, uint32_t ncols)
+{
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(ncols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair()
+{
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols)
+{
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Completion of the pair MMAs issued so far arrives on the mbarrier at this offset in
+// both CTAs of the pair.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar)
+{
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"((uint16_t) 3)
+        : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (fp16 inputs, fp32 accumulate)
 __device__ __forceinline__ void tc_mma(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate)
 {
@@ -345,10 +456,11 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr)
     return ((uint64_t) hi << 32) | lo;
 }
 
-// Instruction descriptor, kind::f16: fp32 D, fp16 A and B, both K-major, M = 128.
-__device__ __forceinline__ uint32_t tc_idesc(int n)
+// Instruction descriptor, kind::f16: fp32 D, fp16 A and B, both K-major, M = 128
+// (M = 256 for a CTA pair).
+__device__ __forceinline__ uint32_t tc_idesc(int n, int m = 128)
 {
-    return (1u << 4) | ((uint32_t) (n >> 3) << 17) | ((uint32_t) (128 >> 4) << 24);
+    return (1u << 4) | ((uint32_t) (n >> 3) << 17) | ((uint32_t) (m >> 4) << 24);
 }
 
 __device__ __forceinline__ uint32_t hadd2_u32(uint32_t a, uint32_t b)
@@ -1289,31 +1401,349 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
     }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair matmul (dense modes, large M): a 2-CTA cluster computes 512 x 256 tiles
+// with tcgen05.mma.cta_group::2 (M = 256 per MMA, two accumulators).  Each CTA holds
+// two 128-row accumulators (pair rows 256 acc + 128 rank + [0, 128)) and decodes only
+// its half of the tile's 256 B columns (rank 0: columns 0..127, rank 1: 128..255; the
+// SwiGLU mode: gate block / up block), so every decoded code tile feeds 512 rows
+// instead of 256 - half the decode work per output of the single-CTA kernel, at the
+// same MMA work per SM.  Roles as in exl3_tc_gemm_kernel; warp 1 of the leader (rank
+// 0) issues the MMAs, warp 1 of the other CTA forwards "stage full" (its own A copies
+// and B decode done) to the leader's pfull barrier.  The leader's commits arrive on
+// the empty and accumulator barriers of both CTAs (multicast); the epilogue warps of
+// both CTAs arrive on the leader's acc_empty.  Every wait is bounded as in the
+// single-CTA kernel.
+// ---------------------------------------------------------------------------
+constexpr int kTpStages = 4;  // activation, B and code ring depth of the pair kernel
+
+template <int K>
+struct TcPairSmem {
+    static constexpr int kBars = 2 * kTpStages * 3 + kTpStages + 2;  // a, t, b full/empty; pfull; acc
+    static constexpr uint32_t kBStage = 128 * 64 * 2;                // 16 KB: 128 columns x 64 k
+    static constexpr uint32_t kTChunk = 4u * 8u * 32u * K;           // codes of 4 k-tiles x 8 n-tiles
+    static constexpr uint32_t kA = 0;
+    static constexpr uint32_t kB = kA + kTpStages * 2 * kTcABlock;
+    static constexpr uint32_t kT = kB + kTpStages * kBStage;
+    static constexpr uint32_t kBar = kT + kTpStages * kTChunk;
+    static constexpr uint32_t kMisc = kBar + 8 * kBars;
+    static constexpr uint32_t kBytes = kMisc + 16;
+    static constexpr uint32_t kLaunchBytes = kBytes + 1024;
+};
+
+template <int K, int CB, int MODE>
+__global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_pair_kernel(const __grid_constant__ TcArgs a)
+{
+    static_assert(MODE == kTcDense || MODE == kTcDenseSwiglu, "pair tiles: dense modes");
+    constexpr int S = kTpStages;
+    using L = TcPairSmem<K>;
+    static_assert(L::kLaunchBytes <= 232448, "shared memory per CTA");
+    extern __shared__ uint8_t tc_smem_raw[];
+    const uint32_t raw = smem_u32(tc_smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    uint8_t* gbase = tc_smem_raw + (base - raw);
+    const uint32_t sA = base + L::kA, sB = base + L::kB, sT = base + L::kT, sBar = base + L::kBar;
+    const uint32_t full_a = sBar, empty_a = full_a + 8 * S;
+    const uint32_t full_t = empty_a + 8 * S, empty_t = full_t + 8 * S;
+    const uint32_t full_b = empty_t + 8 * S, empty_b = full_b + 8 * S;
+    const uint32_t pfull = empty_b + 8 * S;
+    const uint32_t acc_full = pfull + 8 * S, acc_empty = acc_full + 8;
+    volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + L::kMisc);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(gbase + L::kMisc + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int npairs = gridDim.x >> 1;
+    const int pair = blockIdx.x >> 1;
+    const int nkc = a.nkc;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(full_a + 8 * i, 1);
+            mbar_init(empty_a + 8 * i, 1);
+            mbar_init(full_t + 8 * i, 1);
+            mbar_init(empty_t + 8 * i, kTcDecWarps);
+            mbar_init(full_b + 8 * i, kTcDecWarps);
+            mbar_init(empty_b + 8 * i, 1);
+            mbar_init(pfull + 8 * i, 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 2 * (kTcWarps - 3));  // every decoder and epilogue-only warp of both CTAs
+        *abort_flag = 0;
+        *reinterpret_cast<volatile unsigned long long*>(gbase + L::kMisc + 8) = a.wait_ns;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        tmem_alloc_pair(base + L::kMisc, 512);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    tc_griddep_launch();
+    const TcRanges rg = tc_ranges(a.iters, nkc, npairs, pair);
+    const int mpad = (a.m + 127) & ~127;
+
+    if (warp == 0) {
+        // activation producer: this CTA's two 128-row blocks of the pair tile
+        tc_griddep_wait();
+        if (lane == 0) {
+            uint32_t s = 0, ph = 0, used = 0, par = 0;
+            bool ok = true;
+            for (int r = 0; r < 2; ++r)
+            for (long long it = rg.b[r], it_end = rg.e[r]; it < it_end && ok;) {
+                const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
+                const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
+                const int mt = tile % a.mtiles;
+                const int blk0 = 4 * mt + (int) rank, blk1 = blk0 + 2;
+                const bool has0 = blk0 * 128 < mpad, has1 = blk1 * 128 < mpad;
+                const uint32_t bytes = (has0 ? kTcABlock : 0) + (has1 ? kTcABlock : 0);
+                for (int kc = kc0; kc < kc1; ++kc) {
+                    if (!mbar_wait(empty_a + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
+                    if (bytes) {
+                        mbar_expect_tx(full_a + 8 * s, bytes);
+                        if (has0) bulk_g2s(sA + (s * 2) * kTcABlock, a.xt + (((size_t) blk0 * nkc + kc) << 14), kTcABlock,
+                                           full_a + 8 * s);
+                        if (has1)
+                            bulk_g2s(sA + (s * 2 + 1) * kTcABlock, a.xt + (((size_t) blk1 * nkc + kc) << 14), kTcABlock,
+                                     full_a + 8 * s);
+                        used |= 1u << s;
+                        par = (par & ~(1u << s)) | (ph << s);
+                    } else {
+                        mbar_arrive(full_a + 8 * s);  // nothing of this CTA's rows: the stage is ready as is
+                    }
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                it += kc1 - kc0;
+            }
+            for (uint32_t j = 0; j < S; ++j)
+                if (used >> j & 1) mbar_wait(full_a + 8 * j, par >> j & 1, abort_flag, false);
+        }
+    } else if (warp == 2) {
+        // code producer: this CTA's 8 n-tiles of each of the stage's 4 k-tile rows
+        if (lane == 0) {
+            const size_t row_bytes = (size_t) (a.n >> 4) * 32 * K;
+            constexpr uint32_t seg = 8u * 32u * K;
+            uint32_t s = 0, ph = 0, used = 0, par = 0;
+            bool ok = true;
+            for (int r = 0; r < 2; ++r)
+            for (long long it = rg.b[r], it_end = rg.e[r]; it < it_end && ok;) {
+                const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
+                const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
+                const int nt = tile / a.mtiles;
+                // dense: columns 256 nt + 128 rank; swiglu: gate block nt (rank 0) or up block nt (rank 1)
+                const size_t col_off = MODE == kTcDenseSwiglu
+                                           ? ((size_t) nt * 8 + (size_t) rank * (a.inter >> 4)) * 32 * K
+                                           : ((size_t) nt * 16 + (size_t) rank * 8) * 32 * K;
+                const uint8_t* src = a.trellis + (size_t) kc0 * 4 * row_bytes + col_off;
+                for (int kc = kc0; kc < kc1; ++kc, src += 4 * row_bytes) {
+                    if (!mbar_wait(empty_t + 8 * s, ph ^ 1, abort_flag, true)) { ok = false; break; }
+                    mbar_expect_tx(full_t + 8 * s, 4 * seg);
+                    const uint32_t dst = sT + s * L::kTChunk;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) bulk_g2s(dst + i * seg, src + i * row_bytes, seg, full_t + 8 * s);
+                    used |= 1u << s;
+                    par = (par & ~(1u << s)) | (ph << s);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                it += kc1 - kc0;
+            }
+            for (uint32_t j = 0; j < S; ++j)
+                if (used >> j & 1) mbar_wait(full_t + 8 * j, par >> j & 1, abort_flag, false);
+        }
+    } else if (warp == 1) {
+        if (lane == 0 && rank == 0) {
+            // MMA issuer (leader): both CTAs' stage s ready -> 8 pair MMAs
+            uint32_t s = 0, ph = 0;
+            int seg_i = 0;
+            bool ok = true;
+            const uint64_t a_desc0 = sw128_desc(sA), b_desc0 = sw128_desc(sB);
+            const uint32_t idesc = tc_idesc(256, 256);
+            for (int r = 0; r < 2; ++r)
+            for (long long it = rg.b[r], it_end = rg.e[r]; it < it_end && ok; ++seg_i) {
+                const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
+                const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
+                const int mt = tile % a.mtiles;
+                const int nacc = a.m - mt * 512 > 256 ? 2 : 1;
+                if (!mbar_wait_cl(acc_empty, (uint32_t) (seg_i & 1) ^ 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int kc = kc0; kc < kc1; ++kc) {
+                    // the other CTA's arrival on pfull is a cluster-scope release: acquire at cluster scope
+                    if (!mbar_wait(full_a + 8 * s, ph, abort_flag, true) || !mbar_wait(full_b + 8 * s, ph, abort_flag, true) ||
+                        !mbar_wait_cl(pfull + 8 * s, ph, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint64_t ad = a_desc0 + s * (2 * kTcABlock >> 4);
+                    const uint64_t bd = b_desc0 + s * (L::kBStage >> 4);
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks) {
+                        const uint32_t acc_flag = (kc != kc0 || ks != 0) ? 1u : 0u;
+                        tc_mma_pair(tmem, ad + 2 * ks, bd + 2 * ks, idesc, acc_flag);
+                        if (nacc == 2) tc_mma_pair(tmem + 256, ad + (kTcABlock >> 4) + 2 * ks, bd + 2 * ks, idesc, acc_flag);
+                    }
+                    tc_commit_pair(empty_a + 8 * s);
+                    tc_commit_pair(empty_b + 8 * s);
+                    if (++s == S) { s = 0; ph ^= 1; }
+                }
+                tc_commit_pair(acc_full);
+                it += kc1 - kc0;
+            }
+            if (seg_i > 0) mbar_wait(acc_full, (uint32_t) ((seg_i - 1) & 1), abort_flag, false);
+        } else if (lane == 0) {
+            // forwarder (rank 1): this CTA's A blocks and B half of stage s are in place
+            const uint32_t remote_pfull = mapa_shared(pfull, 0);
+            uint32_t s = 0, ph = 0;
+            bool ok = true;
+            for (int r = 0; r < 2; ++r)
+            for (long long it = rg.b[r], it_end = rg.e[r]; it < it_end && ok; ++it) {
+                if (!mbar_wait(full_a + 8 * s, ph, abort_flag, true) || !mbar_wait(full_b + 8 * s, ph, abort_flag, true)) {
+                    ok = false;
+                    break;
+                }
+                mbar_arrive_cluster(remote_pfull + 8 * s);
+                if (++s == S) { s = 0; ph ^= 1; }
+            }
+        }
+    } else {
+        // decoders (and the epilogue of their TMEM lane quarter) or epilogue-only warps
+        const int q = warp & 3;
+        const int hq = q == 3 ? warp >> 2 : (warp >> 2) - 1;
+        const bool decoder = q != 1;
+        const int dw = (warp - 3) - (warp - 2) / 4;
+        const uint32_t acc_empty_leader = mapa_shared(acc_empty, 0);
+
+        tc_griddep_wait();
+        const LaneWords lw = lane_words<K>(lane);
+        uint32_t st = 0, pt = 0;
+        int seg_i = 0;
+        bool ok = true;
+        for (int r = 0; r < 2; ++r)
+        for (long long it = rg.b[r], it_end = rg.e[r]; it < it_end && ok; ++seg_i) {
+            const int tile = (int) (it / nkc), kc0 = (int) (it - (long long) tile * nkc);
+            const int kc1 = (int) min((long long) nkc, kc0 + (it_end - it));
+            const int mt = tile % a.mtiles, nt = tile / a.mtiles;
+            if (decoder) {
+                for (int kc = kc0; kc < kc1; ++kc) {
+                    if (!mbar_wait(full_t + 8 * st, pt, abort_flag, true) ||
+                        !mbar_wait(empty_b + 8 * st, pt ^ 1, abort_flag, true)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_decode_stage<K, CB, 8>(sT + st * L::kTChunk, sB + st * L::kBStage, dw, lane, lw);
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(full_b + 8 * st);
+                        mbar_arrive(empty_t + 8 * st);
+                    }
+                    if (++st == S) { st = 0; pt ^= 1; }
+                }
+            }
+            if (!ok || !mbar_wait(acc_full, (uint32_t) (seg_i & 1), abort_flag, true)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int nacc = a.m - mt * 512 > 256 ? 2 : 1;
+            if (hq < 2 * nacc) {
+                const int acc = hq >> 1, cb = hq & 1;
+                const int srow = acc * 128 + q * 32 + lane;  // row of this CTA's accumulators (and slot)
+                const int row = mt * 512 + acc * 256 + (int) rank * 128 + q * 32 + lane;
+                const bool whole = kc0 == 0 && kc1 == nkc;
+                const uint32_t taddr = tmem + ((uint32_t) (q * 32) << 16) + acc * 256 + cb * 128;
+                float* slot_row = nullptr;
+                if (!whole) {
+                    const int slot = 2 * tc_cta_of(a.iters, nkc, npairs, (long long) tile * nkc) + (int) rank;
+                    slot_row = a.slots + (size_t) slot * kTcSlotFloats + (size_t) srow * kTcCols;
+                }
+                if constexpr (MODE == kTcDenseSwiglu) {
+                    uint8_t* img = a.img;
+                    const int nkc2 = a.inter >> 6;
+                    const bool row_ok = row < a.m;
+                    tc_epilogue_swiglu(taddr - cb * 128, cb, 1 + 2 * q + acc, a.svh + nt * 128,
+                                       a.svh + a.inter + nt * 128, a.suh2 + nt * 128, a.swiglu_limit, whole,
+                                       slot_row, row_ok, [&](int col, uint4 v) {
+                                           if (!row_ok) return;
+                                           const int c = nt * 128 + col, rr = row & 127;
+                                           *reinterpret_cast<uint4*>(
+                                               img + ((((size_t) (row >> 7) * nkc2 + (c >> 6)) << 14) + rr * 128 +
+                                                      ((((c & 63) >> 3) ^ (rr & 7)) << 4))) = v;
+                                       });
+                } else {
+                    tc_epilogue_block(a, taddr, row, nt * kTcCols + cb * 128, whole, slot_row ? slot_row + cb * 128 : nullptr);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                if (rank == 0) mbar_arrive(acc_empty);
+                else mbar_arrive_cluster(acc_empty_leader);
+            }
+            it += kc1 - kc0;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // the leader's MMAs into this CTA's TMEM are complete
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc_pair(tmem, 512);
+    }
+}
+
 // Split tiles: the slot of CTA c holds the tile that contains the end of c's
 // stream-K range, when that tile starts inside the range.  One CTA per slot.
+// Slot row sr of CTA c's split tile -> row of the output (or -1 past m).  Single-CTA
+// tiles: 256 rows, slot row = tile row; pair tiles: 512 rows, the slot holds the CTA's
+// two 128-row accumulators (pair rows 256 acc + 128 rank + [0, 128)).
+__device__ __forceinline__ int tc_slot_row(const TcArgs& a, int c, int mt, int sr)
+{
+    const int row = a.pair ? mt * 512 + (sr >> 7) * 256 + (c & 1) * 128 + (sr & 127) : mt * kTcRows + sr;
+    return row < a.m ? row : -1;
+}
+
+// The split tile whose partial sums CTA c's slot holds, or -1.
+__device__ __forceinline__ int tc_slot_tile(const TcArgs& a, int c, int grid)
+{
+    const TcRanges rg = a.pair ? tc_ranges(a.iters, a.nkc, grid >> 1, c >> 1) : tc_ranges(a.iters, a.nkc, grid, c);
+    const long long start = rg.b[1];
+    const long long end = rg.e[1];
+    if (end >= a.iters || end % a.nkc == 0) return -1;
+    const int tile = (int) (end / a.nkc);
+    if ((long long) tile * a.nkc < start) return -1;
+    return tile;
+}
+
 __global__ __launch_bounds__(256) void exl3_tc_finish_kernel(const __grid_constant__ TcArgs a, int grid)
 {
     tc_griddep_wait();
     const int c = blockIdx.x;
-    const TcRanges rg = tc_ranges(a.iters, a.nkc, grid, c);
-    const long long start = rg.b[1];
-    const long long end = rg.e[1];
-    if (end >= a.iters || end % a.nkc == 0) return;
-    const int tile = (int) (end / a.nkc);
-    if ((long long) tile * a.nkc < start) return;
+    const int tile = tc_slot_tile(a, c, grid);
+    if (tile < 0) return;
     const int mt = tile % a.mtiles, nt = tile / a.mtiles;
-    const int rows = min(kTcRows, a.m - mt * kTcRows);
     const int cols = min(kTcCols, a.n - nt * kTcCols);
     float* slot = a.slots + (size_t) c * kTcSlotFloats;
     const int cols8 = cols >> 3;
-    for (int e = threadIdx.x; e < rows * cols8; e += blockDim.x) {
+    for (int e = threadIdx.x; e < kTcRows * cols8; e += blockDim.x) {
         const int r = e / cols8, c8 = (e - r * cols8) * 8;
+        const int row = tc_slot_row(a, c, mt, r);
+        if (row < 0) continue;  // never written: still zero
         float4* src = reinterpret_cast<float4*>(slot + (size_t) r * kTcCols + c8);
         const float4 p0 = __ldcg(src), p1 = __ldcg(src + 1);
         __stcg(src, make_float4(0.f, 0.f, 0.f, 0.f));
         __stcg(src + 1, make_float4(0.f, 0.f, 0.f, 0.f));
         const float v[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-        store8(a, mt * kTcRows + r, nt * kTcCols + c8, v);
+        store8(a, row, nt * kTcCols + c8, v);
     }
 }
 
@@ -1324,18 +1754,15 @@ __global__ __launch_bounds__(256) void exl3_tc_finish_swiglu_kernel(const __grid
 {
     tc_griddep_wait();
     const int c = blockIdx.x;
-    const TcRanges rg = tc_ranges(a.iters, a.nkc, grid, c);
-    const long long start = rg.b[1];
-    const long long end = rg.e[1];
-    if (end >= a.iters || end % a.nkc == 0) return;
-    const int tile = (int) (end / a.nkc);
-    if ((long long) tile * a.nkc < start) return;
+    const int tile = tc_slot_tile(a, c, grid);
+    if (tile < 0) return;
     const int mt = tile % a.mtiles, nt = tile / a.mtiles;
-    const int rows = min(kTcRows, a.m - mt * kTcRows);
     const int lane = threadIdx.x & 31;
     const int nkc2 = a.inter >> 6;
     float* slot = a.slots + (size_t) c * kTcSlotFloats;
-    for (int r = threadIdx.x >> 5; r < rows; r += blockDim.x >> 5) {
+    for (int r = threadIdx.x >> 5; r < kTcRows; r += blockDim.x >> 5) {
+        const int row = tc_slot_row(a, c, mt, r);
+        if (row < 0) continue;  // never written: still zero
         float* sr = slot + (size_t) r * kTcCols;
         float v[4];
 #pragma unroll
@@ -1347,7 +1774,7 @@ __global__ __launch_bounds__(256) void exl3_tc_finish_swiglu_kernel(const __grid
             v[i] = swiglu_pre(g, u, a.swiglu_limit, __half2float(a.suh2[nt * 128 + col]));
         }
         warp_fwht128(v, lane);
-        const int row = mt * kTcRows + r, rr = row & 127;
+        const int rr = row & 127;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int col = nt * 128 + lane + 32 * i;
@@ -1387,6 +1814,57 @@ static cudaError_t tc_launch(const void* kern, int grid, int block, size_t smem,
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     return cudaLaunchKernelExC(&cfg, kern, args);
+}
+
+// The CTA-pair kernel: clusters of 2 CTAs, programmatic dependent launch.
+template <int K, int CB, int MODE>
+static int tc_launch_pair(const TcArgs& a, int grid, cudaStream_t stream)
+{
+    using L = TcPairSmem<K>;
+    static bool configured[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kErrLaunch;
+    if (!configured[dev]) {
+        if (cudaFuncSetAttribute(exl3_tc_pair_kernel<K, CB, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int) L::kLaunchBytes) != cudaSuccess)
+            return kErrLaunch;
+        configured[dev] = true;
+    }
+    TcArgs arg = a;
+    arg.wait_ns = wait_limit_ns(kTcTimeoutNs);
+    void* args[] = {&arg};
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned) grid);
+    cfg.blockDim = dim3((unsigned) kTcThreads);
+    cfg.dynamicSmemBytes = L::kLaunchBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelExC(&cfg, (const void*) exl3_tc_pair_kernel<K, CB, MODE>, args) == cudaSuccess ? kOk
+                                                                                                          : kErrLaunch;
+}
+
+template <int MODE>
+static int tc_launch_pair_k(const TcArgs& a, int K, int cb, int grid, cudaStream_t stream)
+{
+    switch (K * 4 + cb) {
+        case 8: return tc_launch_pair<2, 0, MODE>(a, grid, stream);
+        case 9: return tc_launch_pair<2, 1, MODE>(a, grid, stream);
+        case 10: return tc_launch_pair<2, 2, MODE>(a, grid, stream);
+        case 12: return tc_launch_pair<3, 0, MODE>(a, grid, stream);
+        case 13: return tc_launch_pair<3, 1, MODE>(a, grid, stream);
+        case 14: return tc_launch_pair<3, 2, MODE>(a, grid, stream);
+        case 16: return tc_launch_pair<4, 0, MODE>(a, grid, stream);
+        case 17: return tc_launch_pair<4, 1, MODE>(a, grid, stream);
+        default: return tc_launch_pair<4, 2, MODE>(a, grid, stream);
+    }
 }
 
 template <int K, int CB, int MODE>
@@ -1473,13 +1951,16 @@ size_t tc_state_bytes() { return (size_t) tc_sm_count() * kTcSlotFloats * sizeof
 int tc_dense_run(const TcDenseRun& r, cudaStream_t st)
 {
     const bool swiglu = r.img != nullptr;
-    const int mtiles = (r.m + kTcRows - 1) / kTcRows;
+    // CTA pairs (512-row tiles) from kTcPairMinRows rows, where every 256-column tile is whole
+    const bool pair = r.pair != 0 && r.m >= kTcPairMinRows && (swiglu || r.n % kTcCols == 0) && tc_sm_count() >= 2;
+    const int mtiles = pair ? (r.m + 511) / 512 : (r.m + kTcRows - 1) / kTcRows;
     const int ntiles = swiglu ? r.n / 256 : (r.n + kTcCols - 1) / kTcCols;
     const long long tiles = (long long) mtiles * ntiles;
     if (tiles > 0x7fffffffLL) return kErrBadShape;
     const int nkc = r.k / 64;
     const long long iters = tiles * nkc;
-    const int grid = (int) std::min<long long>(tc_sm_count(), iters);
+    const int grid = pair ? 2 * (int) std::min<long long>(tc_sm_count() / 2, iters)
+                          : (int) std::min<long long>(tc_sm_count(), iters);
 
     if (r.run_input) {
         const int mpad = (r.m + 127) / 128 * 128;
@@ -1511,9 +1992,15 @@ int tc_dense_run(const TcDenseRun& r, cudaStream_t st)
     a.suh2 = r.suh2;
     a.swiglu_limit = r.swiglu_limit;
     a.inter = r.n / 2;
-    const int rc = swiglu ? tc_launch_k<kTcDenseSwiglu>(a, r.K, r.cb, grid, st) : tc_launch_k<kTcDense>(a, r.K, r.cb, grid, st);
+    a.pair = pair ? 1 : 0;
+    int rc;
+    if (pair)
+        rc = swiglu ? tc_launch_pair_k<kTcDenseSwiglu>(a, r.K, r.cb, grid, st)
+                    : tc_launch_pair_k<kTcDense>(a, r.K, r.cb, grid, st);
+    else
+        rc = swiglu ? tc_launch_k<kTcDenseSwiglu>(a, r.K, r.cb, grid, st) : tc_launch_k<kTcDense>(a, r.K, r.cb, grid, st);
     if (rc != kOk) return rc;
-    if (grid > 1) {
+    if (grid > (pair ? 2 : 1)) {
         int g = grid;
         void* args[] = {&a, &g};
         const void* fin = swiglu ? (const void*) exl3_tc_finish_swiglu_kernel : (const void*) exl3_tc_finish_kernel;
@@ -1552,6 +2039,7 @@ extern "C" int exl3b200_gemm(const void* x, long long x_stride, int m, int k, co
     if ((uintptr_t) state & 15) return kErrUnaligned;
     if (scratch_bytes < tc_xt_bytes(m, k) || state_bytes < tc_state_bytes()) return kErrWorkspace;
     TcDenseRun r = {};
+    r.pair = (flags & EXL3B200_FLAG_SINGLE_CTA) ? 0 : -1;
     r.x = x;
     r.x_stride = x_stride;
     r.suh = pre_rotated ? nullptr : reinterpret_cast<const __half*>(suh);

@@ -92,7 +92,11 @@ struct TcDenseRun {
     const __half* suh2;     // swiglu: down projection suh [n / 2]
     float swiglu_limit;
     float* slots;           // tc_state_bytes(), zeroed, left zeroed
+    int pair = -1;          // CTA-pair tiles: -1 from kTcPairMinRows rows, 0 never
 };
+
+// Rows from which a dense launch uses the CTA-pair kernel (512-row tiles).
+constexpr int kTcPairMinRows = 512;
 int tc_dense_run(const TcDenseRun& r, cudaStream_t stream);
 size_t tc_xt_bytes(int m, int k);
 size_t tc_state_bytes();

@@ -5,7 +5,8 @@ Reference: the oracle's fp32 matmul on the dequantised fused gate|up weights, th
 clipped SwiGLU rounded to fp16 where the reference keeps it, then the fp32 matmul on
 the dequantised down weights.  The block carries an fp16 intermediate, so it is held
 to normwise 4e-3 (as the routed MoE).  Row counts cover both kernel families (small-M
-up to 16 rows, tensor cores from 17) and, at 300 rows, tiles split between CTAs.
+up to 16 rows, tensor cores from 17), tiles split between CTAs (300 rows) and the
+CTA-pair tiles of 512 rows (600, 1030 rows).
 """
 
 import numpy as np
@@ -40,7 +41,7 @@ def _ref(x, gu, dn, Kg, cbg, Kd, cbd, limit=0.0):
     return O.gemv_ref(act, *dn, Kd, cbd)
 
 
-@pytest.mark.parametrize("m", [1, 5, 16, 17, 40, 300])
+@pytest.mark.parametrize("m", [1, 5, 16, 17, 40, 300, 600, 1030])
 @pytest.mark.parametrize("Kg,cbg,Kd,cbd", [(3, 0, 4, 1), (4, 0, 4, 0), (2, 2, 3, 2)])
 def test_mlp_parity(cuda_device, m, Kg, cbg, Kd, cbd):
     x, gu, dn = _case(7000 + m + 10 * Kg + cbg, m, 256, 384, Kg, Kd)

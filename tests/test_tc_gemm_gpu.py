@@ -136,3 +136,30 @@ def test_tc_rejects_bad_input(cuda_device):
     assert L.exl3b200_gemm(*args(4, 100, tr.data_ptr(), scr.numel())) == _lib.EBADSHAPE
     assert L.exl3b200_gemm(*args(4, 128, tr.data_ptr() + 4, scr.numel())) == _lib.EUNALIGNED
     assert L.exl3b200_gemm(*args(4, 128, tr.data_ptr(), 16)) == _lib.EWORKSPACE
+
+
+@pytest.mark.parametrize("K,cb", [(2, 2), (3, 0), (4, 1)])
+@pytest.mark.parametrize("m", [512, 700, 1100])
+def test_tc_pair_tiles(cuda_device, K, cb, m):
+    """From 512 rows the tensor-core GEMM runs on CTA pairs (512 x 256 tiles, each CTA
+    decoding half of the B columns): against the oracle, and against the single-CTA
+    kernel.  With 2-6 tiles over 74 pairs nearly every tile is split between pairs
+    (stream-K slots and the finish kernel)."""
+    x, tr, su, sv = _case(3300 + m + 10 * K + cb, m, 512, 512, K)
+    y = _run(cuda_device, x, tr, su, sv, K, cb, out_dtype=torch.float32)
+    assert O.normwise_rel_err(y.cpu().numpy(), O.gemv_ref(x, tr, su, sv, K, cb)) < TOL_F32_ACC
+    y1 = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), K, cb,
+                    out_dtype=torch.float32, path="tc1")
+    assert float((y - y1).abs().max() / y1.abs().max()) < 1e-5  # same sums, other fp32 order
+    assert ops.device_status(cuda_device) == 0
+
+
+def test_tc_pair_long_k(cuda_device):
+    """Pair tiles with whole tiles per pair and a long k (the stream-K part small)."""
+    x, tr, su, sv = _case(3400, 1024, 2048, 2048 + 256, 4)
+    y = _run(cuda_device, x, tr, su, sv, 4, 1, out_dtype=torch.float32)
+    y1 = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), 4, 1,
+                    out_dtype=torch.float32, path="tc1")
+    assert float((y - y1).abs().max() / y1.abs().max()) < 1e-5
+    assert O.normwise_rel_err(y[:64].cpu().numpy(), O.gemv_ref(x[:64], tr, su, sv, 4, 1)) < TOL_F32_ACC
+    assert ops.device_status(cuda_device) == 0
