@@ -1415,17 +1415,18 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
 // both CTAs arrive on the leader's acc_empty.  Every wait is bounded as in the
 // single-CTA kernel.
 // ---------------------------------------------------------------------------
-constexpr int kTpStages = 4;  // activation, B and code ring depth of the pair kernel
+constexpr int kTpStages = 4;   // activation and B ring depth of the pair kernel
+constexpr int kTpStagesT = 8;  // code ring depth of the pair kernel
 
 template <int K>
 struct TcPairSmem {
-    static constexpr int kBars = 2 * kTpStages * 3 + kTpStages + 2;  // a, t, b full/empty; pfull; acc
+    static constexpr int kBars = 4 * kTpStages + 2 * kTpStagesT + kTpStages + 2;  // a, b, t; pfull; acc
     static constexpr uint32_t kBStage = 128 * 64 * 2;                // 16 KB: 128 columns x 64 k
     static constexpr uint32_t kTChunk = 4u * 8u * 32u * K;           // codes of 4 k-tiles x 8 n-tiles
     static constexpr uint32_t kA = 0;
     static constexpr uint32_t kB = kA + kTpStages * 2 * kTcABlock;
     static constexpr uint32_t kT = kB + kTpStages * kBStage;
-    static constexpr uint32_t kBar = kT + kTpStages * kTChunk;
+    static constexpr uint32_t kBar = kT + kTpStagesT * kTChunk;
     static constexpr uint32_t kMisc = kBar + 8 * kBars;
     static constexpr uint32_t kBytes = kMisc + 16;
     static constexpr uint32_t kLaunchBytes = kBytes + 1024;
@@ -1435,7 +1436,7 @@ template <int K, int CB, int MODE>
 __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_pair_kernel(const __grid_constant__ TcArgs a)
 {
     static_assert(MODE == kTcDense || MODE == kTcDenseSwiglu, "pair tiles: dense modes");
-    constexpr int S = kTpStages;
+    constexpr int S = kTpStages, ST = kTpStagesT;
     using L = TcPairSmem<K>;
     static_assert(L::kLaunchBytes <= 232448, "shared memory per CTA");
     extern __shared__ uint8_t tc_smem_raw[];
@@ -1444,8 +1445,8 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_pair_kernel(const __gri
     uint8_t* gbase = tc_smem_raw + (base - raw);
     const uint32_t sA = base + L::kA, sB = base + L::kB, sT = base + L::kT, sBar = base + L::kBar;
     const uint32_t full_a = sBar, empty_a = full_a + 8 * S;
-    const uint32_t full_t = empty_a + 8 * S, empty_t = full_t + 8 * S;
-    const uint32_t full_b = empty_t + 8 * S, empty_b = full_b + 8 * S;
+    const uint32_t full_t = empty_a + 8 * S, empty_t = full_t + 8 * ST;
+    const uint32_t full_b = empty_t + 8 * ST, empty_b = full_b + 8 * S;
     const uint32_t pfull = empty_b + 8 * S;
     const uint32_t acc_full = pfull + 8 * S, acc_empty = acc_full + 8;
     volatile uint32_t* tmem_slot = reinterpret_cast<volatile uint32_t*>(gbase + L::kMisc);
@@ -1462,11 +1463,13 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_pair_kernel(const __gri
         for (int i = 0; i < S; ++i) {
             mbar_init(full_a + 8 * i, 1);
             mbar_init(empty_a + 8 * i, 1);
-            mbar_init(full_t + 8 * i, 1);
-            mbar_init(empty_t + 8 * i, kTcDecWarps);
             mbar_init(full_b + 8 * i, kTcDecWarps);
             mbar_init(empty_b + 8 * i, 1);
             mbar_init(pfull + 8 * i, 1);
+        }
+        for (int i = 0; i < ST; ++i) {
+            mbar_init(full_t + 8 * i, 1);
+            mbar_init(empty_t + 8 * i, kTcDecWarps);
         }
         mbar_init(acc_full, 1);
         mbar_init(acc_empty, 2 * (kTcWarps - 3));  // every decoder and epilogue-only warp of both CTAs
@@ -1547,11 +1550,11 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_pair_kernel(const __gri
                     for (int i = 0; i < 4; ++i) bulk_g2s(dst + i * seg, src + i * row_bytes, seg, full_t + 8 * s);
                     used |= 1u << s;
                     par = (par & ~(1u << s)) | (ph << s);
-                    if (++s == S) { s = 0; ph ^= 1; }
+                    if (++s == ST) { s = 0; ph ^= 1; }
                 }
                 it += kc1 - kc0;
             }
-            for (uint32_t j = 0; j < S; ++j)
+            for (uint32_t j = 0; j < ST; ++j)
                 if (used >> j & 1) mbar_wait(full_t + 8 * j, par >> j & 1, abort_flag, false);
         }
     } else if (warp == 1) {
@@ -1622,7 +1625,7 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_pair_kernel(const __gri
 
         tc_griddep_wait();
         const LaneWords lw = lane_words<K>(lane);
-        uint32_t st = 0, pt = 0;
+        uint32_t st = 0, pt = 0, sb = 0, pb = 0;
         int seg_i = 0;
         bool ok = true;
         for (int r = 0; r < 2; ++r)
@@ -1633,18 +1636,19 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_pair_kernel(const __gri
             if (decoder) {
                 for (int kc = kc0; kc < kc1; ++kc) {
                     if (!mbar_wait(full_t + 8 * st, pt, abort_flag, true) ||
-                        !mbar_wait(empty_b + 8 * st, pt ^ 1, abort_flag, true)) {
+                        !mbar_wait(empty_b + 8 * sb, pb ^ 1, abort_flag, true)) {
                         ok = false;
                         break;
                     }
-                    tc_decode_stage<K, CB, 8>(sT + st * L::kTChunk, sB + st * L::kBStage, dw, lane, lw);
+                    tc_decode_stage<K, CB, 8>(sT + st * L::kTChunk, sB + sb * L::kBStage, dw, lane, lw);
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0) {
-                        mbar_arrive(full_b + 8 * st);
+                        mbar_arrive(full_b + 8 * sb);
                         mbar_arrive(empty_t + 8 * st);
                     }
-                    if (++st == S) { st = 0; pt ^= 1; }
+                    if (++st == ST) { st = 0; pt ^= 1; }
+                    if (++sb == S) { sb = 0; pb ^= 1; }
                 }
             }
             if (!ok || !mbar_wait(acc_full, (uint32_t) (seg_i & 1), abort_flag, true)) {
@@ -1952,7 +1956,8 @@ int tc_dense_run(const TcDenseRun& r, cudaStream_t st)
 {
     const bool swiglu = r.img != nullptr;
     // CTA pairs (512-row tiles) from kTcPairMinRows rows, where every 256-column tile is whole
-    const bool pair = r.pair != 0 && r.m >= kTcPairMinRows && (swiglu || r.n % kTcCols == 0) && tc_sm_count() >= 2;
+    const bool pair = r.pair != 0 && (r.pair > 0 || r.m >= kTcPairMinRows) && (swiglu || r.n % kTcCols == 0) &&
+                      tc_sm_count() >= 2;
     const int mtiles = pair ? (r.m + 511) / 512 : (r.m + kTcRows - 1) / kTcRows;
     const int ntiles = swiglu ? r.n / 256 : (r.n + kTcCols - 1) / kTcCols;
     const long long tiles = (long long) mtiles * ntiles;
@@ -2039,7 +2044,7 @@ extern "C" int exl3b200_gemm(const void* x, long long x_stride, int m, int k, co
     if ((uintptr_t) state & 15) return kErrUnaligned;
     if (scratch_bytes < tc_xt_bytes(m, k) || state_bytes < tc_state_bytes()) return kErrWorkspace;
     TcDenseRun r = {};
-    r.pair = (flags & EXL3B200_FLAG_SINGLE_CTA) ? 0 : -1;
+    r.pair = (flags & EXL3B200_FLAG_SINGLE_CTA) ? 0 : (flags & EXL3B200_FLAG_PAIR_CTA) ? 1 : -1;
     r.x = x;
     r.x_stride = x_stride;
     r.suh = pre_rotated ? nullptr : reinterpret_cast<const __half*>(suh);

@@ -92,7 +92,7 @@ struct TcDenseRun {
     const __half* suh2;     // swiglu: down projection suh [n / 2]
     float swiglu_limit;
     float* slots;           // tc_state_bytes(), zeroed, left zeroed
-    int pair = -1;          // CTA-pair tiles: -1 from kTcPairMinRows rows, 0 never
+    int pair = -1;          // CTA-pair tiles: -1 from kTcPairMinRows rows, 0 never, 1 always
 };
 
 // Rows from which a dense launch uses the CTA-pair kernel (512-row tiles).

@@ -32,6 +32,7 @@ EBADSHAPE, EBADBITS, EBADCODEBOOK, EUNALIGNED, ELAUNCH, EWORKSPACE, ENULL, EBADA
 DTYPE_F16, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
 FLAG_INPUT_ROTATED = 1
 FLAG_SINGLE_CTA = 2
+FLAG_PAIR_CTA = 4
 GEMV_MAX_M = 16
 
 _vp = ctypes.c_void_p

@@ -233,8 +233,8 @@ def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], 
 
     Where the kernel-shape map says so (17 rows and more; or ``path="tc"``), one
     tensor-core GEMM over all rows (512-row CTA-pair tiles from 512 rows; ``path="tc1"``
-    keeps single-CTA tiles); below, the small-M kernel in chunks of at most 16 rows
-    (``path="gemv"``).
+    keeps single-CTA tiles, ``path="tc2"`` takes pair tiles at any row count); below, the
+    small-M kernel in chunks of at most 16 rows (``path="gemv"``).
     Replaces ``exl3_gemm_cuda`` (``csrc/exl3_gemm.cu:9-31``).  ``out`` may be a
     row-strided 2D view (e.g. a column slice of a fused qkv output)."""
     if K is None:
@@ -258,11 +258,13 @@ def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], 
     flags = _lib.FLAG_INPUT_ROTATED if input_rotated else 0
     if variant is not None:
         flags |= (int(variant) & 3) << 8
-    if path not in (None, "tc", "tc1", "gemv"):
-        raise RuntimeError("path must be None, 'tc', 'tc1' or 'gemv'")
+    if path not in (None, "tc", "tc1", "tc2", "gemv"):
+        raise RuntimeError("path must be None, 'tc', 'tc1', 'tc2' or 'gemv'")
     if path == "tc1":  # the tensor-core kernel without CTA-pair tiles
         flags |= _lib.FLAG_SINGLE_CTA
-    use_tc = path in ("tc", "tc1") or (path is None and trellis.data_ptr() % 16 == 0 and _tc_rows(m, x2.size(1), n, K, cb))
+    elif path == "tc2":  # CTA-pair tiles at any row count
+        flags |= _lib.FLAG_PAIR_CTA
+    use_tc = path in ("tc", "tc1", "tc2") or (path is None and trellis.data_ptr() % 16 == 0 and _tc_rows(m, x2.size(1), n, K, cb))
     if use_tc:
         _gemm_into(x2, trellis.contiguous(), suh, svh, K, cb, out2, flags)
     else:

@@ -154,6 +154,19 @@ def test_tc_pair_tiles(cuda_device, K, cb, m):
     assert ops.device_status(cuda_device) == 0
 
 
+@pytest.mark.parametrize("m", [1, 130, 300])
+def test_tc_pair_forced_small(cuda_device, m):
+    """Pair tiles forced below 512 rows: most of a 512-row tile is padding (rows of the
+    second CTA or accumulator past m, image blocks that do not exist)."""
+    x, tr, su, sv = _case(3500 + m, m, 384, 512, 3)
+    y = _run(cuda_device, x, tr, su, sv, 3, 0, out_dtype=torch.float32)
+    y2 = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), 3, 0,
+                    out_dtype=torch.float32, path="tc2")
+    assert float((y - y2).abs().max() / y.abs().max()) < 1e-5
+    assert O.normwise_rel_err(y2.cpu().numpy(), O.gemv_ref(x, tr, su, sv, 3, 0)) < TOL_F32_ACC
+    assert ops.device_status(cuda_device) == 0
+
+
 def test_tc_pair_long_k(cuda_device):
     """Pair tiles with whole tiles per pair and a long k (the stream-K part small)."""
     x, tr, su, sv = _case(3400, 1024, 2048, 2048 + 256, 4)
