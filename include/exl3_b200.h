@@ -52,7 +52,7 @@ extern "C" {
 
 /* flags of the matmul entry points */
 #define EXL3B200_FLAG_INPUT_ROTATED 1 /* x is already H128(x*suh)/sqrt(128) in fp16; suh unused */
-#define EXL3B200_FLAG_SINGLE_CTA 2    /* exl3b200_gemm: no CTA-pair tiles (otherwise used from 512 rows) */
+#define EXL3B200_FLAG_SINGLE_CTA 2    /* exl3b200_gemm: no CTA-pair tiles (otherwise from 2048 rows, k >= 16384) */
 #define EXL3B200_FLAG_PAIR_CTA 4      /* exl3b200_gemm: CTA-pair tiles at any row count (n a multiple of 256) */
 
 /* largest row count of the small-M matmul */

@@ -1955,9 +1955,11 @@ size_t tc_state_bytes() { return (size_t) tc_sm_count() * kTcSlotFloats * sizeof
 int tc_dense_run(const TcDenseRun& r, cudaStream_t st)
 {
     const bool swiglu = r.img != nullptr;
-    // CTA pairs (512-row tiles) from kTcPairMinRows rows, where every 256-column tile is whole
-    const bool pair = r.pair != 0 && (r.pair > 0 || r.m >= kTcPairMinRows) && (swiglu || r.n % kTcCols == 0) &&
-                      tc_sm_count() >= 2;
+    // CTA pairs (512-row tiles) where they measured faster: the SwiGLU gate|up from
+    // kTcPairMinRows rows; plain GEMMs from kTcPairDenseMinRows rows with a long k (every
+    // 256-column tile whole)
+    const bool auto_pair = swiglu ? r.m >= kTcPairMinRows : (r.m >= kTcPairDenseMinRows && r.k >= kTcPairDenseMinK);
+    const bool pair = r.pair != 0 && (r.pair > 0 || auto_pair) && (swiglu || r.n % kTcCols == 0) && tc_sm_count() >= 2;
     const int mtiles = pair ? (r.m + 511) / 512 : (r.m + kTcRows - 1) / kTcRows;
     const int ntiles = swiglu ? r.n / 256 : (r.n + kTcCols - 1) / kTcCols;
     const long long tiles = (long long) mtiles * ntiles;

@@ -95,8 +95,14 @@ struct TcDenseRun {
     int pair = -1;          // CTA-pair tiles: -1 from kTcPairMinRows rows, 0 never, 1 always
 };
 
-// Rows from which a dense launch uses the CTA-pair kernel (512-row tiles).
+// When a dense launch uses the CTA-pair kernel (512-row tiles), from measured crossovers
+// on one B200 (CUDA-graph replays, weights above L2): the fused SwiGLU gate|up (config 2
+// block: 1.891 -> 1.661 ms at 2048 rows, equal at 512) from 512 rows; plain GEMMs only
+// from 2048 rows with k >= 16384 (25600 -> 5120 K=4: 606 -> 570 us; but 8192 -> 28672
+// K=4: 985 -> 1040 us, and 768 rows lose everywhere to half-empty pair tiles).
 constexpr int kTcPairMinRows = 512;
+constexpr int kTcPairDenseMinRows = 2048;
+constexpr int kTcPairDenseMinK = 16384;
 int tc_dense_run(const TcDenseRun& r, cudaStream_t stream);
 size_t tc_xt_bytes(int m, int k);
 size_t tc_state_bytes();

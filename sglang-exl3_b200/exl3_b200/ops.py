@@ -232,9 +232,9 @@ def matmul(x: torch.Tensor, trellis: torch.Tensor, suh: Optional[torch.Tensor], 
     """``y = x @ W`` for any number of rows: ``x [..., k]`` fp16 -> ``[..., n]``.
 
     Where the kernel-shape map says so (17 rows and more; or ``path="tc"``), one
-    tensor-core GEMM over all rows (512-row CTA-pair tiles from 512 rows; ``path="tc1"``
-    keeps single-CTA tiles, ``path="tc2"`` takes pair tiles at any row count); below, the
-    small-M kernel in chunks of at most 16 rows (``path="gemv"``).
+    tensor-core GEMM over all rows (512-row CTA-pair tiles from 2048 rows when k >= 16384;
+    ``path="tc1"`` keeps single-CTA tiles, ``path="tc2"`` takes pair tiles at any row
+    count); below, the small-M kernel in chunks of at most 16 rows (``path="gemv"``).
     Replaces ``exl3_gemm_cuda`` (``csrc/exl3_gemm.cu:9-31``).  ``out`` may be a
     row-strided 2D view (e.g. a column slice of a fused qkv output)."""
     if K is None:

@@ -141,12 +141,13 @@ def test_tc_rejects_bad_input(cuda_device):
 @pytest.mark.parametrize("K,cb", [(2, 2), (3, 0), (4, 1)])
 @pytest.mark.parametrize("m", [512, 700, 1100])
 def test_tc_pair_tiles(cuda_device, K, cb, m):
-    """From 512 rows the tensor-core GEMM runs on CTA pairs (512 x 256 tiles, each CTA
-    decoding half of the B columns): against the oracle, and against the single-CTA
-    kernel.  With 2-6 tiles over 74 pairs nearly every tile is split between pairs
-    (stream-K slots and the finish kernel)."""
+    """The tensor-core GEMM on CTA pairs (512 x 256 tiles, each CTA decoding half of the
+    B columns; forced here, by default from 2048 rows with a long k): against the oracle,
+    and against the single-CTA kernel.  With 2-6 tiles over 74 pairs nearly every tile
+    is split between pairs (stream-K slots and the finish kernel)."""
     x, tr, su, sv = _case(3300 + m + 10 * K + cb, m, 512, 512, K)
-    y = _run(cuda_device, x, tr, su, sv, K, cb, out_dtype=torch.float32)
+    y = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), K, cb,
+                   out_dtype=torch.float32, path="tc2")
     assert O.normwise_rel_err(y.cpu().numpy(), O.gemv_ref(x, tr, su, sv, K, cb)) < TOL_F32_ACC
     y1 = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), K, cb,
                     out_dtype=torch.float32, path="tc1")
@@ -170,7 +171,8 @@ def test_tc_pair_forced_small(cuda_device, m):
 def test_tc_pair_long_k(cuda_device):
     """Pair tiles with whole tiles per pair and a long k (the stream-K part small)."""
     x, tr, su, sv = _case(3400, 1024, 2048, 2048 + 256, 4)
-    y = _run(cuda_device, x, tr, su, sv, 4, 1, out_dtype=torch.float32)
+    y = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), 4, 1,
+                   out_dtype=torch.float32, path="tc2")
     y1 = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), 4, 1,
                     out_dtype=torch.float32, path="tc1")
     assert float((y - y1).abs().max() / y1.abs().max()) < 1e-5
