@@ -847,6 +847,8 @@ def run_verify(args, world, rank, local, device):
                    "experts_touched_per_layer": round(sum(touched) / len(touched), 1), "logits_finite": finite,
                    "moe_path": _moe_path_name(world * R, cfg.topk, cfg.experts // world),
                    "kv_cache": "bf16, random contents for the context",
+                   "attention": ("fused decode sub-layer, 5 rows per sequence (exl3b200_decode_attention_rows)"
+                                 if model.fused else "EXL3 projections + torch RoPE / SDPA glue"),
                    "l2": "no flush needed: expert codes per step >> 126 MB L2"},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                      "traffic": None, "peak_kind": peak_kind,

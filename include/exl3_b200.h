@@ -466,6 +466,24 @@ EXL3B200_API int exl3b200_decode_attention(int batch, int hidden, int q_heads, i
                                            const long long* pos, const float* inv_freq, float* y_out,
                                            long long y_stride, const exl3b200_peers* peers, void* state,
                                            size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream);
+/*
+ * The same attention sub-layer for several rows per sequence (speculative verify:
+ * the last accepted token and the draft tokens): rows r = rows_per_seq * s + j
+ * (rows % rows_per_seq == 0, rows <= 16) are sequence s at position *pos + j.  The
+ * caches hold rows / rows_per_seq sequences; the call appends positions *pos ..
+ * *pos + rows_per_seq - 1 of each, and row j attends to positions 0 .. *pos + j
+ * (causal among the new rows).  rows_per_seq = 1 is exl3b200_decode_attention.
+ * Workspace: exl3b200_decode_attention_workspace(rows, ...).  Replaces the per-token
+ * verify loop around the reference's EXL3 ops (src/sglang_exl3/exl3.py:932-956).
+ */
+EXL3B200_API int exl3b200_decode_attention_rows(int rows, int rows_per_seq, int hidden, int q_heads, int kv_heads,
+                                                int K, int cb, float* h, long long h_stride, const float* ss_in,
+                                                float* ss_out, const void* norm_w, float eps, const exl3b200_linear* q,
+                                                const exl3b200_linear* k, const exl3b200_linear* v,
+                                                const exl3b200_linear* o, void* k_cache, void* v_cache, int max_ctx,
+                                                const long long* pos, const float* inv_freq, float* y_out,
+                                                long long y_stride, const exl3b200_peers* peers, void* state,
+                                                size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream);
 EXL3B200_API int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int cb, float* h, long long h_stride,
                                      const float* ss_in, float* ss_out, const void* norm_w, float eps,
                                      const exl3b200_linear* gate, const exl3b200_linear* up,

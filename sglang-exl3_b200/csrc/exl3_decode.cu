@@ -46,6 +46,7 @@
 // attention and activation kernels around the EXL3 ops); the arithmetic of each
 // step follows the unfused model in exl3_b200/harness.py.
 #include <algorithm>
+#include <climits>
 #include <cstring>
 
 #include <cooperative_groups.h>
@@ -240,12 +241,13 @@ __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __gri
     const int rank = (int) cluster.block_rank();
     const int t = blockIdx.x / csize;
     const int kvh = t % x.kv_heads;
-    const int b = t / x.kv_heads;
-    // pos and the cache rows before it were written before this step's kernels
-    // (graph replays are separated by ordinary launches); only q and the new row at
-    // pos come from the RoPE epilogue this kernel depends on
-    const long long pos = *x.pos;
-    if (pos < 0 || pos >= x.max_ctx) return;  // grid-uniform; recorded in the device status by the RoPE epilogue
+    const int b = t / x.kv_heads;  // row; its sequence b / rows_per_seq, position *pos + b % rows_per_seq
+    // *pos and the cache rows before it were written before this step's kernels
+    // (graph replays are separated by ordinary launches); only q and the new rows at
+    // *pos .. *pos + rows_per_seq - 1 come from the RoPE epilogue this kernel depends on
+    const long long pos0 = *x.pos;
+    const long long pos = pos0 + b % x.rows_per_seq;
+    if (pos0 < 0 || pos >= x.max_ctx) return;  // cluster-uniform; recorded in the device status by the RoPE epilogue
     const int L = (int) pos + 1;
     const int nch = (L + kDecChunk - 1) / kDecChunk;
     const int nloc = rank < nch ? (nch - 1 - rank) / csize + 1 : 0;
@@ -256,38 +258,38 @@ __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __gri
     if (tid < 2 * group && (tid >> 1) % csize == rank && po.suh)  // into L2: the o input scales of this rank's heads
         prefetch_l2_256(po.suh + (size_t) (kvh * group + (tid >> 1)) * 128, tid & 1);
 
-    const size_t hbase = (size_t) b * x.cache_b_stride + (size_t) kvh * x.cache_h_stride;
-    // local chunk i -> buffer; rows >= its length are zero-filled; with skip_new the
-    // row at pos is left out (returned) for a load after the wait
-    auto stage = [&](int i, int buf, bool skip_new) -> int {
+    const size_t hbase = (size_t) (b / x.rows_per_seq) * x.cache_b_stride + (size_t) kvh * x.cache_h_stride;
+    // local chunk i -> buffer; rows >= its length are zero-filled; rows at positions
+    // >= cut (this step's new rows) are left out for a load after the wait
+    auto stage = [&](int i, int buf, long long cut) {
         const int p0 = (rank + i * csize) * kDecChunk;
         const int np = min(kDecChunk, L - p0);
         const __nv_bfloat16* kg = x.k_cache + hbase + (size_t) p0 * kHeadDim;
         const __nv_bfloat16* vg = x.v_cache + hbase + (size_t) p0 * kHeadDim;
-        const int new_row = (skip_new && p0 + np - 1 == (int) pos) ? np - 1 : kDecChunk;
         for (int e = tid; e < kDecChunk * 16; e += kAttnThreads) {
             const int row = e >> 4, seg = (e & 15) * 8;
-            if (row == new_row) continue;
             const bool ok = row < np;
+            if (ok && p0 + row >= cut) continue;
             const size_t off = ok ? (size_t) row * kHeadDim + seg : 0;
             cp_async16_zfill(&sm.kv[buf][0][row][seg], kg + off, ok ? 16 : 0);
             cp_async16_zfill(&sm.kv[buf][1][row][seg], vg + off, ok ? 16 : 0);
         }
-        return new_row;
     };
-    // first fill of the ring: rows written by earlier steps; the new row (position
-    // pos, in the rank's local chunk jn if it owns the last chunk) after the wait
-    const int jn = (rank < nch && (nch - 1 - rank) % csize == 0) ? (nch - 1 - rank) / csize : -1;
-    int new_row = kDecChunk;
-    for (int i = 0; i < min(nloc, kAttnBufs); ++i) {
-        const int nr = stage(i, i, true);
-        if (i == jn) new_row = nr;
-    }
-    griddep_wait();  // q (scaled) and the new K/V row come from the RoPE epilogue
-    if (new_row < kDecChunk && tid < 16) {
-        const size_t off = hbase + (size_t) pos * kHeadDim + tid * 8;
-        cp_async16_zfill(&sm.kv[jn][0][new_row][tid * 8], x.k_cache + off, 16);
-        cp_async16_zfill(&sm.kv[jn][1][new_row][tid * 8], x.v_cache + off, 16);
+    // first fill of the ring: rows written by earlier steps; the rows of positions
+    // pos0 .. pos (this step's, from the RoPE epilogue) after the wait
+    const int nfirst = min(nloc, kAttnBufs);
+    for (int i = 0; i < nfirst; ++i) stage(i, i, pos0);
+    griddep_wait();  // q (scaled) and the new K/V rows come from the RoPE epilogue
+    for (int i = 0; i < nfirst; ++i) {
+        const int p0 = (rank + i * csize) * kDecChunk;
+        const int np = min(kDecChunk, L - p0);
+        const int from = (int) max(0ll, pos0 - p0);
+        for (int e = tid; e < (np - from) * 16; e += kAttnThreads) {
+            const int row = from + (e >> 4), seg = (e & 15) * 8;
+            const size_t off = hbase + (size_t) (p0 + row) * kHeadDim + seg;
+            cp_async16_zfill(&sm.kv[i][0][row][seg], x.k_cache + off, 16);
+            cp_async16_zfill(&sm.kv[i][1][row][seg], x.v_cache + off, 16);
+        }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
 
@@ -328,7 +330,7 @@ __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __gri
         else asm volatile("cp.async.wait_group 1;" ::: "memory");
         __syncthreads();  // ... for every thread; and every warp is done with chunk i - 1
         if (i >= 1) {
-            if (i + kAttnBufs - 1 < nloc) stage(i + kAttnBufs - 1, (i - 1) % kAttnBufs, false);  // new row included
+            if (i + kAttnBufs - 1 < nloc) stage(i + kAttnBufs - 1, (i - 1) % kAttnBufs, LLONG_MAX);  // new rows included
             asm volatile("cp.async.commit_group;" ::: "memory");  // one group per iteration, maybe empty
         }
         const int np = min(kDecChunk, L - (rank + i * csize) * kDecChunk);
@@ -936,14 +938,15 @@ extern "C" int exl3b200_decode_mlp_workspace(int batch, int hidden, int inter, s
     return kOk;
 }
 
-extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int kv_heads, int K, int cb, float* h,
-                                         long long h_stride, const float* ss_in, float* ss_out, const void* norm_w,
-                                         float eps, const exl3b200_linear* q, const exl3b200_linear* k,
-                                         const exl3b200_linear* v, const exl3b200_linear* o, void* k_cache,
-                                         void* v_cache, int max_ctx, const long long* pos, const float* inv_freq,
-                                         float* y_out, long long y_stride, const exl3b200_peers* peers, void* state,
-                                         size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream)
+// batch rows; rows r = R s + j of sequence s (cache slot s) at position *pos + j.
+static int dec_attention(int batch, int rows_per_seq, int hidden, int q_heads, int kv_heads, int K, int cb, float* h,
+                         long long h_stride, const float* ss_in, float* ss_out, const void* norm_w, float eps,
+                         const exl3b200_linear* q, const exl3b200_linear* k, const exl3b200_linear* v,
+                         const exl3b200_linear* o, void* k_cache, void* v_cache, int max_ctx, const long long* pos,
+                         const float* inv_freq, float* y_out, long long y_stride, const exl3b200_peers* peers,
+                         void* state, size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream)
 {
+    if (rows_per_seq < 1 || batch % rows_per_seq) return kErrBadShape;
     int rc = dec_common_checks(batch, hidden, K, cb, h, h_stride, ss_in, ss_out, norm_w, state, scratch);
     if (rc != kOk) return rc;
     rc = dec_peers_check(peers, batch, hidden);
@@ -984,6 +987,7 @@ extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int
     x.max_ctx = max_ctx;
     x.q_heads = q_heads;
     x.kv_heads = kv_heads;
+    x.rows_per_seq = rows_per_seq;
 
     // 1-3: norm input stage, q/k/v matmul, RoPE + KV append epilogue
     GvArgs a = {};
@@ -1015,6 +1019,33 @@ extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int
     rc = gv_launch_matmul(b, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
     return dec_finish(b, x, cb, h, h_stride, ss_out, y_out, y_stride, peers, batch, hidden, st);
+}
+
+extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int kv_heads, int K, int cb, float* h,
+                                         long long h_stride, const float* ss_in, float* ss_out, const void* norm_w,
+                                         float eps, const exl3b200_linear* q, const exl3b200_linear* k,
+                                         const exl3b200_linear* v, const exl3b200_linear* o, void* k_cache,
+                                         void* v_cache, int max_ctx, const long long* pos, const float* inv_freq,
+                                         float* y_out, long long y_stride, const exl3b200_peers* peers, void* state,
+                                         size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream)
+{
+    return dec_attention(batch, 1, hidden, q_heads, kv_heads, K, cb, h, h_stride, ss_in, ss_out, norm_w, eps, q, k,
+                         v, o, k_cache, v_cache, max_ctx, pos, inv_freq, y_out, y_stride, peers, state, state_bytes,
+                         scratch, scratch_bytes, stream);
+}
+
+extern "C" int exl3b200_decode_attention_rows(int rows, int rows_per_seq, int hidden, int q_heads, int kv_heads,
+                                              int K, int cb, float* h, long long h_stride, const float* ss_in,
+                                              float* ss_out, const void* norm_w, float eps, const exl3b200_linear* q,
+                                              const exl3b200_linear* k, const exl3b200_linear* v,
+                                              const exl3b200_linear* o, void* k_cache, void* v_cache, int max_ctx,
+                                              const long long* pos, const float* inv_freq, float* y_out,
+                                              long long y_stride, const exl3b200_peers* peers, void* state,
+                                              size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream)
+{
+    return dec_attention(rows, rows_per_seq, hidden, q_heads, kv_heads, K, cb, h, h_stride, ss_in, ss_out, norm_w,
+                         eps, q, k, v, o, k_cache, v_cache, max_ctx, pos, inv_freq, y_out, y_stride, peers, state,
+                         state_bytes, scratch, scratch_bytes, stream);
 }
 
 extern "C" int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int cb, float* h, long long h_stride,

@@ -54,6 +54,7 @@ struct DecAux {
     __nv_bfloat16* v_cache;
     long long cache_b_stride, cache_h_stride;
     int max_ctx, q_heads, kv_heads;
+    int rows_per_seq;        // rows r = R s + j (j < R) are sequence s at position *pos + j
     // residual epilogue
     float* resid;
     long long resid_stride;
@@ -119,7 +120,7 @@ __device__ __forceinline__ EpiPre epi_preload(const GvProblem& p, const DecAux& 
 #pragma unroll
         for (int e = 0; e < 4; ++e) pre[e] = hr[lane + 32 * e];
     } else if (mode == kEpiRopeKV) {
-        pos = *x.pos;
+        pos = *x.pos + r % x.rows_per_seq;
         if (pi < 2) {
             const float fpos = (float) pos;
             sincosf(fpos * x.inv_freq[lane], &pre[0], &pre[1]);
@@ -200,7 +201,7 @@ __device__ __forceinline__ void epi_apply(const GvArgs& a, const DecAux& x, int 
 #pragma unroll
             for (int e = 0; e < 4; ++e) q[lane + 32 * e] = v[e] * kHadScale;  // 1/sqrt(head_dim), head_dim = 128
         } else {
-            __nv_bfloat16* c = (pi == 1 ? x.k_cache : x.v_cache) + (size_t) r * x.cache_b_stride +
+            __nv_bfloat16* c = (pi == 1 ? x.k_cache : x.v_cache) + (size_t) (r / x.rows_per_seq) * x.cache_b_stride +
                                (size_t) nb * x.cache_h_stride + (size_t) pos * kHeadDim;
 #pragma unroll
             for (int e = 0; e < 4; ++e) c[lane + 32 * e] = __float2bfloat16_rn(v[e]);

@@ -114,6 +114,8 @@ SIGNATURES = {
     "exl3b200_decode_mlp_workspace": (_i, [_i, _i, _i, _vp, _vp]),
     "exl3b200_decode_attention": (_i, [_i, _i, _i, _i, _i, _i, _vp, _ll, _vp, _vp, _vp, _f, _vp, _vp, _vp, _vp,
                                        _vp, _vp, _i, _vp, _vp, _vp, _ll, _vp, _vp, _sz, _vp, _sz, _vp]),
+    "exl3b200_decode_attention_rows": (_i, [_i, _i, _i, _i, _i, _i, _i, _vp, _ll, _vp, _vp, _vp, _f, _vp, _vp, _vp,
+                                            _vp, _vp, _vp, _i, _vp, _vp, _vp, _ll, _vp, _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_decode_mlp": (_i, [_i, _i, _i, _i, _i, _vp, _ll, _vp, _vp, _vp, _f, _vp, _vp, _vp, _f, _vp, _ll, _vp,
                                  _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_peer_buffer_size": (_sz, [_i, _i]),

@@ -52,14 +52,19 @@ def _peers_arg(peers):
 def decode_attention(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor, norm_w: torch.Tensor, eps: float,
                      qkv: Sequence, o: Sequence, K: int, cb: int, k_cache: torch.Tensor, v_cache: torch.Tensor,
                      pos: torch.Tensor, inv_freq: torch.Tensor, y: Optional[torch.Tensor] = None,
-                     peers=None) -> None:
-    """Attention sub-layer for one new token per row of ``h``.  ``qkv`` = three
-    (trellis, suh, svh) linears, ``o`` one; caches bf16 [batch, kv_heads, max_ctx, 128]."""
+                     peers=None, rows_per_seq: int = 1) -> None:
+    """Attention sub-layer.  ``rows_per_seq = 1``: one new token per row of ``h``, each
+    row a sequence; ``rows_per_seq = R`` (speculative verify): rows ``R s + j`` are
+    sequence ``s`` at position ``pos + j``, causal among themselves.  ``qkv`` = three
+    (trellis, suh, svh) linears, ``o`` one; caches bf16 [sequences, kv_heads, max_ctx, 128]."""
     _check_state(h, ss_in, ss_out, norm_w)
     B, H = h.shape
+    R = int(rows_per_seq)
+    if R < 1 or B % R:
+        raise RuntimeError("rows must be a multiple of rows_per_seq")
     if k_cache.dtype != torch.bfloat16 or k_cache.dim() != 4 or k_cache.size(-1) != 128 or not k_cache.is_contiguous():
-        raise RuntimeError("caches must be contiguous bf16 [batch, kv_heads, max_ctx, 128]")
-    if v_cache.shape != k_cache.shape or not v_cache.is_contiguous() or k_cache.size(0) != B:
+        raise RuntimeError("caches must be contiguous bf16 [sequences, kv_heads, max_ctx, 128]")
+    if v_cache.shape != k_cache.shape or not v_cache.is_contiguous() or k_cache.size(0) != B // R:
         raise RuntimeError("k and v caches must match and have one row per sequence")
     if pos.dtype != torch.int64 or inv_freq.dtype != torch.float32 or inv_freq.numel() != 64:
         raise RuntimeError("pos must be int64 and inv_freq fp32 [64]")
@@ -74,8 +79,8 @@ def decode_attention(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor,
     lo = linear_desc(*o)
     with torch.cuda.device(dev):
         state, scratch = _ws(dev, st_n.value, sc_n.value)
-        rc = L.exl3b200_decode_attention(
-            B, H, q_heads, kv_heads, int(K), int(cb), h.data_ptr(), h.stride(0), ss_in.data_ptr(), ss_out.data_ptr(),
+        rc = L.exl3b200_decode_attention_rows(
+            B, R, H, q_heads, kv_heads, int(K), int(cb), h.data_ptr(), h.stride(0), ss_in.data_ptr(), ss_out.data_ptr(),
             norm_w.data_ptr(), float(eps), ctypes.byref(lq), ctypes.byref(lk), ctypes.byref(lv), ctypes.byref(lo),
             k_cache.data_ptr(), v_cache.data_ptr(), max_ctx, pos.data_ptr(), inv_freq.data_ptr(),
             y.data_ptr() if y is not None else None, y.stride(0) if y is not None else 0, _peers_arg(peers),

@@ -10,6 +10,12 @@ ctx .. ctx+4 (each row attends to the cache and to the new rows before it), and
 returns the logits of all rows; the caller compares them with the draft.  The
 step is captured in one CUDA graph.
 
+Up to 16 rows (batch <= 3) the attention sub-layer is the fused decode sub-layer
+(``decode.decode_attention`` with ``rows_per_seq = 5``: RMSNorm, q/k/v, RoPE and the
+append of the 5 new positions, cluster attention causal among the new rows, o and the
+residual, in 6 PDL-chained kernels on an fp32 residual stream); the MoE sub-layer
+reads the row sums of squares it leaves.  Otherwise (and with ``fused=False``):
+
 Per layer: RMSNorm -> q/k/v (one grouped EXL3 launch for 5*batch rows) -> RoPE ->
 KV append -> attention (``scaled_dot_product_attention`` over the bf16 cache with
 an explicit causal mask; the query heads of a KV head folded into the query
@@ -32,6 +38,7 @@ from typing import Optional
 import torch
 import torch.nn.functional as F
 
+from . import decode as _dec
 from . import moe as _moe
 from . import ops
 from .ep import ExpertParallelMoE
@@ -62,7 +69,7 @@ CONFIG5 = VerifyConfig()
 
 class VerifyModel:
     def __init__(self, cfg: VerifyConfig, batch: int, max_ctx: int, device: torch.device, world: int = 1,
-                 rank: int = 0, group=None, seed: int = 4):
+                 rank: int = 0, group=None, seed: int = 4, fused: Optional[bool] = None):
         if cfg.experts % world:
             raise ValueError(f"{cfg.experts} experts do not split over {world} ranks")
         self.cfg, self.batch, self.max_ctx, self.device = cfg, batch, max_ctx, device
@@ -70,6 +77,10 @@ class VerifyModel:
         H, hd, K = cfg.hidden, cfg.head_dim, cfg.K_attn
         qd, kvd = cfg.heads * hd, cfg.kv_heads * hd
         self.rows = batch * cfg.rows_per_seq
+        fusable = self.rows <= 16 and cfg.head_dim == 128 and cfg.heads // cfg.kv_heads <= 16
+        if fused and not fusable:
+            raise ValueError("the fused attention sub-layer takes up to 16 rows and head_dim 128")
+        self.fused = fusable if fused is None else bool(fused)
         gen = torch.Generator(device=device)
         gen.manual_seed(seed)  # dense parts are the same on every rank
         egen = torch.Generator(device=device)
@@ -125,6 +136,8 @@ class VerifyModel:
         self.tokens = torch.zeros((batch, cfg.rows_per_seq), dtype=torch.long, device=device)
         self.pos = torch.zeros((), dtype=torch.long, device=device)  # first new position (= cached tokens)
         self.logits: Optional[torch.Tensor] = None
+        self.h = torch.empty((self.rows, H), dtype=torch.float32, device=device)  # fused: residual stream
+        self.ss = torch.zeros((2, self.rows), dtype=torch.float32, device=device)  # fused: row sums of h^2
         self.qkv = torch.empty((self.rows, qd + 2 * kvd), dtype=torch.float16, device=device)
         self.o = torch.empty((self.rows, H), dtype=torch.float16, device=device)
         self.ep = ExpertParallelMoE(cfg.experts, world, rank, group) if world > 1 else None
@@ -160,8 +173,37 @@ class VerifyModel:
         return _moe.moe_forward(x16, ids, w, L["tables"], cfg.K_expert, cfg.K_expert, cfg.K_expert, cfg.cb,
                                 cfg.inter)
 
+    def _moe_sublayer(self, li, L, xn: torch.Tensor) -> torch.Tensor:
+        cfg = self.cfg
+        logits = xn.float() @ L["router"].t() + self.route_noise[li]
+        w, ids = torch.topk(torch.softmax(logits, dim=-1), cfg.topk, dim=-1)
+        w = w / w.sum(-1, keepdim=True)
+        if self.record is not None:
+            self.record.append(int(torch.unique(ids).numel()))
+        if self.ep is None:
+            return self._local_moe(L, xn, ids.to(torch.int32), w)
+        return self.ep(xn, ids, w, lambda xr, lids, lw, L=L: self._local_moe(L, xr, lids, lw))
+
+    def _step_fused(self) -> torch.Tensor:
+        cfg = self.cfg
+        h, ss = self.h, self.ss
+        h.copy_(self.embed[self.tokens.reshape(-1)].float())
+        torch.sum(h * h, dim=-1, out=ss[0])
+        for li, L in enumerate(self.layers):
+            _dec.decode_attention(h, ss[0], ss[1], L["ln1"], cfg.eps, L["qkv"], L["o"], cfg.K_attn, cfg.cb,
+                                  self.k_cache[li], self.v_cache[li], self.pos, self.inv_freq,
+                                  rows_per_seq=cfg.rows_per_seq)
+            # RMSNorm from the row sums of squares the attention sub-layer accumulated
+            xn = (h * torch.rsqrt(ss[1, :, None] / cfg.hidden + cfg.eps) * L["ln2"].float()).to(torch.float16)
+            h.add_(self._moe_sublayer(li, L, xn))
+            torch.sum(h * h, dim=-1, out=ss[0])
+        xf = self._rms(h, self.ln_f).to(torch.bfloat16)
+        return (xf @ self.lm_head.t()).float()
+
     def step(self) -> torch.Tensor:
         """One verify step over the rows in ``self.tokens``; logits [batch*5, vocab] fp32."""
+        if self.fused:
+            return self._step_fused()
         cfg = self.cfg
         B, S, R = self.batch, cfg.rows_per_seq, self.rows
         hd, nh, nkv = cfg.head_dim, cfg.heads, cfg.kv_heads
@@ -195,16 +237,7 @@ class VerifyModel:
             ops.matmul(att, *L["o"], cfg.K_attn, cfg.cb, out=self.o)
             h = h + self.o.float()
             xn = self._rms(h, L["ln2"])
-            logits = xn.float() @ L["router"].t() + self.route_noise[li]
-            w, ids = torch.topk(torch.softmax(logits, dim=-1), cfg.topk, dim=-1)
-            w = w / w.sum(-1, keepdim=True)
-            if self.record is not None:
-                self.record.append(int(torch.unique(ids).numel()))
-            if self.ep is None:
-                y = self._local_moe(L, xn, ids.to(torch.int32), w)
-            else:
-                y = self.ep(xn, ids, w, lambda xr, lids, lw, L=L: self._local_moe(L, xr, lids, lw))
-            h = h + y
+            h = h + self._moe_sublayer(li, L, xn)
         xf = self._rms(h, self.ln_f).to(torch.bfloat16)
         return (xf @ self.lm_head.t()).float()
 

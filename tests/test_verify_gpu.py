@@ -109,13 +109,16 @@ def _torch_verify_step(m):
 TOL_LOGITS = 1e-2
 
 
-@pytest.mark.parametrize("batch", [1, 7])
-def test_verify_step_matches_fp32_torch(cuda_device, batch):
+# batch 1 and 3 (5 and 15 rows) run the fused attention sub-layer (rows_per_seq = 5),
+# batch 7 and the fused=False case the unfused torch-glue path
+@pytest.mark.parametrize("batch,fused", [(1, None), (3, None), (1, False), (7, None)])
+def test_verify_step_matches_fp32_torch(cuda_device, batch, fused):
     torch.backends.cuda.matmul.allow_tf32 = False
     cfg = dataclasses.replace(CONFIG5, layers=2, hidden=1024, heads=8, kv_heads=2, experts=16, inter=512,
                               vocab=2048)
     ctx = 64
-    m = VerifyModel(cfg, batch, ctx + cfg.rows_per_seq, cuda_device)
+    m = VerifyModel(cfg, batch, ctx + cfg.rows_per_seq, cuda_device, fused=fused)
+    assert m.fused == (batch * cfg.rows_per_seq <= 16 and fused is None)
     m.fill_random_kv(ctx)
     m.tokens.random_(0, cfg.vocab, generator=torch.Generator(device=cuda_device).manual_seed(2))
     ref, tie = _torch_verify_step(m)
@@ -128,3 +131,48 @@ def test_verify_step_matches_fp32_torch(cuda_device, batch):
     print(f"verify step vs fp32 torch: {err:.2e} over {int(keep.sum())} of {m.rows} rows")
     assert err < TOL_LOGITS
     m.close()
+
+
+# appended cache entries: bf16 of the same fp32 projections, within two bf16 ulps
+TOL_KV = 2e-2
+
+
+@pytest.mark.parametrize("batch,ctx", [(2, 64), (3, 61)])  # 61: the 5 new positions straddle a 64-position chunk
+def test_verify_fused_attention_matches_unfused(cuda_device, batch, ctx):
+    """The fused path (decode attention with 5 rows per sequence at positions
+    ctx..ctx+4, causal among them) against the unfused torch-glue step on the same
+    model: appended K/V, the step's logits, and a CUDA graph of the fused step."""
+    cfg = dataclasses.replace(CONFIG5, layers=2, hidden=1024, heads=8, kv_heads=2, experts=16, inter=512,
+                              vocab=2048)
+    models = [VerifyModel(cfg, batch, ctx + 8, cuda_device, fused=f) for f in (True, False)]
+    gen = torch.Generator(device=cuda_device).manual_seed(3)
+    toks = torch.randint(0, cfg.vocab, (batch, cfg.rows_per_seq), device=cuda_device, generator=gen)
+    outs = []
+    for m in models:
+        m.fill_random_kv(ctx)
+        m.tokens.copy_(toks)
+        with torch.cuda.stream(m.stream):
+            outs.append(m.step().clone())
+    torch.cuda.synchronize()
+    fz, uf = models
+    new = slice(ctx, ctx + cfg.rows_per_seq)
+    for c in ("k_cache", "v_cache"):  # layer 0: the same inputs on both paths
+        a, b = getattr(fz, c)[0, :, :, new].float(), getattr(uf, c)[0, :, :, new].float()
+        assert a.abs().sum() > 0
+        assert _rel(a, b) < TOL_KV, c
+    assert torch.equal(fz.k_cache[:, :, :, :ctx], uf.k_cache[:, :, :, :ctx])  # older positions untouched
+    # per row: a row whose top-k routing is within rounding of a tie may pick another
+    # expert on one path; at most one such row is allowed
+    row_err = (outs[0] - outs[1]).norm(dim=-1) / outs[1].norm(dim=-1)
+    print(f"fused vs unfused verify logits per row: {row_err.tolist()}")
+    assert int((row_err >= TOL_LOGITS).sum()) <= 1
+    with torch.cuda.stream(fz.stream):
+        again = fz.step().clone()
+    fz.capture()
+    fz.replay()
+    torch.cuda.synchronize()
+    noise, err = _rel(again, outs[0]), _rel(fz.logits, outs[0])
+    print(f"fused eager vs eager {noise:.2e}, graph vs eager {err:.2e}")
+    assert err < max(1e-3, 10 * noise)  # routed-MoE fp32 atomics may add in another order
+    for m in models:
+        m.close()
