@@ -677,8 +677,7 @@ def run_moe(args, world, rank, local, device):
               "down_trellis": ptrs(w2), "down_suh": ptrs(w2_suh), "down_svh": ptrs(w2_svh)}
     shared_gen = torch.Generator(device=device)
     shared_gen.manual_seed(2)  # the shared expert is replicated
-    sh_gate = make_linear(shared_gen, H, I, 4, device)
-    sh_up = make_linear(shared_gen, H, I, 4, device)
+    sh_gate_up = make_linear(shared_gen, H, 2 * I, 4, device)  # merged gate|up, as the dense MLP's
     sh_down = make_linear(shared_gen, I, H, 4, device)
     rgen = torch.Generator(device=device)
     rgen.manual_seed(seed + 1000 * rank)  # every rank holds its own T tokens
@@ -687,8 +686,6 @@ def run_moe(args, world, rank, local, device):
     local_fn = exl3_local_experts(tables, K, K, K, 0, I)
     # expert parallelism: dispatch and combine over NVLink peer memory by the library
     ep = PeerExpertParallelMoE(E, T, topk, H, group=torch.distributed.group.WORLD) if world > 1 else None
-    sh_gu = [torch.empty(T, I, dtype=torch.float16, device=device) for _ in range(2)]
-    sh_act = torch.empty(T, I, dtype=torch.float16, device=device)
     sh_out = torch.empty(T, H, dtype=torch.float16, device=device)
 
     def step():
@@ -699,25 +696,34 @@ def run_moe(args, world, rank, local, device):
             out = local_fn(x, ids.to(torch.int32), w)
         else:
             out = ep(x, ids, w, tables, K, K, K, 0, I)
-        if not c5:  # config 3's shared expert (config 5 has none)
-            ops.matmul_multi(x, [sh_gate, sh_up], 4, 0, outs=sh_gu)
-            torch.mul(torch.nn.functional.silu(sh_gu[0]), sh_gu[1], out=sh_act)
-            ops.matmul(sh_act, *sh_down, 4, 0, out=sh_out)
+        if not c5:  # config 3's shared expert (config 5 has none): the fused SwiGLU MLP block
+            ops.mlp(x, sh_gate_up, sh_down, 4, 0, 4, 0, out=sh_out)
             out += sh_out.float()
         return out
 
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    with ClockSampler(local) as clk:
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
+    # the layer step as one CUDA graph (as a serving step runs it), replayed
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        for _ in range(2):
             step()
-        e1.record()
-        e1.synchronize()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            out_g = step()
+        for _ in range(args.warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        barrier(world)
+        with ClockSampler(local) as clk:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(s)
+            e1.synchronize()
+    torch.cuda.current_stream(device).wait_stream(s)
     ms = max_over_ranks(world, e0.elapsed_time(e1) / args.steps)
     # distinct experts touched by the job's tokens (every rank's) and their code bytes:
     # the HBM roofline of the step; a rank streams its own share of them
@@ -746,6 +752,7 @@ def run_moe(args, world, rank, local, device):
     e2e_ms = max_over_ranks(world, (time.perf_counter() - t0) / n_e2e * 1e3)
     name = (f"config 5 MoE layer, speculative verify of {args.batch} sequences x 5 tokens (T={T})" if c5
             else f"config 3 MoE layer, T={T}")
+    del graph
     if ep is not None:
         ep.close()
     # every rank holds its own T tokens: the job processes world x T tokens per step
@@ -758,19 +765,19 @@ def run_moe(args, world, rank, local, device):
                        "ep_exchange": ("NVLink peer stores: each token row once to every rank owning one of its "
                                        "experts, weighted results back (exl3b200_ep_moe)") if world > 1 else "none",
                        "l2": (f"expert codes {expert_bytes / 1e6:.2f} MB each, {touched * expert_bytes / 1e6:.0f} MB "
-                              "touched per step (> 126 MB L2), no flush; time includes routing (softmax/top-k)"
-                              + ("" if c5 else " and the shared expert"))},
+                              "touched per step (> 126 MB L2), no flush; one CUDA graph per step, time includes "
+                              "routing (softmax/top-k)" + ("" if c5 else " and the shared expert (fused MLP block)"))},
             "exl3_gbs_per_rank": gbs,
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s", "frac": gbs / hbm_peak,
                          "traffic": None, "peak_kind": peak_kind,
                          "kernel": "whole MoE layer per rank (touched experts' codes / step time)"},
             "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tok/s", "ms_per_step": e2e_ms,
                     "h2d_bytes_per_step": px.numel() * 2, "d2h_bytes_per_step": py.numel() * 4},
-            # routed layer: 6 launches (small-M pipeline) or 5 (tensor-core pipeline, equal K);
-            # under EP + plan, dispatch, receive, return, combine; config 3's shared expert:
-            # 3 (gate+up) + 3 (down)
-            "gpu_launches": args.steps * ((5 if M.moe_path(T, topk, el) == "tc" else 6) + (5 if world > 1 else 0)
-                                          + (0 if c5 else 6)),
+            # routed layer: 6 launches (small-M pipeline) or 4 (tensor-core pipeline, SwiGLU in
+            # the gate|up epilogue); under EP + plan, dispatch, receive, return, combine;
+            # config 3's shared expert: the fused MLP block, 5
+            "gpu_launches": args.steps * ((4 if M.moe_path(T, topk, el) == "tc" else 6) + (5 if world > 1 else 0)
+                                          + (0 if c5 else 5)),
             "clocks": clk.summary()}
     return finish(line, args, world)
 

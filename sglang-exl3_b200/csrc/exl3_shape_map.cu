@@ -17,6 +17,10 @@
 // * the 4-tiles-per-warp tiling at 3 CTAs per SM was slower than 8 tiles at 2 CTAs
 //   at every M=1 shape measured (TP8 shards to the full 70B gate/up; K 3 and 4), so
 //   the map never selects it (it stays reachable through the flags for tests).
+// * inside the tcgen05 family the dense launch takes CTA-pair tiles (512 x 256 over a
+//   2-CTA cluster) for the fused SwiGLU gate|up from 512 rows and for plain GEMMs from
+//   2048 rows with k >= 16384 (kTcPairMinRows / kTcPairDenseMinRows / kTcPairDenseMinK,
+//   exl3_tc_internal.h, with the measurements).
 // * routed MoE: the tensor-core pipeline wins from 10-14 average rows per local
 //   expert (config 5 at 7.5 rows: small-M 1.11 vs 1.32 ms; 10 rows: 1.20 vs 1.34;
 //   config 3 at 14 rows: 1.29 vs 1.52; config 5 at 20 rows: 1.37 vs 2.10), hence 12.
