@@ -109,16 +109,16 @@ def _torch_verify_step(m):
 TOL_LOGITS = 1e-2
 
 
-# batch 1 and 3 (5 and 15 rows) run the fused attention sub-layer (rows_per_seq = 5),
-# batch 7 and the fused=False case the unfused torch-glue path
-@pytest.mark.parametrize("batch,fused", [(1, None), (3, None), (1, False), (7, None)])
+# batch 1, 3 and 7 run the fused attention sub-layer (rows_per_seq = 5; batch 7 in three
+# calls of 3, 3 and 1 sequences), batch 9 and the fused=False case the torch-glue path
+@pytest.mark.parametrize("batch,fused", [(1, None), (3, None), (7, None), (1, False), (9, None)])
 def test_verify_step_matches_fp32_torch(cuda_device, batch, fused):
     torch.backends.cuda.matmul.allow_tf32 = False
     cfg = dataclasses.replace(CONFIG5, layers=2, hidden=1024, heads=8, kv_heads=2, experts=16, inter=512,
                               vocab=2048)
     ctx = 64
     m = VerifyModel(cfg, batch, ctx + cfg.rows_per_seq, cuda_device, fused=fused)
-    assert m.fused == (batch * cfg.rows_per_seq <= 16 and fused is None)
+    assert m.fused == (batch <= 8 and fused is None)
     m.fill_random_kv(ctx)
     m.tokens.random_(0, cfg.vocab, generator=torch.Generator(device=cuda_device).manual_seed(2))
     ref, tie = _torch_verify_step(m)
@@ -137,7 +137,8 @@ def test_verify_step_matches_fp32_torch(cuda_device, batch, fused):
 TOL_KV = 2e-2
 
 
-@pytest.mark.parametrize("batch,ctx", [(2, 64), (3, 61)])  # 61: the 5 new positions straddle a 64-position chunk
+# 61: the 5 new positions straddle a 64-position chunk; batch 4: two calls of 3 and 1 sequences
+@pytest.mark.parametrize("batch,ctx", [(2, 64), (3, 61), (4, 64)])
 def test_verify_fused_attention_matches_unfused(cuda_device, batch, ctx):
     """The fused path (decode attention with 5 rows per sequence at positions
     ctx..ctx+4, causal among them) against the unfused torch-glue step on the same
