@@ -72,8 +72,9 @@ EXL3B200_API const char* exl3b200_status_string(int status);
  * reference's select_gemm_shape / exl3_gemm_num_kernel_shapes /
  * exl3_gemm_shape_compat (csrc/quant/exl3_kernel_map.cuh:3-5), whose table of
  * mma.sync tile shapes lives in the unvendored exllamav3.  The B200 table is keyed
- * by rows (per problem, or per expert for routed MoE) and K, from crossovers
- * measured on a B200 (the numbers are in the table's comments).
+ * by rows (per problem, or per expert for routed MoE), K and the matrix size, from
+ * crossovers measured on a B200 (the numbers are in the table's comments).
+ * GV16 above 16 rows means 16-row chunks of the small-M kernel.
  */
 #define EXL3B200_SHAPE_GV8 1       /* small-M, one 8-row group, 8 tiles per warp, 2 CTAs per SM */
 #define EXL3B200_SHAPE_GV8_NARROW 2 /* small-M, one 8-row group, 4 tiles per warp, 3 CTAs per SM */

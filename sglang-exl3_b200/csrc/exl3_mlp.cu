@@ -38,7 +38,8 @@ struct MlpLayout {
 static MlpLayout mlp_layout(int m, int hidden, int inter, int K, int cb)
 {
     MlpLayout L = {};
-    L.tc = exl3b200_select_shape(m, hidden, 2 * inter, K, cb, 0, 0) == EXL3B200_SHAPE_TC;
+    // the small-M path runs one 16-row group: more rows go to the tensor cores
+    L.tc = m > EXL3B200_GEMV_MAX_M || exl3b200_select_shape(m, hidden, 2 * inter, K, cb, 0, 0) == EXL3B200_SHAPE_TC;
     if (L.tc) {
         L.state = tc_state_bytes();
         L.img1 = 0;

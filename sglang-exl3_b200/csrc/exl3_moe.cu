@@ -240,16 +240,16 @@ __global__ __launch_bounds__(kRouteThreads) void exl3_moe_route_kernel(const Moe
         tot[8] = total_probs;     tot[9] = 0; tot[10] = 0; tot[11] = total_rows * (I / 128);
         tot[12] = total_probs;    tot[13] = 0; tot[14] = 0; tot[15] = total_rows * (H / 128);
     }
-    if (!t.accumulate) {
-        for (int i = tid; i < t.tokens * H; i += kRouteThreads) {
-            const int r = i / H, col = i - r * H;
-            t.out[(size_t) r * t.out_stride + col] = 0.f;
-        }
-    }
 }
 
 static int launch_route(const MoeTables& t, const MoeLayout& L, cudaStream_t stream)
 {
+    // the combine epilogue adds into out: zero it over the whole GPU first (a 2D memset,
+    // not the single routing CTA)
+    if (!t.accumulate &&
+        cudaMemset2DAsync(t.out, (size_t) t.out_stride * sizeof(float), 0, (size_t) t.hidden * sizeof(float),
+                          (size_t) t.tokens, stream) != cudaSuccess)
+        return kErrLaunch;
     exl3_moe_route_kernel<<<1, kRouteThreads, 0, stream>>>(t, L);
     return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }

@@ -13,7 +13,11 @@
 //   8192x28672, 5120x25600, 25600x5120, 2048x1024, 8192x1024; K 2, 3, 4; e.g.
 //   8192x28672 K=4: 94.9 us vs 117.5 us); 24 rows - the tensor-core kernel wins
 //   everywhere (153.8 us vs 121.2 us), and from there on the gap widens (96 rows:
-//   565.5 vs 152.3 us).  So the tensor-core kernel takes 17 rows and more.
+//   565.5 vs 152.3 us).  So the tensor-core kernel takes 17 rows and more - for large
+//   matrices.  Up to 2^24 weights (2048x2048, 1024x2048, 4096x1536 K=3, 8192x1024,
+//   2048x8192; us per launch, 16-row chunks / tensor cores, later kernels) two chunks
+//   still win at 32 rows (e.g. 8192x1024 K=4: 21.5 / 23.3; 4096x1536 K=3: 22.4 / 27.3)
+//   and lose from 48 (32.6 / 24.2; 33.4 / 28.1): the tensor cores from 33 rows there.
 // * the 4-tiles-per-warp tiling at 3 CTAs per SM was slower than 8 tiles at 2 CTAs
 //   at every M=1 shape measured (TP8 shards to the full 70B gate/up; K 3 and 4), so
 //   the map never selects it (it stays reachable through the flags for tests).
@@ -30,16 +34,21 @@ namespace exl3b200 {
 
 struct ShapeRule {
     int K;
-    int gv8_max_rows;   // small-M with one 8-row group up to here, then two 8-row groups
-    int tc_min_rows;    // tensor-core kernel from here (below: 16-row small-M chunks)
-    int moe_tc_rows;    // routed MoE: tensor-core pipeline from this many rows per expert
+    int gv8_max_rows;       // small-M with one 8-row group up to here, then two 8-row groups
+    int tc_min_rows;        // tensor-core kernel from here (below: 16-row small-M chunks)
+    int tc_min_rows_small;  // the same for matrices of at most kSmallWeights weights
+    int moe_tc_rows;        // routed MoE: tensor-core pipeline from this many rows per expert
 };
 
 constexpr ShapeRule kShapeRules[] = {
-    {2, 8, 17, 12},
-    {3, 8, 17, 12},
-    {4, 8, 17, 12},
+    {2, 8, 17, 33, 12},
+    {3, 8, 17, 33, 12},
+    {4, 8, 17, 33, 12},
 };
+
+// Below this many weights (k x n) a tensor-core launch has few 256 x 256 tiles and two
+// 16-row small-M chunks stay faster up to 32 rows.
+constexpr long long kSmallWeights = 1ll << 24;
 
 constexpr exl3b200_shape_desc kShapes[] = {
     {"none", 0, 0, 0, 0},
@@ -75,8 +84,6 @@ extern "C" int exl3b200_shape_compat(int shape, int m, int k, int n, int K)
 
 extern "C" int exl3b200_select_shape(int m, int k, int n, int K, int cb, int experts, int topk)
 {
-    (void) k;
-    (void) n;
     if (cb < 0 || cb > 2 || m < 1) return 0;
     const ShapeRule* r = rule_for(K);
     if (!r) return 0;
@@ -85,7 +92,8 @@ extern "C" int exl3b200_select_shape(int m, int k, int n, int K, int cb, int exp
         return pairs >= (long long) r->moe_tc_rows * experts ? EXL3B200_SHAPE_MOE_TC : EXL3B200_SHAPE_MOE_SMALL;
     }
     if (m <= r->gv8_max_rows) return EXL3B200_SHAPE_GV8;
-    if (m < r->tc_min_rows) return EXL3B200_SHAPE_GV16;
+    const bool small = (long long) k * n <= kSmallWeights;
+    if (m < (small ? r->tc_min_rows_small : r->tc_min_rows)) return EXL3B200_SHAPE_GV16;
     return EXL3B200_SHAPE_TC;
 }
 

@@ -1,7 +1,8 @@
 """The kernel-shape map (exl3b200_select_shape; CPU: no kernel runs).  Pins the
 selections to the crossovers measured on a B200: small-M with one 8-row group up to 8
-rows, two groups up to 16, the tensor-core kernel from 17 rows (for every K and the
-config shapes); routed MoE on the tensor-core pipeline from 12 rows per expert."""
+rows, two groups up to 16, the tensor-core kernel from 17 rows (from 33 for matrices of
+at most 2^24 weights; for every K); routed MoE on the tensor-core pipeline from 12 rows
+per expert."""
 
 import ctypes
 
@@ -13,13 +14,17 @@ SHAPES_C4 = [(8192, 8192), (8192, 1024), (8192, 28672), (28672, 8192), (8192, 35
 SHAPES_C2 = [(5120, 51200), (25600, 5120)]
 
 
+SHAPES_SMALL = [(2048, 2048), (1024, 2048), (4096, 1536), (2048, 8192)]  # config 3/5 experts, shared expert
+
+
 @pytest.mark.parametrize("K", [2, 3, 4])
-@pytest.mark.parametrize("k,n", SHAPES_C4 + SHAPES_C2)
+@pytest.mark.parametrize("k,n", SHAPES_C4 + SHAPES_C2 + SHAPES_SMALL)
 def test_dense_selection(K, k, n):
     sel = [ops.select_shape(m, k, n, K, 0) for m in range(1, 65)]
+    tc_from = 33 if k * n <= 1 << 24 else 17  # matrices of at most 2^24 weights: two 16-row chunks to 32 rows
     assert sel[:8] == [_lib.SHAPE_GV8] * 8
-    assert sel[8:16] == [_lib.SHAPE_GV16] * 8
-    assert sel[16:] == [_lib.SHAPE_TC] * 48
+    assert sel[8:tc_from - 1] == [_lib.SHAPE_GV16] * (tc_from - 9)
+    assert sel[tc_from - 1:] == [_lib.SHAPE_TC] * (65 - tc_from)
     assert ops.select_shape(2048, k, n, K, 1) == _lib.SHAPE_TC
 
 
