@@ -24,8 +24,9 @@ length, so the cache is read once per KV head) -> o (EXL3) -> residual -> RMSNor
 -> router (fp32, plus a fixed N(0, 1) term per row, below) ->
 softmax, top-8, renormalised -> routed MoE (``moe.moe_forward``: the small-M or
 the tensor-core pipeline by rows per expert) -> residual.  Under a process group
-the experts are split over the ranks (expert parallelism with the static
-exchange of ``ep.ExpertParallelMoE``); attention and the dense parts are
+the experts are split over the ranks (expert parallelism over NVLink peer memory,
+``ep.PeerExpertParallelMoE``: each row goes once to every rank owning one of its
+experts, the weighted results come back); attention and the dense parts are
 replicated, every rank verifying the same sequences.
 
 The prompt is not run: the KV cache holds random values for ``ctx`` positions.
@@ -42,7 +43,7 @@ import torch.nn.functional as F
 from . import decode as _dec
 from . import moe as _moe
 from . import ops
-from .ep import ExpertParallelMoE
+from .ep import PeerExpertParallelMoE
 from .harness import _random_linear
 
 
@@ -147,7 +148,8 @@ class VerifyModel:
         self.ss = torch.zeros((2, self.rows), dtype=torch.float32, device=device)  # fused: row sums of h^2
         self.qkv = torch.empty((self.rows, qd + 2 * kvd), dtype=torch.float16, device=device)
         self.o = torch.empty((self.rows, H), dtype=torch.float16, device=device)
-        self.ep = ExpertParallelMoE(cfg.experts, world, rank, group) if world > 1 else None
+        self.ep = (PeerExpertParallelMoE(cfg.experts, self.rows, cfg.topk, H, group=group)
+                   if world > 1 else None)
         # The random-init model's hidden states collapse onto a few routes (a handful of
         # experts per layer whatever the batch).  A fixed N(0, 1) term per (layer, row)
         # in the router logits spreads the routing the way a trained router does (the
@@ -189,7 +191,7 @@ class VerifyModel:
             self.record.append(int(torch.unique(ids).numel()))
         if self.ep is None:
             return self._local_moe(L, xn, ids.to(torch.int32), w)
-        return self.ep(xn, ids, w, lambda xr, lids, lw, L=L: self._local_moe(L, xr, lids, lw))
+        return self.ep(xn, ids, w, L["tables"], cfg.K_expert, cfg.K_expert, cfg.K_expert, cfg.cb, cfg.inter)
 
     def _step_fused(self) -> torch.Tensor:
         cfg = self.cfg
@@ -273,4 +275,8 @@ class VerifyModel:
                 self.graph.replay()
 
     def close(self) -> None:
+        """Every rank, before the process group goes away (the peer buffers)."""
         self.graph = None
+        if self.ep is not None:
+            self.ep.close()
+            self.ep = None
