@@ -77,6 +77,7 @@ struct MoeTables {
     char* scratch;
     char* state;
     int tokens, topk, experts, hidden, inter, pmax, mul1, accumulate;
+    int prob_rows;  // rows per grouped problem: 8 (one row group, 8 tiles per warp) or 16
 };
 
 __global__ __launch_bounds__(kRouteThreads) void exl3_moe_route_kernel(const MoeTables t, MoeLayout L)
@@ -108,7 +109,7 @@ __global__ __launch_bounds__(kRouteThreads) void exl3_moe_route_kernel(const Moe
             rows[j] = rsum;
             probs[j] = psum;
             rsum += c;
-            psum += (c + kGvMaxRows - 1) / kGvMaxRows;
+            psum += (c + t.prob_rows - 1) / t.prob_rows;
         }
         const int lane = tid & 31, warp = tid >> 5;
         int ri = rsum, pi = psum;
@@ -176,10 +177,10 @@ __global__ __launch_bounds__(kRouteThreads) void exl3_moe_route_kernel(const Moe
     const int H = t.hidden, I = t.inter, pmax = t.pmax;
     for (int e = tid; e < t.experts; e += kRouteThreads) {
         const int c = s_count[e];
-        for (int j = 0; j * kGvMaxRows < c; ++j) {
+        for (int j = 0; j * t.prob_rows < c; ++j) {
             const int q = s_prob[e] + j;
-            const int first = s_slot[e] + j * kGvMaxRows;
-            const int m = min(kGvMaxRows, c - j * kGvMaxRows);
+            const int first = s_slot[e] + j * t.prob_rows;
+            const int m = min(t.prob_rows, c - j * t.prob_rows);
             GvProblem g = {};
             g.k = H;
             g.n = I;
@@ -362,13 +363,17 @@ extern "C" int exl3b200_moe(const void* x, long long x_stride, int tokens, int h
     t.pmax = pmax;
     t.mul1 = cb == 2;
     t.accumulate = accumulate;
+    // few rows per expert (at most 4 on average): problems of up to 8 rows on the
+    // one-row-group kernel (8 tiles per warp), whose tile rate is the higher; an expert
+    // with more rows then streams its codes once per 8 rows
+    t.prob_rows = (long long) tokens * topk <= 4ll * num_experts ? 8 : kGvMaxRows;
     int rc = launch_route(t, L, st);
     if (rc != kOk) return rc;
 
     const int* tot = reinterpret_cast<const int*>(sc + L.tot);
     const GvProblem* gu = reinterpret_cast<const GvProblem*>(sc + L.tab_gu);
     const GvProblem* dn = reinterpret_cast<const GvProblem*>(sc + L.tab_d);
-    const int rows = std::min(tokens, kGvMaxRows);
+    const int rows = std::min(tokens, t.prob_rows);
     const int pairs = tokens * topk;
 
     GvArgs a = {};

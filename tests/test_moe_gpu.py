@@ -104,6 +104,29 @@ def test_moe_forward(cuda_device, T, topk, E, cb, path):
     assert O.normwise_rel_err(y.cpu().numpy(), ref) < TOL_MOE
 
 
+@pytest.mark.parametrize("T,topk,E", [(40, 1, 16), (64, 2, 64)])
+def test_moe_small_eight_row_problems(cuda_device, T, topk, E):
+    """At most 4 rows per expert on average: the small-M pipeline groups an expert's rows
+    in problems of up to 8 (one row group); a skewed routing gives one expert 20 rows
+    (three problems) and leaves others empty."""
+    rng = np.random.default_rng(77 + T + E)
+    H, I, K, cb = 256, 384, 3, 0
+    experts = _with_cb(_experts(rng, E, H, I, K), cb)
+    tabs, keep = _tables(experts, cuda_device, cb)
+    x = rng.standard_normal((T, H)).astype(np.float16)
+    ids = rng.integers(0, E, size=(T, topk)).astype(np.int32)
+    ids[:20, 0] = 3  # expert 3: at least 20 rows
+    for r in range(20):  # keep a token's experts distinct
+        for j in range(1, topk):
+            if ids[r, j] == 3:
+                ids[r, j] = 4
+    w = rng.random((T, topk)).astype(np.float32)
+    w /= w.sum(1, keepdims=True)
+    y = moe.moe_forward(_t(x, cuda_device), _t(ids, cuda_device), _t(w, cuda_device), tabs, K, K, K, cb, I,
+                        path="small")
+    assert O.normwise_rel_err(y.cpu().numpy(), O.moe_ref(x, experts, ids, w)) < TOL_MOE
+
+
 @pytest.mark.parametrize("path", ["small", "tc"])
 def test_moe_invalid_ids_and_clip(cuda_device, path):
     rng = np.random.default_rng(77)
