@@ -1516,7 +1516,11 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_pair_kernel(const __gri
                         used |= 1u << s;
                         par = (par & ~(1u << s)) | (ph << s);
                     } else {
-                        mbar_arrive(full_a + 8 * s);  // nothing of this CTA's rows: the stage is ready as is
+                        // nothing of this CTA's rows: the stage is ready as is.  Its last use
+                        // now has no copy in flight, and the drain below must not wait on the
+                        // parity of an older copy (the barrier may have wrapped back to it)
+                        mbar_arrive(full_a + 8 * s);
+                        used &= ~(1u << s);
                     }
                     if (++s == S) { s = 0; ph ^= 1; }
                 }

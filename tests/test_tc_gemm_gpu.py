@@ -178,3 +178,26 @@ def test_tc_pair_long_k(cuda_device):
     assert float((y - y1).abs().max() / y1.abs().max()) < 1e-5
     assert O.normwise_rel_err(y[:64].cpu().numpy(), O.gemv_ref(x[:64], tr, su, sv, 4, 1)) < TOL_F32_ACC
     assert ops.device_status(cuda_device) == 0
+
+
+@pytest.mark.parametrize("m,k,n", [(600, 8192, 768), (1030, 2048, 2048), (520, 8192, 512)])
+def test_tc_pair_one_sided_tiles(cuda_device, m, k, n):
+    """Pair tiles whose rows all sit on one CTA of the pair (the other copies nothing for
+    them), after tiles with rows on both: the launch must end without any bounded wait
+    running out (a 0.2 s limit here; a wait on a stale phase would hit it), and match
+    the single-CTA kernel."""
+    rng = np.random.default_rng(3600 + m)
+    tr = O.random_trellis(rng, k, n, 4)
+    su, sv = O.random_signs(rng, k), O.random_signs(rng, n)
+    x = rng.standard_normal((m, k)).astype(np.float16)
+    ops.device_status(cuda_device)
+    ops.set_wait_limit(0.2)
+    try:
+        y2 = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), 4, 0,
+                        out_dtype=torch.float32, path="tc2")
+        assert ops.device_status(cuda_device) == 0
+    finally:
+        ops.set_wait_limit(None)
+    y1 = ops.matmul(_t(x, cuda_device), _t(tr, cuda_device), _t(su, cuda_device), _t(sv, cuda_device), 4, 0,
+                    out_dtype=torch.float32, path="tc1")
+    assert float((y2 - y1).abs().max() / y1.abs().max()) < 1e-5
