@@ -41,6 +41,8 @@
 //   linear).
 // * exl3_tc_finish_kernel: converts the split tiles' slots to the output dtype
 //   and re-zeroes them.
+// * exl3_tc_pair_kernel: the same matmul on 2-CTA clusters (tcgen05.mma.cta_group::2,
+//   512 x 256 tiles) for large M, where each decoded code tile then feeds 512 rows.
 // Every wait on an mbarrier is bounded (1 s of %globaltimer); a wait that runs
 // out raises the CTA's abort flag and the library's sticky device status; every
 // role then leaves its loop, waits (bounded) for its own copies and MMAs in
@@ -1413,7 +1415,8 @@ __global__ __launch_bounds__(kTcThreads, 1) void exl3_tc_gemm_kernel(const __gri
 // and B decode done) to the leader's pfull barrier.  The leader's commits arrive on
 // the empty and accumulator barriers of both CTAs (multicast); the epilogue warps of
 // both CTAs arrive on the leader's acc_empty.  Every wait is bounded as in the
-// single-CTA kernel.
+// single-CTA kernel.  All copies are unicast bulk copies into the issuing CTA's own
+// shared memory (no multicast loads).
 // ---------------------------------------------------------------------------
 constexpr int kTpStages = 4;   // activation and B ring depth of the pair kernel
 constexpr int kTpStagesT = 8;  // code ring depth of the pair kernel
