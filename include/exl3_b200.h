@@ -376,7 +376,9 @@ EXL3B200_API int exl3b200_peer_buffer_close(void* ptr);
 EXL3B200_API int exl3b200_peer_buffer_free(void* ptr);
 /*
  * Enqueue on stream the re-arming of this rank's own peer buffer (call epoch 0, no
- * arrivals, not poisoned).  Only while no exchange is in flight on any rank.
+ * arrivals, not poisoned, next generation: values written before the reset are
+ * never taken for a later call).  Every rank resets its own buffer once, while no
+ * exchange is in flight on any rank.
  */
 EXL3B200_API int exl3b200_peer_reset(void* own_buffer, void* stream);
 
@@ -438,12 +440,14 @@ EXL3B200_API int exl3b200_ep_moe(const exl3b200_ep_args* args, const exl3b200_pe
  * (tensor parallelism) it stores its fp32 partial output in y_out instead; after
  * the all-reduce, exl3b200_residual_add(h, y, ss_out) completes the sub-layer.
  * With peers (non-NULL; y_out ignored) the sub-layer exchanges the partials itself
- * through the peer buffers (stores over NVLink, an arrival counter per call, a
- * bounded wait - 2 s unless exl3b200_set_wait_limit says otherwise) and adds their
- * sum into h; every rank must make the same sequence of calls.  A wait that gives
- * up records EXL3B200_ETIMEOUT in the device status, leaves h, the counters and the
- * call epoch as they are, and poisons this rank's buffer: every later exchange on
- * it returns at once (recording EXL3B200_ETIMEOUT again) until
+ * through the peer buffers (each fp32 value stored over NVLink together with the
+ * call's tag in one 8-byte store; a warp waits, bounded - 2 s unless
+ * exl3b200_set_wait_limit says otherwise - until every rank's values of its block
+ * row carry the tag) and adds their sum into h; every rank must make the same
+ * sequence of calls.  A wait that gives up records EXL3B200_ETIMEOUT in the device
+ * status, leaves the call epoch as it is and poisons this rank's buffer (block rows
+ * already complete may have been added into h: the step is lost); every later
+ * exchange on it returns at once (recording EXL3B200_ETIMEOUT again) until
  * exl3b200_peer_reset.  The caller checks exl3b200_device_status and recovers by
  * draining every rank's stream, then exl3b200_peer_reset on every rank's own
  * buffer, with a host barrier before and after the resets.

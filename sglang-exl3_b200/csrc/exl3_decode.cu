@@ -539,90 +539,94 @@ __global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __gri
     const int lane = threadIdx.x & 31;
     gv_prefetch_epilogue(a, lane);
     griddep_wait();
-    __shared__ int ok;
     PeerCtl* ctl = reinterpret_cast<PeerCtl*>(x.peer[x.peer_rank]);
     // an earlier exchange gave up: the partial sums are still consumed (the matmul
-    // state is left zeroed for the next call), but nothing is stored, no arrival is
-    // made and h is not updated
+    // state is left zeroed for the next call), but nothing is stored or updated
     const bool poisoned = *reinterpret_cast<volatile unsigned int*>(&ctl->poisoned) != 0u;
     const unsigned int epoch = *reinterpret_cast<volatile unsigned int*>(&ctl->epoch) + 1u;
     const unsigned int parity = epoch & 1u;
+    const unsigned int gen = *reinterpret_cast<volatile unsigned int*>(x.peer[x.peer_rank] + kPeerGen);
+    // call tag: bit 31 set (zeroed slots never match), generation, call epoch
+    const unsigned int tag = 0x80000000u | ((gen & 0x7fu) << 24) | (epoch & 0xffffffu);
     const int warps = gridDim.x * (blockDim.x >> 5);
     const int task0 = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    bool gave_up = false;
     for (int task = task0; task < a.out_tasks; task += warps) {
         const GvProblem& p = gv_prob(a, 0);
         const int nblocks = p.n >> 7;
         const int r = task / nblocks, nb = task - r * nblocks;
         float v[4];
         gv_finish<CB>(p, nb, r, lane, v);
-        if (poisoned) continue;
+        if (poisoned || gave_up) continue;
+        // this rank's block row into its slot of every rank's buffer, then every rank's
+        // slot of the same block row from this rank's own buffer, each as soon as its tag
+        // shows (per warp: no grid-wide wait)
         for (int q = 0; q < x.peer_world; ++q) {
-            float* dst = peer_slot(x, q, parity, x.peer_rank, r) + nb * 128;
+            unsigned long long* dst = peer_slot(x, q, parity, x.peer_rank, r) + nb * 128;
 #pragma unroll
-            for (int e = 0; e < 4; ++e) dst[lane + 32 * e] = v[e];
+            for (int e = 0; e < 4; ++e) st_slot_sys(dst + lane + 32 * e, v[e], tag);
         }
-    }
-    if (poisoned) {
-        if (threadIdx.x == 0 && x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
-        return;
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x < x.peer_world)
-        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(peer_flag(x, threadIdx.x, parity, 0)) : "memory");
-    if (threadIdx.x == 0) {
-        const unsigned int expect = (unsigned int) x.peer_world * gridDim.x;
-        const unsigned int* cnt = peer_flag(x, x.peer_rank, parity, 0);
-        int good = 1;
+        float sum[4] = {0.f, 0.f, 0.f, 0.f};
+        bool ok = true;
         const unsigned long long t0 = globaltimer_ns();
-        while (ld_acquire_sys(cnt) < expect) {
-            if (globaltimer_ns() - t0 > x.peer_wait_ns) {
-                good = 0;
-                if (x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
-                atomicExch(&ctl->poisoned, 1u);
-                break;
-            }
-            __nanosleep(32);
-        }
-        ok = good;
-    }
-    __syncthreads();
-    if (ok) {
-        for (int task = task0; task < a.out_tasks; task += warps) {
-            const GvProblem& p = gv_prob(a, 0);
-            const int nblocks = p.n >> 7;
-            const int r = task / nblocks, b = task - r * nblocks;
-            float sum[4] = {0.f, 0.f, 0.f, 0.f};
-            for (int q = 0; q < x.peer_world; ++q) {
-                const float* src = peer_slot(x, x.peer_rank, parity, q, r) + b * 128;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) sum[e] += __ldcv(src + lane + 32 * e);
-            }
-            float* hr = x.resid + (size_t) r * x.resid_stride + b * 128;
-            float sq = 0.f;
+        for (int q = 0; q < x.peer_world && ok; ++q) {
+            const unsigned long long* src = peer_slot(x, x.peer_rank, parity, q, r) + nb * 128;
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float nv = hr[lane + 32 * e] + sum[e];
-                hr[lane + 32 * e] = nv;
-                sq += nv * nv;
+                unsigned long long w = ld_slot_sys(src + lane + 32 * e);
+                while ((unsigned int) (w >> 32) != tag) {
+                    if (globaltimer_ns() - t0 > x.peer_wait_ns) {
+                        ok = false;
+                        break;
+                    }
+                    w = ld_slot_sys(src + lane + 32 * e);
+                }
+                if (!ok) break;
+                sum[e] += __uint_as_float((unsigned int) w);
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-            if (lane == 0) atomicAdd(x.ss_acc + r, sq);
         }
+        if (!__all_sync(0xffffffffu, ok)) {
+            // a rank did not answer in time: status, poison; this and later block rows
+            // of this warp are not updated (h is left partly updated: the step is lost)
+            if (lane == 0) {
+                if (x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
+                atomicExch(&ctl->poisoned, 1u);
+            }
+            gave_up = true;
+            continue;
+        }
+        float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
+        float sq = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float nv = hr[lane + 32 * e] + sum[e];
+            hr[lane + 32 * e] = nv;
+            sq += nv * nv;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if (lane == 0) atomicAdd(x.ss_acc + r, sq);
     }
+    if (poisoned && threadIdx.x == 0 && x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
         if (atomicAdd(&ctl->done, 1u) == gridDim.x - 1) {
             ctl->done = 0u;
             if (!*reinterpret_cast<volatile unsigned int*>(&ctl->poisoned)) {
-                *peer_flag(x, x.peer_rank, parity, 0) = 0u;  // every rank's arrivals of this call are in
                 __threadfence();
                 *reinterpret_cast<volatile unsigned int*>(&ctl->epoch) = epoch;
             }
         }
     }
+}
+
+__global__ void exl3_peer_reset_kernel(char* buf)
+{
+    unsigned int* w = reinterpret_cast<unsigned int*>(buf);
+    const unsigned int gen = w[kPeerGen / 4];
+    for (int i = 0; i < (int) (kPeerData / 4); ++i) w[i] = 0u;
+    w[kPeerGen / 4] = gen + 1u;
 }
 
 // ---------------------------------------------------------------------------
@@ -864,7 +868,7 @@ using namespace exl3b200;
 extern "C" size_t exl3b200_peer_buffer_size(int max_rows, int hidden)
 {
     if (max_rows < 1 || hidden <= 0 || hidden % 128) return 0;
-    return kPeerData + (size_t) 2 * kPeerMaxRanks * max_rows * hidden * sizeof(float);
+    return kPeerData + (size_t) 2 * kPeerMaxRanks * max_rows * hidden * sizeof(unsigned long long);
 }
 
 extern "C" int exl3b200_peer_buffer_alloc(size_t bytes, void** ptr, void* ipc_handle)
@@ -901,10 +905,11 @@ extern "C" int exl3b200_peer_reset(void* own_buffer, void* stream)
 {
     if (!own_buffer) return kErrNullPointer;
     if ((uintptr_t) own_buffer & 255) return kErrUnaligned;
-    // control word and both parities' arrival counters
-    return cudaMemsetAsync(own_buffer, 0, kPeerData, reinterpret_cast<cudaStream_t>(stream)) == cudaSuccess
-               ? kOk
-               : kErrLaunch;
+    // control block zeroed (the exchange's and the expert-parallel exchange's counters,
+    // epochs and poison word), the generation advanced: slots written before the reset
+    // carry older tags and are never taken for this generation's calls
+    exl3_peer_reset_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(reinterpret_cast<char*>(own_buffer));
+    return cudaGetLastError() == cudaSuccess ? kOk : kErrLaunch;
 }
 
 extern "C" int exl3b200_peer_buffer_free(void* ptr)

@@ -23,10 +23,12 @@ constexpr int kHeadDim = 128;
 
 enum DecEpiMode : int { kEpiRopeKV = 10, kEpiResidual = 11 };
 
-// peer buffer: [control 128 B][arrival counters: 2 parities (u32; room for 2 x 8),
-//              padded to 128 B][data: 2 parities x 8 ranks x max_rows x hidden fp32]
+// peer buffer: [control 256 B: PeerCtl at 0, generation word at kPeerGen]
+//              [data: 2 parities x 8 ranks x max_rows x hidden 8-byte slots]
+// A slot holds one fp32 partial and the tag of the call that wrote it in one
+// 8-byte store, so a reader that sees the tag sees the value (no fence, no counter).
 constexpr int kPeerMaxRanks = 8;
-constexpr size_t kPeerFlags = 128;
+constexpr size_t kPeerGen = 64;    // u32: generation, advanced by every exl3b200_peer_reset
 constexpr size_t kPeerData = 256;
 constexpr unsigned long long kPeerTimeoutNs = 2000000000ull;
 
@@ -66,15 +68,24 @@ struct DecAux {
     int* status;
 };
 
-__device__ __forceinline__ float* peer_slot(const DecAux& x, int q, unsigned int parity, int src, int row)
+// Slots of row `row` written by rank `src` in rank q's buffer (hidden slots).
+__device__ __forceinline__ unsigned long long* peer_slot(const DecAux& x, int q, unsigned int parity, int src, int row)
 {
-    return reinterpret_cast<float*>(x.peer[q] + kPeerData) +
+    return reinterpret_cast<unsigned long long*>(x.peer[q] + kPeerData) +
            (((size_t) parity * kPeerMaxRanks + src) * x.peer_rows + row) * x.peer_hidden;
 }
 
-__device__ __forceinline__ unsigned int* peer_flag(const DecAux& x, int q, unsigned int parity, int src)
+__device__ __forceinline__ void st_slot_sys(unsigned long long* p, float v, unsigned int tag)
 {
-    return reinterpret_cast<unsigned int*>(x.peer[q] + kPeerFlags) + parity * kPeerMaxRanks + src;
+    const unsigned long long w = ((unsigned long long) tag << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_slot_sys(const unsigned long long* p)
+{
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return w;
 }
 
 __device__ __forceinline__ unsigned long long globaltimer_ns()
