@@ -397,8 +397,10 @@ def decode_config(args, world, fused=None):
     cfg = LLAMA_70B if args.layers == LLAMA_70B.layers else dataclasses.replace(LLAMA_70B, layers=args.layers)
     if fused is None:
         fused = args.batch <= 16
+    fold = fused and getattr(args, "fold", True)
     return {"workload": "llama70b-shape decode (config 4), greedy, one CUDA graph per step"
-                        + (", fused decode layers" if fused else ", unfused torch glue"),
+                        + ((", fused decode layers, RMSNorm folded into the residual epilogues" if fold
+                            else ", fused decode layers") if fused else ", unfused torch glue"),
             "model": "llama-70b-shape (random init)", "layers": cfg.layers, "global_batch": args.batch,
             "seq_len": args.ctx, "new_tokens_timed": decode_steps(args), "parallelism": f"tp{world}", "bpw": cfg.K,
             "codebook": "3INST", "kv_cache": "bf16, random contents for the 2048-token prompt",
@@ -890,7 +892,7 @@ def run_decode(args, world, rank, local, device):
     batch = args.batch
     new_tokens = 512
     group = torch.distributed.group.WORLD if world > 1 else None
-    model = DecodeModel(cfg, batch, args.ctx + new_tokens, device, world, rank, group)
+    model = DecodeModel(cfg, batch, args.ctx + new_tokens, device, world, rank, group, fold=args.fold)
     model.fill_random_kv(args.ctx)
     model.capture()
     steps = decode_steps(args)
@@ -961,9 +963,11 @@ def run_decode(args, world, rank, local, device):
                 "path": "DecodeModel.generate: per step, tokens H2D from pinned host memory, graph replay, tokens "
                         "and the device status word D2H, stream sync"},
         # fused: per layer 6 (attention) + 5 (MLP) launches (the NVLink exchange runs inside the o/down
-        # epilogues); + 2 residual-add kernels per layer when TP goes through NCCL instead
-        "gpu_launches": steps * cfg.layers * ((11 + (2 if world > 1 and not peer_exchange else 0))
-                                              if model.fused else 12),
+        # epilogues); + 2 residual-add kernels per layer when TP goes through NCCL instead; with the
+        # norm fold 9 per layer and the first layer's input stage
+        "gpu_launches": steps * ((9 * cfg.layers + 1) if model.fold else
+                                 cfg.layers * ((11 + (2 if world > 1 and not peer_exchange else 0))
+                                               if model.fused else 12)),
         "clocks": clk.summary(),
     }
     return finish(line, args, world)
@@ -1054,6 +1058,8 @@ def main():
                     help="moe workload: c3 = 288 experts, hidden 2048 (+ shared expert); c5 = the MoE layer of "
                          "config 5's speculative verify: 128 experts, hidden 4096, 5 rows per sequence")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--no-fold", dest="fold", action="store_false",
+                    help="decode: keep the RMSNorm input stages as kernels (two sub-layer calls per layer)")
     ap.add_argument("--no-extra", dest="extra", action="store_false",
                     help="default decode run: skip the other configs' summaries")
     args = ap.parse_args()

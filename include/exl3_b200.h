@@ -499,6 +499,50 @@ EXL3B200_API int exl3b200_residual_add(int batch, int hidden, float* h, long lon
                                        long long y_stride, float* ss_out, void* stream);
 
 /*
+ * A whole decoder layer (the attention sub-layer, then the MLP sub-layer) with the
+ * RMSNorm input stages folded into the residual epilogues: the attention's residual
+ * epilogue writes the MLP's normalised, rotated gate/up inputs itself, and - when
+ * next is not NULL - the MLP's residual epilogue writes the next layer's q/k/v
+ * inputs, which the next call (same rows, shapes, state and scratch; input_ready 1)
+ * takes instead of running its input stage.  A residual epilogue does not know the
+ * row's new norm yet, so it writes fp16(h * w * c) with c = rsqrt(ss_old/hidden +
+ * eps) / 16 (the row's factor before the add, with 16x headroom) and the consuming
+ * epilogue (RoPE/KV, SwiGLU) multiplies its outputs by rsqrt(ss_new/hidden + eps) / c:
+ * the same linear map, rounded at other points (within the unfused sub-layers' fp16
+ * tolerance); a row whose norm grows more than ~10^4-fold across one sub-layer
+ * would overflow the fp16 input.  Two kernels fewer per layer than the two sub-layer
+ * calls.
+ *
+ * ss_a: the rows' sum of squares of h on entry, and of the new h on return; ss_b: a
+ * second fp32 [rows] buffer used in between.  The first layer of a step passes
+ * input_ready 0 (its input stage normalises h).  Single GPU, or tensor parallel with
+ * peers (the all-reduce form has no residual epilogue to fold into).  Everything
+ * else as exl3b200_decode_attention_rows and exl3b200_decode_mlp; workspace:
+ * exl3b200_decode_layer_workspace (state zeroed once, left zeroed).
+ */
+typedef struct exl3b200_decode_layer {
+    const void* attn_norm_w;  /* bf16 [hidden] */
+    const exl3b200_linear* q;
+    const exl3b200_linear* k;
+    const exl3b200_linear* v;
+    const exl3b200_linear* o;
+    const void* mlp_norm_w;   /* bf16 [hidden] */
+    const exl3b200_linear* gate;
+    const exl3b200_linear* up;
+    const exl3b200_linear* down;
+} exl3b200_decode_layer;
+
+EXL3B200_API int exl3b200_decode_layer_workspace(int rows, int hidden, int q_heads, int kv_heads, int inter,
+                                                 int max_ctx, size_t* state_bytes, size_t* scratch_bytes);
+EXL3B200_API int exl3b200_decode_layer_step(int rows, int rows_per_seq, int hidden, int q_heads, int kv_heads,
+                                            int inter, int K, int cb, float* h, long long h_stride, float* ss_a,
+                                            float* ss_b, float eps, const exl3b200_decode_layer* layer,
+                                            const exl3b200_decode_layer* next, int input_ready, void* k_cache,
+                                            void* v_cache, int max_ctx, const long long* pos, const float* inv_freq,
+                                            float swiglu_limit, const exl3b200_peers* peers, void* state,
+                                            size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream);
+
+/*
  * Checkpoint reader: copies count byte ranges of the open file fd (offsets[i],
  * sizes[i] bytes) to dst[i].  Replaces the pread() loop of the reference's
  * exl3_mmap load format (src/sglang_exl3/loader.py:121-168), which reads every

@@ -1,7 +1,7 @@
 // Fused decode layer around the EXL3 small-M matmul: the glue of a Llama-style
 // decoder layer (RMSNorm, RoPE, KV-cache append, attention, residual adds,
 // SwiGLU) moved into the matmul pipeline's own input stages and epilogues, so a
-// decode step runs eleven kernels per layer instead of ~75.
+// decode step runs eleven kernels per layer instead of ~75 (nine with the norm fold).
 //
 // Attention sub-layer (exl3b200_decode_attention), all launches chained by
 // programmatic dependent launch:
@@ -34,13 +34,18 @@
 // input, the down matmul and the residual epilogue.
 //
 // Tensor parallelism without NCCL (peers != NULL): the o / down matmul's epilogue
-// kernel does the exchange itself - it stores each fp32 partial straight into a
-// slot of every rank's peer buffer (CUDA IPC mapping, plain stores over NVLink),
-// adds one arrival per CTA to a counter in every rank's buffer, waits (bounded, 2 s)
-// until its own counter holds every rank's arrivals, then sums the slots into h
-// and accumulates the sum of squares.  Counters and slots alternate between two
-// parities by call; a rank cannot reach call k+2 before every peer has finished
-// reading call k (its call k+1 waits for their call k+1 arrivals).
+// kernel does the exchange itself - each warp stores its block row's fp32 partials,
+// each with the call's tag in one 8-byte store, into its slot of every rank's peer
+// buffer (CUDA IPC mapping, plain stores over NVLink), reads every rank's slots of
+// the same block row from its own buffer until they carry the tag (bounded, 2 s),
+// then adds their sum into h and accumulates the sum of squares.  Slots alternate
+// between two parities by call.
+//
+// Whole layers (exl3b200_decode_layer_step) fold the RMSNorm input stages into the
+// residual epilogues: the attention's residual epilogue writes the MLP's gate/up
+// inputs and the MLP's writes the next layer's q/k/v inputs, pre-scaled by the row's
+// norm factor before the add; the RoPE and SwiGLU epilogues multiply by the ratio of
+// the exact factor to it.  Nine kernels per layer instead of eleven.
 //
 // The reference has no decode-layer fusion (its layers call SGLang's norm,
 // attention and activation kernels around the EXL3 ops); the arithmetic of each
@@ -62,37 +67,6 @@ namespace exl3b200 {
 namespace cg = cooperative_groups;
 
 constexpr int kDecChunk = 64;   // attention positions per CTA
-
-// fp16 values (already rounded) of one 128-block -> rotated input of a problem
-// (the GEMV input stage's layout: duplicated fp16 pairs, block sums for mul1).
-__device__ __forceinline__ void dec_store_rotated(const GvProblem& p, int r, int b, int lane, float (&xv)[4])
-{
-    float v[4];
-    if (p.suh) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            v[i] = __half2float(__float2half_rn(__fmul_rn(xv[i], __half2float(p.suh[b * 128 + lane + 32 * i]))));
-        warp_fwht128(v, lane);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], kHadScale);
-    } else {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) v[i] = xv[i];
-    }
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const __half hh = __float2half_rn(v[i]);
-        const uint32_t u = __half_as_ushort(hh);
-        p.xd[(size_t) r * p.k + b * 128 + lane + 32 * i] = u | (u << 16);
-        s += __half2float(hh);
-    }
-    if (p.sblk) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-        if (lane == 0) p.sblk[(size_t) r * (p.k >> 7) + b] = s;
-    }
-}
 
 __global__ __launch_bounds__(256) void exl3_dec_input_kernel(const __grid_constant__ GvArgs a,
                                                              const __grid_constant__ DecAux x)
@@ -130,10 +104,13 @@ __global__ __launch_bounds__(256) void exl3_dec_input_kernel(const __grid_consta
                 xv[i] = __half2float(__float2half_rn(hr[c] * rs * __bfloat162float(x.norm_w[b * 128 + c])));
             }
         }
-        dec_store_rotated(p, r, b, lane, xv);
+        store_rotated(p.xd, p.sblk, p.suh, p.k, r, b, lane, xv);
     }
 }
 
+// Decode epilogues (RoPE/KV, SwiGLU, residual).  With the norm fold the RoPE and
+// SwiGLU epilogues take over the skipped input stage's duty of zeroing the sum of
+// squares that the sub-layer's residual epilogue accumulates (zero_ss).
 template <int CB, int MODE>
 __global__ __launch_bounds__(256) void exl3_dec_epilogue_kernel(const __grid_constant__ GvArgs a,
                                                                 const __grid_constant__ DecAux x)
@@ -141,7 +118,13 @@ __global__ __launch_bounds__(256) void exl3_dec_epilogue_kernel(const __grid_con
     griddep_launch();
     const int lane = threadIdx.x & 31;
     gv_prefetch_epilogue(a, lane);
+    if (MODE == kEpiResidual && x.fold_n) {
+        const int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        if (task < a.out_tasks) fold_prefetch(x, task % (gv_prob(a, 0).n >> 7), lane);
+    }
     griddep_wait();
+    if (x.zero_ss && blockIdx.x == 0)
+        for (int i = threadIdx.x; i < x.zero_rows; i += blockDim.x) x.zero_ss[i] = 0.f;
     const int warps = gridDim.x * (blockDim.x >> 5);
     for (int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); task < a.out_tasks; task += warps) {
         const int pi = gv_find<1>(a, a.nprob, task);
@@ -150,7 +133,13 @@ __global__ __launch_bounds__(256) void exl3_dec_epilogue_kernel(const __grid_con
         const int local = task - p.out_task_begin;
         const int r = local / nblocks;
         const int nb = local - r * nblocks;
-        epi_block_row<CB>(a, x, MODE, pi, p, nullptr, nb, r, lane);
+        if constexpr (MODE == kEpiSwiglu) {
+            // (gate, up) = table entries j and j + 1 (a stride-2 view of the table)
+            const GvProblem& pu = a.inl[pi * a.stride + a.offset + 1];
+            epi_block_row<CB>(a, x, MODE, pi, p, &pu, nb, r, lane);
+        } else {
+            epi_block_row<CB>(a, x, MODE, pi, p, nullptr, nb, r, lane);
+        }
     }
 }
 
@@ -483,7 +472,7 @@ __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __gri
         float xv[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) xv[i] = sm.o[0][hh][lane + 32 * i];
-        dec_store_rotated(po, b, kvh * group + hh, lane, xv);
+        store_rotated(po.xd, po.sblk, po.suh, po.k, b, kvh * group + hh, lane, xv);
     }
     asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");  // partials stay readable until every rank has merged
 }
@@ -516,21 +505,22 @@ __global__ __launch_bounds__(256) void exl3_dec_residual_kernel(float* __restric
 }
 
 // Tensor-parallel output epilogue with the exchange folded in (o / down projection,
-// one launch per sub-layer).  Every CTA: finishes its (row, block) tasks and stores
-// each fp32 partial into this rank's slot of every rank's peer buffer (NVLink); a
-// system fence; one arrival on the call's counter in every rank's buffer; a
-// bounded wait (2 s of %globaltimer, then EXL3B200_ETIMEOUT in the device status
-// and no update) until its own counter holds world x grid arrivals; then h += the
-// sum of the slots for the same tasks, and the rows' sums of squares.  The last
-// CTA to finish re-arms the counter and advances the epoch.  A CTA whose wait gives
-// up poisons the buffer instead: the counter and the epoch stay as they are (a slow
-// peer's late arrivals and stores cannot be mistaken for the next call's), h is not
-// updated, and every later launch on the buffer returns at once with
-// EXL3B200_ETIMEOUT until the host re-arms it (exl3b200_peer_reset).  The grid is at most
-// one CTA per SM, so every CTA is resident while it waits, and it is the same on
-// every rank (same shapes).  Counters and slots alternate between two parities by
-// call; a rank cannot reach call k+2 before every peer has finished reading call k
-// (its call k+1 needs their call k+1 arrivals).
+// one launch per sub-layer).  Each warp, per (row, block) task: finishes the block
+// row, stores each fp32 partial with the call's tag (bit 31, the buffer's
+// generation, the call epoch) in one 8-byte store into this rank's slot of every
+// rank's peer buffer (NVLink), then reads every rank's slots of the same block row
+// from its own buffer until each carries the tag - a reader that sees the tag sees
+// the value, so no fence and no arrival counter - bounded by 2 s of %globaltimer;
+// then h += the sum, the row's sum of squares, and (norm fold) the next sub-layer's
+// inputs.  A warp whose wait gives up records EXL3B200_ETIMEOUT and poisons the
+// buffer: later block rows are not updated, the epoch is not advanced, and every
+// later launch on the buffer returns at once with EXL3B200_ETIMEOUT until the host
+// re-arms it (exl3b200_peer_reset, which also advances the generation so that
+// slots written before it never match).  The last CTA to finish advances the
+// epoch.  The grid is at most one CTA per SM, so every CTA is resident while it
+// waits, and it is the same on every rank (same shapes).  Slots alternate between
+// two parities by call; a rank cannot reach call k+2 before every peer has finished
+// call k (its call k+1 values only leave after its call k epilogue ended).
 template <int CB>
 __global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __grid_constant__ GvArgs a,
                                                                      const __grid_constant__ DecAux x)
@@ -538,6 +528,10 @@ __global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __gri
     griddep_launch();
     const int lane = threadIdx.x & 31;
     gv_prefetch_epilogue(a, lane);
+    if (x.fold_n) {
+        const int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        if (task < a.out_tasks) fold_prefetch(x, task % (gv_prob(a, 0).n >> 7), lane);
+    }
     griddep_wait();
     PeerCtl* ctl = reinterpret_cast<PeerCtl*>(x.peer[x.peer_rank]);
     // an earlier exchange gave up: the partial sums are still consumed (the matmul
@@ -555,6 +549,8 @@ __global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __gri
         const GvProblem& p = gv_prob(a, 0);
         const int nblocks = p.n >> 7;
         const int r = task / nblocks, nb = task - r * nblocks;
+        FoldPre fp;
+        if (x.fold_n) fold_preload(x, r, nb, lane, fp);
         float v[4];
         gv_finish<CB>(p, nb, r, lane, v);
         if (poisoned || gave_up) continue;
@@ -597,15 +593,17 @@ __global__ __launch_bounds__(256) void exl3_dec_peer_epilogue_kernel(const __gri
         }
         float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
         float sq = 0.f;
+        float nv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const float nv = hr[lane + 32 * e] + sum[e];
-            hr[lane + 32 * e] = nv;
-            sq += nv * nv;
+            nv[e] = hr[lane + 32 * e] + sum[e];
+            hr[lane + 32 * e] = nv[e];
+            sq += nv[e] * nv[e];
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
         if (lane == 0) atomicAdd(x.ss_acc + r, sq);
+        if (x.fold_n) fold_out(x, r, nb, lane, nv, fp);
     }
     if (poisoned && threadIdx.x == 0 && x.status) atomicCAS(x.status, 0, (int) kErrTimeout);
     __syncthreads();
@@ -802,11 +800,49 @@ static DecMlpLayout dec_mlp_layout(int batch, int hidden, int inter)
     return L;
 }
 
-// Final epilogue of a sub-layer: residual add into h (+ sum of squares), or an
-// fp32 store of the partial for a tensor-parallel all-reduce.
-static int dec_finish(GvArgs& a, DecAux& x, int cb, float* h, long long h_stride, float* ss_out, float* y_out,
-                      long long y_stride, const exl3b200_peers* peers, int batch, int hidden, cudaStream_t st)
+// Norm fold into a sub-layer's residual epilogue: the next sub-layer's inputs.
+struct DecFoldOut {
+    int n;
+    FoldTarget t[kFoldMax];
+    const void* norm_w;  // bf16 [hidden]
+    float* fold_c;       // [rows]
+};
+
+// Workspace of a whole layer with the norm fold: the attention sub-layer's, the
+// MLP sub-layer's, and the per-row pre-scale the residual epilogues write.
+struct DecLayerLayout {
+    DecAttnLayout A;
+    DecMlpLayout M;
+    size_t fold_c, state_bytes, scratch_bytes;
+};
+
+static DecLayerLayout dec_layer_layout(int rows, int hidden, int q_heads, int kv_heads, int inter, int max_ctx)
 {
+    DecLayerLayout L = {};
+    L.A = dec_attn_layout(rows, hidden, q_heads, kv_heads, max_ctx);
+    L.M = dec_mlp_layout(rows, hidden, inter);
+    L.state_bytes = L.A.state_bytes + L.M.state_bytes;
+    L.fold_c = L.A.scratch_bytes + L.M.scratch_bytes;
+    L.scratch_bytes = L.fold_c + al256((size_t) rows * sizeof(float));
+    return L;
+}
+
+// Final epilogue of a sub-layer: residual add into h (+ sum of squares), or an
+// fp32 store of the partial for a tensor-parallel all-reduce.  x arrives with the
+// consumer-side fold fields cleared; fold (optional) is applied to the residual.
+static int dec_finish(GvArgs& a, DecAux& x, int cb, float* h, long long h_stride, float* ss_out, float* y_out,
+                      long long y_stride, const exl3b200_peers* peers, int batch, int hidden, cudaStream_t st,
+                      const DecFoldOut* fold = nullptr)
+{
+    x.fold_c_in = nullptr;
+    x.zero_ss = nullptr;
+    if (fold && fold->n > 0) {
+        if (y_out) return kErrBadArgument;  // the all-reduce path finishes the residual outside
+        x.fold_n = fold->n;
+        for (int i = 0; i < kFoldMax; ++i) x.fold[i] = i < fold->n ? fold->t[i] : FoldTarget{};
+        x.fold_norm_w = reinterpret_cast<const __nv_bfloat16*>(fold->norm_w);
+        x.fold_c = fold->fold_c;
+    }
     if (peers) {
         for (int q = 0; q < kPeerMaxRanks; ++q) x.peer[q] = q < peers->world ? (char*) peers->buffers[q] : nullptr;
         x.peer_world = peers->world;
@@ -949,7 +985,8 @@ static int dec_attention(int batch, int rows_per_seq, int hidden, int q_heads, i
                          const exl3b200_linear* q, const exl3b200_linear* k, const exl3b200_linear* v,
                          const exl3b200_linear* o, void* k_cache, void* v_cache, int max_ctx, const long long* pos,
                          const float* inv_freq, float* y_out, long long y_stride, const exl3b200_peers* peers,
-                         void* state, size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream)
+                         void* state, size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream,
+                         const float* fold_c_in = nullptr, const DecFoldOut* fold_out = nullptr)
 {
     if (rows_per_seq < 1 || batch % rows_per_seq) return kErrBadShape;
     int rc = dec_common_checks(batch, hidden, K, cb, h, h_stride, ss_in, ss_out, norm_w, state, scratch);
@@ -1004,11 +1041,18 @@ static int dec_attention(int batch, int rows_per_seq, int hidden, int q_heads, i
     dec_problem(a.inl[2], v, batch, reinterpret_cast<uint32_t*>(W + L.xd_v),
                 mul1 ? reinterpret_cast<float*>(W + L.sb_v) : nullptr, reinterpret_cast<float*>(S + L.st_v));
     gv_prefix_inline(a);
-    rc = dec_launch(exl3_dec_input_kernel, dec_grid(a.in_tasks), 256, st, a, x);
-    if (rc != kOk) return rc;
+    DecAux xe = x;  // the RoPE epilogue's view: with the norm fold it scales and zeroes ss_out
+    if (fold_c_in) {
+        // the previous sub-layer's residual epilogue wrote the q/k/v inputs
+        xe.fold_c_in = fold_c_in;
+        xe.zero_ss = ss_out;
+    } else {
+        rc = dec_launch(exl3_dec_input_kernel, dec_grid(a.in_tasks), 256, st, a, x);
+        if (rc != kOk) return rc;
+    }
     rc = gv_launch_matmul(a, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
-    rc = dec_launch_epilogue<kEpiRopeKV>(a, x, cb, st);
+    rc = dec_launch_epilogue<kEpiRopeKV>(a, xe, cb, st);
     if (rc != kOk) return rc;
 
     // 4: attention (a cluster per row and kv head; its merge writes the o input)
@@ -1023,7 +1067,7 @@ static int dec_attention(int batch, int rows_per_seq, int hidden, int q_heads, i
     // 5-6: o matmul, residual (or fp32 partial for the all-reduce)
     rc = gv_launch_matmul(b, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
-    return dec_finish(b, x, cb, h, h_stride, ss_out, y_out, y_stride, peers, batch, hidden, st);
+    return dec_finish(b, x, cb, h, h_stride, ss_out, y_out, y_stride, peers, batch, hidden, st, fold_out);
 }
 
 extern "C" int exl3b200_decode_attention(int batch, int hidden, int q_heads, int kv_heads, int K, int cb, float* h,
@@ -1053,12 +1097,12 @@ extern "C" int exl3b200_decode_attention_rows(int rows, int rows_per_seq, int hi
                          state_bytes, scratch, scratch_bytes, stream);
 }
 
-extern "C" int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int cb, float* h, long long h_stride,
-                                   const float* ss_in, float* ss_out, const void* norm_w, float eps,
-                                   const exl3b200_linear* gate, const exl3b200_linear* up,
-                                   const exl3b200_linear* down, float swiglu_limit, float* y_out, long long y_stride,
-                                   const exl3b200_peers* peers, void* state, size_t state_bytes, void* scratch,
-                                   size_t scratch_bytes, void* stream)
+static int dec_mlp(int batch, int hidden, int inter, int K, int cb, float* h, long long h_stride, const float* ss_in,
+                   float* ss_out, const void* norm_w, float eps, const exl3b200_linear* gate,
+                   const exl3b200_linear* up, const exl3b200_linear* down, float swiglu_limit, float* y_out,
+                   long long y_stride, const exl3b200_peers* peers, void* state, size_t state_bytes, void* scratch,
+                   size_t scratch_bytes, void* stream, const float* fold_c_in = nullptr,
+                   const DecFoldOut* fold_out = nullptr)
 {
     int rc = dec_common_checks(batch, hidden, K, cb, h, h_stride, ss_in, ss_out, norm_w, state, scratch);
     if (rc != kOk) return rc;
@@ -1097,8 +1141,14 @@ extern "C" int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int 
     a.inl[0].out_suh = reinterpret_cast<const __half*>(down->suh);
     a.inl[0].out_sblk = mul1 ? reinterpret_cast<float*>(W + L.sb_d) : nullptr;
     gv_prefix_inline(a);
-    rc = dec_launch(exl3_dec_input_kernel, dec_grid(a.in_tasks), 256, st, a, x);
-    if (rc != kOk) return rc;
+    DecAux xe = x;  // the SwiGLU epilogue's view: with the norm fold it scales and zeroes ss_out
+    if (fold_c_in) {
+        xe.fold_c_in = fold_c_in;
+        xe.zero_ss = ss_out;
+    } else {
+        rc = dec_launch(exl3_dec_input_kernel, dec_grid(a.in_tasks), 256, st, a, x);
+        if (rc != kOk) return rc;
+    }
     rc = gv_launch_matmul(a, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
 
@@ -1109,7 +1159,7 @@ extern "C" int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int 
     e.out_tasks = batch * (inter / 128);
     e.epi_mode = kEpiSwiglu;
     e.swiglu_limit = swiglu_limit;
-    rc = gv_launch_epilogue(e, cb, e.out_tasks, true, st);
+    rc = dec_launch_epilogue<kEpiSwiglu>(e, xe, cb, st);
     if (rc != kOk) return rc;
 
     GvArgs d = {};
@@ -1119,7 +1169,18 @@ extern "C" int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int 
     gv_prefix_inline(d);
     rc = gv_launch_matmul(d, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
-    return dec_finish(d, x, cb, h, h_stride, ss_out, y_out, y_stride, peers, batch, hidden, st);
+    return dec_finish(d, x, cb, h, h_stride, ss_out, y_out, y_stride, peers, batch, hidden, st, fold_out);
+}
+
+extern "C" int exl3b200_decode_mlp(int batch, int hidden, int inter, int K, int cb, float* h, long long h_stride,
+                                   const float* ss_in, float* ss_out, const void* norm_w, float eps,
+                                   const exl3b200_linear* gate, const exl3b200_linear* up,
+                                   const exl3b200_linear* down, float swiglu_limit, float* y_out, long long y_stride,
+                                   const exl3b200_peers* peers, void* state, size_t state_bytes, void* scratch,
+                                   size_t scratch_bytes, void* stream)
+{
+    return dec_mlp(batch, hidden, inter, K, cb, h, h_stride, ss_in, ss_out, norm_w, eps, gate, up, down,
+                   swiglu_limit, y_out, y_stride, peers, state, state_bytes, scratch, scratch_bytes, stream);
 }
 
 extern "C" int exl3b200_residual_add(int batch, int hidden, float* h, long long h_stride, const float* y,
@@ -1130,4 +1191,77 @@ extern "C" int exl3b200_residual_add(int batch, int hidden, float* h, long long 
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     return dec_launch(exl3_dec_residual_kernel, dec_grid(batch * (hidden / 128)), 256, st, h, h_stride, y, y_stride,
                       ss_out, batch, hidden);
+}
+
+extern "C" int exl3b200_decode_layer_workspace(int rows, int hidden, int q_heads, int kv_heads, int inter, int max_ctx,
+                                               size_t* state_bytes, size_t* scratch_bytes)
+{
+    if (!state_bytes || !scratch_bytes) return kErrNullPointer;
+    if (rows < 1 || rows > EXL3B200_GEMV_MAX_M || hidden <= 0 || hidden % 128 || q_heads < 1 || kv_heads < 1 ||
+        q_heads % kv_heads || q_heads / kv_heads > kAttnMaxGroup || max_ctx < 1 || inter <= 0 || inter % 128)
+        return kErrBadShape;
+    const DecLayerLayout L = dec_layer_layout(rows, hidden, q_heads, kv_heads, inter, max_ctx);
+    *state_bytes = L.state_bytes;
+    *scratch_bytes = L.scratch_bytes;
+    return kOk;
+}
+
+// One decoder layer (attention sub-layer, then MLP sub-layer) with the RMSNorm input
+// stages folded into the residual epilogues: the attention's residual epilogue writes
+// the MLP's gate/up inputs, the MLP's writes the next layer's q/k/v inputs (when next
+// is given), and the consumers (SwiGLU, RoPE) apply the rows' exact norm factors.
+extern "C" int exl3b200_decode_layer_step(int rows, int rows_per_seq, int hidden, int q_heads, int kv_heads, int inter,
+                                          int K, int cb, float* h, long long h_stride, float* ss_a, float* ss_b,
+                                          float eps, const exl3b200_decode_layer* layer,
+                                          const exl3b200_decode_layer* next, int input_ready, void* k_cache,
+                                          void* v_cache, int max_ctx, const long long* pos, const float* inv_freq,
+                                          float swiglu_limit, const exl3b200_peers* peers, void* state,
+                                          size_t state_bytes, void* scratch, size_t scratch_bytes, void* stream)
+{
+    if (!layer || !ss_a || !ss_b || !state || !scratch) return kErrNullPointer;
+    if (!layer->attn_norm_w || !layer->mlp_norm_w) return kErrNullPointer;
+    size_t need_state = 0, need_scratch = 0;
+    int rc = exl3b200_decode_layer_workspace(rows, hidden, q_heads, kv_heads, inter, max_ctx, &need_state,
+                                             &need_scratch);
+    if (rc != kOk) return rc;
+    if (state_bytes < need_state || scratch_bytes < need_scratch) return kErrWorkspace;
+    if (((uintptr_t) state & 255) || ((uintptr_t) scratch & 255)) return kErrUnaligned;
+    const int nq = q_heads * kHeadDim, nkv = kv_heads * kHeadDim;
+    if (!dec_linear_ok(layer->gate, hidden, inter) || !dec_linear_ok(layer->up, hidden, inter)) return kErrBadShape;
+    if (next && (!next->attn_norm_w || !dec_linear_ok(next->q, hidden, nq) || !dec_linear_ok(next->k, hidden, nkv) ||
+                 !dec_linear_ok(next->v, hidden, nkv)))
+        return next->attn_norm_w ? kErrBadShape : kErrNullPointer;
+    const DecLayerLayout L = dec_layer_layout(rows, hidden, q_heads, kv_heads, inter, max_ctx);
+    char* S = reinterpret_cast<char*>(state);
+    char* W = reinterpret_cast<char*>(scratch);
+    char* WM = W + L.A.scratch_bytes;
+    float* fold_c = reinterpret_cast<float*>(W + L.fold_c);
+    const bool mul1 = cb == 2;
+    auto target = [&](char* base, size_t xd, size_t sb, const exl3b200_linear* l) {
+        return FoldTarget{reinterpret_cast<uint32_t*>(base + xd), mul1 ? reinterpret_cast<float*>(base + sb) : nullptr,
+                          reinterpret_cast<const __half*>(l->suh), hidden};
+    };
+    DecFoldOut fa = {};  // attention residual -> this layer's gate/up inputs
+    fa.n = 2;
+    fa.t[0] = target(WM, L.M.xd_g, L.M.sb_g, layer->gate);
+    fa.t[1] = target(WM, L.M.xd_u, L.M.sb_u, layer->up);
+    fa.norm_w = layer->mlp_norm_w;
+    fa.fold_c = fold_c;
+    DecFoldOut fm = {};  // MLP residual -> the next layer's q/k/v inputs
+    if (next) {
+        fm.n = 3;
+        fm.t[0] = target(W, L.A.xd_q, L.A.sb_q, next->q);
+        fm.t[1] = target(W, L.A.xd_k, L.A.sb_k, next->k);
+        fm.t[2] = target(W, L.A.xd_v, L.A.sb_v, next->v);
+        fm.norm_w = next->attn_norm_w;
+        fm.fold_c = fold_c;
+    }
+    rc = dec_attention(rows, rows_per_seq, hidden, q_heads, kv_heads, K, cb, h, h_stride, ss_a, ss_b,
+                       layer->attn_norm_w, eps, layer->q, layer->k, layer->v, layer->o, k_cache, v_cache, max_ctx, pos,
+                       inv_freq, nullptr, 0, peers, S, L.A.state_bytes, W, L.A.scratch_bytes, stream,
+                       input_ready ? fold_c : nullptr, &fa);
+    if (rc != kOk) return rc;
+    return dec_mlp(rows, hidden, inter, K, cb, h, h_stride, ss_b, ss_a, layer->mlp_norm_w, eps, layer->gate, layer->up,
+                   layer->down, swiglu_limit, nullptr, 0, peers, S + L.A.state_bytes, L.M.state_bytes, WM,
+                   L.M.scratch_bytes, stream, fold_c, next ? &fm : nullptr);
 }

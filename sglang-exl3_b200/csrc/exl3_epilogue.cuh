@@ -8,7 +8,8 @@
 //                 of the reference)
 //   kEpiRopeKV    decode q/k/v: RoPE (rotate-half), q scaled into the attention
 //                 buffer, k and v appended to the bf16 cache
-//   kEpiResidual  decode: h += y and the row's sum of squares
+//   kEpiResidual  decode: h += y and the row's sum of squares (with the norm fold,
+//                 also the next sub-layer's normalised, rotated inputs)
 #pragma once
 
 #include <cuda_bf16.h>
@@ -38,6 +39,23 @@ struct PeerCtl {
     unsigned int poisoned;  // a wait gave up: exchanges return at once until the host re-arms
 };
 
+// One input of the next sub-layer that a residual epilogue writes itself (norm fold):
+// the rotated-input image (duplicated fp16 pairs) and, for mul1, its block sums.
+struct FoldTarget {
+    uint32_t* xd;        // [rows][k]
+    float* sblk;         // [rows][k/128] or null
+    const __half* suh;   // [k]
+    int k;
+};
+
+constexpr int kFoldMax = 3;
+// The folded input is fp16(h * c * w) with c = rsqrt(ss_old/hidden + eps) / 16 (ss_old:
+// the row's sum of squares before the residual add, known while the add runs); the
+// consumer multiplies its finished outputs by rsqrt(ss_new/hidden + eps) / c.  The
+// power-of-two factor keeps 16x headroom below the fp16 range for rows whose norm
+// grows across the add, and is exact.
+constexpr float kFoldHeadroom = 0.0625f;
+
 struct DecAux {
     // norm input stage
     const float* h;
@@ -61,6 +79,15 @@ struct DecAux {
     float* resid;
     long long resid_stride;
     float* ss_acc;
+    // norm fold, output side (residual epilogues): write the next sub-layer's inputs
+    int fold_n;                          // 0: off
+    FoldTarget fold[kFoldMax];
+    const __nv_bfloat16* fold_norm_w;    // the next sub-layer's RMSNorm weight
+    float* fold_c;                       // [rows]: the pre-scale c written for the consumer
+    // norm fold, input side (RoPE / SwiGLU epilogue): finished values *=
+    // rsqrt(ss_in/hidden + eps) / fold_c_in[r]; the consumer also zeroes zero_ss
+    const float* fold_c_in;
+    float* zero_ss;
     // tensor-parallel partial exchange
     char* peer[kPeerMaxRanks];
     int peer_world, peer_rank, peer_rows, peer_hidden;
@@ -107,11 +134,103 @@ __device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v)
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// fp16 values (already rounded) of one 128-block -> a problem's rotated input
+// (the GEMV input stage's layout: fp16 x*suh, H128, /sqrt(128) as duplicated fp16
+// pairs; block sums for mul1).
+// The input scales of one 128-block (suh[b * 128 + lane + 32 i]) are passed loaded.
+__device__ __forceinline__ void store_rotated_s(uint32_t* xd, float* sblk, bool rotate, const float (&su)[4], int k,
+                                                int r, int b, int lane, const float (&xv)[4])
+{
+    float v[4];
+    if (rotate) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __half2float(__float2half_rn(__fmul_rn(xv[i], su[i])));
+        warp_fwht128(v, lane);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = __fmul_rn(v[i], kHadScale);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = xv[i];
+    }
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const __half hh = __float2half_rn(v[i]);
+        const uint32_t u = __half_as_ushort(hh);
+        xd[(size_t) r * k + b * 128 + lane + 32 * i] = u | (u << 16);
+        s += __half2float(hh);
+    }
+    if (sblk) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        if (lane == 0) sblk[(size_t) r * (k >> 7) + b] = s;
+    }
+}
+
+__device__ __forceinline__ void store_rotated(uint32_t* xd, float* sblk, const __half* suh, int k, int r, int b,
+                                              int lane, const float (&xv)[4])
+{
+    float su[4] = {1.f, 1.f, 1.f, 1.f};
+    if (suh) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) su[i] = __half2float(suh[b * 128 + lane + 32 * i]);
+    }
+    store_rotated_s(xd, sblk, suh != nullptr, su, k, r, b, lane, xv);
+}
+
+// Norm fold, output side.  Everything a residual epilogue task needs besides the new
+// row values, loaded at the task's start so the loads overlap the partial sums' read:
+// the pre-scale c (from the row's sum of squares before the add), the next
+// sub-layer's norm weights and every target's input scales of block nb.
+struct FoldPre {
+    float c;
+    float w[4];
+    float su[kFoldMax][4];
+};
+
+__device__ __forceinline__ void fold_preload(const DecAux& x, int r, int nb, int lane, FoldPre& f)
+{
+    f.c = rsqrtf(x.ss_in[r] * x.inv_hidden + x.eps) * kFoldHeadroom;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) f.w[e] = __bfloat162float(x.fold_norm_w[nb * 128 + lane + 32 * e]);
+#pragma unroll
+    for (int i = 0; i < kFoldMax; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+            f.su[i][e] = i < x.fold_n ? __half2float(x.fold[i].suh[nb * 128 + lane + 32 * e]) : 0.f;
+}
+
+// Before a residual epilogue's dependency wait: its first task's fold inputs into L2.
+__device__ __forceinline__ void fold_prefetch(const DecAux& x, int nb, int lane)
+{
+    prefetch_l2_256(x.fold_norm_w + nb * 128, lane);
+    for (int i = 0; i < x.fold_n; ++i) prefetch_l2_256(x.fold[i].suh + nb * 128, lane);
+}
+
+// Block nb of row r of the new residual stream (nv) -> the next sub-layer's rotated
+// inputs, pre-scaled by c (see kFoldHeadroom).
+__device__ __forceinline__ void fold_out(const DecAux& x, int r, int nb, int lane, const float (&nv)[4],
+                                         const FoldPre& f)
+{
+    float xv[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) xv[e] = __half2float(__float2half_rn(nv[e] * f.c * f.w[e]));
+#pragma unroll
+    for (int i = 0; i < kFoldMax; ++i) {
+        if (i < x.fold_n) {
+            const FoldTarget& t = x.fold[i];
+            store_rotated_s(t.xd, t.sblk, true, f.su[i], t.k, r, nb, lane, xv);
+        }
+    }
+    if (nb == 0 && lane == 0) x.fold_c[r] = f.c;
+}
+
 // Loads and math of an epilogue that do not depend on the partial sums (issued
 // first so their round trips overlap the partials' read).
 struct EpiPre {
     float pre[4];
     long long pos;
+    FoldPre fold;  // residual with the norm fold
 };
 
 __device__ __forceinline__ EpiPre epi_preload(const GvProblem& p, const DecAux& x, int mode, int pi, int nb, int r,
@@ -130,6 +249,7 @@ __device__ __forceinline__ EpiPre epi_preload(const GvProblem& p, const DecAux& 
         const float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
 #pragma unroll
         for (int e = 0; e < 4; ++e) pre[e] = hr[lane + 32 * e];
+        if (x.fold_n) fold_preload(x, r, nb, lane, ep.fold);
     } else if (mode == kEpiRopeKV) {
         pos = *x.pos + r % x.rows_per_seq;
         if (pi < 2) {
@@ -220,16 +340,25 @@ __device__ __forceinline__ void epi_apply(const GvArgs& a, const DecAux& x, int 
     } else {  // kEpiResidual: pre = h
         float* hr = x.resid + (size_t) r * x.resid_stride + nb * 128;
         float sq = 0.f;
+        float nv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const float nv = pre[e] + v[e];
-            hr[lane + 32 * e] = nv;
-            sq += nv * nv;
+            nv[e] = pre[e] + v[e];
+            hr[lane + 32 * e] = nv[e];
+            sq += nv[e] * nv[e];
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
         if (lane == 0) atomicAdd(x.ss_acc + r, sq);
+        if (x.fold_n) fold_out(x, r, nb, lane, nv, ep.fold);
     }
+}
+
+// Norm fold, input side: the factor that turns outputs computed from the pre-scaled
+// input into those of the normalised input (1 when the input stage normalised).
+__device__ __forceinline__ float fold_factor(const DecAux& x, int r)
+{
+    return x.fold_c_in ? rsqrtf(x.ss_in[r] * x.inv_hidden + x.eps) / x.fold_c_in[r] : 1.f;
 }
 
 template <int CB>
@@ -237,9 +366,17 @@ __device__ __forceinline__ void epi_block_row(const GvArgs& a, const DecAux& x, 
                                               const GvProblem* up, int nb, int r, int lane)
 {
     const EpiPre ep = epi_preload(p, x, mode, pi, nb, r, lane);
+    const float f = fold_factor(x, r);  // loaded before the partial sums are read and re-zeroed
     float v[4], u[4] = {0.f, 0.f, 0.f, 0.f};
     gv_finish<CB>(p, nb, r, lane, v);
     if (mode == kEpiSwiglu) gv_finish<CB>(*up, nb, r, lane, u);
+    if (x.fold_c_in) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            v[e] *= f;
+            u[e] *= f;
+        }
+    }
     epi_apply<CB>(a, x, mode, pi, p, nb, r, lane, v, u, ep);
 }
 

@@ -75,6 +75,14 @@ class EpArgs(ctypes.Structure):
                 ("out", _vp), ("out_stride", _ll), ("path", _i)]
 
 
+class DecodeLayer(ctypes.Structure):
+    """``exl3b200_decode_layer``: one decoder layer's norms and linears (pointers to
+    ``Linear`` descriptors, which the caller keeps alive)."""
+
+    _fields_ = [("attn_norm_w", _vp), ("q", _vp), ("k", _vp), ("v", _vp), ("o", _vp), ("mlp_norm_w", _vp),
+                ("gate", _vp), ("up", _vp), ("down", _vp)]
+
+
 class Peers(ctypes.Structure):
     """``exl3b200_peers``: every rank's peer buffer as mapped in this process."""
 
@@ -128,6 +136,9 @@ SIGNATURES = {
     "exl3b200_ep_workspace": (_i, [_vp, _vp, _vp, _vp]),
     "exl3b200_ep_moe": (_i, [_vp, _vp, _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_residual_add": (_i, [_i, _i, _vp, _ll, _vp, _ll, _vp, _vp]),
+    "exl3b200_decode_layer_workspace": (_i, [_i, _i, _i, _i, _i, _i, _vp, _vp]),
+    "exl3b200_decode_layer_step": (_i, [_i, _i, _i, _i, _i, _i, _i, _i, _vp, _ll, _vp, _vp, _f, _vp, _vp, _i, _vp,
+                                        _vp, _i, _vp, _vp, _f, _vp, _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_mlp_workspace": (_i, [_i, _i, _i, _i, _i, _vp, _vp]),
     "exl3b200_mlp": (_i, [_vp, _vp, _sz, _vp, _sz, _vp]),
     "exl3b200_moe_tc_scratch_size": (_sz, [_i, _i, _i, _i, _i]),

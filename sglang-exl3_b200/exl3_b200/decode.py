@@ -111,6 +111,62 @@ def decode_mlp(h: torch.Tensor, ss_in: torch.Tensor, ss_out: torch.Tensor, norm_
     _lib.check(rc, "exl3b200_decode_mlp")
 
 
+class LayerDesc:
+    """One decoder layer for ``decode_layer``: the ``exl3b200_decode_layer`` struct and
+    the ``Linear`` descriptors it points to (kept alive with the tensors' pointers)."""
+
+    def __init__(self, attn_norm_w: torch.Tensor, qkv: Sequence, o: Sequence, mlp_norm_w: torch.Tensor,
+                 gate: Sequence, up: Sequence, down: Sequence):
+        for w in (attn_norm_w, mlp_norm_w):
+            if w.dtype != torch.bfloat16 or not w.is_contiguous():
+                raise RuntimeError("norm weights must be contiguous bf16 [hidden]")
+        self.norms = (attn_norm_w, mlp_norm_w)
+        self.lins = [linear_desc(*lin) for lin in (*qkv, o, gate, up, down)]
+        q, k, v, lo, g, u, d = (ctypes.addressof(lin) for lin in self.lins)
+        self.struct = _lib.DecodeLayer(attn_norm_w.data_ptr(), q, k, v, lo, mlp_norm_w.data_ptr(), g, u, d)
+        self.q_heads = qkv[0][0].size(1) * 16 // 128
+        self.inter = gate[0].size(1) * 16
+
+
+def decode_layer(h: torch.Tensor, ss_a: torch.Tensor, ss_b: torch.Tensor, eps: float, layer: LayerDesc,
+                 next_layer: Optional[LayerDesc], input_ready: bool, K: int, cb: int, k_cache: torch.Tensor,
+                 v_cache: torch.Tensor, pos: torch.Tensor, inv_freq: torch.Tensor, swiglu_limit: float = 0.0,
+                 peers=None, rows_per_seq: int = 1) -> None:
+    """A whole decoder layer (attention, then MLP) with the RMSNorm input stages folded
+    into the residual epilogues.  ``ss_a``: the rows' sum of squares of ``h`` on entry
+    and of the new ``h`` on return; ``ss_b`` a second [rows] buffer.  With
+    ``next_layer`` the MLP's residual epilogue writes that layer's q/k/v inputs and its
+    call passes ``input_ready=True`` (same rows and shapes: the workspace is shared)."""
+    _check_state(h, ss_a, ss_b, layer.norms[0])
+    B, H = h.shape
+    R = int(rows_per_seq)
+    if R < 1 or B % R:
+        raise RuntimeError("rows must be a multiple of rows_per_seq")
+    if k_cache.dtype != torch.bfloat16 or k_cache.dim() != 4 or k_cache.size(-1) != 128 or not k_cache.is_contiguous():
+        raise RuntimeError("caches must be contiguous bf16 [sequences, kv_heads, max_ctx, 128]")
+    if v_cache.shape != k_cache.shape or not v_cache.is_contiguous() or k_cache.size(0) != B // R:
+        raise RuntimeError("k and v caches must match and have one row per sequence")
+    if pos.dtype != torch.int64 or inv_freq.dtype != torch.float32 or inv_freq.numel() != 64:
+        raise RuntimeError("pos must be int64 and inv_freq fp32 [64]")
+    kv_heads, max_ctx = k_cache.size(1), k_cache.size(2)
+    dev = h.device
+    L = _lib.lib()
+    st_n, sc_n = ctypes.c_size_t(), ctypes.c_size_t()
+    _lib.check(L.exl3b200_decode_layer_workspace(B, H, layer.q_heads, kv_heads, layer.inter, max_ctx,
+                                                 ctypes.byref(st_n), ctypes.byref(sc_n)),
+               "exl3b200_decode_layer_workspace")
+    with torch.cuda.device(dev):
+        state, scratch = _ws(dev, st_n.value, sc_n.value)
+        rc = L.exl3b200_decode_layer_step(
+            B, R, H, layer.q_heads, kv_heads, layer.inter, int(K), int(cb), h.data_ptr(), h.stride(0),
+            ss_a.data_ptr(), ss_b.data_ptr(), float(eps), ctypes.byref(layer.struct),
+            ctypes.byref(next_layer.struct) if next_layer is not None else None, int(bool(input_ready)),
+            k_cache.data_ptr(), v_cache.data_ptr(), max_ctx, pos.data_ptr(), inv_freq.data_ptr(),
+            float(swiglu_limit), _peers_arg(peers), state.data_ptr(), state.numel(), scratch.data_ptr(),
+            scratch.numel(), _stream(dev))
+    _lib.check(rc, "exl3b200_decode_layer_step")
+
+
 def residual_add(h: torch.Tensor, y: torch.Tensor, ss_out: torch.Tensor) -> None:
     """``h += y`` and the new per-row sum of squares into (zeroed) ``ss_out``."""
     if y.dtype != torch.float32 or y.shape != h.shape:

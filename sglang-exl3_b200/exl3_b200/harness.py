@@ -71,7 +71,8 @@ def exl3_weight_bytes(cfg: DecoderConfig, world: int = 1) -> int:
 
 class DecodeModel:
     def __init__(self, cfg: DecoderConfig, batch: int, max_ctx: int, device: torch.device, world: int = 1,
-                 rank: int = 0, group=None, seed: int = 3, fused: Optional[bool] = None, peer: bool = True):
+                 rank: int = 0, group=None, seed: int = 3, fused: Optional[bool] = None, peer: bool = True,
+                 fold: bool = True):
         if cfg.heads % world or cfg.kv_heads % world or cfg.inter % (128 * world) or cfg.vocab % world:
             raise ValueError(f"config does not shard over tp={world}")
         self.cfg, self.batch, self.max_ctx, self.device = cfg, batch, max_ctx, device
@@ -125,6 +126,15 @@ class DecodeModel:
             from .decode import PeerExchange
 
             self.peers = PeerExchange(batch, H, group)  # partial sums over NVLink, no NCCL in the layers
+        # whole layers with the RMSNorm input stages folded into the residual epilogues
+        # (single GPU, or the peer exchange: the all-reduce form has no residual epilogue)
+        self.fold = bool(fold) and self.fused and (world == 1 or self.peers is not None)
+        self.layer_descs = []
+        if self.fold:
+            from .decode import LayerDesc
+
+            self.layer_descs = [LayerDesc(L["ln1"], L["qkv"], L["o"], L["ln2"], L["gu"][0], L["gu"][1], L["down"])
+                                for L in self.layers]
 
     def fill_random_kv(self, ctx: int, seed: int = 11):
         g = torch.Generator(device=self.device)
@@ -165,6 +175,13 @@ class DecodeModel:
         h.copy_(self.embed[self.tokens].float())
         torch.sum(h * h, dim=-1, out=ss[0])
         pe = self.peers
+        if self.fold:
+            descs = self.layer_descs
+            for li, desc in enumerate(descs):
+                D.decode_layer(h, ss[0], ss[1], cfg.eps, desc, descs[li + 1] if li + 1 < len(descs) else None, li > 0,
+                               cfg.K, cfg.cb, self.k_cache[li], self.v_cache[li], self.pos, self.inv_freq, peers=pe)
+            self._finish(h)
+            return
         y = self.y if (self.world > 1 and pe is None) else None
         for li, L in enumerate(self.layers):
             D.decode_attention(h, ss[0], ss[1], L["ln1"], cfg.eps, L["qkv"], L["o"], cfg.K, cfg.cb,

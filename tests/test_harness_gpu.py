@@ -48,24 +48,7 @@ def test_graph_replay_matches_eager(cuda_device):
     torch.manual_seed(0)
     m = DecodeModel(TINY, batch=2, max_ctx=64, device=cuda_device)
     m.fill_random_kv(16)
-    m.tokens.copy_(torch.tensor([3, 7], device=cuda_device))
-    eager = []
-    kv0 = (m.k_cache.clone(), m.v_cache.clone())
-    for _ in range(4):
-        m.step()
-        eager.append(m.next_tokens.clone())
-    m.k_cache.copy_(kv0[0])
-    m.v_cache.copy_(kv0[1])
-    m.pos.fill_(16)
-    m.tokens.copy_(torch.tensor([3, 7], device=cuda_device))
-    m.capture()
-    m.pos.fill_(16)
-    m.tokens.copy_(torch.tensor([3, 7], device=cuda_device))
-    for i in range(4):
-        m.decode(1)
-        torch.cuda.synchronize()
-        assert torch.equal(m.next_tokens, eager[i])
-    m.release()
+    _replay_matches_eager(m, torch.tensor([3, 7], device=cuda_device), 16, 4)
 
 
 def _rel(a, b):
@@ -118,4 +101,39 @@ def test_generate_public_api(cuda_device):
     out = m.generate(torch.tensor([1]), 5)
     assert out.shape == (1, 5) and out.dtype == torch.long
     assert int(out.min()) >= 0 and int(out.max()) < TINY.vocab
+    m.release()
+
+
+def _replay_matches_eager(m, tokens0, pos0, steps):
+    """Eager steps, then the captured graph from the same state.  Each replay is fed the
+    eager step's input tokens.  The fused step is not bitwise repeatable: the order of
+    the fp32 atomic sums (split-K partials, the rows' sums of squares) moves values by
+    ulps, and where that flips the bf16 rounding of an appended K/V entry (2^-8) the
+    attention output follows - two eager runs of this model differ by ~1e-3 of the
+    residual stream.  So the residual stream must agree to 5e-3, the bf16 logits to
+    1e-2, and a greedy token may differ only at a near-tie."""
+    rel = lambda a, b: ((a.float() - b.float()).abs().max() / b.float().abs().max()).item()  # noqa: E731
+    kv0 = (m.k_cache.clone(), m.v_cache.clone())
+    m.pos.fill_(pos0)
+    m.tokens.copy_(tokens0)
+    eager = []
+    for _ in range(steps):
+        tin = m.tokens.clone()
+        m.step()
+        eager.append((tin, m.h.clone(), m.last_logits.float().clone(), m.next_tokens.clone()))
+    m.k_cache.copy_(kv0[0])
+    m.v_cache.copy_(kv0[1])
+    m.pos.fill_(pos0)
+    m.tokens.copy_(tokens0)
+    m.capture()
+    m.pos.fill_(pos0)
+    for tin, h, logits, tok in eager:
+        m.tokens.copy_(tin)
+        m.decode(1)
+        torch.cuda.synchronize()
+        assert rel(m.h, h) < 5e-3
+        assert rel(m.last_logits, logits) < 1e-2
+        top = logits.max(-1).values
+        picked = logits.gather(-1, m.next_tokens.view(-1, 1)).squeeze(-1)
+        assert bool(torch.all((m.next_tokens == tok) | (top - picked <= 2.0 ** -7 * top.abs())))
     m.release()
