@@ -1010,6 +1010,9 @@ EXTRA_WORKLOADS = [
     ("config 3 MoE layer T=64", dict(workload="moe", moe="c3", batch=64), False),
     ("config 3 MoE layer T=512", dict(workload="moe", moe="c3", batch=512), True),
     ("config 5 MoE layer, verify batch 64", dict(workload="moe", moe="c5", batch=64), True),
+    # config 4 at its other batch sizes (one GPU: the default line carries the TP scaling)
+    ("config 4 decode batch 8", dict(workload="decode", batch=8), False),
+    ("config 4 decode batch 64", dict(workload="decode", batch=64), False),
 ]
 
 
