@@ -124,3 +124,52 @@ def test_tensor_core_moe_and_combine_validation_without_gpu():
     assert comb(K=1) == _lib.EBADBITS
     assert comb(svh=f + 8) == _lib.EUNALIGNED
     assert comb(scb=0) == _lib.EWORKSPACE
+
+
+def test_decode_layer_validation_without_gpu():
+    """Whole-layer decode entry point: workspace sizes and the argument checks that run
+    before any CUDA call (fake device pointers, never dereferenced)."""
+    import ctypes
+
+    L = _lib.lib()
+    st, sc = ctypes.c_size_t(), ctypes.c_size_t()
+    ast, asc, mst, msc = (ctypes.c_size_t() for _ in range(4))
+    assert L.exl3b200_decode_layer_workspace(2, 512, 8, 2, 1024, 96, ctypes.byref(st), ctypes.byref(sc)) == 0
+    assert L.exl3b200_decode_attention_workspace(2, 512, 8, 2, 96, ctypes.byref(ast), ctypes.byref(asc)) == 0
+    assert L.exl3b200_decode_mlp_workspace(2, 512, 1024, ctypes.byref(mst), ctypes.byref(msc)) == 0
+    # one state and one scratch hold both sub-layers' (no aliasing) and the per-row pre-scale
+    assert st.value == ast.value + mst.value
+    assert sc.value == asc.value + msc.value + 256
+    for bad in ((17, 512, 8, 2, 1024, 96), (2, 500, 8, 2, 1024, 96), (2, 512, 8, 3, 1024, 96),
+                (2, 512, 34, 2, 1024, 96), (2, 512, 8, 2, 1000, 96), (2, 512, 8, 2, 1024, 0)):
+        assert L.exl3b200_decode_layer_workspace(*bad, ctypes.byref(st), ctypes.byref(sc)) == 1, bad
+    assert L.exl3b200_decode_layer_workspace(2, 512, 8, 2, 1024, 96, None, None) == 7
+
+    fake = 1 << 20  # 256-byte aligned, never dereferenced
+
+    def lin(k, n):
+        return _lib.Linear(fake, fake, fake, k, n)
+
+    lins = [lin(512, 1024), lin(512, 256), lin(512, 256), lin(1024, 512), lin(512, 1024), lin(512, 1024),
+            lin(1024, 512)]
+    q, k, v, o, g, u, d = (ctypes.addressof(x) for x in lins)
+    layer = _lib.DecodeLayer(fake, q, k, v, o, fake, g, u, d)
+    L.exl3b200_decode_layer_workspace(2, 512, 8, 2, 1024, 96, ctypes.byref(st), ctypes.byref(sc))
+
+    def step(layer_p, next_p=None, state_n=None, scratch_n=None, ss_a=fake, rows=2):
+        return L.exl3b200_decode_layer_step(
+            rows, 1, 512, 8, 2, 1024, 4, 0, fake, 512, ss_a, fake, 1e-5, layer_p, next_p, 0, fake, fake, 96, fake,
+            fake, 0.0, None, fake, st.value if state_n is None else state_n, fake,
+            sc.value if scratch_n is None else scratch_n, None)
+
+    assert step(None) == 7                                     # no layer
+    assert step(ctypes.byref(layer), ss_a=None) == 7           # no sum-of-squares buffer
+    assert step(ctypes.byref(layer), scratch_n=sc.value - 1) == 6  # workspace too small
+    assert step(ctypes.byref(layer), rows=17) == 1             # more rows than the small-M kernels take
+    wrong_gate = _lib.DecodeLayer(fake, q, k, v, o, fake, ctypes.addressof(lins[3]), u, d)
+    assert step(ctypes.byref(wrong_gate)) == 1                 # gate is not hidden -> inter
+    no_norm = _lib.DecodeLayer(0, q, k, v, o, fake, g, u, d)
+    assert step(ctypes.byref(layer), ctypes.byref(no_norm)) == 7  # next layer without its norm weight
+    wrong_q = _lib.DecodeLayer(fake, ctypes.addressof(lins[3]), k, v, o, fake, g, u, d)
+    assert step(ctypes.byref(layer), ctypes.byref(wrong_q)) == 1  # next layer's q shape
+

@@ -46,7 +46,9 @@ def _torch_step(model, tokens, pos):
 
 def test_graph_replay_matches_eager(cuda_device):
     torch.manual_seed(0)
-    m = DecodeModel(TINY, batch=2, max_ctx=64, device=cuda_device)
+    # O(1) activations, as a served model has them: the untamed random model's residual
+    # stream reaches ~1e4 and its run-to-run spread is larger than the tolerance
+    m = _tame(DecodeModel(TINY, batch=2, max_ctx=64, device=cuda_device))
     m.fill_random_kv(16)
     _replay_matches_eager(m, torch.tensor([3, 7], device=cuda_device), 16, 4)
 
