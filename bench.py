@@ -962,11 +962,11 @@ def run_decode(args, world, rank, local, device):
                 "h2d_bytes_per_step": 8 * batch, "d2h_bytes_per_step": 8 * batch + 4,
                 "path": "DecodeModel.generate: per step, tokens H2D from pinned host memory, graph replay, tokens "
                         "and the device status word D2H, stream sync"},
-        # fused: per layer 6 (attention) + 5 (MLP) launches (the NVLink exchange runs inside the o/down
-        # epilogues); + 2 residual-add kernels per layer when TP goes through NCCL instead; with the
-        # norm fold 9 per layer and the first layer's input stage
-        "gpu_launches": steps * ((9 * cfg.layers + 1) if model.fold else
-                                 cfg.layers * ((11 + (2 if world > 1 and not peer_exchange else 0))
+        # fused: per layer 5 (attention, whose kernel also finishes q/k/v) + 5 (MLP) launches (the
+        # NVLink exchange runs inside the o/down epilogues); + 2 residual-add kernels per layer when
+        # TP goes through NCCL instead; with the norm fold 8 per layer and the first layer's input stage
+        "gpu_launches": steps * ((8 * cfg.layers + 1) if model.fold else
+                                 cfg.layers * ((10 + (2 if world > 1 and not peer_exchange else 0))
                                                if model.fused else 12)),
         "clocks": clk.summary(),
     }

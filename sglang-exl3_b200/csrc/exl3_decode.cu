@@ -1,7 +1,7 @@
 // Fused decode layer around the EXL3 small-M matmul: the glue of a Llama-style
 // decoder layer (RMSNorm, RoPE, KV-cache append, attention, residual adds,
 // SwiGLU) moved into the matmul pipeline's own input stages and epilogues, so a
-// decode step runs eleven kernels per layer instead of ~75 (nine with the norm fold).
+// decode step runs ten kernels per layer instead of ~75 (eight with the norm fold).
 //
 // Attention sub-layer (exl3b200_decode_attention), all launches chained by
 // programmatic dependent launch:
@@ -13,7 +13,8 @@
 //   3. epilogue, RoPE/KV mode: each (row, head) block of q and k is rotated
 //      (rotate-half pairs (d, d+64) sit in one lane of the warp-wide H128 layout),
 //      q is stored scaled by 1/sqrt(head_dim), k and v are appended to the bf16
-//      cache at the current position;
+//      cache at the current position - with one row per sequence done by the
+//      attention kernel's own warps (its cluster's blocks) instead of a kernel;
 //   4. split-K attention on the tensor cores: one thread-block cluster of up to
 //      16 CTAs per (row, kv head); each CTA takes every 16th 64-position chunk
 //      through a three-buffer cp.async ring whose first fill is requested before
@@ -45,7 +46,7 @@
 // residual epilogues: the attention's residual epilogue writes the MLP's gate/up
 // inputs and the MLP's writes the next layer's q/k/v inputs, pre-scaled by the row's
 // norm factor before the add; the RoPE and SwiGLU epilogues multiply by the ratio of
-// the exact factor to it.  Nine kernels per layer instead of eleven.
+// the exact factor to it.  Eight kernels per layer instead of ten.
 //
 // The reference has no decode-layer fusion (its layers call SGLang's norm,
 // attention and activation kernels around the EXL3 ops); the arithmetic of each
@@ -220,8 +221,15 @@ __device__ __forceinline__ void split_bf16(float a, float b, uint32_t& hi, uint3
 // memory), normalises, rounds to fp16 and writes the o projection's rotated input
 // (`ob` problem 0); the second barrier keeps every partial alive until then.
 // Every CTA reaches both barriers (the only early exit is grid-uniform).
+// With one row per sequence (qkv.nprob = 3) the kernel also does the RoPE/KV
+// epilogue's work for its own (row, kv head) - the group's q head blocks and the k
+// and v blocks, one warp each, read from the q/k/v matmul's partial sums - and a
+// cluster barrier (release / acquire) makes q and the new K/V row visible to the
+// cluster: one kernel fewer per layer.  (Several rows per sequence need every row's
+// K/V before any row attends, across clusters; they keep the separate epilogue.)
 __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __grid_constant__ GvArgs ob,
-                                                                     const __grid_constant__ DecAux x, int csize)
+                                                                     const __grid_constant__ DecAux x, int csize,
+                                                                     const __grid_constant__ GvArgs qkv, int qkv_cb)
 {
     griddep_launch();
     extern __shared__ __align__(128) unsigned char attn_smem_raw[];
@@ -236,8 +244,12 @@ __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __gri
     // *pos .. *pos + rows_per_seq - 1 come from the RoPE epilogue this kernel depends on
     const long long pos0 = *x.pos;
     const long long pos = pos0 + b % x.rows_per_seq;
-    if (pos0 < 0 || pos >= x.max_ctx) return;  // cluster-uniform; recorded in the device status by the RoPE epilogue
-    const int L = (int) pos + 1;
+    const bool fused = qkv.nprob > 0;
+    // a position past the cache: cluster-uniform; recorded in the device status by the
+    // RoPE/KV epilogue's code (here, or in the separate kernel)
+    const bool bad = pos0 < 0 || pos >= x.max_ctx;
+    if (bad && !fused) return;
+    const int L = bad ? 0 : (int) pos + 1;
     const int nch = (L + kDecChunk - 1) / kDecChunk;
     const int nloc = rank < nch ? (nch - 1 - rank) / csize + 1 : 0;
     const int group = x.q_heads / x.kv_heads;
@@ -246,6 +258,13 @@ __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __gri
     const GvProblem& po = gv_prob(ob, 0);
     if (tid < 2 * group && (tid >> 1) % csize == rank && po.suh)  // into L2: the o input scales of this rank's heads
         prefetch_l2_256(po.suh + (size_t) (kvh * group + (tid >> 1)) * 128, tid & 1);
+    // fused: the q/k/v blocks of this warp - task tk < group is q head kvh * group + tk,
+    // then k and v of head kvh; their output scales into L2 before the wait
+    const int ntask = fused ? group + 2 : 0;
+    for (int tk = rank * kAttnWarps + warp; tk < ntask; tk += kAttnWarps * csize) {
+        const int pi = tk < group ? 0 : tk - group + 1;
+        prefetch_l2_256(gv_prob(qkv, pi).svh + (size_t) (pi == 0 ? kvh * group + tk : kvh) * 128, lane);
+    }
 
     const size_t hbase = (size_t) (b / x.rows_per_seq) * x.cache_b_stride + (size_t) kvh * x.cache_h_stride;
     // local chunk i -> buffer; rows >= its length are zero-filled; rows at positions
@@ -268,7 +287,20 @@ __global__ __launch_bounds__(kAttnThreads) void exl3_dec_attn_kernel(const __gri
     // pos0 .. pos (this step's, from the RoPE epilogue) after the wait
     const int nfirst = min(nloc, kAttnBufs);
     for (int i = 0; i < nfirst; ++i) stage(i, i, pos0);
-    griddep_wait();  // q (scaled) and the new K/V rows come from the RoPE epilogue
+    griddep_wait();  // q (scaled) and the new K/V rows come from the RoPE epilogue, or the q/k/v matmul
+    if (fused) {
+        for (int tk = rank * kAttnWarps + warp; tk < ntask; tk += kAttnWarps * csize) {
+            const int pi = tk < group ? 0 : tk - group + 1;
+            const int nb = pi == 0 ? kvh * group + tk : kvh;
+            const GvProblem& pp = gv_prob(qkv, pi);
+            if (qkv_cb == 2) epi_block_row<2>(qkv, x, kEpiRopeKV, pi, pp, nullptr, nb, b, lane);
+            else epi_block_row<0>(qkv, x, kEpiRopeKV, pi, pp, nullptr, nb, b, lane);
+        }
+        if (x.zero_ss && blockIdx.x == 0)  // the norm fold's duty of the skipped epilogue
+            for (int i = tid; i < x.zero_rows; i += kAttnThreads) x.zero_ss[i] = 0.f;
+        cluster.sync();  // release / acquire at cluster scope: the cluster's q and new K/V row are written
+        if (bad) return;
+    }
     for (int i = 0; i < nfirst; ++i) {
         const int p0 = (rank + i * csize) * kDecChunk;
         const int np = min(kDecChunk, L - p0);
@@ -692,7 +724,8 @@ static int dec_attn_setup(int max_chunks, int* csize)
     return kErrLaunch;
 }
 
-static int dec_launch_attn(const GvArgs& ob, const DecAux& x, int groups, cudaStream_t stream)
+static int dec_launch_attn(const GvArgs& ob, const DecAux& x, int groups, cudaStream_t stream,
+                           const GvArgs* qkv = nullptr, int qkv_cb = 0)
 {
     int csize = 1;
     const int rc = dec_attn_setup((x.max_ctx + kDecChunk - 1) / kDecChunk, &csize);
@@ -711,7 +744,10 @@ static int dec_launch_attn(const GvArgs& ob, const DecAux& x, int groups, cudaSt
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, exl3_dec_attn_kernel, ob, x, csize) == cudaSuccess ? kOk : kErrLaunch;
+    GvArgs none = {};  // nprob 0: q, k and v were finished by the RoPE/KV epilogue
+    return cudaLaunchKernelEx(&cfg, exl3_dec_attn_kernel, ob, x, csize, qkv ? *qkv : none, qkv_cb) == cudaSuccess
+               ? kOk
+               : kErrLaunch;
 }
 
 static int dec_grid(int tasks) { return std::min((tasks + 7) / 8, 8 * gv_sm_count()); }
@@ -1052,8 +1088,12 @@ static int dec_attention(int batch, int rows_per_seq, int hidden, int q_heads, i
     }
     rc = gv_launch_matmul(a, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
-    rc = dec_launch_epilogue<kEpiRopeKV>(a, xe, cb, st);
-    if (rc != kOk) return rc;
+    // one row per sequence: the attention kernel finishes q/k/v itself
+    const bool rope_in_attn = rows_per_seq == 1;
+    if (!rope_in_attn) {
+        rc = dec_launch_epilogue<kEpiRopeKV>(a, xe, cb, st);
+        if (rc != kOk) return rc;
+    }
 
     // 4: attention (a cluster per row and kv head; its merge writes the o input)
     GvArgs b = {};
@@ -1061,7 +1101,8 @@ static int dec_attention(int batch, int rows_per_seq, int hidden, int q_heads, i
     dec_problem(b.inl[0], o, batch, reinterpret_cast<uint32_t*>(W + L.xd_o),
                 mul1 ? reinterpret_cast<float*>(W + L.sb_o) : nullptr, reinterpret_cast<float*>(S + L.st_o));
     gv_prefix_inline(b);
-    rc = dec_launch_attn(b, x, batch * kv_heads, st);
+    rc = rope_in_attn ? dec_launch_attn(b, xe, batch * kv_heads, st, &a, cb == 2 ? 2 : 0)
+                      : dec_launch_attn(b, x, batch * kv_heads, st);
     if (rc != kOk) return rc;
 
     // 5-6: o matmul, residual (or fp32 partial for the all-reduce)
