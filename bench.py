@@ -944,6 +944,7 @@ def run_decode(args, world, rank, local, device):
     torch.cuda.nvtx.range_pop()
     torch.cuda.current_stream(device).wait_stream(s)
     peer_exchange = model.peers is not None
+    rope_kernel = 0 if batch * model.hkv <= 8 else 1  # a separate RoPE/KV epilogue per layer
     kbytes = 2 * (cfg.hidden * model.i_loc * cfg.K // 8) + 2 * batch * (cfg.hidden + 2 * model.i_loc)
     k_gbs = kbytes / (kt * 1e-3) / 1e9
     del g
@@ -962,11 +963,12 @@ def run_decode(args, world, rank, local, device):
                 "h2d_bytes_per_step": 8 * batch, "d2h_bytes_per_step": 8 * batch + 4,
                 "path": "DecodeModel.generate: per step, tokens H2D from pinned host memory, graph replay, tokens "
                         "and the device status word D2H, stream sync"},
-        # fused: per layer 5 (attention, whose kernel also finishes q/k/v) + 5 (MLP) launches (the
-        # NVLink exchange runs inside the o/down epilogues); + 2 residual-add kernels per layer when
-        # TP goes through NCCL instead; with the norm fold 8 per layer and the first layer's input stage
-        "gpu_launches": steps * ((8 * cfg.layers + 1) if model.fold else
-                                 cfg.layers * ((10 + (2 if world > 1 and not peer_exchange else 0))
+        # fused: per layer 5 (attention, whose kernel also finishes q/k/v when all its clusters are
+        # resident at once - batch 1 - else + the RoPE/KV epilogue) + 5 (MLP) launches (the NVLink
+        # exchange runs inside the o/down epilogues); + 2 residual-add kernels per layer when TP goes
+        # through NCCL instead; with the norm fold 8 per layer and the first layer's input stage
+        "gpu_launches": steps * (((8 + rope_kernel) * cfg.layers + 1) if model.fold else
+                                 cfg.layers * ((10 + rope_kernel + (2 if world > 1 and not peer_exchange else 0))
                                                if model.fused else 12)),
         "clocks": clk.summary(),
     }

@@ -13,8 +13,9 @@
 //   3. epilogue, RoPE/KV mode: each (row, head) block of q and k is rotated
 //      (rotate-half pairs (d, d+64) sit in one lane of the warp-wide H128 layout),
 //      q is stored scaled by 1/sqrt(head_dim), k and v are appended to the bf16
-//      cache at the current position - with one row per sequence done by the
-//      attention kernel's own warps (its cluster's blocks) instead of a kernel;
+//      cache at the current position - with one row per sequence and every
+//      cluster resident at once, done by the attention kernel's own warps (its
+//      cluster's blocks) instead of a kernel;
 //   4. split-K attention on the tensor cores: one thread-block cluster of up to
 //      16 CTAs per (row, kv head); each CTA takes every 16th 64-position chunk
 //      through a three-buffer cp.async ring whose first fill is requested before
@@ -680,10 +681,11 @@ static int dec_launch(Kern kern, int grid, int block, cudaStream_t stream, Args.
 // The attention kernel: shared memory beyond the 48 KB default and clusters of up
 // to 16 CTAs (beyond the portable 8), set once per device; the cluster size is the
 // largest power of two <= min(16, chunks of the cache) that the device can hold.
-static int dec_attn_setup(int max_chunks, int* csize)
+static int dec_attn_setup(int max_chunks, int* csize, int* max_clusters = nullptr)
 {
     static int done[64] = {0};
-    static int fits[64][5] = {{0}};  // per device, cluster size 1, 2, 4, 8, 16: 0 unknown, 1 yes, 2 no
+    static int fits[64][5] = {{0}};    // per device, cluster size 1, 2, 4, 8, 16: 0 unknown, 1 yes, 2 no
+    static int resident[64][5] = {{0}};  // clusters of that size the device holds at once
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kErrLaunch;
     if (!done[dev]) {
@@ -715,9 +717,11 @@ static int dec_attn_setup(int max_chunks, int* csize)
             int n = 0;
             fits[dev][li] = (cudaOccupancyMaxActiveClusters(&n, exl3_dec_attn_kernel, &cfg) == cudaSuccess && n > 0)
                                 ? 1 : 2;
+            resident[dev][li] = n;
         }
         if (fits[dev][li] == 1) {
             *csize = c;
+            if (max_clusters) *max_clusters = resident[dev][li];
             return kOk;
         }
     }
@@ -1088,8 +1092,14 @@ static int dec_attention(int batch, int rows_per_seq, int hidden, int q_heads, i
     }
     rc = gv_launch_matmul(a, K, cb, batch, 0, true, st);
     if (rc != kOk) return rc;
-    // one row per sequence: the attention kernel finishes q/k/v itself
-    const bool rope_in_attn = rows_per_seq == 1;
+    // one row per sequence and every cluster resident at once: the attention kernel
+    // finishes q/k/v itself (with more clusters than one wave, each later wave would
+    // pay the finishing round trips again; the separate epilogue spreads them over
+    // the whole GPU once)
+    int csize = 1, max_clusters = 0;
+    rc = dec_attn_setup((max_ctx + kDecChunk - 1) / kDecChunk, &csize, &max_clusters);
+    if (rc != kOk) return rc;
+    const bool rope_in_attn = rows_per_seq == 1 && batch * kv_heads <= max_clusters;
     if (!rope_in_attn) {
         rc = dec_launch_epilogue<kEpiRopeKV>(a, xe, cb, st);
         if (rc != kOk) return rc;
